@@ -1,0 +1,229 @@
+"""Model architecture configs and the named presets.
+
+The presets are the architectures of the benchmark configurations: a tiny
+Qwen3-style decoder, Qwen2.5-7B, Qwen3-30B-A3B (MoE), a Qwen3-Next-style
+hybrid (gated DeltaNet + full attention + MoE) and Qwen3-32B.  Field names
+follow the Hugging Face config keys so an HF ``config.json`` maps directly
+(:meth:`ModelConfig.from_hf_dict`).
+"""
+
+from __future__ import annotations
+
+from dataclasses import asdict, dataclass, replace
+from typing import Any, Literal
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    name: str
+    family: Literal["qwen2", "qwen3", "qwen3_moe", "qwen3_next"]
+    vocab_size: int
+    hidden_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    head_dim: int
+    intermediate_size: int
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e6
+    max_position_embeddings: int = 131072
+    attention_bias: bool = False  # Qwen2: bias on q/k/v
+    qk_norm: bool = False  # Qwen3: RMSNorm over head_dim on q and k
+    tie_word_embeddings: bool = False
+    sliding_window: int | None = None
+    # MoE
+    num_experts: int = 0
+    num_experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    norm_topk_prob: bool = True
+    shared_expert_intermediate_size: int = 0
+    # hybrid linear attention (gated DeltaNet)
+    full_attention_interval: int = 0  # every k-th layer is full attention; 0 = all full
+    linear_num_key_heads: int = 0
+    linear_num_value_heads: int = 0
+    linear_key_head_dim: int = 0
+    linear_value_head_dim: int = 0
+    linear_conv_kernel_dim: int = 4
+    linear_chunk_size: int = 64
+    attn_output_gate: bool = False
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    def layer_kind(self, i: int) -> Literal["attention", "linear_attention"]:
+        if self.full_attention_interval and (i + 1) % self.full_attention_interval != 0:
+            return "linear_attention"
+        return "attention"
+
+    @property
+    def q_size(self) -> int:
+        return self.num_attention_heads * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return self.num_key_value_heads * self.head_dim
+
+    def to_dict(self) -> dict[str, Any]:
+        return asdict(self)
+
+    def scaled(self, **kw: Any) -> "ModelConfig":
+        return replace(self, **kw)
+
+    @classmethod
+    def from_hf_dict(cls, d: dict[str, Any], name: str = "custom") -> "ModelConfig":
+        mt = d.get("model_type", "qwen3")
+        family = {"qwen2": "qwen2", "qwen3": "qwen3", "qwen3_moe": "qwen3_moe", "qwen3_next": "qwen3_next"}.get(mt, "qwen3")
+        heads = d["num_attention_heads"]
+        return cls(
+            name=name,
+            family=family,  # type: ignore[arg-type]
+            vocab_size=d["vocab_size"],
+            hidden_size=d["hidden_size"],
+            num_hidden_layers=d["num_hidden_layers"],
+            num_attention_heads=heads,
+            num_key_value_heads=d.get("num_key_value_heads", heads),
+            head_dim=d.get("head_dim") or d["hidden_size"] // heads,
+            intermediate_size=d.get("intermediate_size", 0),
+            rms_norm_eps=d.get("rms_norm_eps", 1e-6),
+            rope_theta=d.get("rope_theta", 1e6),
+            attention_bias=family == "qwen2" or d.get("attention_bias", False),
+            qk_norm=family in ("qwen3", "qwen3_moe", "qwen3_next"),
+            tie_word_embeddings=d.get("tie_word_embeddings", False),
+            num_experts=d.get("num_experts", 0),
+            num_experts_per_tok=d.get("num_experts_per_tok", 0),
+            moe_intermediate_size=d.get("moe_intermediate_size", 0),
+            norm_topk_prob=d.get("norm_topk_prob", True),
+            shared_expert_intermediate_size=d.get("shared_expert_intermediate_size", 0),
+            full_attention_interval=d.get("full_attention_interval", 0),
+            linear_num_key_heads=d.get("linear_num_key_heads", 0),
+            linear_num_value_heads=d.get("linear_num_value_heads", 0),
+            linear_key_head_dim=d.get("linear_key_head_dim", 0),
+            linear_value_head_dim=d.get("linear_value_head_dim", 0),
+            linear_conv_kernel_dim=d.get("linear_conv_kernel_dim", 4),
+        )
+
+
+PRESETS: dict[str, ModelConfig] = {
+    "tiny-qwen3": ModelConfig(
+        name="tiny-qwen3",
+        family="qwen3",
+        vocab_size=1024,
+        hidden_size=256,
+        num_hidden_layers=4,
+        num_attention_heads=4,
+        num_key_value_heads=2,
+        head_dim=64,
+        intermediate_size=704,
+        qk_norm=True,
+    ),
+    "qwen2.5-7b": ModelConfig(
+        name="qwen2.5-7b",
+        family="qwen2",
+        vocab_size=152064,
+        hidden_size=3584,
+        num_hidden_layers=28,
+        num_attention_heads=28,
+        num_key_value_heads=4,
+        head_dim=128,
+        intermediate_size=18944,
+        attention_bias=True,
+    ),
+    "qwen3-30b-a3b": ModelConfig(
+        name="qwen3-30b-a3b",
+        family="qwen3_moe",
+        vocab_size=151936,
+        hidden_size=2048,
+        num_hidden_layers=48,
+        num_attention_heads=32,
+        num_key_value_heads=4,
+        head_dim=128,
+        intermediate_size=6144,
+        qk_norm=True,
+        num_experts=128,
+        num_experts_per_tok=8,
+        moe_intermediate_size=768,
+    ),
+    "qwen3-next-hybrid": ModelConfig(
+        name="qwen3-next-hybrid",
+        family="qwen3_next",
+        vocab_size=151936,
+        hidden_size=2048,
+        num_hidden_layers=48,
+        num_attention_heads=16,
+        num_key_value_heads=2,
+        head_dim=128,
+        intermediate_size=5120,
+        qk_norm=True,
+        num_experts=512,
+        num_experts_per_tok=10,
+        moe_intermediate_size=512,
+        shared_expert_intermediate_size=512,
+        full_attention_interval=4,
+        linear_num_key_heads=16,
+        linear_num_value_heads=16,
+        linear_key_head_dim=128,
+        linear_value_head_dim=128,
+        attn_output_gate=True,
+    ),
+    "qwen3-32b": ModelConfig(
+        name="qwen3-32b",
+        family="qwen3",
+        vocab_size=151936,
+        hidden_size=5120,
+        num_hidden_layers=64,
+        num_attention_heads=64,
+        num_key_value_heads=8,
+        head_dim=128,
+        intermediate_size=25600,
+        qk_norm=True,
+    ),
+}
+
+# Hugging Face ids that map onto a preset shape (weights are random-init here).
+HF_ALIASES = {
+    "Qwen/Qwen2.5-7B-Instruct": "qwen2.5-7b",
+    "Qwen/Qwen2.5-7B": "qwen2.5-7b",
+    "Qwen/Qwen3-30B-A3B": "qwen3-30b-a3b",
+    "Qwen/Qwen3-30B-A3B-Instruct-2507": "qwen3-30b-a3b",
+    "Qwen/Qwen3-Next-80B-A3B-Instruct": "qwen3-next-hybrid",
+    "Qwen/Qwen3-32B": "qwen3-32b",
+}
+
+
+def get_config(name: str) -> ModelConfig:
+    key = HF_ALIASES.get(name, name)
+    if key not in PRESETS:
+        raise KeyError(f"unknown model preset {name!r}; known: {sorted(PRESETS)}")
+    return PRESETS[key]
+
+
+@dataclass(frozen=True)
+class LoRASpec:
+    r: int = 8
+    alpha: int = 16
+    target_modules: tuple[str, ...] = (
+        "q_proj",
+        "k_proj",
+        "v_proj",
+        "o_proj",
+        "gate_proj",
+        "up_proj",
+        "down_proj",
+    )
+    # MoE experts carry LoRA on their gate/up/down; the GDN in/out projections
+    # on ``in_proj_qkvz``/``in_proj_ba``/``out_proj`` when targeted.
+    expert_targets: tuple[str, ...] = ("gate_proj", "up_proj", "down_proj")
+
+    @property
+    def scale(self) -> float:
+        return self.alpha / self.r
+
+    @classmethod
+    def from_peft(cls, d: dict[str, Any]) -> "LoRASpec":
+        return cls(
+            r=int(d.get("r", 8)),
+            alpha=int(d.get("lora_alpha", 16)),
+            target_modules=tuple(d.get("target_modules") or cls.target_modules),
+        )
+

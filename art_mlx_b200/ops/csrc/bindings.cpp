@@ -1,0 +1,50 @@
+// Python bindings of the art_mlx_b200 native kernels.
+#include <torch/extension.h>
+
+namespace art {
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> res,
+                                       torch::Tensor w, double eps);
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor xs, torch::Tensor w, torch::Tensor rstd,
+                          c10::optional<torch::Tensor> dres);
+std::vector<torch::Tensor> rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
+                                    int64_t nq, int64_t nkv, int64_t D,
+                                    c10::optional<torch::Tensor> qn_w,
+                                    c10::optional<torch::Tensor> kn_w, double eps);
+void rope_bwd(torch::Tensor dqk, torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
+              int64_t nq, int64_t nkv, int64_t D, c10::optional<torch::Tensor> qn_w,
+              c10::optional<torch::Tensor> kn_w, c10::optional<torch::Tensor> rstd,
+              torch::Tensor dqkv);
+torch::Tensor swiglu_fwd(torch::Tensor gu);
+torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu);
+std::vector<torch::Tensor> logits_stats(torch::Tensor logits, torch::Tensor targets, bool entropy);
+void logits_grad_(torch::Tensor logits, torch::Tensor targets, torch::Tensor lse, torch::Tensor g);
+std::vector<torch::Tensor> grpo_token_loss(torch::Tensor newlp, torch::Tensor oldlp,
+                                           torch::Tensor adv, torch::Tensor w, torch::Tensor mask,
+                                           c10::optional<torch::Tensor> reflp,
+                                           c10::optional<torch::Tensor> origlp, torch::Tensor cfg);
+torch::Tensor grad_sumsq(torch::Tensor g);
+void adamw_step(torch::Tensor p, torch::Tensor p16, torch::Tensor g, torch::Tensor m,
+                torch::Tensor v, torch::Tensor hp, torch::Tensor norm_sq, torch::Tensor norm_out);
+std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                    torch::Tensor kend, torch::Tensor tile_kmax, double scale);
+torch::Tensor attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                       torch::Tensor out, torch::Tensor lse, torch::Tensor kend,
+                       torch::Tensor tile_kmax, double scale, torch::Tensor dk, torch::Tensor dv);
+}  // namespace art
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "art_mlx_b200 sm_100a kernels";
+  m.def("rmsnorm_fwd", &art::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &art::rmsnorm_bwd);
+  m.def("rope_fwd", &art::rope_fwd);
+  m.def("rope_bwd", &art::rope_bwd);
+  m.def("swiglu_fwd", &art::swiglu_fwd);
+  m.def("swiglu_bwd", &art::swiglu_bwd);
+  m.def("logits_stats", &art::logits_stats);
+  m.def("logits_grad_", &art::logits_grad_);
+  m.def("grpo_token_loss", &art::grpo_token_loss);
+  m.def("grad_sumsq", &art::grad_sumsq);
+  m.def("adamw_step", &art::adamw_step);
+  m.def("attn_fwd", &art::attn_fwd);
+  m.def("attn_bwd", &art::attn_bwd);
+}

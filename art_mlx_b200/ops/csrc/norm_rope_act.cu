@@ -1,0 +1,452 @@
+// RMSNorm (+ fused residual add), qk-RMSNorm + RoPE on packed positions, and
+// SwiGLU, forward and backward.  All memory-bound: one pass over the data,
+// 16-byte vector accesses, fp32 math, bf16 storage.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include "common.cuh"
+
+namespace art {
+
+// ----------------------------------------------------------------------------
+// RMSNorm.  y = x_sum * rstd * w, x_sum = x (+ residual).  One CTA per row.
+// The base-model norm weights are frozen, so the backward returns dx only.
+// ----------------------------------------------------------------------------
+template <int VEC>
+__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
+                                   const __nv_bfloat16* __restrict__ res,
+                                   const __nv_bfloat16* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ y,
+                                   __nv_bfloat16* __restrict__ xsum,
+                                   float* __restrict__ rstd, int H, float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * H;
+  const __nv_bfloat16* rr = res ? res + row * H : nullptr;
+  float acc = 0.f;
+  // pass 1: sum of squares (values kept in registers when they fit)
+  constexpr int MAXV = 8;  // up to 8 vectors of 8 elements per thread (H <= 8*8*blockDim)
+  float vals[MAXV][VEC];
+  int nv = 0;
+  for (int base = threadIdx.x * VEC; base < H; base += blockDim.x * VEC, ++nv) {
+    uint4 xv = *reinterpret_cast<const uint4*>(xr + base);
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
+    uint4 rv;
+    const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv);
+    if (rr) rv = *reinterpret_cast<const uint4*>(rr + base);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      float v = bf2f(xe[k]);
+      if (rr) v = bf2f(f2bf(v + bf2f(re[k])));  // residual stream is stored in bf16
+      vals[nv][k] = v;
+      acc += v * v;
+    }
+  }
+  float ss = block_sum(acc, red);
+  float r = rsqrtf(ss / H + eps);
+  if (threadIdx.x == 0) rstd[row] = r;
+  nv = 0;
+  for (int base = threadIdx.x * VEC; base < H; base += blockDim.x * VEC, ++nv) {
+    uint4 wv = *reinterpret_cast<const uint4*>(w + base);
+    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+    uint4 out, sumv;
+    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&out);
+    __nv_bfloat16* se = reinterpret_cast<__nv_bfloat16*>(&sumv);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      // HF order: normalise in fp32, cast to bf16, then scale by the weight
+      float n = bf2f(f2bf(vals[nv][k] * r));
+      oe[k] = f2bf(n * bf2f(we[k]));
+      se[k] = f2bf(vals[nv][k]);
+    }
+    *reinterpret_cast<uint4*>(y + row * H + base) = out;
+    if (xsum) *reinterpret_cast<uint4*>(xsum + row * H + base) = sumv;
+  }
+}
+
+// dx = rstd * (w*dy - xhat * mean(w*dy*xhat)) (+ dres)
+template <int VEC>
+__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
+                                   const __nv_bfloat16* __restrict__ xs,
+                                   const __nv_bfloat16* __restrict__ w,
+                                   const float* __restrict__ rstd,
+                                   const __nv_bfloat16* __restrict__ dres,
+                                   __nv_bfloat16* __restrict__ dx, int H) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const float r = rstd[row];
+  constexpr int MAXV = 8;
+  float g[MAXV][VEC], xh[MAXV][VEC];
+  float acc = 0.f;
+  int nv = 0;
+  for (int base = threadIdx.x * VEC; base < H; base += blockDim.x * VEC, ++nv) {
+    uint4 dv = *reinterpret_cast<const uint4*>(dy + row * H + base);
+    uint4 xv = *reinterpret_cast<const uint4*>(xs + row * H + base);
+    uint4 wv = *reinterpret_cast<const uint4*>(w + base);
+    const __nv_bfloat16* de = reinterpret_cast<const __nv_bfloat16*>(&dv);
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
+    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      g[nv][k] = bf2f(de[k]) * bf2f(we[k]);
+      xh[nv][k] = bf2f(xe[k]) * r;
+      acc += g[nv][k] * xh[nv][k];
+    }
+  }
+  const float mean = block_sum(acc, red) / H;
+  nv = 0;
+  for (int base = threadIdx.x * VEC; base < H; base += blockDim.x * VEC, ++nv) {
+    uint4 out;
+    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&out);
+    uint4 rv;
+    const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv);
+    if (dres) rv = *reinterpret_cast<const uint4*>(dres + row * H + base);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      float v = r * (g[nv][k] - xh[nv][k] * mean);
+      if (dres) v += bf2f(re[k]);
+      oe[k] = f2bf(v);
+    }
+    *reinterpret_cast<uint4*>(dx + row * H + base) = out;
+  }
+}
+
+static int norm_threads(int H) {
+  int t = (H / 8 + 7) / 8;  // 8 vectors of 8 per thread at most
+  t = ((t + 31) / 32) * 32;
+  if (t < 64) t = 64;
+  if (t > 1024) t = 1024;
+  return t;
+}
+
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> res,
+                                       torch::Tensor w, double eps) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous());
+  const int H = x.size(-1);
+  TORCH_CHECK(H % 8 == 0 && H <= 8 * 8 * 1024, "rmsnorm: hidden size must be a multiple of 8");
+  const int64_t T = x.numel() / H;
+  auto y = torch::empty_like(x);
+  auto rstd = torch::empty({T}, x.options().dtype(at::kFloat));
+  torch::Tensor xs;
+  const __nv_bfloat16* rp = nullptr;
+  __nv_bfloat16* xsp = nullptr;
+  if (res.has_value()) {
+    TORCH_CHECK(res->is_contiguous() && res->sizes() == x.sizes());
+    xs = torch::empty_like(x);
+    rp = reinterpret_cast<const __nv_bfloat16*>(res->data_ptr());
+    xsp = reinterpret_cast<__nv_bfloat16*>(xs.data_ptr());
+  } else {
+    xs = x;
+  }
+  if (T > 0)
+    rmsnorm_fwd_kernel<8><<<T, norm_threads(H), 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), rp,
+        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), xsp, rstd.data_ptr<float>(), H, (float)eps);
+  ART_CUDA_CHECK(cudaGetLastError());
+  return {y, xs, rstd};
+}
+
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor xs, torch::Tensor w, torch::Tensor rstd,
+                          c10::optional<torch::Tensor> dres) {
+  TORCH_CHECK(dy.is_contiguous() && xs.is_contiguous());
+  const int H = dy.size(-1);
+  const int64_t T = dy.numel() / H;
+  auto dx = torch::empty_like(dy);
+  const __nv_bfloat16* dr = nullptr;
+  if (dres.has_value()) {
+    TORCH_CHECK(dres->is_contiguous());
+    dr = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
+  }
+  if (T > 0)
+    rmsnorm_bwd_kernel<8><<<T, norm_threads(H), 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(xs.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), rstd.data_ptr<float>(), dr,
+        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), H);
+  ART_CUDA_CHECK(cudaGetLastError());
+  return dx;
+}
+
+// ----------------------------------------------------------------------------
+// qk-RMSNorm (optional) + RoPE (rotate-half convention) on packed positions.
+// Input: raw projection output qkv [T, (nq + 2*nkv) * D] (row stride ld).
+// Output: qk [T, (nq + nkv) * D] rotated q then k heads; rstd [T, nq + nkv].
+// One warp per (token, head); D in {64, 128, 256}.
+// ----------------------------------------------------------------------------
+template <int D>
+__global__ void rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld,
+                                const int* __restrict__ pos, const float* __restrict__ inv_freq,
+                                const __nv_bfloat16* __restrict__ qn_w,
+                                const __nv_bfloat16* __restrict__ kn_w,
+                                __nv_bfloat16* __restrict__ out, float* __restrict__ rstd_out,
+                                int64_t T, int nq, int nkv, float eps) {
+  constexpr int PER = D / 32;  // elements per lane; lane owns pairs (i, i + D/2)
+  const int nh = nq + nkv;
+  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x / 32);
+  const int lane = threadIdx.x & 31;
+  if (gw >= T * nh) return;
+  const int64_t t = gw / nh;
+  const int h = gw % nh;
+  const bool is_q = h < nq;
+  const __nv_bfloat16* src = qkv + t * ld + (int64_t)h * D;
+  const __nv_bfloat16* nw = is_q ? qn_w : kn_w;
+  // lane holds x[i] for i = lane*PER/2 .. and the rotation partner at +D/2
+  float a[PER / 2], b[PER / 2];
+#pragma unroll
+  for (int k = 0; k < PER / 2; ++k) {
+    a[k] = bf2f(src[lane * (PER / 2) + k]);
+    b[k] = bf2f(src[D / 2 + lane * (PER / 2) + k]);
+  }
+  float r = 1.f;
+  if (nw) {
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < PER / 2; ++k) ss += a[k] * a[k] + b[k] * b[k];
+    ss = warp_sum(ss);
+    r = rsqrtf(ss / D + eps);
+#pragma unroll
+    for (int k = 0; k < PER / 2; ++k) {
+      const int i = lane * (PER / 2) + k;
+      a[k] = bf2f(f2bf(a[k] * r)) * bf2f(nw[i]);
+      b[k] = bf2f(f2bf(b[k] * r)) * bf2f(nw[i + D / 2]);
+      a[k] = bf2f(f2bf(a[k]));
+      b[k] = bf2f(f2bf(b[k]));
+    }
+  }
+  if (rstd_out && lane == 0) rstd_out[t * nh + h] = r;
+  const float p = (float)pos[t];
+  __nv_bfloat16* dst = out + t * (int64_t)nh * D + (int64_t)h * D;
+#pragma unroll
+  for (int k = 0; k < PER / 2; ++k) {
+    const int i = lane * (PER / 2) + k;
+    float s, c;
+    sincosf(p * inv_freq[i], &s, &c);
+    dst[i] = f2bf(a[k] * c - b[k] * s);
+    dst[i + D / 2] = f2bf(b[k] * c + a[k] * s);
+  }
+}
+
+// Backward: dqk [T, nh*D] (bf16) -> writes dq, dk into dqkv [T, ld] columns of q and k.
+// Needs the raw (pre-norm) input to redo the norm when qk-norm is on.
+template <int D>
+__global__ void rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqk,
+                                const __nv_bfloat16* __restrict__ qkv, int64_t ld,
+                                const int* __restrict__ pos, const float* __restrict__ inv_freq,
+                                const __nv_bfloat16* __restrict__ qn_w,
+                                const __nv_bfloat16* __restrict__ kn_w,
+                                const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dqkv,
+                                int64_t T, int nq, int nkv) {
+  constexpr int PER = D / 32;
+  const int nh = nq + nkv;
+  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x / 32);
+  const int lane = threadIdx.x & 31;
+  if (gw >= T * nh) return;
+  const int64_t t = gw / nh;
+  const int h = gw % nh;
+  const bool is_q = h < nq;
+  const __nv_bfloat16* g = dqk + t * (int64_t)nh * D + (int64_t)h * D;
+  const float p = (float)pos[t];
+  float ga[PER / 2], gb[PER / 2];
+#pragma unroll
+  for (int k = 0; k < PER / 2; ++k) {
+    const int i = lane * (PER / 2) + k;
+    float s, c;
+    sincosf(p * inv_freq[i], &s, &c);
+    const float u = bf2f(g[i]), v = bf2f(g[i + D / 2]);
+    // transpose of the rotation
+    ga[k] = u * c + v * s;
+    gb[k] = v * c - u * s;
+  }
+  const __nv_bfloat16* nw = is_q ? qn_w : kn_w;
+  __nv_bfloat16* dst = dqkv + t * ld + (int64_t)h * D;
+  if (nw) {
+    const __nv_bfloat16* src = qkv + t * ld + (int64_t)h * D;
+    const float r = rstd[t * nh + h];
+    float xa[PER / 2], xb[PER / 2];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < PER / 2; ++k) {
+      const int i = lane * (PER / 2) + k;
+      xa[k] = bf2f(src[i]) * r;
+      xb[k] = bf2f(src[i + D / 2]) * r;
+      ga[k] *= bf2f(nw[i]);
+      gb[k] *= bf2f(nw[i + D / 2]);
+      dot += ga[k] * xa[k] + gb[k] * xb[k];
+    }
+    const float mean = warp_sum(dot) / D;
+#pragma unroll
+    for (int k = 0; k < PER / 2; ++k) {
+      const int i = lane * (PER / 2) + k;
+      dst[i] = f2bf(r * (ga[k] - xa[k] * mean));
+      dst[i + D / 2] = f2bf(r * (gb[k] - xb[k] * mean));
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < PER / 2; ++k) {
+      const int i = lane * (PER / 2) + k;
+      dst[i] = f2bf(ga[k]);
+      dst[i + D / 2] = f2bf(gb[k]);
+    }
+  }
+}
+
+#define ART_DISPATCH_HEAD_DIM(D, ...)                       \
+  [&] {                                                     \
+    if (D == 64) {                                          \
+      constexpr int kD = 64;                                \
+      return __VA_ARGS__();                                 \
+    } else if (D == 128) {                                  \
+      constexpr int kD = 128;                               \
+      return __VA_ARGS__();                                 \
+    } else if (D == 256) {                                  \
+      constexpr int kD = 256;                               \
+      return __VA_ARGS__();                                 \
+    }                                                       \
+    TORCH_CHECK(false, "unsupported head_dim ", D);         \
+  }()
+
+std::vector<torch::Tensor> rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
+                                    int64_t nq, int64_t nkv, int64_t D,
+                                    c10::optional<torch::Tensor> qn_w,
+                                    c10::optional<torch::Tensor> kn_w, double eps) {
+  TORCH_CHECK(qkv.stride(-1) == 1 && pos.scalar_type() == at::kInt && pos.is_contiguous());
+  const int64_t T = qkv.size(0);
+  const int64_t ld = qkv.stride(0);
+  const int nh = nq + nkv;
+  auto out = torch::empty({T, nh * D}, qkv.options());
+  const bool norm = qn_w.has_value();
+  auto rstd = norm ? torch::empty({T, nh}, qkv.options().dtype(at::kFloat)) : torch::Tensor();
+  const int64_t warps = T * nh;
+  const int threads = 256;
+  const int64_t blocks = (warps + threads / 32 - 1) / (threads / 32);
+  if (warps > 0)
+    ART_DISPATCH_HEAD_DIM(D, [&] {
+      rope_fwd_kernel<kD><<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+          reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), ld, pos.data_ptr<int>(),
+          inv_freq.data_ptr<float>(),
+          norm ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,
+          norm ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr,
+          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), norm ? rstd.data_ptr<float>() : nullptr,
+          T, (int)nq, (int)nkv, (float)eps);
+    });
+  ART_CUDA_CHECK(cudaGetLastError());
+  return {out, rstd};
+}
+
+void rope_bwd(torch::Tensor dqk, torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
+              int64_t nq, int64_t nkv, int64_t D, c10::optional<torch::Tensor> qn_w,
+              c10::optional<torch::Tensor> kn_w, c10::optional<torch::Tensor> rstd,
+              torch::Tensor dqkv) {
+  TORCH_CHECK(dqk.is_contiguous() && dqkv.stride(-1) == 1 && dqkv.stride(0) == qkv.stride(0));
+  const int64_t T = dqk.size(0);
+  const int nh = nq + nkv;
+  const int64_t warps = T * nh;
+  const int threads = 256;
+  const int64_t blocks = (warps + threads / 32 - 1) / (threads / 32);
+  const bool norm = qn_w.has_value();
+  if (warps > 0)
+    ART_DISPATCH_HEAD_DIM(D, [&] {
+      rope_bwd_kernel<kD><<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+          reinterpret_cast<const __nv_bfloat16*>(dqk.data_ptr()),
+          reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0),
+          pos.data_ptr<int>(), inv_freq.data_ptr<float>(),
+          norm ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,
+          norm ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr,
+          norm ? rstd->data_ptr<float>() : nullptr,
+          reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), T, (int)nq, (int)nkv);
+    });
+  ART_CUDA_CHECK(cudaGetLastError());
+}
+
+// ----------------------------------------------------------------------------
+// SwiGLU: gu = [gate | up] per row (width 2F) -> a = silu(gate) * up.
+// ----------------------------------------------------------------------------
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ a,
+                                  int64_t T, int F) {
+  const int64_t nvec = T * (F / 8);
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = v / (F / 8);
+    const int c = (v % (F / 8)) * 8;
+    uint4 gv = *reinterpret_cast<const uint4*>(gu + t * 2 * F + c);
+    uint4 uv = *reinterpret_cast<const uint4*>(gu + t * 2 * F + F + c);
+    const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv);
+    const __nv_bfloat16* ue = reinterpret_cast<const __nv_bfloat16*>(&uv);
+    uint4 ov;
+    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float g = bf2f(ge[k]);
+      const float s = g / (1.f + __expf(-g));
+      oe[k] = f2bf(bf2f(f2bf(s)) * bf2f(ue[k]));
+    }
+    *reinterpret_cast<uint4*>(a + t * F + c) = ov;
+  }
+}
+
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ da,
+                                  const __nv_bfloat16* __restrict__ gu,
+                                  __nv_bfloat16* __restrict__ dgu, int64_t T, int F) {
+  const int64_t nvec = T * (F / 8);
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = v / (F / 8);
+    const int c = (v % (F / 8)) * 8;
+    uint4 dv = *reinterpret_cast<const uint4*>(da + t * F + c);
+    uint4 gv = *reinterpret_cast<const uint4*>(gu + t * 2 * F + c);
+    uint4 uv = *reinterpret_cast<const uint4*>(gu + t * 2 * F + F + c);
+    const __nv_bfloat16* de = reinterpret_cast<const __nv_bfloat16*>(&dv);
+    const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv);
+    const __nv_bfloat16* ue = reinterpret_cast<const __nv_bfloat16*>(&uv);
+    uint4 dg, du;
+    __nv_bfloat16* dge = reinterpret_cast<__nv_bfloat16*>(&dg);
+    __nv_bfloat16* due = reinterpret_cast<__nv_bfloat16*>(&du);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float g = bf2f(ge[k]), u = bf2f(ue[k]), d = bf2f(de[k]);
+      const float sg = 1.f / (1.f + __expf(-g));
+      const float s = g * sg;
+      due[k] = f2bf(d * s);
+      dge[k] = f2bf(d * u * sg * (1.f + g * (1.f - sg)));
+    }
+    *reinterpret_cast<uint4*>(dgu + t * 2 * F + c) = dg;
+    *reinterpret_cast<uint4*>(dgu + t * 2 * F + F + c) = du;
+  }
+}
+
+static int64_t ew_blocks(int64_t n) {
+  int64_t b = (n + 255) / 256;
+  const int64_t cap = 148 * 16;
+  return b < 1 ? 1 : (b > cap ? cap : b);
+}
+
+torch::Tensor swiglu_fwd(torch::Tensor gu) {
+  TORCH_CHECK(gu.is_contiguous() && gu.size(-1) % 16 == 0);
+  const int F = gu.size(-1) / 2;
+  const int64_t T = gu.numel() / (2 * F);
+  auto sizes = gu.sizes().vec();
+  sizes.back() = F;
+  auto a = torch::empty(sizes, gu.options());
+  if (T > 0)
+    swiglu_fwd_kernel<<<ew_blocks(T * F / 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(a.data_ptr()), T, F);
+  ART_CUDA_CHECK(cudaGetLastError());
+  return a;
+}
+
+torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu) {
+  TORCH_CHECK(da.is_contiguous() && gu.is_contiguous());
+  const int F = gu.size(-1) / 2;
+  const int64_t T = gu.numel() / (2 * F);
+  auto dgu = torch::empty_like(gu);
+  if (T > 0)
+    swiglu_bwd_kernel<<<ew_blocks(T * F / 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(da.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), T, F);
+  ART_CUDA_CHECK(cudaGetLastError());
+  return dgu;
+}
+
+}  // namespace art

@@ -1,0 +1,468 @@
+"""Autograd wrappers of the fused kernels.
+
+Every op has one implementation per device: CUDA tensors run the sm_100a
+kernels of ``ops/csrc`` (and raise if the extension is missing), CPU tensors
+run the same math in plain PyTorch (the fp32 plumbing configuration and the
+numerics oracle of the GPU tests).
+
+Ops:
+* :func:`add_rmsnorm` - residual add fused with RMSNorm (frozen weight).
+* :func:`rope_attention` - qk-RMSNorm + RoPE on packed positions + prefix-tree
+  attention, returning the attention output; its backward produces the
+  gradient of the whole raw QKV projection in one buffer.
+* :func:`swiglu` - ``silu(gate) * up`` on a fused ``[gate | up]`` projection.
+* :func:`lora_linear` - frozen base GEMM plus LoRA, accumulating the LoRA
+  gradients straight into the flat fp32 gradient buffer.
+* :func:`lm_head_logprobs` - chunked LM head + log-softmax gather + entropy.
+* :func:`grpo_token_loss` - the token-level GRPO/CISPO/PPO loss with its
+  closed-form gradient.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Any, Sequence
+
+import torch
+
+from . import native
+
+
+def _cuda(t: torch.Tensor) -> bool:
+    return t.device.type == "cuda"
+
+
+# ---------------------------------------------------------------------------
+# Attention metadata (per packed row)
+# ---------------------------------------------------------------------------
+
+
+@dataclass
+class AttnMeta:
+    """Per-row attention metadata shared by every layer of one micro step.
+
+    ``kend[j]``: query ``i`` may attend key ``j`` iff ``j <= i < kend[j]``.
+    ``tile_kmax[t]``: max of ``kend`` over keys ``[64t, 64t+64)`` (tile skip).
+    """
+
+    positions: torch.Tensor  # int32 [T]
+    kend: torch.Tensor  # int32 [T]
+    tile_kmax: torch.Tensor  # int32 [ceil(T/64)]
+    T: int
+
+    @staticmethod
+    def build(positions: torch.Tensor, kend: torch.Tensor, device: torch.device) -> "AttnMeta":
+        T = int(kend.numel())
+        pad = (-T) % 64
+        k = kend.to(torch.int32)
+        kp = torch.nn.functional.pad(k, (0, pad), value=0)
+        tile = kp.view(-1, 64).amax(dim=1).to(torch.int32)
+        return AttnMeta(
+            positions=positions.to(device=device, dtype=torch.int32, non_blocking=True),
+            kend=k.to(device, non_blocking=True),
+            tile_kmax=tile.to(device, non_blocking=True),
+            T=T,
+        )
+
+
+def rope_inv_freq(head_dim: int, theta: float, device: torch.device) -> torch.Tensor:
+    return 1.0 / (
+        theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64, device="cpu") / head_dim)
+    ).to(device=device, dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm with fused residual add
+# ---------------------------------------------------------------------------
+
+
+def _rmsnorm_ref(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (xf * r).to(x.dtype) * w
+
+
+class _AddRMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, res, w, eps):
+        y, xs, rstd = native.lib().rmsnorm_fwd(x, res, w, eps)
+        ctx.save_for_backward(xs, w, rstd)
+        ctx.has_res = res is not None
+        return y, xs
+
+    @staticmethod
+    def backward(ctx, dy, dxs):
+        xs, w, rstd = ctx.saved_tensors
+        dres = dxs.contiguous() if dxs is not None else None
+        dx = native.lib().rmsnorm_bwd(dy.contiguous(), xs, w, rstd, dres)
+        return dx, (dx if ctx.has_res else None), None, None
+
+
+def add_rmsnorm(
+    x: torch.Tensor, res: torch.Tensor | None, w: torch.Tensor, eps: float
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Returns ``(rmsnorm(x + res) * w, x + res)``; ``res=None`` skips the add."""
+    if _cuda(x):
+        return _AddRMSNorm.apply(x, res, w, eps)
+    s = x if res is None else x + res
+    return _rmsnorm_ref(s, w, eps), s
+
+
+# ---------------------------------------------------------------------------
+# RoPE + prefix-tree attention
+# ---------------------------------------------------------------------------
+
+
+def _rope_ref(x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor) -> torch.Tensor:
+    # x [T, H, D]; rotate-half convention
+    ang = pos.float().unsqueeze(-1) * inv_freq.unsqueeze(0)  # [T, D/2]
+    cos = torch.cat([ang.cos(), ang.cos()], -1).unsqueeze(1).to(x.dtype)
+    sin = torch.cat([ang.sin(), ang.sin()], -1).unsqueeze(1).to(x.dtype)
+    d = x.shape[-1] // 2
+    rot = torch.cat([-x[..., d:], x[..., :d]], -1)
+    return x * cos + rot * sin
+
+
+def attention_ref(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kend: torch.Tensor, scale: float
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Dense-mask prefix-tree attention in fp32 math (oracle). q [T,Hq,D]."""
+    T, Hq, D = q.shape
+    G = Hq // k.shape[1]
+    kx = k.float().repeat_interleave(G, dim=1)
+    vx = v.float().repeat_interleave(G, dim=1)
+    s = torch.einsum("ihd,jhd->hij", q.float(), kx) * scale
+    i = torch.arange(T, device=q.device).view(T, 1)
+    j = torch.arange(T, device=q.device).view(1, T)
+    mask = (j <= i) & (i < kend.to(q.device).long().view(1, T))
+    s = s.masked_fill(~mask.unsqueeze(0), float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)  # [Hq, T]
+    p = torch.softmax(s, dim=-1)
+    o = torch.einsum("hij,jhd->ihd", p, vx)
+    return o.to(q.dtype), lse
+
+
+class _RopeAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale):
+        C = native.lib()
+        T = qkv.shape[0]
+        qk, rstd = C.rope_fwd(qkv, meta.positions, inv_freq, nq, nkv, D, qn_w, kn_w, eps)
+        q = qk[:, : nq * D].view(T, nq, D)
+        k = qk[:, nq * D :].view(T, nkv, D)
+        v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
+        o, lse = C.attn_fwd(q, k, v, meta.kend, meta.tile_kmax, scale)
+        ctx.save_for_backward(qkv, qk, o, lse, inv_freq, qn_w if qn_w is not None else qkv.new_empty(0),
+                              kn_w if kn_w is not None else qkv.new_empty(0),
+                              rstd if rstd is not None and rstd.numel() else qkv.new_empty(0, dtype=torch.float32))
+        ctx.meta = meta
+        ctx.dims = (nq, nkv, D, scale, qn_w is not None)
+        return o.view(T, nq * D)
+
+    @staticmethod
+    def backward(ctx, do):
+        C = native.lib()
+        qkv, qk, o, lse, inv_freq, qn_w, kn_w, rstd = ctx.saved_tensors
+        nq, nkv, D, scale, has_norm = ctx.dims
+        meta = ctx.meta
+        T = qkv.shape[0]
+        do = do.contiguous().view(T, nq, D)
+        q = qk[:, : nq * D].view(T, nq, D)
+        k = qk[:, nq * D :].view(T, nkv, D)
+        v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
+        dqkv = torch.empty_like(qkv)
+        dqk = torch.empty_like(qk)
+        dk = dqk[:, nq * D :].view(T, nkv, D)
+        dv = dqkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
+        dq_acc = C.attn_bwd(do, q, k, v, o, lse, meta.kend, meta.tile_kmax, scale, dk, dv)
+        dqk[:, : nq * D].copy_(dq_acc.view(T, nq * D))
+        C.rope_bwd(dqk, qkv, meta.positions, inv_freq, nq, nkv, D,
+                   qn_w if has_norm else None, kn_w if has_norm else None,
+                   rstd if has_norm else None, dqkv)
+        return dqkv, None, None, None, None, None, None, None, None, None
+
+
+def rope_attention(
+    qkv: torch.Tensor,
+    meta: AttnMeta,
+    inv_freq: torch.Tensor,
+    nq: int,
+    nkv: int,
+    D: int,
+    qn_w: torch.Tensor | None,
+    kn_w: torch.Tensor | None,
+    eps: float,
+) -> torch.Tensor:
+    """Raw QKV projection ``[T, (nq+2nkv)*D]`` -> attention output ``[T, nq*D]``."""
+    scale = 1.0 / math.sqrt(D)
+    if _cuda(qkv):
+        return _RopeAttention.apply(qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale)
+    T = qkv.shape[0]
+    q = qkv[:, : nq * D].view(T, nq, D)
+    k = qkv[:, nq * D : (nq + nkv) * D].view(T, nkv, D)
+    v = qkv[:, (nq + nkv) * D :].reshape(T, nkv, D)
+    if qn_w is not None:
+        q = _rmsnorm_ref(q, qn_w, eps)
+        k = _rmsnorm_ref(k, kn_w, eps)
+    pos = meta.positions
+    q = _rope_ref(q, pos, inv_freq)
+    k = _rope_ref(k, pos, inv_freq)
+    o, _ = attention_ref(q, k, v, meta.kend, scale)
+    return o.reshape(T, nq * D)
+
+
+# ---------------------------------------------------------------------------
+# SwiGLU
+# ---------------------------------------------------------------------------
+
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        ctx.save_for_backward(gu)
+        return native.lib().swiglu_fwd(gu)
+
+    @staticmethod
+    def backward(ctx, da):
+        (gu,) = ctx.saved_tensors
+        return native.lib().swiglu_bwd(da.contiguous(), gu)
+
+
+def swiglu(gu: torch.Tensor) -> torch.Tensor:
+    if _cuda(gu):
+        return _SwiGLU.apply(gu)
+    F = gu.shape[-1] // 2
+    g, u = gu[..., :F], gu[..., F:]
+    return torch.nn.functional.silu(g) * u
+
+
+# ---------------------------------------------------------------------------
+# LoRA linear
+# ---------------------------------------------------------------------------
+
+
+@dataclass
+class LoRABinding:
+    """The LoRA factors of one (possibly fused) projection.
+
+    ``A`` is the row-concatenation of the per-slice ``A`` matrices
+    ``[n*r, in]``; ``B_blocks[k]`` is slice ``k``'s ``B`` ``[out_k, r]``,
+    placed at output rows ``slices[k]`` and LoRA columns ``[k*r, (k+1)*r)``.
+    ``gA``/``gB_blocks`` are the matching fp32 gradient slots.
+    """
+
+    A: torch.Tensor
+    B_blocks: Sequence[torch.Tensor | None]
+    gA: torch.Tensor
+    gB_blocks: Sequence[torch.Tensor | None]
+    slices: Sequence[tuple[int, int]]
+    r: int
+    scale: float
+    out_features: int
+    _bd: torch.Tensor | None = None
+    _bd_version: int = -1
+
+    def block_diag(self, version: int) -> torch.Tensor:
+        """Dense ``[out, n*r]`` B with the slice blocks on its diagonal (cached
+        until the parameters change)."""
+        if len(self.B_blocks) == 1 and self.B_blocks[0] is not None:
+            return self.B_blocks[0]
+        if self._bd is None or self._bd_version != version:
+            n = len(self.B_blocks)
+            bd = self.A.new_zeros(self.out_features, n * self.r)
+            for k, (blk, (s, e)) in enumerate(zip(self.B_blocks, self.slices)):
+                if blk is not None:
+                    bd[s:e, k * self.r : (k + 1) * self.r] = blk
+            self._bd = bd
+            self._bd_version = version
+        return self._bd
+
+
+def _accum_mm(slot: torch.Tensor, a: torch.Tensor, b: torch.Tensor, alpha: float) -> None:
+    """``slot += alpha * a @ b`` with fp32 accumulation into the fp32 slot."""
+    if _cuda(slot) and a.dtype != torch.float32:
+        torch.addmm(slot, a, b, beta=1.0, alpha=alpha, out_dtype=torch.float32, out=slot)
+    else:
+        slot.addmm_(a.to(slot.dtype), b.to(slot.dtype), alpha=alpha)
+
+
+_ANCHORS: dict[torch.device, torch.Tensor] = {}
+
+
+def grad_anchor(device: torch.device) -> torch.Tensor:
+    """A scalar that requires grad.  Ops whose trainable state lives outside
+    autograd (the flat LoRA store) take it as an input so their outputs join
+    the graph and their backward runs even when no other input needs a grad."""
+    a = _ANCHORS.get(device)
+    if a is None:
+        a = torch.zeros((), device=device, requires_grad=True)
+        _ANCHORS[device] = a
+    return a
+
+
+class _LoRALinear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, W, bias, lora, version, enabled, anchor):
+        y = torch.nn.functional.linear(x, W, bias)
+        u = None
+        if enabled and lora is not None:
+            u = x @ lora.A.t()  # [T, n*r]
+            y.addmm_(u, lora.block_diag(version).t(), alpha=lora.scale)
+        ctx.save_for_backward(x, W, u if u is not None else x.new_empty(0))
+        ctx.lora = lora if enabled else None
+        ctx.version = version
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, W, u = ctx.saved_tensors
+        lora = ctx.lora
+        dy = dy.contiguous()
+        dx = dy @ W
+        if lora is not None:
+            bd = lora.block_diag(ctx.version)
+            dyB = dy @ bd  # [T, n*r]
+            s = lora.scale
+            # dA = s * dyB^T x
+            _accum_mm(lora.gA, dyB.t(), x, s)
+            # dB_k = s * dy[:, slice_k]^T u[:, k-block]
+            for k, (gB, (a, b)) in enumerate(zip(lora.gB_blocks, lora.slices)):
+                if gB is None:
+                    continue
+                _accum_mm(gB, dy[:, a:b].t(), u[:, k * lora.r : (k + 1) * lora.r], s)
+            dx.addmm_(dyB, lora.A, alpha=s)
+        return dx, None, None, None, None, None, None
+
+
+def lora_linear(
+    x: torch.Tensor,
+    W: torch.Tensor,
+    bias: torch.Tensor | None,
+    lora: LoRABinding | None,
+    version: int = 0,
+    enabled: bool = True,
+) -> torch.Tensor:
+    """``y = x W^T + b + scale * (x A^T) B^T`` with frozen ``W``/``b``; the LoRA
+    gradients are accumulated into ``lora.gA`` / ``lora.gB_blocks``."""
+    anchor = grad_anchor(x.device) if (enabled and lora is not None) else None
+    return _LoRALinear.apply(x, W, bias, lora, version, enabled, anchor)
+
+
+# ---------------------------------------------------------------------------
+# LM head log-probabilities
+# ---------------------------------------------------------------------------
+
+
+class _LMHeadLogprobs(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, W, targets, chunk, want_entropy):
+        C = native.lib()
+        T = h.shape[0]
+        lp = torch.empty(T, device=h.device, dtype=torch.float32)
+        ent = torch.empty(T, device=h.device, dtype=torch.float32) if want_entropy else None
+        saved_logits = []
+        lses = []
+        for s in range(0, T, chunk):
+            e = min(T, s + chunk)
+            logits = h[s:e] @ W.t()  # [c, V] bf16, fp32 accumulate
+            lse, tgt, en = C.logits_stats(logits, targets[s:e], want_entropy)
+            lp[s:e] = tgt - lse
+            if want_entropy:
+                ent[s:e] = en
+            saved_logits.append(logits)
+            lses.append(lse)
+        ctx.saved_logits = saved_logits
+        ctx.save_for_backward(W, targets, torch.cat(lses) if lses else lp.new_empty(0))
+        ctx.chunk = chunk
+        ctx.mark_non_differentiable(*( [ent] if ent is not None else [] ))
+        return lp, ent
+
+    @staticmethod
+    def backward(ctx, glp, gent):
+        C = native.lib()
+        W, targets, lse = ctx.saved_tensors
+        chunk = ctx.chunk
+        T = targets.shape[0]
+        dh = torch.empty(T, W.shape[1], device=W.device, dtype=W.dtype)
+        glp = glp.float().contiguous()
+        for idx, s in enumerate(range(0, T, chunk)):
+            e = min(T, s + chunk)
+            logits = ctx.saved_logits[idx]
+            C.logits_grad_(logits, targets[s:e], lse[s:e], glp[s:e])
+            torch.mm(logits, W, out=dh[s:e])
+        ctx.saved_logits = None
+        return dh, None, None, None, None
+
+
+def lm_head_logprobs(
+    h: torch.Tensor, W: torch.Tensor, targets: torch.Tensor, chunk: int = 4096, entropy: bool = True
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Per-row ``log softmax(h W^T)[target]`` (fp32) and entropy (no grad)."""
+    if _cuda(h):
+        return _LMHeadLogprobs.apply(h, W, targets, chunk, entropy)
+    logits = (h @ W.t()).float()
+    lse = torch.logsumexp(logits, dim=-1)
+    lp = logits.gather(-1, targets.clamp_min(0).unsqueeze(-1)).squeeze(-1) - lse
+    ent = None
+    if entropy:
+        with torch.no_grad():
+            logp = logits - lse.unsqueeze(-1)
+            ent = -(logp.exp() * logp).sum(-1)
+    return lp, ent
+
+
+# ---------------------------------------------------------------------------
+# GRPO token loss (token-level importance ratio)
+# ---------------------------------------------------------------------------
+
+
+def grpo_loss_config(cfg: dict[str, Any], T: int, denominator: float) -> list[float]:
+    from ..loss import resolve_clip
+
+    ppo, eps, eps_hi = resolve_clip(cfg)
+    return [
+        float(ppo),
+        eps,
+        eps_hi,
+        float(cfg.get("kl_penalty_coef", 0.0) or 0.0),
+        1.0 if cfg.get("kl_penalty_source", "current_learner") == "sample" else 0.0,
+        float(cfg.get("truncated_importance_sampling") or 0.0),
+        1.0 if cfg.get("mask_prob_ratio", False) else 0.0,
+        float(cfg.get("kimi_k2_tau") or 0.0),
+        float(cfg.get("max_negative_advantage_importance_sampling_weight") or 0.0),
+        float(denominator),
+        float(T),
+    ]
+
+
+class _GRPOTokenLoss(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, newlp, oldlp, adv, w, mask, reflp, origlp, cfg):
+        grad, out = native.lib().grpo_token_loss(
+            newlp.contiguous(), oldlp.contiguous(), adv.contiguous(), w.contiguous(),
+            mask.contiguous(), reflp, origlp, cfg
+        )
+        ctx.save_for_backward(grad)
+        ctx.mark_non_differentiable(out)
+        return out[0] / out[1], out
+
+    @staticmethod
+    def backward(ctx, gloss, gout):
+        (grad,) = ctx.saved_tensors
+        return grad * gloss, None, None, None, None, None, None, None
+
+
+def grpo_token_loss(
+    newlp: torch.Tensor,
+    oldlp: torch.Tensor,
+    adv: torch.Tensor,
+    w: torch.Tensor,
+    mask: torch.Tensor,
+    reflp: torch.Tensor | None,
+    origlp: torch.Tensor | None,
+    cfg: torch.Tensor,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Fused token-level loss on 1-D aligned vectors (CUDA).  Returns
+    ``(reduced_loss, stats[3] = {loss_sum, denominator, mean_kl})``."""
+    return _GRPOTokenLoss.apply(newlp, oldlp, adv, w, mask, reflp, origlp, cfg)

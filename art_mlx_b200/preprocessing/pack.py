@@ -1,0 +1,292 @@
+"""Packing tokenized results into fixed-length training rows.
+
+Format and normalisations follow the reference
+``src/art/preprocessing/pack.py:26-625``:
+
+* ``PackedTensors`` is a dict of ``[num_rows, seq_len]`` tensors: tokens,
+  group_ids, parent_ids, input_pos, assistant_mask, logprobs, advantages,
+  weights (+ optional MoE routing replay);
+* results are appended to the current row while the prefix-tree-packed row
+  still fits ``seq_len``; rows are shuffled;
+* weights are zeroed off-mask and normalised to mean 1 over the mask;
+  ``advantage_balance`` scales one sign down; advantages are then divided by
+  ``mean(|A| * w)`` over the mask;
+* on disk each tensor is its own raw file, memory-mapped back with
+  ``torch.from_file(shared=True)``.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import random
+from dataclasses import dataclass
+from typing import Any, NamedTuple, TypedDict
+
+import torch
+from typing_extensions import NotRequired
+
+from .prefix_tree import estimate_prefix_tree_packed_tokens, prefix_tree_pack
+from .tokenize import TokenizedResult
+
+
+@dataclass
+class PackedMoeRoutingReplay:
+    """Replayed expert ids ``[rows, S, layers, topk]`` with a coverage mask."""
+
+    expert_indices: torch.Tensor
+    token_mask: torch.Tensor
+    num_layers: int
+    topk: int
+    num_experts: int
+
+
+class PackedTensors(TypedDict):
+    tokens: torch.Tensor
+    group_ids: torch.Tensor
+    parent_ids: torch.Tensor
+    input_pos: torch.Tensor
+    assistant_mask: torch.Tensor
+    logprobs: torch.Tensor
+    advantages: torch.Tensor
+    weights: torch.Tensor
+    pixel_values: list[torch.Tensor | None]
+    image_grid_thw: list[torch.Tensor | None]
+    moe_routing_replay: PackedMoeRoutingReplay | None
+
+
+class DiskPackedTensors(TypedDict):
+    dir: str
+    num_sequences: int
+    sequence_length: int
+    pixel_values: NotRequired[tuple[int, list[int]]]
+    image_grid_thw: NotRequired[tuple[int, list[int]]]
+
+
+DISK_DTYPES: dict[str, torch.dtype] = {
+    "tokens": torch.long,
+    "group_ids": torch.long,
+    "parent_ids": torch.long,
+    "input_pos": torch.long,
+    "assistant_mask": torch.bool,
+    "logprobs": torch.float32,
+    "advantages": torch.float32,
+    "weights": torch.float32,
+}
+
+
+class _Item(NamedTuple):
+    token_ids: tuple[int, ...]
+    input_pos: tuple[int, ...]
+    assistant_mask: tuple[int, ...]
+    logprobs: tuple[float, ...]
+    advantage: float
+    weight: float
+    prompt_id: int
+    shareable: int
+    routes: tuple[Any, ...] | None
+
+
+def _first_trainable(r: TokenizedResult) -> int:
+    for i, (m, lp) in enumerate(zip(r.assistant_mask, r.logprobs)):
+        if m or not math.isnan(float(lp)):
+            return i
+    return len(r.token_ids)
+
+
+def _item(r: TokenizedResult, seq_len: int) -> _Item:
+    share = min(int(r.prompt_length), max(_first_trainable(r) - 1, 0))
+    it = _Item(
+        tuple(int(v) for v in r.token_ids),
+        tuple(int(v) for v in r.input_pos),
+        tuple(int(v) for v in r.assistant_mask),
+        tuple(float(v) for v in r.logprobs),
+        float(r.advantage),
+        float(r.weight),
+        int(r.prompt_id),
+        share,
+        tuple(r.moe_routed_experts) if r.moe_routed_experts is not None else None,
+    )
+    return _truncate(it, seq_len)
+
+
+def _truncate(it: _Item, seq_len: int) -> _Item:
+    if len(it.token_ids) <= seq_len:
+        return it
+    return it._replace(
+        token_ids=it.token_ids[:seq_len],
+        input_pos=it.input_pos[:seq_len],
+        assistant_mask=it.assistant_mask[:seq_len],
+        logprobs=it.logprobs[:seq_len],
+        shareable=min(it.shareable, seq_len),
+        routes=it.routes[:seq_len] if it.routes is not None else None,
+    )
+
+
+def _row_len(row: list[_Item], seq_len: int) -> int:
+    n = estimate_prefix_tree_packed_tokens(
+        (torch.tensor(i.token_ids, dtype=torch.long) for i in row),
+        max_depth=seq_len,
+        shareable_lengths=(i.shareable for i in row),
+    )
+    assert n is not None
+    return n
+
+
+def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
+    if not row:
+        return {k: [] for k in ("tokens", "group_ids", "parent_ids", "input_pos", "assistant_mask", "logprobs", "advantages", "weights", "routes")}
+    tree = prefix_tree_pack(
+        (torch.tensor(i.token_ids, dtype=torch.long) for i in row),
+        max_depth=seq_len if share else 0,
+        shareable_lengths=(i.shareable if share else 0 for i in row),
+    )
+    toks = tree.tokens.reshape(-1).tolist()
+    n = len(toks)
+    owned = [False] * n
+    pos = [0] * n
+    mask = [0] * n
+    lps = [float("nan")] * n
+    adv = [0.0] * n
+    w = [0.0] * n
+    routes: list[Any] = [None] * n
+    for k, it in enumerate(row):
+        for src, dst in enumerate(tree.positions_by_sequence[k].tolist()):
+            if toks[dst] != it.token_ids[src]:
+                raise RuntimeError("Prefix-tree pack token assignment mismatch")
+            if owned[dst]:
+                if pos[dst] != it.input_pos[src]:
+                    raise RuntimeError("Prefix-tree pack cannot share mismatched input positions")
+                if it.assistant_mask[src] or not math.isnan(it.logprobs[src]):
+                    raise RuntimeError("Prefix-tree pack attempted to share a trainable token")
+                continue
+            owned[dst] = True
+            pos[dst] = it.input_pos[src]
+            mask[dst] = it.assistant_mask[src]
+            lps[dst] = it.logprobs[src]
+            adv[dst] = it.advantage
+            w[dst] = it.weight
+            if it.routes is not None and src < len(it.routes):
+                routes[dst] = it.routes[src]
+    return {
+        "tokens": toks[:seq_len],
+        "group_ids": tree.group_ids.reshape(-1).tolist()[:seq_len],
+        "parent_ids": tree.parent_ids.reshape(-1).tolist()[:seq_len],
+        "input_pos": pos[:seq_len],
+        "assistant_mask": mask[:seq_len],
+        "logprobs": lps[:seq_len],
+        "advantages": adv[:seq_len],
+        "weights": w[:seq_len],
+        "routes": routes[:seq_len],
+    }
+
+
+def _padded(rows: list[list], seq_len: int, value: Any, dtype: torch.dtype) -> torch.Tensor:
+    out = torch.full((len(rows), seq_len), value, dtype=dtype)
+    for r, vals in enumerate(rows):
+        if vals:
+            out[r, : len(vals)] = torch.tensor(vals, dtype=dtype)
+    return out
+
+
+def packed_tensors_from_tokenized_results(
+    tokenized_results: list[TokenizedResult],
+    seq_len: int,
+    pad_token_id: int = -100,
+    truncate_long_results: bool = True,
+    advantage_balance: float = 0.0,
+    verbosity: int = 1,
+    pack_results: bool = True,
+    include_moe_routing: bool = False,
+    rng: random.Random | None = None,
+) -> PackedTensors:
+    rows: list[list[_Item]] = [[]]
+    for r in tokenized_results:
+        if len(r.token_ids) > seq_len and not truncate_long_results:
+            continue
+        if include_moe_routing and r.moe_routed_experts is None:
+            raise RuntimeError("MoE routing replay requested but a result has no routes")
+        if sum(r.assistant_mask[r.prompt_length :]) == 0:
+            continue
+        it = _item(r, seq_len)
+        if rows[-1] and (not pack_results or _row_len([*rows[-1], it], seq_len) > seq_len):
+            rows.append([])
+        rows[-1].append(it)
+    (rng or random).shuffle(rows)
+    packed = [_pack_row(row, seq_len, pack_results) for row in rows]
+
+    mask = _padded([p["assistant_mask"] for p in packed], seq_len, 0, torch.bool)
+    weights = _padded([p["weights"] for p in packed], seq_len, 0.0, torch.float32)
+    weights = torch.where(mask, weights, torch.zeros_like(weights))
+    if mask.any():
+        weights[mask] /= weights[mask].mean()
+    adv = _padded([p["advantages"] for p in packed], seq_len, 0.0, torch.float32)
+    adv = torch.where(mask, adv, torch.zeros_like(adv))
+    if advantage_balance > 0.0:
+        adv = torch.where(adv > 0, adv, adv * (1 - advantage_balance))
+    elif advantage_balance < 0.0:
+        adv = torch.where(adv < 0, adv, adv * (1 + advantage_balance))
+    if mask.any():
+        adv[mask] /= (adv[mask].abs() * weights[mask]).mean()
+
+    out: PackedTensors = {
+        "tokens": _padded([p["tokens"] for p in packed], seq_len, pad_token_id, torch.long),
+        "group_ids": _padded([p["group_ids"] for p in packed], seq_len, -1, torch.long),
+        "parent_ids": _padded([p["parent_ids"] for p in packed], seq_len, -1, torch.long),
+        "input_pos": _padded([p["input_pos"] for p in packed], seq_len, 0, torch.long),
+        "assistant_mask": mask,
+        "logprobs": _padded([p["logprobs"] for p in packed], seq_len, float("nan"), torch.float32),
+        "advantages": adv,
+        "weights": weights,
+        "pixel_values": [None] * len(packed),
+        "image_grid_thw": [None] * len(packed),
+        "moe_routing_replay": None,
+    }
+    if include_moe_routing:
+        out["moe_routing_replay"] = tensorize_routes([p["routes"] for p in packed], seq_len)
+    return out
+
+
+def tensorize_routes(rows: list[list[Any]], seq_len: int) -> PackedMoeRoutingReplay:
+    first = next((r for row in rows for r in row if r is not None), None)
+    if first is None:
+        raise RuntimeError("No MoE routes were packed")
+    L, K = len(first), len(first[0])
+    idx = torch.zeros(len(rows), seq_len, L, K, dtype=torch.int32)
+    have = torch.zeros(len(rows), seq_len, dtype=torch.bool)
+    for b, row in enumerate(rows):
+        for s, route in enumerate(row[:seq_len]):
+            if route is None:
+                continue
+            t = torch.as_tensor(route, dtype=torch.int32)
+            if tuple(t.shape) != (L, K):
+                raise RuntimeError("Packed MoE routes must have one rectangular shape")
+            idx[b, s] = t
+            have[b, s] = True
+    return PackedMoeRoutingReplay(idx, have, L, K, max(K, int(idx.max().item()) + 1))
+
+
+def packed_tensors_from_dir(**kwargs: Any) -> PackedTensors:
+    d = kwargs["dir"]
+    n, s = kwargs["num_sequences"], kwargs["sequence_length"]
+    os.makedirs(d, exist_ok=True)
+    out: dict[str, Any] = {
+        key: torch.from_file(f"{d}/{key}.pt", shared=True, size=n * s, dtype=dt).view(n, s)
+        for key, dt in DISK_DTYPES.items()
+    }
+    out["pixel_values"] = [None] * n
+    out["image_grid_thw"] = [None] * n
+    out["moe_routing_replay"] = None
+    return out  # type: ignore[return-value]
+
+
+def packed_tensors_to_dir(tensors: PackedTensors, dir: str) -> DiskPackedTensors:
+    disk: DiskPackedTensors = {
+        "dir": dir,
+        "num_sequences": int(tensors["tokens"].shape[0]),
+        "sequence_length": int(tensors["tokens"].shape[1]),
+    }
+    mapped = packed_tensors_from_dir(**disk)
+    for key in DISK_DTYPES:
+        mapped[key].copy_(tensors[key])  # type: ignore[literal-required]
+    return disk

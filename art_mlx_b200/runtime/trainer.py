@@ -1,0 +1,280 @@
+"""GRPO training step over packed prefix-tree rows.
+
+Semantics follow the reference's multi-GPU trainer
+(``src/art/megatron/train.py:1407-1605``, ``training/microbatches.py:145-170``):
+
+* one packed row per micro step; rows are interleaved across data-parallel
+  ranks (rank ``r`` takes rows ``r, r+N, ...``);
+* new logprobs are the model's log-softmax at the next packed token; the loss
+  is summed over tokens and normalised by the number of trainable tokens of
+  the whole step (all micro steps, all ranks);
+* gradients are reduced over the data-parallel group, then one clipped AdamW
+  update is applied;
+* with ``kl_penalty_coef > 0`` the reference logprobs come from the same
+  model with the adapter disabled (the frozen base).
+
+B200 specifics: the LM head runs only on trainable positions (all other
+positions have zero loss weight), in vocab chunks whose logits are reused
+in place for the gradient; the loss, its gradient and the optimizer are
+fused kernels; there is no host synchronisation inside a step except the
+final metric read.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Any, Mapping
+
+import torch
+import torch.distributed as dist
+
+from ..loss import AlignedLossInputs, loss_fn, resolve_clip
+from ..models.config import LoRASpec, ModelConfig
+from ..models.transformer import DecoderLM
+from ..ops import fused
+from ..ops.fused import AttnMeta
+from ..preprocessing.prefix_tree import visibility_ends
+from .optimizer import AdamWConfig, FlatAdamW
+
+
+@dataclass
+class MicroBatch:
+    """One packed row staged on the device."""
+
+    tokens: torch.Tensor  # [L] int64
+    meta: AttnMeta
+    sel: torch.Tensor  # [n] int64 positions with a trainable next token
+    targets: torch.Tensor  # [n] int64
+    old: torch.Tensor  # [n] fp32 (NaN = missing)
+    adv: torch.Tensor  # [n]
+    w: torch.Tensor  # [n]
+    group: torch.Tensor  # [n] group id of the scored token
+    original: torch.Tensor | None = None
+    routes: torch.Tensor | None = None  # [L, layers, k] replayed MoE routes
+    n_tokens: int = 0  # valid (non-padding) tokens in the row
+    n_train: int = 0
+
+    @property
+    def L(self) -> int:
+        return int(self.tokens.numel())
+
+
+def _valid_length(group_ids: torch.Tensor) -> int:
+    nz = (group_ids >= 0).nonzero()
+    return int(nz[-1].item()) + 1 if nz.numel() else 0
+
+
+def stage_row(
+    packed: Mapping[str, Any],
+    row: int,
+    device: torch.device,
+    pad_to: int = 64,
+    pin: bool = True,
+) -> MicroBatch:
+    """Slice one row of CPU packed tensors, trim trailing padding (rounded up
+    to ``pad_to``), build the attention metadata and copy it to ``device``."""
+    gids = packed["group_ids"][row]
+    n_valid = max(_valid_length(gids), 1)
+    L = min(int(gids.numel()), (n_valid + pad_to - 1) // pad_to * pad_to)
+    tokens = packed["tokens"][row, :L].clone()
+    tokens[tokens < 0] = 0
+    mask = packed["assistant_mask"][row, :L]
+    # aligned (shifted) views: position t scores token t+1
+    m_al = torch.zeros(L, dtype=torch.bool)
+    m_al[:-1] = mask[1:]
+    sel = m_al.nonzero().squeeze(1)
+    nxt = sel + 1
+    kend = visibility_ends(packed["group_ids"][row : row + 1, :L], packed["parent_ids"][row : row + 1, :L])[0]
+    pos = packed["input_pos"][row, :L]
+
+    def dev(t: torch.Tensor) -> torch.Tensor:
+        t = t.contiguous()
+        if pin and device.type == "cuda":
+            t = t.pin_memory()
+        return t.to(device, non_blocking=True)
+
+    routes = None
+    rr = packed.get("moe_routing_replay")
+    if rr is not None:
+        routes = dev(rr.expert_indices[row, :L])
+    orig = packed.get("original_logprobs")
+    return MicroBatch(
+        tokens=dev(tokens),
+        meta=AttnMeta.build(dev(pos), dev(kend), device),
+        sel=dev(sel),
+        targets=dev(packed["tokens"][row, nxt]),
+        old=dev(packed["logprobs"][row, nxt].float()),
+        adv=dev(packed["advantages"][row, nxt].float()),
+        w=dev(packed["weights"][row, nxt].float()),
+        group=dev(packed["group_ids"][row, nxt]),
+        original=dev(orig[row, nxt].float()) if orig is not None else None,
+        routes=routes,
+        n_tokens=n_valid,
+        n_train=int(sel.numel()),
+    )
+
+
+@dataclass
+class StepMetrics:
+    loss: torch.Tensor
+    entropy: torch.Tensor
+    probs_corr: torch.Tensor
+    kl: torch.Tensor
+    grad_norm: torch.Tensor
+    n_train: int
+    n_tokens: int
+
+    def to_host(self) -> dict[str, float]:
+        vals = torch.stack([self.loss, self.entropy, self.probs_corr, self.kl, self.grad_norm.reshape(())])
+        loss, ent, pc, kl, gn = vals.float().cpu().tolist()
+        return {
+            "loss/train": loss,
+            "loss/entropy": ent,
+            "loss/probs_corr": pc,
+            "loss/kl_policy_ref": kl,
+            "loss/grad_norm": gn,
+            "data/step_trainer_tokens": float(self.n_train),
+            "data/step_packed_tokens": float(self.n_tokens),
+        }
+
+
+def _probs_corr_device(old: torch.Tensor, new: torch.Tensor) -> torch.Tensor:
+    """Pearson correlation of exp(old) and exp(new) over non-NaN ``old``
+    without host synchronisation (0 when undefined)."""
+    have = ~torch.isnan(old)
+    n = have.sum().float()
+    po = torch.where(have, old, torch.zeros_like(old)).exp() * have
+    pn = new.detach().exp() * have
+    mo = po.sum() / n.clamp_min(1)
+    mn = pn.sum() / n.clamp_min(1)
+    do = (po - mo) * have
+    dn = (pn - mn) * have
+    cov = (do * dn).sum()
+    so = (do * do).sum().sqrt()
+    sn = (dn * dn).sum().sqrt()
+    den = so * sn
+    ok = (n >= 2) & (den > 0)
+    return torch.where(ok, cov / torch.where(den > 0, den, torch.ones_like(den)), torch.zeros_like(den))
+
+
+class GRPOTrainer:
+    """Owns the model, the LoRA store and the optimizer on one device/rank."""
+
+    def __init__(
+        self,
+        cfg: ModelConfig,
+        lora: LoRASpec,
+        device: torch.device | str = "cpu",
+        seed: int = 0,
+        adamw: AdamWConfig | None = None,
+        group: dist.ProcessGroup | None = None,
+        logprob_chunk: int = 4096,
+    ) -> None:
+        self.device = torch.device(device)
+        self.model = DecoderLM(cfg, lora, self.device, seed=seed)
+        self.store = self.model.store
+        self.optim = FlatAdamW(self.store, adamw)
+        self.group = group
+        self.world = dist.get_world_size(group) if (group is not None or dist.is_initialized()) and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        self.logprob_chunk = logprob_chunk
+        self.grad_sync = None  # optional fused data-parallel reducer (parallel/dp.py)
+
+    # ------------------------------------------------------------------
+    def _logprobs(self, mb: MicroBatch, ctx: dict[str, Any], entropy: bool) -> tuple[torch.Tensor, torch.Tensor | None]:
+        h = self.model.forward(mb.tokens, mb.meta, ctx)
+        hs = h.index_select(0, mb.sel)
+        return fused.lm_head_logprobs(hs, self.model.lm_head, mb.targets, self.logprob_chunk, entropy)
+
+    def micro_step(
+        self, mb: MicroBatch, cfg: Mapping[str, Any], total_tokens: float
+    ) -> dict[str, torch.Tensor]:
+        """Forward + backward of one packed row; gradients accumulate into the
+        store.  Returns device scalars (loss contribution, entropy sum, ...)."""
+        ctx: dict[str, Any] = {}
+        if mb.routes is not None:
+            ctx["replay_routes"] = mb.routes
+        ref = None
+        kl_coef = float(cfg.get("kl_penalty_coef", 0.0) or 0.0)
+        if kl_coef > 0:
+            with torch.no_grad():
+                self.model.lora_enabled = False
+                try:
+                    ref, _ = self._logprobs(mb, dict(ctx), entropy=False)
+                finally:
+                    self.model.lora_enabled = True
+        lp, ent = self._logprobs(mb, ctx, entropy=True)
+        n = lp.numel()
+        level = cfg.get("importance_sampling_level", "token")
+        if self.device.type == "cuda" and level == "token":
+            cfg_t = torch.tensor(fused.grpo_loss_config(dict(cfg), n, total_tokens), dtype=torch.float32)
+            cfg_t = cfg_t.to(self.device, non_blocking=True)
+            ones = torch.ones(n, device=self.device, dtype=torch.float32)
+            loss, stats = fused.grpo_token_loss(lp, mb.old, mb.adv, mb.w, ones, ref, mb.original, cfg_t)
+            kl = stats[2]
+        else:
+            inputs = AlignedLossInputs(
+                assistant_mask=torch.ones(1, n, dtype=torch.bool, device=self.device),
+                old_logprobs=mb.old.view(1, n),
+                advantages=mb.adv.view(1, n),
+                weights=mb.w.view(1, n),
+                group_ids=mb.group.view(1, n),
+                original_logprobs=None if mb.original is None else mb.original.view(1, n),
+                entropies_are_aligned=True,
+            )
+            out = loss_fn(inputs, lp.view(1, n), None if ref is None else ref.view(1, n), None, cfg, reduction="sum")
+            loss = out.policy_loss / total_tokens
+            kl = out.kl_policy_ref if out.kl_policy_ref is not None else lp.new_zeros(())
+        loss.backward()
+        ent_sum = (ent * mb.w).sum() / total_tokens if ent is not None else lp.new_zeros(())
+        return {
+            "loss": loss.detach(),
+            "entropy": ent_sum.detach(),
+            "probs_corr": _probs_corr_device(mb.old, lp),
+            "kl": kl.detach() if torch.is_tensor(kl) else lp.new_tensor(float(kl)),
+        }
+
+    def train_step(
+        self,
+        packed: Mapping[str, Any],
+        learning_rate: float,
+        cfg: Mapping[str, Any] | None = None,
+        micro_batches: list[MicroBatch] | None = None,
+    ) -> StepMetrics:
+        """One optimizer step over every row of ``packed`` (CPU tensors).
+
+        ``micro_batches`` may carry rows already staged on the device (this
+        rank's rows, in order); the step then performs no host→device copy.
+        """
+        cfg = dict(cfg or {})
+        mask = packed["assistant_mask"]
+        total = float(mask[:, 1:].sum().item())  # trainable (scored) tokens of the whole step
+        rows = list(range(int(mask.shape[0])))[self.rank :: self.world]
+        if micro_batches is None:
+            micro_batches = [stage_row(packed, r, self.device) for r in rows]
+        acc = {k: torch.zeros((), device=self.device) for k in ("loss", "entropy", "probs_corr", "kl")}
+        n_tokens = 0
+        for mb in micro_batches:
+            out = self.micro_step(mb, cfg, max(total, 1.0))
+            for k in acc:
+                acc[k] += out[k]
+            n_tokens += mb.n_tokens
+        nmb = max(len(micro_batches), 1)
+        acc["probs_corr"] /= nmb
+        acc["kl"] /= nmb
+        if self.world > 1:
+            stats = torch.stack([acc["loss"], acc["entropy"], acc["probs_corr"] / self.world, acc["kl"] / self.world])
+            if self.grad_sync is not None:
+                self.grad_sync.reduce_and_step(self.optim, learning_rate, stats)
+            else:
+                dist.all_reduce(self.store.grad, group=self.group)
+                dist.all_reduce(stats, group=self.group)
+                self.optim.step(learning_rate)
+            acc["loss"], acc["entropy"], acc["probs_corr"], acc["kl"] = stats.unbind(0)
+        else:
+            self.optim.step(learning_rate)
+        return StepMetrics(
+            loss=acc["loss"], entropy=acc["entropy"], probs_corr=acc["probs_corr"], kl=acc["kl"],
+            grad_norm=self.optim.grad_norm, n_train=int(total), n_tokens=n_tokens,
+        )

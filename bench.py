@@ -1,0 +1,359 @@
+#!/usr/bin/env python
+"""Headline benchmark: trained tokens/sec per GRPO step.
+
+Config (the data-parallel benchmark configuration): Qwen2.5-7B-shape dense
+model, random init, bf16; LoRA rank 16 on q/k/v/o/gate/up/down; 8 groups x 16
+rollouts per step, each group a shared 1024-token prompt + 16 completions of
+512 tokens packed into one prefix-tree row; uniform token ids; Bernoulli(0.5)
+rewards.  The global batch is fixed (strong scaling): with N GPUs each rank
+trains 8/N rows per step, then gradients are reduced and one AdamW step runs.
+
+``value`` = trainable tokens per step (65,536) / device step time (CUDA events,
+max over ranks).  ``e2e`` times the same step through the public API
+(``LocalBackend.train`` on ``TrajectoryGroup`` objects: tokenize, pack, pinned
+H2D copy of the packed batch, train, D2H read of the metrics, checkpoint).
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Multi-GPU: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def parse_args() -> argparse.Namespace:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--model", default="qwen2.5-7b")
+    p.add_argument("--groups", type=int, default=8)
+    p.add_argument("--rollouts", type=int, default=16)
+    p.add_argument("--prompt-len", type=int, default=1024)
+    p.add_argument("--completion-len", type=int, default=512)
+    p.add_argument("--lora-rank", type=int, default=16)
+    p.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the headline)")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--e2e-steps", type=int, default=2)
+    return p.parse_args()
+
+
+BASELINE_VALUE = None  # BASELINE.md publishes no GPU number for this metric
+METRIC = "trained tokens/sec per GRPO step (whole box, device-timed, max over ranks) 1/2/4/8 B200"
+
+
+def reference_arm(args: argparse.Namespace) -> None:
+    """The reference's own trainer cannot run here; say why in one line."""
+    ref = os.path.join(HERE, "baseline", "_ref")
+    reason = None
+    if not os.path.isdir(os.path.join(ref, "art")):
+        reason = (
+            "reference not installable offline: its build backend 'hatchling' is not in "
+            "/opt/wheelhouse, and its trainers need unsloth/peft/trl (LocalBackend) or "
+            "megatron-core/transformer-engine (MegatronBackend), none of which are installed"
+        )
+    else:
+        sys.path.insert(0, ref)
+        try:
+            import art  # noqa: F401
+            from art.megatron import backend  # noqa: F401
+        except Exception as exc:  # pragma: no cover - depends on the box
+            reason = f"reference import failed: {type(exc).__name__}: {str(exc)[:160]}"
+    if reason is None:
+        reason = "reference Megatron trainer requires megatron-core, which is not installed"
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons in the background."""
+
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self) -> None:
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except Exception:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self) -> None:
+        assert self.proc is not None and self.proc.stdout is not None
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self, gpu_indices: list[int]) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self._t is not None:
+            self._t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if gpu_indices and idx not in gpu_indices:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                pass
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() in ("active", "1", "yes"):
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(smax) if smax else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, HERE)
+    from art_mlx_b200.models.config import LoRASpec, get_config
+    from art_mlx_b200.preprocessing.pack import packed_tensors_from_tokenized_results
+    from art_mlx_b200.preprocessing.synthetic import synthetic_groups
+    from art_mlx_b200.preprocessing.tokenize import tokenize_trajectory_groups
+    from art_mlx_b200.runtime.trainer import GRPOTrainer, stage_row
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch one rank per GPU")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
+
+    cfg = get_config(args.model)
+    if args.layers:
+        cfg = cfg.scaled(num_hidden_layers=args.layers)
+    lora = LoRASpec(r=args.lora_rank, alpha=2 * args.lora_rank)
+    random.seed(1234)
+    torch.manual_seed(1234)
+    groups = synthetic_groups(
+        num_groups=args.groups, rollouts_per_group=args.rollouts, prompt_len=args.prompt_len,
+        completion_len=args.completion_len, vocab_size=cfg.vocab_size, seed=1234, reward="bernoulli",
+    )
+    results = list(tokenize_trajectory_groups(None, groups, False, True, rng=random.Random(1)))
+    row_len = args.prompt_len + args.rollouts * (args.completion_len + 1)
+    seq_len = (row_len + 127) // 128 * 128
+    packed = packed_tensors_from_tokenized_results(results, seq_len, rng=random.Random(2))
+    n_rows = int(packed["tokens"].shape[0])
+    train_tokens = float(packed["assistant_mask"][:, 1:].sum())
+    packed_tokens = int((packed["group_ids"] >= 0).sum())
+
+    trainer = GRPOTrainer(cfg, lora, device, seed=0, group=dist.group.WORLD if world > 1 else None)
+    lr = 1e-5
+    loss_cfg: dict = {}
+    my_rows = list(range(n_rows))[rank::world]
+    staged = [stage_row(packed, r, device) for r in my_rows]
+    l2_flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+
+    def step() -> None:
+        l2_flush.fill_(1)  # evict L2 between timed iterations
+        trainer.train_step(packed, lr, loss_cfg, micro_batches=staged)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(args.steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    clocks = sampler.stop(list(range(world))) if rank == 0 else {}
+    metrics = trainer.train_step(packed, lr, loss_cfg, micro_batches=staged).to_host()
+
+    # kernel launch count of one step (separate, untimed step under the profiler)
+    launches = None
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize()
+        names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+        ours = [n for n in names if "art::" in n]
+        launches = len(ours) * args.steps
+        lib_kernels = len(names) - len(ours)
+    except Exception:
+        lib_kernels = None
+
+    # end-to-end through the public API
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, cfg, lora, groups, trainer, device, world, rank, train_tokens)
+
+    value = train_tokens / (ms / 1000.0)
+    if rank == 0:
+        out = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "trained tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
+            "dtype": "bf16",
+            "data": "synthetic (uniform token ids, Bernoulli(0.5) rewards, random-init weights)",
+            "config": {
+                "model": cfg.name + ("" if not args.layers else f"-{args.layers}L(INVALID)"),
+                "global_batch": f"{args.groups} groups x {args.rollouts} rollouts",
+                "seq_len": seq_len,
+                "prompt_len": args.prompt_len,
+                "completion_len": args.completion_len,
+                "lora_rank": args.lora_rank,
+                "parallelism": f"dp{world}",
+                "rows_per_step": n_rows,
+                "trained_tokens_per_step": int(train_tokens),
+                "packed_tokens_per_step": packed_tokens,
+                "packed_tokens_per_s": round(packed_tokens / (ms / 1000.0), 1),
+                "l2": "256 MiB buffer written before every step; weights (15 GB) exceed L2",
+                "loss": "cispo (default)",
+                "library_kernels_per_step": lib_kernels,
+                "final_metrics": metrics,
+            },
+            "clocks": clocks,
+            "gpu_launches": launches,
+            "impl": "ours",
+        }
+        if e2e is not None:
+            out["e2e"] = e2e
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, cfg, lora, groups, trainer, device, world, rank, train_tokens) -> dict | None:
+    """Time the public ``LocalBackend.train`` call (tokenize, pack, pinned H2D,
+    train, D2H metrics, checkpoint) on the already-built trainer."""
+    import asyncio
+
+    import torch
+    import torch.distributed as dist
+
+    try:
+        from art_mlx_b200 import TrainableModel
+        from art_mlx_b200.backends.local import LocalBackend
+    except Exception as exc:  # pragma: no cover
+        return {"value": None, "unavailable": f"{type(exc).__name__}: {exc}"}
+
+    tmp = tempfile.mkdtemp(prefix="artb200_bench_")
+    backend = LocalBackend(path=tmp, trainer=trainer)
+    model = TrainableModel(
+        name="bench", project="bench", base_model=cfg.name,
+        _internal_config={"peft_args": {"r": lora.r, "lora_alpha": lora.alpha}},
+    )
+
+    async def go():
+        await model.register(backend)
+        times = []
+        h2d = d2h = 0
+        for i in range(args.e2e_steps + 1):
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            res = await backend.train(model, groups, learning_rate=1e-5, packed_sequence_length=None)
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+            if i > 0:  # first call is warm-up
+                times.append(dt)
+            h2d = backend.last_h2d_bytes
+            d2h = backend.last_d2h_bytes
+        return times, h2d, d2h
+
+    times, h2d, d2h = asyncio.run(go())
+    dt = max(times) if times else float("nan")
+    t = torch.tensor([dt], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    return {
+        "value": round(train_tokens / dt, 1),
+        "unit": "trained tokens/s",
+        "seconds_per_step": round(dt, 4),
+        "steps": len(times),
+        "h2d_bytes_per_step": int(h2d),
+        "d2h_bytes_per_step": int(d2h),
+        "api": "LocalBackend.train(model, groups)",
+    }
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,230 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference."""
+
+import math
+import random
+
+import pytest
+import torch
+
+from art_mlx_b200.ops import fused, native
+from art_mlx_b200.preprocessing.prefix_tree import prefix_tree_pack, visibility_ends
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / (b.norm() + 1e-12))
+
+
+def test_rmsnorm_fwd_bwd(cuda):
+    torch.manual_seed(0)
+    for H in (256, 3584, 5120):
+        x = torch.randn(37, H, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+        r = torch.randn(37, H, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+        w = (torch.rand(H, device=cuda) + 0.5).to(torch.bfloat16)
+        y, s = fused.add_rmsnorm(x, r, w, 1e-6)
+        xr = x.detach().float().requires_grad_()
+        rr = r.detach().float().requires_grad_()
+        sr = xr + rr
+        yr = sr * torch.rsqrt(sr.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+        assert rel_err(y, yr) < 1e-2
+        assert rel_err(s, sr) < 1e-2
+        gy = torch.randn_like(y)
+        gs = torch.randn_like(s)
+        torch.autograd.backward([y, s], [gy, gs])
+        torch.autograd.backward([yr, sr], [gy.float(), gs.float()])
+        assert rel_err(x.grad, xr.grad) < 2e-2
+        assert rel_err(r.grad, rr.grad) < 2e-2
+
+
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_rope_fwd_bwd(cuda, qk_norm):
+    torch.manual_seed(1)
+    T, nq, nkv, D = 300, 4, 2, 128
+    C = native.lib()
+    qkv = torch.randn(T, (nq + 2 * nkv) * D, device=cuda, dtype=torch.bfloat16)
+    pos = torch.randint(0, 5000, (T,), device=cuda, dtype=torch.int32)
+    inv = fused.rope_inv_freq(D, 1e6, cuda)
+    qw = (torch.rand(D, device=cuda) + 0.5).to(torch.bfloat16) if qk_norm else None
+    kw = (torch.rand(D, device=cuda) + 0.5).to(torch.bfloat16) if qk_norm else None
+    out, rstd = C.rope_fwd(qkv, pos, inv, nq, nkv, D, qw, kw, 1e-6)
+    # reference
+    x = qkv.float()[:, : (nq + nkv) * D].view(T, nq + nkv, D).requires_grad_()
+    xx = x
+    if qk_norm:
+        wv = torch.cat([qw.float().expand(nq, D), kw.float().expand(nkv, D)]).view(1, nq + nkv, D)
+        xx = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * wv
+    ref = fused._rope_ref(xx, pos, inv)
+    assert rel_err(out.view(T, nq + nkv, D), ref) < 1e-2
+    g = torch.randn(T, (nq + nkv) * D, device=cuda, dtype=torch.bfloat16)
+    dqkv = torch.zeros_like(qkv)
+    C.rope_bwd(g, qkv, pos, inv, nq, nkv, D, qw, kw, rstd if qk_norm else None, dqkv)
+    ref.backward(g.float().view(T, nq + nkv, D))
+    assert rel_err(dqkv[:, : (nq + nkv) * D].view(T, nq + nkv, D), x.grad) < 2e-2
+
+
+def test_swiglu(cuda):
+    torch.manual_seed(2)
+    gu = torch.randn(77, 2 * 704, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    a = fused.swiglu(gu)
+    gr = gu.detach().float().requires_grad_()
+    ar = torch.nn.functional.silu(gr[:, :704]) * gr[:, 704:]
+    assert rel_err(a, ar) < 1e-2
+    g = torch.randn_like(a)
+    a.backward(g)
+    ar.backward(g.float())
+    assert rel_err(gu.grad, gr.grad) < 2e-2
+
+
+def _tree_kend(n_completions: int, prompt: int, comp: int, pad_to: int = 64):
+    seqs = []
+    p = torch.randint(0, 1000, (prompt,))
+    for _ in range(n_completions):
+        seqs.append(torch.cat([p, torch.randint(0, 1000, (comp,))]))
+    pack = prefix_tree_pack(seqs, max_depth=4096, shareable_lengths=[prompt - 1] * n_completions)
+    kend = visibility_ends(pack.group_ids, pack.parent_ids)[0]
+    return kend, pack.position_ids[0]
+
+
+@pytest.mark.parametrize("shape", [(3, 200, 90, 4, 2), (5, 130, 64, 8, 1), (1, 333, 0, 4, 4)])
+def test_attention_fwd_bwd(cuda, shape):
+    n, prompt, comp, Hq, Hkv = shape
+    torch.manual_seed(3)
+    kend, _ = _tree_kend(n, prompt, comp)
+    T = kend.numel()
+    D = 128
+    q = torch.randn(T, Hq, D, device=cuda, dtype=torch.bfloat16)
+    k = torch.randn(T, Hkv, D, device=cuda, dtype=torch.bfloat16)
+    v = torch.randn(T, Hkv, D, device=cuda, dtype=torch.bfloat16)
+    meta = fused.AttnMeta.build(torch.arange(T), kend, cuda)
+    scale = 1 / math.sqrt(D)
+    C = native.lib()
+    o, lse = C.attn_fwd(q, k, v, meta.kend, meta.tile_kmax, scale)
+    qr, kr, vr = (t.float().requires_grad_() for t in (q, k, v))
+    orf, lser = fused.attention_ref(qr, kr, vr, kend.to(cuda), scale)
+    assert rel_err(o, orf) < 1e-2
+    assert torch.allclose(lse, lser.float(), atol=2e-2, rtol=1e-3)
+    do = torch.randn_like(o)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    dq = C.attn_bwd(do, q, k, v, o, lse, meta.kend, meta.tile_kmax, scale, dk, dv)
+    orf.backward(do.float())
+    assert rel_err(dq, qr.grad) < 2e-2
+    assert rel_err(dk, kr.grad) < 2e-2
+    assert rel_err(dv, vr.grad) < 2e-2
+
+
+def test_logits_stats_and_grad(cuda):
+    torch.manual_seed(4)
+    T, V = 50, 152064
+    logits = (torch.randn(T, V, device=cuda) * 3).to(torch.bfloat16)
+    tgt = torch.randint(0, V, (T,), device=cuda)
+    C = native.lib()
+    lse, tl, ent = C.logits_stats(logits, tgt, True)
+    lf = logits.float()
+    lse_r = torch.logsumexp(lf, -1)
+    assert torch.allclose(lse, lse_r, atol=1e-3, rtol=1e-4)
+    assert torch.allclose(tl, lf.gather(1, tgt[:, None])[:, 0])
+    logp = lf - lse_r[:, None]
+    ent_r = -(logp.exp() * logp).sum(-1)
+    assert torch.allclose(ent, ent_r, atol=1e-2, rtol=1e-3)
+    g = torch.randn(T, device=cuda)
+    work = logits.clone()
+    C.logits_grad_(work, tgt, lse, g)
+    ref = g[:, None] * (torch.nn.functional.one_hot(tgt, V).float() - logp.exp())
+    assert rel_err(work, ref) < 1e-2
+
+
+@pytest.mark.parametrize("cfg", [{}, {"ppo": True}, {"kl_penalty_coef": 0.1}, {"ppo": True, "truncated_importance_sampling": 2.0}])
+def test_grpo_token_loss_matches_reference(cuda, cfg):
+    from art_mlx_b200.loss import AlignedLossInputs, loss_fn
+
+    torch.manual_seed(5)
+    n = 1000
+    new = (-torch.rand(n, device=cuda) * 3).requires_grad_()
+    old = -torch.rand(n, device=cuda) * 3
+    old[::17] = float("nan")
+    adv = torch.randn(n, device=cuda)
+    w = torch.rand(n, device=cuda)
+    ref = -torch.rand(n, device=cuda) * 3
+    denom = 777.0
+    ct = torch.tensor(fused.grpo_loss_config(cfg, n, denom), device=cuda)
+    loss, stats = fused.grpo_token_loss(new, old, adv, w, torch.ones(n, device=cuda), ref, None, ct)
+    loss.backward()
+    g_ours = new.grad.clone()
+    new.grad = None
+    inp = AlignedLossInputs(
+        assistant_mask=torch.ones(1, n, dtype=torch.bool, device=cuda), old_logprobs=old.view(1, n),
+        advantages=adv.view(1, n), weights=w.view(1, n), group_ids=torch.zeros(1, n, dtype=torch.long, device=cuda),
+    )
+    out = loss_fn(inp, new.view(1, n), ref.view(1, n), None, cfg, reduction="sum")
+    (out.policy_loss / denom).backward()
+    assert abs(float(loss) - float(out.policy_loss) / denom) < 1e-4 * max(1.0, abs(float(loss)))
+    assert rel_err(g_ours, new.grad) < 1e-4
+
+
+def test_adamw_matches_cpu(cuda):
+    from art_mlx_b200.models.lora import LoRAStore
+    from art_mlx_b200.runtime.optimizer import FlatAdamW
+
+    specs = [("a", (8, 100), "A"), ("b", (100, 8), "B")]
+    gpu = LoRAStore(specs, cuda, torch.bfloat16)
+    cpu = LoRAStore(specs, "cpu", torch.float32)
+    gpu.init_(0)
+    cpu.init_(0)
+    opt_g, opt_c = FlatAdamW(gpu), FlatAdamW(cpu)
+    for step in range(3):
+        g = torch.randn(cpu.numel) * 0.05
+        gpu.grad.copy_(g)
+        cpu.grad.copy_(g)
+        opt_g.step(1e-3, grad_scale=0.5)
+        opt_c.step(1e-3, grad_scale=0.5)
+    assert torch.allclose(gpu.master.cpu(), cpu.master, atol=1e-6, rtol=1e-5)
+    assert abs(float(opt_g.grad_norm) - float(opt_c.grad_norm)) < 1e-4
+
+
+def test_model_step_matches_cpu_fp32(cuda):
+    """One GRPO step of a small Qwen2-style model: GPU (bf16, fused kernels)
+    vs CPU fp32 PyTorch; logprob-level loss and LoRA gradients agree."""
+    from art_mlx_b200.models.config import LoRASpec, ModelConfig
+    from art_mlx_b200.preprocessing.pack import packed_tensors_from_tokenized_results
+    from art_mlx_b200.preprocessing.synthetic import synthetic_groups
+    from art_mlx_b200.preprocessing.tokenize import tokenize_trajectory_groups
+    from art_mlx_b200.runtime.trainer import GRPOTrainer
+
+    cfg = ModelConfig(
+        name="small", family="qwen3", vocab_size=2048, hidden_size=512, num_hidden_layers=2,
+        num_attention_heads=4, num_key_value_heads=2, head_dim=128, intermediate_size=1024,
+        qk_norm=True, attention_bias=True,
+    )
+    groups = synthetic_groups(num_groups=2, rollouts_per_group=4, prompt_len=100, completion_len=40, vocab_size=2048, seed=3)
+    res = list(tokenize_trajectory_groups(None, groups, False, True, rng=random.Random(0)))
+    packed = packed_tensors_from_tokenized_results(res, 1024, rng=random.Random(0))
+    lora = LoRASpec(r=8, alpha=16)
+    tg = GRPOTrainer(cfg, lora, cuda, seed=0)
+    tc = GRPOTrainer(cfg, lora, "cpu", seed=0)
+    # same weights: copy GPU bf16 weights into the CPU fp32 model
+    for lg, lc in zip(tg.model.layers, tc.model.layers):
+        for name in ("in_norm", "post_norm", "qkv_w", "qkv_b", "q_norm", "k_norm", "o_w"):
+            getattr(lc, name).copy_(getattr(lg, name).float().cpu())
+        lc.mlp.gu_w.copy_(lg.mlp.gu_w.float().cpu())
+        lc.mlp.down_w.copy_(lg.mlp.down_w.float().cpu())
+    tc.model.embed.copy_(tg.model.embed.float().cpu())
+    tc.model.lm_head.copy_(tg.model.lm_head.float().cpu())
+    # non-zero B so every LoRA factor gets a gradient
+    g = torch.Generator().manual_seed(0)
+    vals = torch.randn(tc.store.numel, generator=g) * 0.02
+    tc.store.master.copy_(vals)
+    tc.store.sync_compute()
+    tg.store.master.copy_(vals.to(cuda))
+    tg.store.sync_compute()
+    # compute gradients only (no optimizer step): run micro steps directly
+    from art_mlx_b200.runtime.trainer import stage_row
+
+    total = float(packed["assistant_mask"][:, 1:].sum())
+    for row in range(packed["tokens"].shape[0]):
+        og = tg.micro_step(stage_row(packed, row, cuda), {}, total)
+        oc = tc.micro_step(stage_row(packed, row, torch.device("cpu")), {}, total)
+        assert abs(float(og["loss"]) - float(oc["loss"])) < 2e-2 * max(1.0, abs(float(oc["loss"])))
+    assert rel_err(tg.store.grad.cpu(), tc.store.grad) < 5e-2
