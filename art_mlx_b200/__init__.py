@@ -1,0 +1,78 @@
+"""art_mlx_b200: a Blackwell-native (B200 / sm_100a) GRPO trainer for LLM agents.
+
+Public API (same names and call shapes as OpenPipe ART):
+
+    import art_mlx_b200 as art
+    model = art.TrainableModel(name=..., project=..., base_model=...)
+    await model.register(art.LocalBackend())
+    groups = await art.gather_trajectory_groups(...)
+    result = await backend.train(model, groups, learning_rate=5e-6)
+"""
+
+from . import dev
+from .backend import Backend
+from .gather import gather_trajectories, gather_trajectory_groups, trajectory_group_batches
+from .model import Model, TrainableModel
+from .trajectories import History, Trajectory, TrajectoryGroup
+from .types import (
+    LocalTrainResult,
+    MegatronRuntimeConfig,
+    MegatronTopologyConfig,
+    Messages,
+    MessagesAndChoices,
+    RuntimeConfig,
+    ServerlessTrainResult,
+    TopologyConfig,
+    Tools,
+    TrainConfig,
+    TrainResult,
+    TrainSFTConfig,
+)
+
+__version__ = "0.1.0"
+
+
+def __getattr__(name: str):
+    # heavy submodules (torch models, kernels) load on first use
+    if name == "LocalBackend":
+        from .backends.local import LocalBackend
+
+        return LocalBackend
+    if name == "MultiGPUBackend":
+        from .backends.multigpu import MultiGPUBackend
+
+        return MultiGPUBackend
+    if name == "PipelineTrainer":
+        from .pipeline_trainer.trainer import PipelineTrainer
+
+        return PipelineTrainer
+    raise AttributeError(name)
+
+
+__all__ = [
+    "Backend",
+    "History",
+    "LocalBackend",
+    "LocalTrainResult",
+    "MegatronRuntimeConfig",
+    "MegatronTopologyConfig",
+    "Messages",
+    "MessagesAndChoices",
+    "Model",
+    "MultiGPUBackend",
+    "PipelineTrainer",
+    "RuntimeConfig",
+    "ServerlessTrainResult",
+    "TopologyConfig",
+    "Tools",
+    "TrainConfig",
+    "TrainResult",
+    "TrainSFTConfig",
+    "TrainableModel",
+    "Trajectory",
+    "TrajectoryGroup",
+    "dev",
+    "gather_trajectories",
+    "gather_trajectory_groups",
+    "trajectory_group_batches",
+]

@@ -235,9 +235,8 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
     int64_t ldk, const __nv_bfloat16* __restrict__ v, int64_t ldv,
     const __nv_bfloat16* __restrict__ dout, int64_t lddo, const float* __restrict__ lse,
     const float* __restrict__ delta, const int* __restrict__ kend,
-    const int* __restrict__ tile_kmax, float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dk,
-    int64_t lddk, __nv_bfloat16* __restrict__ dv, int64_t lddv, int T, int Hq, int Hkv,
-    float scale) {
+    const int* __restrict__ units, float* __restrict__ dq_acc, float* __restrict__ dk_acc,
+    float* __restrict__ dv_acc, int T, int Hq, int Hkv, float scale) {
   static_assert(D == 128, "head_dim 128");
   constexpr int CH = D / 8;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -249,7 +248,10 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
   float* sL = reinterpret_cast<float*>(sdS + BWD_KEYS * DS_LD);  // 2 x 32 (log2 units)
   float* sDl = sL + 2 * BWD_Q;                                     // 2 x 32
 
-  const int kb = blockIdx.x, hk = blockIdx.y;
+  // work unit: (key block, first q tile, end q tile); the host splits the
+  // query range of heavily attended key blocks (shared prompts) into units
+  const int kb = units[3 * blockIdx.x], qt_lo = units[3 * blockIdx.x + 1], qt_hi = units[3 * blockIdx.x + 2];
+  const int hk = blockIdx.y;
   const int G = Hq / Hkv;
   const int j0 = kb * BWD_KEYS;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -266,14 +268,8 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
   }
   cp_async_commit();
 
-  // query range that can see this key block
-  const int nt64 = (T + 63) / 64;
-  int kmax = __ldg(tile_kmax + 2 * kb);
-  if (2 * kb + 1 < nt64) kmax = max(kmax, __ldg(tile_kmax + 2 * kb + 1));
-  kmax = min(kmax, T);
-  const int qt_begin = j0 / BWD_Q;
-  const int qt_end = (kmax + BWD_Q - 1) / BWD_Q;
-  const int nqt = max(qt_end - qt_begin, 0);
+  const int qt_begin = qt_lo;
+  const int nqt = max(qt_hi - qt_lo, 0);
   const int n_items = nqt * G;
 
   auto load_item = [&](int n, int st) {
@@ -440,18 +436,19 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
   }
   cp_async_wait<0>();
 
-  // write dK (scaled) and dV for this warp's 16 keys
+  // accumulate dK (scaled) and dV for this warp's 16 keys (several units may
+  // cover the same key block)
   const int ja = j0 + kr0, jb = j0 + kr1;
 #pragma unroll
   for (int nd = 0; nd < D / 8; ++nd) {
     const int col = hk * D + nd * 8 + 2 * (lane & 3);
     if (ja < T) {
-      *reinterpret_cast<uint32_t*>(dk + (int64_t)ja * lddk + col) = pack_bf16x2(dkacc[nd][0] * scale, dkacc[nd][1] * scale);
-      *reinterpret_cast<uint32_t*>(dv + (int64_t)ja * lddv + col) = pack_bf16x2(dvacc[nd][0], dvacc[nd][1]);
+      red_add_v2(dk_acc + (int64_t)ja * Hkv * D + col, dkacc[nd][0] * scale, dkacc[nd][1] * scale);
+      red_add_v2(dv_acc + (int64_t)ja * Hkv * D + col, dvacc[nd][0], dvacc[nd][1]);
     }
     if (jb < T) {
-      *reinterpret_cast<uint32_t*>(dk + (int64_t)jb * lddk + col) = pack_bf16x2(dkacc[nd][2] * scale, dkacc[nd][3] * scale);
-      *reinterpret_cast<uint32_t*>(dv + (int64_t)jb * lddv + col) = pack_bf16x2(dvacc[nd][2], dvacc[nd][3]);
+      red_add_v2(dk_acc + (int64_t)jb * Hkv * D + col, dkacc[nd][2] * scale, dkacc[nd][3] * scale);
+      red_add_v2(dv_acc + (int64_t)jb * Hkv * D + col, dvacc[nd][2], dvacc[nd][3]);
     }
   }
 }
@@ -493,10 +490,11 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   return {o, lse};
 }
 
-// Writes dq (fp32 accumulate -> returned), dk, dv into the given views.
-torch::Tensor attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
-                       torch::Tensor out, torch::Tensor lse, torch::Tensor kend,
-                       torch::Tensor tile_kmax, double scale, torch::Tensor dk, torch::Tensor dv) {
+// Backward.  units [n, 3] int32 = (key block of 128, q tile lo, q tile hi) in
+// 32-query tiles.  Returns {dq, dk, dv} fp32 accumulators [T, H, D].
+std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k,
+                                    torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                                    torch::Tensor kend, torch::Tensor units, double scale) {
   const int64_t T = q.size(0), Hq = q.size(1), D = q.size(2), Hkv = k.size(1);
   TORCH_CHECK(D == 128);
   check_view(q, T, Hq, D, "q");
@@ -504,11 +502,14 @@ torch::Tensor attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, tor
   check_view(v, T, Hkv, D, "v");
   check_view(dout, T, Hq, D, "dout");
   check_view(out, T, Hq, D, "out");
-  check_view(dk, T, Hkv, D, "dk");
-  check_view(dv, T, Hkv, D, "dv");
-  auto dq_acc = torch::zeros({T, Hq, D}, q.options().dtype(at::kFloat));
-  if (T == 0) return dq_acc;
-  auto delta = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
+  TORCH_CHECK(units.scalar_type() == at::kInt && units.is_contiguous() && units.dim() == 2 && units.size(1) == 3);
+  auto f32 = q.options().dtype(at::kFloat);
+  auto dq_acc = torch::zeros({T, Hq, D}, f32);
+  auto dk_acc = torch::zeros({T, Hkv, D}, f32);
+  auto dv_acc = torch::zeros({T, Hkv, D}, f32);
+  const int64_t n_units = units.size(0);
+  if (T == 0 || n_units == 0) return {dq_acc, dk_acc, dv_acc};
+  auto delta = torch::empty({Hq, T}, f32);
   auto stream = at::cuda::getCurrentCUDAStream();
   {
     const int64_t warps = T * Hq;
@@ -521,18 +522,16 @@ torch::Tensor attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, tor
                       4 * BWD_Q * sizeof(float);
   auto kern = attn_bwd_kernel<128>;
   ART_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  dim3 grid((T + BWD_KEYS - 1) / BWD_KEYS, Hkv);
+  dim3 grid((unsigned)n_units, Hkv);
   kern<<<grid, 256, smem, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()), k.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), v.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0), lse.data_ptr<float>(),
-      delta.data_ptr<float>(), kend.data_ptr<int>(), tile_kmax.data_ptr<int>(),
-      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), dk.stride(0),
-      reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()), dv.stride(0), (int)T, (int)Hq, (int)Hkv,
-      (float)scale);
+      delta.data_ptr<float>(), kend.data_ptr<int>(), units.data_ptr<int>(), dq_acc.data_ptr<float>(),
+      dk_acc.data_ptr<float>(), dv_acc.data_ptr<float>(), (int)T, (int)Hq, (int)Hkv, (float)scale);
   ART_CUDA_CHECK(cudaGetLastError());
-  return dq_acc;
+  return {dq_acc, dk_acc, dv_acc};
 }
 
 }  // namespace art

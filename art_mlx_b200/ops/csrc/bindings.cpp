@@ -27,9 +27,9 @@ void adamw_step(torch::Tensor p, torch::Tensor p16, torch::Tensor g, torch::Tens
                 torch::Tensor v, torch::Tensor hp, torch::Tensor norm_sq, torch::Tensor norm_out);
 std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                     torch::Tensor kend, torch::Tensor tile_kmax, double scale);
-torch::Tensor attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
-                       torch::Tensor out, torch::Tensor lse, torch::Tensor kend,
-                       torch::Tensor tile_kmax, double scale, torch::Tensor dk, torch::Tensor dv);
+std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k,
+                                    torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                                    torch::Tensor kend, torch::Tensor units, double scale);
 }  // namespace art
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

@@ -33,9 +33,43 @@ def _cuda(t: torch.Tensor) -> bool:
     return t.device.type == "cuda"
 
 
+def _acc(t: torch.Tensor) -> torch.Tensor:
+    """Accumulation precision of the CPU reference path: fp32, or fp64 when
+    the inputs already are fp64."""
+    return t if t.dtype == torch.float64 else t.float()
+
+
 # ---------------------------------------------------------------------------
 # Attention metadata (per packed row)
 # ---------------------------------------------------------------------------
+
+
+BWD_KEYS = 128  # key block of the attention backward kernel
+BWD_Q = 32  # query tile of the attention backward kernel
+BWD_MAX_QTILES = 8  # query tiles per backward work unit
+
+
+def attention_bwd_units(kend: torch.Tensor, max_qtiles: int = BWD_MAX_QTILES) -> torch.Tensor:
+    """Backward work units ``[n, 3]`` = (key block, q tile lo, q tile hi).
+
+    Key block ``kb`` (128 keys) is seen by queries ``[128 kb, max kend)``;
+    that range (in 32-query tiles) is split into units of at most
+    ``max_qtiles`` tiles so a shared prompt attended by every completion is
+    spread over many CTAs instead of serialising on a few.
+    """
+    T = int(kend.numel())
+    if T == 0:
+        return torch.zeros(0, 3, dtype=torch.int32)
+    nkb = (T + BWD_KEYS - 1) // BWD_KEYS
+    kp = torch.nn.functional.pad(kend.to(torch.int64), (0, nkb * BWD_KEYS - T), value=0)
+    kmax = kp.view(nkb, BWD_KEYS).amax(1).clamp(max=T).tolist()
+    units = []
+    for kb in range(nkb):
+        lo = kb * BWD_KEYS // BWD_Q
+        hi = (kmax[kb] + BWD_Q - 1) // BWD_Q
+        for a in range(lo, hi, max_qtiles):
+            units.append((kb, a, min(hi, a + max_qtiles)))
+    return torch.tensor(units, dtype=torch.int32).view(-1, 3)
 
 
 @dataclass
@@ -44,25 +78,32 @@ class AttnMeta:
 
     ``kend[j]``: query ``i`` may attend key ``j`` iff ``j <= i < kend[j]``.
     ``tile_kmax[t]``: max of ``kend`` over keys ``[64t, 64t+64)`` (tile skip).
+    ``bwd_units``: load-balanced work list of the attention backward.
     """
 
     positions: torch.Tensor  # int32 [T]
     kend: torch.Tensor  # int32 [T]
     tile_kmax: torch.Tensor  # int32 [ceil(T/64)]
     T: int
+    bwd_units: torch.Tensor | None = None  # int32 [n, 3]
 
     @staticmethod
     def build(positions: torch.Tensor, kend: torch.Tensor, device: torch.device) -> "AttnMeta":
+        """``kend`` may live on any device; the work list is planned on the CPU."""
         T = int(kend.numel())
         pad = (-T) % 64
-        k = kend.to(torch.int32)
-        kp = torch.nn.functional.pad(k, (0, pad), value=0)
+        k_cpu = kend.detach().to("cpu", torch.int32)
+        kp = torch.nn.functional.pad(k_cpu, (0, pad), value=0)
         tile = kp.view(-1, 64).amax(dim=1).to(torch.int32)
+        units = attention_bwd_units(k_cpu)
+        pin = device.type == "cuda"
+        mv = lambda t: (t.pin_memory() if pin else t).to(device, non_blocking=True)  # noqa: E731
         return AttnMeta(
             positions=positions.to(device=device, dtype=torch.int32, non_blocking=True),
-            kend=k.to(device, non_blocking=True),
-            tile_kmax=tile.to(device, non_blocking=True),
+            kend=mv(k_cpu),
+            tile_kmax=mv(tile),
             T=T,
+            bwd_units=mv(units),
         )
 
 
@@ -78,7 +119,7 @@ def rope_inv_freq(head_dim: int, theta: float, device: torch.device) -> torch.Te
 
 
 def _rmsnorm_ref(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
+    xf = _acc(x)
     r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
     return (xf * r).to(x.dtype) * w
 
@@ -116,7 +157,9 @@ def add_rmsnorm(
 
 def _rope_ref(x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor) -> torch.Tensor:
     # x [T, H, D]; rotate-half convention
-    ang = pos.float().unsqueeze(-1) * inv_freq.unsqueeze(0)  # [T, D/2]
+    ang = _acc(pos.to(x.dtype) if x.dtype == torch.float64 else pos.float()).unsqueeze(-1) * inv_freq.to(
+        torch.float64 if x.dtype == torch.float64 else torch.float32
+    ).unsqueeze(0)  # [T, D/2]
     cos = torch.cat([ang.cos(), ang.cos()], -1).unsqueeze(1).to(x.dtype)
     sin = torch.cat([ang.sin(), ang.sin()], -1).unsqueeze(1).to(x.dtype)
     d = x.shape[-1] // 2
@@ -130,9 +173,9 @@ def attention_ref(
     """Dense-mask prefix-tree attention in fp32 math (oracle). q [T,Hq,D]."""
     T, Hq, D = q.shape
     G = Hq // k.shape[1]
-    kx = k.float().repeat_interleave(G, dim=1)
-    vx = v.float().repeat_interleave(G, dim=1)
-    s = torch.einsum("ihd,jhd->hij", q.float(), kx) * scale
+    kx = _acc(k).repeat_interleave(G, dim=1)
+    vx = _acc(v).repeat_interleave(G, dim=1)
+    s = torch.einsum("ihd,jhd->hij", _acc(q), kx) * scale
     i = torch.arange(T, device=q.device).view(T, 1)
     j = torch.arange(T, device=q.device).view(1, T)
     mask = (j <= i) & (i < kend.to(q.device).long().view(1, T))
@@ -173,10 +216,10 @@ class _RopeAttention(torch.autograd.Function):
         v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
         dqkv = torch.empty_like(qkv)
         dqk = torch.empty_like(qk)
-        dk = dqk[:, nq * D :].view(T, nkv, D)
-        dv = dqkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
-        dq_acc = C.attn_bwd(do, q, k, v, o, lse, meta.kend, meta.tile_kmax, scale, dk, dv)
+        dq_acc, dk_acc, dv_acc = C.attn_bwd(do, q, k, v, o, lse, meta.kend, meta.bwd_units, scale)
         dqk[:, : nq * D].copy_(dq_acc.view(T, nq * D))
+        dqk[:, nq * D :].copy_(dk_acc.view(T, nkv * D))
+        dqkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].copy_(dv_acc.view(T, nkv * D))
         C.rope_bwd(dqk, qkv, meta.positions, inv_freq, nq, nkv, D,
                    qn_w if has_norm else None, kn_w if has_norm else None,
                    rstd if has_norm else None, dqkv)
@@ -401,7 +444,7 @@ def lm_head_logprobs(
     """Per-row ``log softmax(h W^T)[target]`` (fp32) and entropy (no grad)."""
     if _cuda(h):
         return _LMHeadLogprobs.apply(h, W, targets, chunk, entropy)
-    logits = (h @ W.t()).float()
+    logits = _acc(h @ W.t())
     lse = torch.logsumexp(logits, dim=-1)
     lp = logits.gather(-1, targets.clamp_min(0).unsqueeze(-1)).squeeze(-1) - lse
     ent = None

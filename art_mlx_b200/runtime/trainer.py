@@ -54,6 +54,7 @@ class MicroBatch:
     routes: torch.Tensor | None = None  # [L, layers, k] replayed MoE routes
     n_tokens: int = 0  # valid (non-padding) tokens in the row
     n_train: int = 0
+    h2d_bytes: int = 0  # bytes copied host -> device to stage this row
 
     @property
     def L(self) -> int:
@@ -88,8 +89,11 @@ def stage_row(
     kend = visibility_ends(packed["group_ids"][row : row + 1, :L], packed["parent_ids"][row : row + 1, :L])[0]
     pos = packed["input_pos"][row, :L]
 
+    moved = [0]
+
     def dev(t: torch.Tensor) -> torch.Tensor:
         t = t.contiguous()
+        moved[0] += t.numel() * t.element_size()
         if pin and device.type == "cuda":
             t = t.pin_memory()
         return t.to(device, non_blocking=True)
@@ -99,9 +103,11 @@ def stage_row(
     if rr is not None:
         routes = dev(rr.expert_indices[row, :L])
     orig = packed.get("original_logprobs")
+    meta = AttnMeta.build(dev(pos), kend, device)
+    moved[0] += sum(t.numel() * t.element_size() for t in (meta.kend, meta.tile_kmax, meta.bwd_units))
     return MicroBatch(
         tokens=dev(tokens),
-        meta=AttnMeta.build(dev(pos), dev(kend), device),
+        meta=meta,
         sel=dev(sel),
         targets=dev(packed["tokens"][row, nxt]),
         old=dev(packed["logprobs"][row, nxt].float()),
@@ -112,6 +118,7 @@ def stage_row(
         routes=routes,
         n_tokens=n_valid,
         n_train=int(sel.numel()),
+        h2d_bytes=moved[0],
     )
 
 
@@ -180,6 +187,40 @@ class GRPOTrainer:
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         self.logprob_chunk = logprob_chunk
         self.grad_sync = None  # optional fused data-parallel reducer (parallel/dp.py)
+        self.ref_flat: torch.Tensor | None = None  # KL reference adapter (compute dtype)
+
+    def set_reference_adapter(self, state: Mapping[str, torch.Tensor] | None) -> None:
+        """Use a saved adapter (PEFT state dict) as the KL reference; ``None``
+        means the frozen base model (adapter disabled)."""
+        if state is None:
+            self.ref_flat = None
+            return
+        st = self.store
+        flat = torch.zeros_like(st.compute)
+        for name, e in st.entries.items():
+            if name in state:
+                flat[e.offset : e.offset + e.numel].copy_(state[name].reshape(-1).to(flat.dtype))
+        self.ref_flat = flat
+
+    def _reference_logprobs(self, mb: "MicroBatch", ctx: dict[str, Any]) -> torch.Tensor:
+        st = self.store
+        with torch.no_grad():
+            if self.ref_flat is None:
+                self.model.lora_enabled = False
+                try:
+                    ref, _ = self._logprobs(mb, dict(ctx), entropy=False)
+                finally:
+                    self.model.lora_enabled = True
+                return ref
+            saved = st.compute.clone()
+            st.compute.copy_(self.ref_flat)
+            st.version += 1
+            try:
+                ref, _ = self._logprobs(mb, dict(ctx), entropy=False)
+            finally:
+                st.compute.copy_(saved)
+                st.version += 1
+            return ref
 
     # ------------------------------------------------------------------
     def _logprobs(self, mb: MicroBatch, ctx: dict[str, Any], entropy: bool) -> tuple[torch.Tensor, torch.Tensor | None]:
@@ -198,12 +239,7 @@ class GRPOTrainer:
         ref = None
         kl_coef = float(cfg.get("kl_penalty_coef", 0.0) or 0.0)
         if kl_coef > 0:
-            with torch.no_grad():
-                self.model.lora_enabled = False
-                try:
-                    ref, _ = self._logprobs(mb, dict(ctx), entropy=False)
-                finally:
-                    self.model.lora_enabled = True
+            ref = self._reference_logprobs(mb, ctx)
         lp, ent = self._logprobs(mb, ctx, entropy=True)
         n = lp.numel()
         level = cfg.get("importance_sampling_level", "token")
@@ -278,3 +314,31 @@ class GRPOTrainer:
             loss=acc["loss"], entropy=acc["entropy"], probs_corr=acc["probs_corr"], kl=acc["kl"],
             grad_norm=self.optim.grad_norm, n_train=int(total), n_tokens=n_tokens,
         )
+
+    # ------------------------------------------------------------------
+    def sft_step(self, batch: list[tuple[list[int], list[int]]], learning_rate: float) -> dict[str, float]:
+        """One supervised step: mean negative log-likelihood of the label
+        tokens (``-100`` = ignored) over the whole batch, then AdamW."""
+        rows = batch[self.rank :: self.world]
+        total = sum(sum(1 for v in labels[1:] if v != -100) for _, labels in batch)
+        total = max(total, 1)
+        acc = torch.zeros((), device=self.device)
+        for ids, labels in rows:
+            L = len(ids)
+            lab = torch.tensor(labels, dtype=torch.long)
+            sel = (lab[1:] != -100).nonzero().squeeze(1)
+            kend = torch.full((L,), L, dtype=torch.int32)
+            meta = AttnMeta.build(torch.arange(L), kend, self.device)
+            toks = torch.tensor(ids, dtype=torch.long).to(self.device)
+            h = self.model.forward(toks, meta, {})
+            hs = h.index_select(0, sel.to(self.device))
+            lp, _ = fused.lm_head_logprobs(hs, self.model.lm_head, lab[1:][sel].to(self.device), self.logprob_chunk, False)
+            loss = -lp.sum() / total
+            loss.backward()
+            acc += loss.detach()
+        if self.world > 1:
+            dist.all_reduce(self.store.grad, group=self.group)
+            dist.all_reduce(acc, group=self.group)
+        self.optim.step(learning_rate)
+        vals = torch.stack([acc, self.optim.grad_norm.reshape(())]).cpu().tolist()
+        return {"loss/train": vals[0], "loss/grad_norm": vals[1], "data/step_trainer_tokens": float(total)}
