@@ -314,8 +314,10 @@ class LocalBackend:
         self.last_d2h_bytes = 5 * 4
         new_step = step + 1
         ck = get_step_checkpoint_dir(d, new_step)
-        if save_checkpoint and _rank() == 0:
-            save_adapter(ck, tr.store, model.base_model, tr.model.lora_spec, tr.optim.state_dict())
+        if save_checkpoint:
+            tr.prepare_checkpoint()
+            if _rank() == 0:
+                save_adapter(ck, tr.store, model.base_model, tr.model.lora_spec, tr.optim.state_dict())
         _barrier()
         metrics["time/step_trainer_s"] = time.monotonic() - started
         metrics[("data/step_num_gradient_steps")] = 1.0

@@ -40,7 +40,11 @@ class LoRAStore:
         specs: list[tuple[str, tuple[int, ...], str]],
         device: torch.device | str,
         compute_dtype: torch.dtype,
+        compute_buf: torch.Tensor | None = None,
+        grad_buf: torch.Tensor | None = None,
     ) -> None:
+        """``compute_buf`` / ``grad_buf`` (optional) place the compute copy and
+        the gradient in caller-provided memory (e.g. a peer-mapped arena)."""
         self.entries: dict[str, Entry] = {}
         off = 0
         for name, shape, kind in specs:
@@ -50,12 +54,20 @@ class LoRAStore:
         self.device = torch.device(device)
         self.compute_dtype = compute_dtype
         self.master = torch.zeros(off, dtype=torch.float32, device=self.device)
-        self.compute = (
-            self.master
-            if compute_dtype == torch.float32
-            else torch.zeros(off, dtype=compute_dtype, device=self.device)
-        )
-        self.grad = torch.zeros(off, dtype=torch.float32, device=self.device)
+        if compute_buf is not None:
+            assert compute_buf.numel() == off and compute_buf.dtype == compute_dtype
+            self.compute = compute_buf
+        else:
+            self.compute = (
+                self.master
+                if compute_dtype == torch.float32
+                else torch.zeros(off, dtype=compute_dtype, device=self.device)
+            )
+        if grad_buf is not None:
+            assert grad_buf.numel() == off and grad_buf.dtype == torch.float32
+            self.grad = grad_buf
+        else:
+            self.grad = torch.zeros(off, dtype=torch.float32, device=self.device)
         self.exp_avg = torch.zeros(off, dtype=torch.float32, device=self.device)
         self.exp_avg_sq = torch.zeros(off, dtype=torch.float32, device=self.device)
         self.version = 0  # bumped whenever the parameters change
@@ -95,6 +107,10 @@ class LoRAStore:
             else:
                 v.zero_()
         self.sync_compute()
+
+    @staticmethod
+    def numel_for(specs: list[tuple[str, tuple[int, ...], str]]) -> int:
+        return sum((math.prod(s) + ALIGN - 1) // ALIGN * ALIGN for _, s, _ in specs)
 
     def sync_compute(self) -> None:
         if self.compute is not self.master:

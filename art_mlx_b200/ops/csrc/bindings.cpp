@@ -30,6 +30,22 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
 std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k,
                                     torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                                     torch::Tensor kend, torch::Tensor units, double scale);
+std::vector<torch::Tensor> ipc_alloc(int64_t nbytes);
+int64_t ipc_open(torch::Tensor handle);
+void ipc_close(int64_t ptr);
+void peer_barrier(torch::Tensor flag_bases, int64_t rank, int64_t world, int64_t epoch,
+                  int64_t timeout_ns, torch::Tensor status);
+void dp_reduce_sumsq(torch::Tensor grad_bases, int64_t world, int64_t off, int64_t n,
+                     torch::Tensor partial);
+void dp_publish_norm(torch::Tensor norm_bases, int64_t rank, int64_t world, torch::Tensor partial);
+void dp_adamw_allgather(torch::Tensor compute_bases, int64_t world, int64_t off, int64_t n,
+                        torch::Tensor grad_shard, torch::Tensor master, torch::Tensor m,
+                        torch::Tensor v, torch::Tensor hp, torch::Tensor norms,
+                        torch::Tensor norm_out);
+torch::Tensor gemm_tc(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> a2,
+                      c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> bias,
+                      c10::optional<torch::Tensor> out, bool accumulate);
+int64_t tc_error_code();
 }  // namespace art
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -47,4 +63,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &art::adamw_step);
   m.def("attn_fwd", &art::attn_fwd);
   m.def("attn_bwd", &art::attn_bwd);
+  m.def("gemm_tc", &art::gemm_tc);
+  m.def("tc_error_code", &art::tc_error_code);
+  m.def("ipc_alloc", &art::ipc_alloc);
+  m.def("ipc_open", &art::ipc_open);
+  m.def("ipc_close", &art::ipc_close);
+  m.def("peer_barrier", &art::peer_barrier);
+  m.def("dp_reduce_sumsq", &art::dp_reduce_sumsq);
+  m.def("dp_publish_norm", &art::dp_publish_norm);
+  m.def("dp_adamw_allgather", &art::dp_adamw_allgather);
 }

@@ -177,17 +177,41 @@ class GRPOTrainer:
         adamw: AdamWConfig | None = None,
         group: dist.ProcessGroup | None = None,
         logprob_chunk: int = 4096,
+        fused_dp: bool = True,
     ) -> None:
         self.device = torch.device(device)
-        self.model = DecoderLM(cfg, lora, self.device, seed=seed)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        self.grad_sync = None  # fused data-parallel reducer (parallel/dp.py) on GPUs
+        store = None
+        if self.world > 1 and self.device.type == "cuda" and fused_dp:
+            from ..models.lora import LoRAStore
+            from ..models.transformer import lora_specs_for
+            from ..parallel.dp import FusedDataParallel
+
+            specs = lora_specs_for(cfg, lora)
+            dtype = torch.bfloat16
+            self.grad_sync = FusedDataParallel(LoRAStore.numel_for(specs), dtype, group, self.device)
+            store = LoRAStore(specs, self.device, dtype, compute_buf=self.grad_sync.compute,
+                              grad_buf=self.grad_sync.grad)
+            store.init_(seed + 1)
+        self.model = DecoderLM(cfg, lora, self.device, seed=seed, store=store)
         self.store = self.model.store
         self.optim = FlatAdamW(self.store, adamw)
-        self.group = group
-        self.world = dist.get_world_size(group) if (group is not None or dist.is_initialized()) and dist.is_initialized() else 1
-        self.rank = dist.get_rank(group) if self.world > 1 else 0
         self.logprob_chunk = logprob_chunk
-        self.grad_sync = None  # optional fused data-parallel reducer (parallel/dp.py)
         self.ref_flat: torch.Tensor | None = None  # KL reference adapter (compute dtype)
+
+    def prepare_checkpoint(self) -> None:
+        """Collective: make the full master weights / moments current on every
+        rank (with the fused data-parallel optimizer each rank updates only its
+        shard).  Every rank must call it before rank 0 writes a checkpoint."""
+        if self.grad_sync is not None:
+            self.grad_sync.gather_full_state(self.store)
+
+    def check_health(self) -> None:
+        if self.grad_sync is not None:
+            self.grad_sync.check()
 
     def set_reference_adapter(self, state: Mapping[str, torch.Tensor] | None) -> None:
         """Use a saved adapter (PEFT state dict) as the KL reference; ``None``

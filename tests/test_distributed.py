@@ -1,0 +1,97 @@
+"""Data-parallel training equals single-process training on the same rows.
+
+CPU: 2 gloo ranks, NCCL-free gradient all-reduce path.
+GPU (>= 2 devices): 2 NCCL ranks with the fused peer-memory reduce-scatter +
+AdamW + all-gather kernel.
+"""
+
+import os
+import random
+import tempfile
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from art_mlx_b200.models.config import LoRASpec, ModelConfig, get_config
+from art_mlx_b200.preprocessing.pack import packed_tensors_from_tokenized_results
+from art_mlx_b200.preprocessing.synthetic import synthetic_groups
+from art_mlx_b200.preprocessing.tokenize import tokenize_trajectory_groups
+from art_mlx_b200.runtime.trainer import GRPOTrainer
+
+GPU_CFG = ModelConfig(
+    name="dp-small", family="qwen2", vocab_size=2048, hidden_size=256, num_hidden_layers=2,
+    num_attention_heads=2, num_key_value_heads=1, head_dim=128, intermediate_size=512, attention_bias=True,
+)
+
+
+def _packed(vocab: int, prompt: int, comp: int, seq_len: int):
+    groups = synthetic_groups(num_groups=4, rollouts_per_group=4, prompt_len=prompt, completion_len=comp,
+                              vocab_size=vocab, seed=11)
+    res = list(tokenize_trajectory_groups(None, groups, False, True, rng=random.Random(0)))
+    return packed_tensors_from_tokenized_results(res, seq_len, rng=random.Random(0))
+
+
+def _worker(rank, world, init_file, out_path, backend, cfg_name):
+    if backend == "nccl":
+        torch.cuda.set_device(rank)
+        device = torch.device("cuda", rank)
+    else:
+        device = torch.device("cpu")
+    from datetime import timedelta
+
+    dist.init_process_group(backend, init_method=f"file://{init_file}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120))
+    try:
+        cfg = get_config(cfg_name) if cfg_name != "dp-small" else GPU_CFG
+        packed = _packed(cfg.vocab_size, 24 if backend == "gloo" else 96, 12 if backend == "gloo" else 48,
+                         128 if backend == "gloo" else 512)
+        tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), device, seed=0, group=dist.group.WORLD)
+        assert (tr.grad_sync is not None) == (backend == "nccl")
+        for _ in range(2):
+            m = tr.train_step(packed, 1e-3, {})
+        host = m.to_host()
+        tr.check_health()
+        tr.prepare_checkpoint()
+        if rank == 0:
+            torch.save({"master": tr.store.master.cpu(), "metrics": host}, out_path)
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _single(device, cfg, backend):
+    packed = _packed(cfg.vocab_size, 24 if backend == "gloo" else 96, 12 if backend == "gloo" else 48,
+                     128 if backend == "gloo" else 512)
+    tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), device, seed=0)
+    for _ in range(2):
+        m = tr.train_step(packed, 1e-3, {})
+    return tr.store.master.cpu(), m.to_host(), packed
+
+
+def _run(world, backend, cfg_name):
+    d = tempfile.mkdtemp()
+    init = os.path.join(d, "init")
+    out = os.path.join(d, "out.pt")
+    mp.start_processes(_worker, args=(world, init, out, backend, cfg_name), nprocs=world, start_method="spawn")
+    return torch.load(out)
+
+
+def test_dp_gloo_matches_single_process():
+    res = _run(2, "gloo", "tiny-qwen3")
+    master, metrics, packed = _single(torch.device("cpu"), get_config("tiny-qwen3"), "gloo")
+    assert packed["tokens"].shape[0] >= 2
+    assert torch.allclose(res["master"], master, atol=1e-6, rtol=1e-5)
+    assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-5
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_dp_two_gpus_matches_single_gpu():
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    res = _run(2, "nccl", "dp-small")
+    master, metrics, _ = _single(torch.device("cuda", 0), GPU_CFG, "nccl")
+    err = (res["master"] - master).norm() / master.norm()
+    assert err < 1e-3, err
+    assert abs(res["metrics"]["loss/grad_norm"] - metrics["loss/grad_norm"]) < 2e-2 * abs(metrics["loss/grad_norm"])
