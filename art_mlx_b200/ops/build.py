@@ -43,7 +43,7 @@ def build(verbose: bool = False) -> str:
     # torch's own arch list must not add other targets: the -gencode flags
     # above are the only architecture selection.
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
-    extra_ldflags = ["-lcuda", "-lnccl"] if _have_nccl() else ["-lcuda"]
+    extra_ldflags: list[str] = []  # no libcuda link: driver entry points are resolved at run time
     mod = cpp_extension.load(
         name="art_b200_C",
         sources=sources(),
@@ -60,9 +60,6 @@ def build(verbose: bool = False) -> str:
     os.replace(SO_PATH + ".tmp", SO_PATH)
     return SO_PATH
 
-
-def _have_nccl() -> bool:
-    return False
 
 
 if __name__ == "__main__":

@@ -21,6 +21,7 @@
 // Every mbarrier wait is bounded (see tc_common.cuh); TMEM is always freed.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
+#include <cudaTypedefs.h>
 #include "common.cuh"
 #include "tc_common.cuh"
 
@@ -208,6 +209,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 }
 
 // ---------------------------------------------------------------- host side
+// The driver entry point is resolved at run time (through the runtime API) so
+// the extension has no link-time dependency on libcuda and imports on hosts
+// without a GPU driver.
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    ART_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && ptr, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
 static CUtensorMap make_tmap_2d(const torch::Tensor& t, int box_rows) {
   TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.stride(1) == 1, "bf16 row-major 2-D tensor");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0, "TMA base must be 16-byte aligned");
@@ -217,7 +233,7 @@ static CUtensorMap make_tmap_2d(const torch::Tensor& t, int box_rows) {
   cuuint64_t strides[1] = {(cuuint64_t)(t.stride(0) * 2)};
   cuuint32_t box[2] = {(cuuint32_t)GBK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), dims, strides, box,
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), dims, strides, box,
                                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
