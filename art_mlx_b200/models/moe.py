@@ -1,16 +1,20 @@
-"""Mixture-of-experts FFN (Qwen3-MoE style) with per-expert LoRA and
-routing replay.
+"""Mixture-of-experts FFN (Qwen3-MoE style) with per-expert LoRA, routing
+replay and expert parallelism.
 
 Routing: ``softmax(h W_router^T)`` over experts, top-k, renormalised when
 ``norm_topk_prob``.  With routing replay (reference
 ``src/art/megatron/routing_replay.py:696-1084``) the top-k expert ids come
 from the rollout engine's record for each token and layer; the weights are
-still the current router's probabilities at those ids, so the router's
-computation graph matches the sampled policy.
+still the current router's probabilities at those ids, so gradients reach the
+router exactly as for the sampled policy.
 
-Expert compute is a grouped GEMM over tokens sorted by expert.  The LoRA
-factors of all experts of a layer are stacked views ``[E, ...]`` into the
-flat store, so the adapter update is itself two grouped GEMMs.
+Experts run as grouped GEMMs over tokens laid out expert-contiguous.  The
+LoRA factors of all experts of a layer are stacked ``[E, ...]`` views into the
+flat store, so the adapter is itself grouped GEMMs (rank-r).  Under expert
+parallelism (:mod:`art_mlx_b200.parallel.ep`) a rank holds the base weights
+of its ``E / world`` experts; the LoRA store keeps every expert (non-local
+experts simply receive zero gradient on this rank), which lets the
+data-parallel optimizer reduce expert and shared parameters alike.
 """
 
 from __future__ import annotations
@@ -19,8 +23,8 @@ from typing import Any, Callable
 
 import torch
 
-from .config import LoRASpec, ModelConfig
 from ..ops.fused import grad_anchor
+from .config import LoRASpec, ModelConfig
 from .lora import LoRAStore, peft_key
 
 
@@ -43,9 +47,29 @@ def moe_lora_specs(cfg: ModelConfig, i: int, spec: LoRASpec) -> list[tuple[str, 
     return out
 
 
+# ---------------------------------------------------------------------------
+# grouped GEMM helpers
+# ---------------------------------------------------------------------------
+
+
+def _offsets(counts: list[int], device: torch.device) -> torch.Tensor:
+    return torch.tensor(counts, dtype=torch.int64).cumsum(0).to(torch.int32).to(device, non_blocking=True)
+
+
+def _use_library_grouped(x: torch.Tensor, k: int, m: int) -> bool:
+    return (
+        x.device.type == "cuda" and x.dtype == torch.bfloat16 and hasattr(torch, "_grouped_mm")
+        and k % 8 == 0 and m % 8 == 0
+    )
+
+
 def grouped_mm(x: torch.Tensor, w: torch.Tensor, counts: list[int]) -> torch.Tensor:
-    """Rows of ``x`` [N, K] are grouped by expert (``counts``); returns
-    ``[N, M]`` with group ``e`` multiplied by ``w[e]`` ([E, K, M])."""
+    """Rows of ``x`` [N, K] grouped by expert (``counts``) times ``w[e]``
+    ([E, K, M]) -> [N, M].  On GPUs this is one grouped GEMM launch."""
+    if _use_library_grouped(x, x.shape[1], w.shape[-1]):
+        if x.shape[0] == 0:
+            return x.new_zeros(0, w.shape[-1])
+        return torch._grouped_mm(x.contiguous(), w, offs=_offsets(counts, x.device))
     outs = []
     s = 0
     for e, c in enumerate(counts):
@@ -59,6 +83,11 @@ def grouped_mm(x: torch.Tensor, w: torch.Tensor, counts: list[int]) -> torch.Ten
 
 def grouped_wgrad(a: torch.Tensor, b: torch.Tensor, counts: list[int], out: torch.Tensor, alpha: float) -> None:
     """``out[e] += alpha * a_e^T b_e`` (fp32 accumulate) for row groups ``e``."""
+    if _use_library_grouped(a, a.shape[1], b.shape[1]) and a.shape[0] > 0:
+        g = torch._grouped_mm(a.t().contiguous(), b.contiguous(), offs=_offsets(counts, a.device),
+                              out_dtype=torch.float32)
+        out.add_(g.view(out.shape), alpha=alpha)
+        return
     s = 0
     for e, c in enumerate(counts):
         if c:
@@ -66,86 +95,149 @@ def grouped_wgrad(a: torch.Tensor, b: torch.Tensor, counts: list[int], out: torc
             if out.device.type == "cuda" and ae.dtype != torch.float32:
                 torch.addmm(out[e], ae.t(), be, beta=1.0, alpha=alpha, out_dtype=torch.float32, out=out[e])
             else:
-                out[e].addmm_(ae.t().float(), be.float(), alpha=alpha)
+                out[e].addmm_(ae.t().to(out.dtype), be.to(out.dtype), alpha=alpha)
         s += c
 
 
-class _ExpertsFn(torch.autograd.Function):
-    """Grouped SwiGLU experts with LoRA on gate/up and down."""
+class ExpertParams:
+    """Base weights of the experts held by this rank plus their LoRA views."""
 
+    def __init__(self, gu_w_t, down_w_t, A_gu, B_gu, A_d, B_d, g_A_gu, g_B_gu, g_A_d, g_B_d, scale):
+        self.gu_w_t, self.down_w_t = gu_w_t, down_w_t  # [E_l, H, 2F], [E_l, F, H]
+        self.A_gu, self.B_gu, self.A_d, self.B_d = A_gu, B_gu, A_d, B_d
+        self.g_A_gu, self.g_B_gu, self.g_A_d, self.g_B_d = g_A_gu, g_B_gu, g_A_d, g_B_d
+        self.scale = scale
+
+
+def experts_forward(xs: torch.Tensor, counts: list[int], p: ExpertParams, lora: bool):
+    """Grouped SwiGLU experts with LoRA on gate/up and down.  Returns
+    ``(out, saved)`` where ``saved`` feeds :func:`experts_backward`."""
+    s = p.scale
+    gu = grouped_mm(xs, p.gu_w_t, counts)
+    u_gu = u_d = None
+    if lora and p.A_gu is not None:
+        r = p.B_gu.shape[-1]
+        u_gu = grouped_mm(xs, p.A_gu.transpose(1, 2), counts)  # [N, 2r]
+        lo = grouped_mm(u_gu[:, :r].contiguous(), p.B_gu[:, 0].transpose(1, 2), counts)
+        hi = grouped_mm(u_gu[:, r:].contiguous(), p.B_gu[:, 1].transpose(1, 2), counts)
+        gu = gu + s * torch.cat([lo, hi], dim=1)
+    Fh = gu.shape[1] // 2
+    g, up = gu[:, :Fh], gu[:, Fh:]
+    act = (g.float() * torch.sigmoid(g.float())).to(gu.dtype) * up
+    out = grouped_mm(act, p.down_w_t, counts)
+    if lora and p.A_d is not None:
+        u_d = grouped_mm(act, p.A_d.transpose(1, 2), counts)  # [N, r]
+        out = out + s * grouped_mm(u_d, p.B_d.transpose(1, 2), counts)
+    return out, (xs, gu, act, u_gu, u_d, counts, lora)
+
+
+def experts_backward(dout: torch.Tensor, saved, p: ExpertParams) -> torch.Tensor:
+    xs, gu, act, u_gu, u_d, counts, lora = saved
+    s = p.scale
+    dout = dout.contiguous()
+    dact = grouped_mm(dout, p.down_w_t.transpose(1, 2), counts)
+    if lora and p.A_d is not None:
+        dyB = grouped_mm(dout, p.B_d, counts)  # [N, r]
+        grouped_wgrad(dout, u_d, counts, p.g_B_d, s)
+        grouped_wgrad(dyB, act, counts, p.g_A_d, s)
+        dact = dact + s * grouped_mm(dyB, p.A_d, counts)
+    Fh = gu.shape[1] // 2
+    g, up = gu[:, :Fh].float(), gu[:, Fh:].float()
+    sg = torch.sigmoid(g)
+    da = dact.float()
+    dgu = torch.cat([da * up * sg * (1 + g * (1 - sg)), da * g * sg], dim=1).to(gu.dtype)
+    dxs = grouped_mm(dgu, p.gu_w_t.transpose(1, 2), counts)
+    if lora and p.A_gu is not None:
+        r = p.B_gu.shape[-1]
+        dyB = torch.cat(
+            [grouped_mm(dgu[:, :Fh].contiguous(), p.B_gu[:, 0], counts),
+             grouped_mm(dgu[:, Fh:].contiguous(), p.B_gu[:, 1], counts)], dim=1)
+        grouped_wgrad(dgu[:, :Fh], u_gu[:, :r], counts, p.g_B_gu[:, 0], s)
+        grouped_wgrad(dgu[:, Fh:], u_gu[:, r:], counts, p.g_B_gu[:, 1], s)
+        grouped_wgrad(dyB, xs, counts, p.g_A_gu, s)
+        dxs = dxs + s * grouped_mm(dyB, p.A_gu, counts)
+    return dxs
+
+
+class _LocalExperts(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, xs, counts, gu_w_t, down_w_t, A_gu, B_gu, A_d, B_d, g_A_gu, g_B_gu, g_A_d, g_B_d, scale, enabled, anchor):
-        # xs [N, H] sorted by expert; gu_w_t [E, H, 2F]; down_w_t [E, F, H]
-        gu = grouped_mm(xs, gu_w_t, counts)
-        u_gu = None
-        if enabled and A_gu is not None:
-            u_gu = grouped_mm(xs, A_gu.transpose(1, 2), counts)  # [N, 2r]
-            E, _, F, r = B_gu.shape
-            r2 = 2 * r
-            # block-diagonal per expert: gate rows use u[:, :r], up rows u[:, r:]
-            lo = grouped_mm(u_gu[:, :r].contiguous(), B_gu[:, 0].transpose(1, 2), counts)
-            hi = grouped_mm(u_gu[:, r:r2].contiguous(), B_gu[:, 1].transpose(1, 2), counts)
-            gu = gu + scale * torch.cat([lo, hi], dim=1)
-        Fh = gu.shape[1] // 2
-        g, up = gu[:, :Fh], gu[:, Fh:]
-        sg = torch.sigmoid(g.float())
-        act = (g.float() * sg).to(gu.dtype) * up
-        out = grouped_mm(act, down_w_t, counts)
-        u_d = None
-        if enabled and A_d is not None:
-            u_d = grouped_mm(act, A_d.transpose(1, 2), counts)  # [N, r]
-            out = out + scale * grouped_mm(u_d, B_d.transpose(1, 2), counts)
-        ctx.save_for_backward(xs, gu, act, u_gu if u_gu is not None else xs.new_empty(0), u_d if u_d is not None else xs.new_empty(0))
-        ctx.counts = counts
-        ctx.w = (gu_w_t, down_w_t, A_gu, B_gu, A_d, B_d)
-        ctx.g = (g_A_gu, g_B_gu, g_A_d, g_B_d)
-        ctx.scale = scale
-        ctx.enabled = enabled
+    def forward(ctx, xs, counts, params, lora, anchor):
+        out, saved = experts_forward(xs, counts, params, lora)
+        ctx.saved = saved
+        ctx.params = params
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        xs, gu, act, u_gu, u_d = ctx.saved_tensors
-        counts, s = ctx.counts, ctx.scale
-        gu_w_t, down_w_t, A_gu, B_gu, A_d, B_d = ctx.w
-        g_A_gu, g_B_gu, g_A_d, g_B_d = ctx.g
-        dout = dout.contiguous()
-        dact = grouped_mm(dout, down_w_t.transpose(1, 2), counts)
-        if ctx.enabled and A_d is not None:
-            dyB = grouped_mm(dout, B_d, counts)  # [N, r]
-            grouped_wgrad(dout, u_d, counts, g_B_d, s)  # [E, H, r]
-            grouped_wgrad(dyB, act, counts, g_A_d, s)  # [E, r, F]
-            dact = dact + s * grouped_mm(dyB, A_d, counts)
-        Fh = gu.shape[1] // 2
-        g, up = gu[:, :Fh].float(), gu[:, Fh:].float()
-        sg = torch.sigmoid(g)
-        da = dact.float()
-        dup = da * g * sg
-        dg = da * up * sg * (1 + g * (1 - sg))
-        dgu = torch.cat([dg, dup], dim=1).to(gu.dtype)
-        dxs = grouped_mm(dgu, gu_w_t.transpose(1, 2), counts)
-        if ctx.enabled and A_gu is not None:
-            r = B_gu.shape[-1]
-            dyB_lo = grouped_mm(dgu[:, :Fh].contiguous(), B_gu[:, 0], counts)
-            dyB_hi = grouped_mm(dgu[:, Fh:].contiguous(), B_gu[:, 1], counts)
-            grouped_wgrad(dgu[:, :Fh], u_gu[:, :r], counts, g_B_gu[:, 0], s)
-            grouped_wgrad(dgu[:, Fh:], u_gu[:, r:], counts, g_B_gu[:, 1], s)
-            dyB = torch.cat([dyB_lo, dyB_hi], dim=1)
-            grouped_wgrad(dyB, xs, counts, g_A_gu, s)
-            dxs = dxs + s * grouped_mm(dyB, A_gu, counts)
-        return (dxs,) + (None,) * 14
+        dxs = experts_backward(dout, ctx.saved, ctx.params)
+        ctx.saved = None
+        return dxs, None, None, None, None
+
+
+def native_combine(slots: torch.Tensor, w: torch.Tensor | None, k: int) -> torch.Tensor:
+    """``y[t] = sum_j w[t, j] * slots[t*k + j]`` (fused kernel on CUDA)."""
+    if slots.device.type == "cuda":
+        from ..ops import native
+
+        ww = None if w is None else w.reshape(-1).float().contiguous()
+        return native.lib().combine_rows(slots.contiguous(), ww, k)
+    T = slots.shape[0] // k
+    sl = slots.view(T, k, -1).to(torch.float64 if slots.dtype == torch.float64 else torch.float32)
+    if w is not None:
+        sl = sl * w.view(T, k, 1).to(sl.dtype)
+    return sl.sum(1).to(slots.dtype)
+
+
+class _EPExperts(torch.autograd.Function):
+    """Dispatch -> local experts -> combine across the expert-parallel group."""
+
+    @staticmethod
+    def forward(ctx, h, w, idx, ep, params, lora, anchor):
+        plan = ep.plan(idx)
+        tr = ep.transport
+        recv = tr.push(plan, h, None, 0)
+        xs = recv.clone()
+        out, saved = experts_forward(xs, plan.local_counts, params, lora)
+        tr.publish(out, 1)
+        slots = tr.pull(plan, 1)
+        y = native_combine(slots, w, plan.k)
+        ctx.plan, ctx.ep, ctx.params, ctx.saved = plan, ep, params, saved
+        ctx.save_for_backward(slots, w)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        slots, w = ctx.saved_tensors
+        plan, ep, params = ctx.plan, ctx.ep, ctx.params
+        tr = ep.transport
+        dy = dy.contiguous()
+        T, k = plan.T, plan.k
+        dw = (slots.view(T, k, -1).float() * dy.view(T, 1, -1).float()).sum(-1)
+        d_recv = tr.push(plan, dy, w.reshape(-1).float().contiguous(), 2)
+        dxs = experts_backward(d_recv.clone(), ctx.saved, params)
+        tr.publish(dxs, 3)
+        dslots = tr.pull(plan, 3)
+        dh = native_combine(dslots, None, k)
+        ctx.saved = None
+        return dh, dw.to(w.dtype), None, None, None, None, None
 
 
 class MoEBlock:
-    def __init__(self, cfg: ModelConfig, i: int, gen, dev, dt, store: LoRAStore, spec: LoRASpec) -> None:
+    def __init__(self, cfg: ModelConfig, i: int, gen, dev, dt, store: LoRAStore, spec: LoRASpec,
+                 ep: Any = None) -> None:
         from .transformer import _randn
 
-        self.cfg, self.index = cfg, i
+        self.cfg, self.index, self.ep = cfg, i, ep
         E, H, F = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size
         self.router_w = _randn((E, H), gen, dev, dt)
-        # stored transposed for row-major grouped GEMMs: x [N,H] @ [H, 2F]
-        self.gu_w_t = _randn((E, H, 2 * F), gen, dev, dt)
-        self.down_w_t = _randn((E, F, H), gen, dev, dt)
+        e0 = ep.first_expert if ep is not None else 0
+        El = ep.E_local if ep is not None else E
+        # the expert weights are drawn in one piece so the random init does not
+        # depend on the expert-parallel degree; each rank keeps its slice
+        gu = _randn((E, H, 2 * F), gen, dev, dt) if El == E else _randn((E, H, 2 * F), gen, dev, dt)[e0 : e0 + El].clone()
+        dn = _randn((E, F, H), gen, dev, dt) if El == E else _randn((E, F, H), gen, dev, dt)[e0 : e0 + El].clone()
+        self.gu_w_t = gu  # [E_local, H, 2F]
+        self.down_w_t = dn  # [E_local, F, H]
         self.shared = None
         if cfg.shared_expert_intermediate_size:
             Fs = cfg.shared_expert_intermediate_size
@@ -154,26 +246,24 @@ class MoEBlock:
                 _randn((H, Fs), gen, dev, dt),
                 _randn((1, H), gen, dev, dt),
             )
-        self.scale = spec.scale
         r = spec.r
 
         def stacked(names: list[str], shape: tuple[int, ...]):
             if not names or names[0] not in store.entries:
                 return None, None
             off, n = store.contiguous_span(names)
-            return (
-                store.compute[off : off + n].view(shape),
-                store.grad[off : off + n].view(shape),
-            )
+            return store.compute[off : off + n].view(shape), store.grad[off : off + n].view(shape)
 
-        self.A_gu, self.g_A_gu = stacked(
-            [peft_key(i, "mlp", p, "A", e) for e in range(E) for p in ("gate_proj", "up_proj")], (E, 2 * r, H)
+        A_gu, g_A_gu = stacked([peft_key(i, "mlp", p, "A", e) for e in range(E) for p in ("gate_proj", "up_proj")], (E, 2 * r, H))
+        B_gu, g_B_gu = stacked([peft_key(i, "mlp", p, "B", e) for e in range(E) for p in ("gate_proj", "up_proj")], (E, 2, F, r))
+        A_d, g_A_d = stacked([peft_key(i, "mlp", "down_proj", "A", e) for e in range(E)], (E, r, F))
+        B_d, g_B_d = stacked([peft_key(i, "mlp", "down_proj", "B", e) for e in range(E)], (E, H, r))
+        sl = slice(e0, e0 + El)
+        pick = lambda t: None if t is None else t[sl]  # noqa: E731
+        self.params = ExpertParams(
+            self.gu_w_t, self.down_w_t, pick(A_gu), pick(B_gu), pick(A_d), pick(B_d),
+            pick(g_A_gu), pick(g_B_gu), pick(g_A_d), pick(g_B_d), spec.scale,
         )
-        self.B_gu, self.g_B_gu = stacked(
-            [peft_key(i, "mlp", p, "B", e) for e in range(E) for p in ("gate_proj", "up_proj")], (E, 2, F, r)
-        )
-        self.A_d, self.g_A_d = stacked([peft_key(i, "mlp", "down_proj", "A", e) for e in range(E)], (E, r, F))
-        self.B_d, self.g_B_d = stacked([peft_key(i, "mlp", "down_proj", "B", e) for e in range(E)], (E, H, r))
 
     def num_parameters(self) -> int:
         n = self.router_w.numel() + self.gu_w_t.numel() + self.down_w_t.numel()
@@ -202,18 +292,18 @@ class MoEBlock:
         T, H = h.shape
         E, k = self.cfg.num_experts, self.cfg.num_experts_per_tok
         idx, wts = self.route(h, ctx)
-        flat = idx.reshape(-1)
-        order = torch.argsort(flat, stable=True)
-        counts = torch.bincount(flat, minlength=E).tolist()
-        tok = order // k
-        xs = h[tok]
-        ys = _ExpertsFn.apply(
-            xs, counts, self.gu_w_t, self.down_w_t, self.A_gu, self.B_gu, self.A_d, self.B_d,
-            self.g_A_gu, self.g_B_gu, self.g_A_d, self.g_B_d, self.scale, enabled,
-            grad_anchor(h.device) if enabled else None,
-        )
-        w_sorted = wts.reshape(-1)[order].to(ys.dtype).unsqueeze(1)
-        out = torch.zeros(T, H, device=h.device, dtype=ys.dtype).index_add(0, tok, ys * w_sorted)
+        anchor = grad_anchor(h.device) if enabled else None
+        if self.ep is not None and self.ep.world > 1:
+            out = _EPExperts.apply(h, wts, idx, self.ep, self.params, enabled, anchor)
+        else:
+            flat = idx.reshape(-1)
+            order = torch.argsort(flat, stable=True)
+            counts = torch.bincount(flat, minlength=E).tolist()
+            tok = order // k
+            xs = h[tok]
+            ys = _LocalExperts.apply(xs, counts, self.params, enabled, anchor)
+            w_sorted = wts.reshape(-1)[order].to(ys.dtype).unsqueeze(1)
+            out = torch.zeros(T, H, device=h.device, dtype=ys.dtype).index_add(0, tok, ys * w_sorted)
         if self.shared is not None:
             gu_w, down_w, gate_w = self.shared
             gu = h @ gu_w.t()
@@ -224,7 +314,8 @@ class MoEBlock:
 
     def load_hf(self, sd: dict[str, torch.Tensor], prefix: str, g: Callable[[str], torch.Tensor]) -> None:
         self.router_w.copy_(g(prefix + "gate.weight"))
-        for e in range(self.cfg.num_experts):
-            p = f"{prefix}experts.{e}."
-            self.gu_w_t[e].copy_(torch.cat([g(p + "gate_proj.weight"), g(p + "up_proj.weight")]).t())
-            self.down_w_t[e].copy_(g(p + "down_proj.weight").t())
+        e0 = self.ep.first_expert if self.ep is not None else 0
+        for le in range(self.gu_w_t.shape[0]):
+            p = f"{prefix}experts.{e0 + le}."
+            self.gu_w_t[le].copy_(torch.cat([g(p + "gate_proj.weight"), g(p + "up_proj.weight")]).t())
+            self.down_w_t[le].copy_(g(p + "down_proj.weight").t())

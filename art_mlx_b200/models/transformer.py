@@ -152,8 +152,10 @@ class DecoderLM:
         seed: int = 0,
         store: LoRAStore | None = None,
         init_weights: bool = True,
+        ep: Any = None,
     ) -> None:
         self.cfg = cfg
+        self.ep = ep  # expert-parallel context (MoE models on several ranks)
         self.lora_spec = lora
         self.device = torch.device(device)
         self.dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
@@ -201,7 +203,7 @@ class DecoderLM:
 
             layer.gdn = GatedDeltaNet(cfg, i, gen, dev, dt, st, spec)
         if cfg.is_moe:
-            layer.moe = MoEBlock(cfg, i, gen, dev, dt, st, spec)
+            layer.moe = MoEBlock(cfg, i, gen, dev, dt, st, spec, ep=self.ep)
         else:
             F = cfg.intermediate_size
             layer.mlp = DenseMLP(

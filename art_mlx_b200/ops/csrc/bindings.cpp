@@ -46,6 +46,14 @@ torch::Tensor gemm_tc(torch::Tensor a, torch::Tensor b, c10::optional<torch::Ten
                       c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> bias,
                       c10::optional<torch::Tensor> out, bool accumulate);
 int64_t tc_error_code();
+void scatter_rows(torch::Tensor src, c10::optional<torch::Tensor> dst_rank, torch::Tensor dst_row,
+                  c10::optional<torch::Tensor> scale, torch::Tensor bases, int64_t ld_dst,
+                  c10::optional<torch::Tensor> dst_limit);
+void scatter_rows_idx(torch::Tensor src, torch::Tensor src_idx, torch::Tensor dst_rank, torch::Tensor dst_row,
+                      c10::optional<torch::Tensor> scale, torch::Tensor bases, int64_t ld_dst);
+void gather_rows(torch::Tensor dst, c10::optional<torch::Tensor> src_rank, torch::Tensor src_row,
+                 c10::optional<torch::Tensor> scale, torch::Tensor bases, int64_t ld_src);
+torch::Tensor combine_rows(torch::Tensor slots, c10::optional<torch::Tensor> w, int64_t k);
 }  // namespace art
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -65,6 +73,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &art::attn_bwd);
   m.def("gemm_tc", &art::gemm_tc);
   m.def("tc_error_code", &art::tc_error_code);
+  m.def("scatter_rows", &art::scatter_rows);
+  m.def("gather_rows", &art::gather_rows);
+  m.def("scatter_rows_idx", &art::scatter_rows_idx);
+  m.def("combine_rows", &art::combine_rows);
   m.def("ipc_alloc", &art::ipc_alloc);
   m.def("ipc_open", &art::ipc_open);
   m.def("ipc_close", &art::ipc_close);

@@ -122,6 +122,14 @@ def stage_row(
     )
 
 
+def zero_weight(mb: MicroBatch) -> MicroBatch:
+    """A micro batch that contributes nothing to the loss or the gradients."""
+    mb.w = torch.zeros_like(mb.w)
+    mb.adv = torch.zeros_like(mb.adv)
+    mb.n_tokens = 0
+    return mb
+
+
 @dataclass
 class StepMetrics:
     loss: torch.Tensor
@@ -178,6 +186,7 @@ class GRPOTrainer:
         group: dist.ProcessGroup | None = None,
         logprob_chunk: int = 4096,
         fused_dp: bool = True,
+        max_tokens_per_rank: int = 16384,
     ) -> None:
         self.device = torch.device(device)
         self.group = group
@@ -196,7 +205,13 @@ class GRPOTrainer:
             store = LoRAStore(specs, self.device, dtype, compute_buf=self.grad_sync.compute,
                               grad_buf=self.grad_sync.grad)
             store.init_(seed + 1)
-        self.model = DecoderLM(cfg, lora, self.device, seed=seed, store=store)
+        self.ep = None
+        if cfg.is_moe and self.world > 1:
+            from ..parallel.ep import EPContext
+
+            cap = 2 * max_tokens_per_rank * cfg.num_experts_per_tok
+            self.ep = EPContext(group, cfg.num_experts, cfg.hidden_size, self.device, cap)
+        self.model = DecoderLM(cfg, lora, self.device, seed=seed, store=store, ep=self.ep)
         self.store = self.model.store
         self.optim = FlatAdamW(self.store, adamw)
         self.logprob_chunk = logprob_chunk
@@ -310,9 +325,16 @@ class GRPOTrainer:
         cfg = dict(cfg or {})
         mask = packed["assistant_mask"]
         total = float(mask[:, 1:].sum().item())  # trainable (scored) tokens of the whole step
-        rows = list(range(int(mask.shape[0])))[self.rank :: self.world]
+        n_rows = int(mask.shape[0])
+        rows = list(range(n_rows))[self.rank :: self.world]
         if micro_batches is None:
             micro_batches = [stage_row(packed, r, self.device) for r in rows]
+        if self.ep is not None:
+            # expert-parallel layers are collective: every rank runs the same
+            # number of micro steps; missing ones are zero-weight copies
+            per_rank = (n_rows + self.world - 1) // self.world
+            while len(micro_batches) < per_rank:
+                micro_batches.append(zero_weight(stage_row(packed, self.rank % n_rows, self.device)))
         acc = {k: torch.zeros((), device=self.device) for k in ("loss", "entropy", "probs_corr", "kl")}
         n_tokens = 0
         for mb in micro_batches:
