@@ -81,12 +81,34 @@ def grouped_mm(x: torch.Tensor, w: torch.Tensor, counts: list[int]) -> torch.Ten
     return torch.cat(outs)
 
 
+def pad_groups(x: torch.Tensor, counts: list[int], multiple: int = 8) -> tuple[torch.Tensor, list[int]]:
+    """Copy row groups into a buffer where every group starts at a multiple of
+    ``multiple`` rows (zero rows in between); returns (padded, padded counts)."""
+    padded_counts = [(c + multiple - 1) // multiple * multiple for c in counts]
+    if padded_counts == list(counts):
+        return x, list(counts)
+    dst = torch.empty(x.shape[0], dtype=torch.int64)
+    s = d = 0
+    for c, pc in zip(counts, padded_counts):
+        dst[s : s + c] = torch.arange(d, d + c)
+        s += c
+        d += pc
+    out = x.new_zeros(d, *x.shape[1:])
+    out.index_copy_(0, dst.to(x.device, non_blocking=True), x)
+    return out, padded_counts
+
+
 def grouped_wgrad(a: torch.Tensor, b: torch.Tensor, counts: list[int], out: torch.Tensor, alpha: float) -> None:
     """``out[e] += alpha * a_e^T b_e`` (fp32 accumulate) for row groups ``e``."""
     if _use_library_grouped(a, a.shape[1], b.shape[1]) and a.shape[0] > 0:
-        g = torch._grouped_mm(a.t().contiguous(), b.contiguous(), offs=_offsets(counts, a.device),
-                              out_dtype=torch.float32)
-        out.add_(g.view(out.shape), alpha=alpha)
+        # the reduced (token) dimension of each group must span a multiple of
+        # 16 bytes: align every group to 8 rows with zero padding
+        ap, pc = pad_groups(a, counts)
+        bp, _ = pad_groups(b, counts)
+        # one launch for all experts; the per-expert product is rounded to
+        # bf16 once (fp32 accumulation inside the GEMM) before the fp32 add
+        g = torch._grouped_mm(ap.t().contiguous(), bp.contiguous(), offs=_offsets(pc, a.device))
+        out.add_(g.view(out.shape).float(), alpha=alpha)
         return
     s = 0
     for e, c in enumerate(counts):

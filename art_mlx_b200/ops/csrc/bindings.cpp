@@ -46,6 +46,12 @@ torch::Tensor gemm_tc(torch::Tensor a, torch::Tensor b, c10::optional<torch::Ten
                       c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> bias,
                       c10::optional<torch::Tensor> out, bool accumulate);
 int64_t tc_error_code();
+torch::Tensor gemm_tc_ag(std::vector<int64_t> a_ptrs, int64_t rows, int64_t K, int64_t lda, torch::Tensor b,
+                         c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2,
+                         c10::optional<torch::Tensor> bias);
+void gemm_tc_rs(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2,
+                std::vector<int64_t> c_ptrs, int64_t rows, int64_t ldc, int64_t slot);
+torch::Tensor slot_sum(torch::Tensor staging, int64_t nslots, int64_t rows, c10::optional<torch::Tensor> res);
 void scatter_rows(torch::Tensor src, c10::optional<torch::Tensor> dst_rank, torch::Tensor dst_row,
                   c10::optional<torch::Tensor> scale, torch::Tensor bases, int64_t ld_dst,
                   c10::optional<torch::Tensor> dst_limit);
@@ -73,6 +79,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &art::attn_bwd);
   m.def("gemm_tc", &art::gemm_tc);
   m.def("tc_error_code", &art::tc_error_code);
+  m.def("gemm_tc_ag", &art::gemm_tc_ag);
+  m.def("gemm_tc_rs", &art::gemm_tc_rs);
+  m.def("slot_sum", &art::slot_sum);
   m.def("scatter_rows", &art::scatter_rows);
   m.def("gather_rows", &art::gather_rows);
   m.def("scatter_rows_idx", &art::scatter_rows_idx);

@@ -35,6 +35,8 @@ constexpr int STAGE_BYTES = A_TILE + B_TILE;
 constexpr int GEMM_THREADS = 192;
 constexpr int GEMM_SMEM = GSTAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
+constexpr int MAX_SRC = 8;
+
 struct GemmArgs {
   int M, N, K2;
   int nk1, nk2;  // k-blocks of the main and the extension product
@@ -43,10 +45,23 @@ struct GemmArgs {
   const __nv_bfloat16* bias;
   int accumulate_c;
   int* err;
+  // multi-source A (all-gather fused into the load): rows [s*a_src_rows,
+  // (s+1)*a_src_rows) of A are read through tensor map s (0 = single source)
+  int a_src_rows;
+  // scattered output (reduce-scatter fused into the epilogue): rows
+  // [r*c_dst_rows, (r+1)*c_dst_rows) go to c_bases[r] at row offset
+  // c_slot*c_dst_rows (0 = plain C)
+  int c_dst_rows;
+  int c_slot;
+  long long c_bases[MAX_SRC];
+};
+
+struct TmapSet {
+  CUtensorMap m[MAX_SRC];
 };
 
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    gemm_tc_kernel(const __grid_constant__ TmapSet tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                    const GemmArgs p) {
   extern __shared__ uint8_t smem_raw[];
@@ -84,7 +99,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      prefetch_tmap(&tmA);
+      const int nsrc = p.a_src_rows ? (p.M + p.a_src_rows - 1) / p.a_src_rows : 1;
+      for (int q = 0; q < nsrc && q < MAX_SRC; ++q) prefetch_tmap(&tmA.m[q]);
       prefetch_tmap(&tmB);
       if (p.nk2) {
         prefetch_tmap(&tmA2);
@@ -101,7 +117,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint8_t* b = a + A_TILE;
           mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
           if (kb < p.nk1) {
-            tma_load_2d(a, &tmA, &full[s], kb * GBK, m0);
+            if (p.a_src_rows) {
+              const int q = m0 / p.a_src_rows;
+              tma_load_2d(a, &tmA.m[q], &full[s], kb * GBK, m0 - q * p.a_src_rows);
+            } else {
+              tma_load_2d(a, &tmA.m[0], &full[s], kb * GBK, m0);
+            }
             tma_load_2d(b, &tmB, &full[s], kb * GBK, n0);
           } else {
             const int k2 = (kb - p.nk1) * GBK;
@@ -164,7 +185,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tmem_wait_ld();
         const int col0 = n0 + c * 32;
         if (row < p.M && col0 < p.N) {
-          __nv_bfloat16* dst = p.C + (int64_t)row * p.ldc + col0;
+          __nv_bfloat16* dst;
+          if (p.c_dst_rows) {
+            const int rr = row / p.c_dst_rows;
+            dst = reinterpret_cast<__nv_bfloat16*>(p.c_bases[rr]) +
+                  ((int64_t)p.c_slot * p.c_dst_rows + (row - rr * p.c_dst_rows)) * p.ldc + col0;
+          } else {
+            dst = p.C + (int64_t)row * p.ldc + col0;
+          }
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -258,6 +286,38 @@ int64_t tc_error_code() {
   return v;
 }
 
+static void launch_gemm(const TmapSet& ta, const CUtensorMap& tb, const CUtensorMap& ta2, const CUtensorMap& tb2,
+                        GemmArgs& p, int dev) {
+  p.err = error_word(dev).data_ptr<int>();
+  static int num_sms = 0;
+  if (!num_sms) ART_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev));
+  const int tiles = ((p.M + GBM - 1) / GBM) * ((p.N + GBN - 1) / GBN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  static bool attr = false;
+  if (!attr) {
+    ART_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM));
+    attr = true;
+  }
+  if (grid > 0)
+    gemm_tc_kernel<<<grid, GEMM_THREADS, GEMM_SMEM, at::cuda::getCurrentCUDAStream()>>>(ta, tb, ta2, tb2, p);
+  ART_CUDA_CHECK(cudaGetLastError());
+}
+
+static void fill_common(GemmArgs& p, int64_t M, int64_t K, int64_t N, const c10::optional<torch::Tensor>& a2,
+                        const c10::optional<torch::Tensor>& bias, bool accumulate) {
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K2 = a2.has_value() ? (int)a2->size(1) : 0;
+  p.nk1 = (int)((K + GBK - 1) / GBK);
+  p.nk2 = a2.has_value() ? (p.K2 + GBK - 1) / GBK : 0;
+  p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
+  p.accumulate_c = accumulate ? 1 : 0;
+  p.a_src_rows = 0;
+  p.c_dst_rows = 0;
+  p.c_slot = 0;
+  for (int i = 0; i < MAX_SRC; ++i) p.c_bases[i] = 0;
+}
+
 // out = a @ b^T (+ a2 @ b2^T) (+ bias) (+ out if accumulate)
 torch::Tensor gemm_tc(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> a2,
                       c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> bias,
@@ -275,39 +335,119 @@ torch::Tensor gemm_tc(torch::Tensor a, torch::Tensor b, c10::optional<torch::Ten
     c = torch::empty({M, N}, a.options());
   }
   if (M == 0) return c;
-  const bool ext = a2.has_value();
-  int K2 = 0;
-  if (ext) {
-    TORCH_CHECK(b2.has_value() && a2->size(0) == M && b2->size(0) == N && a2->size(1) == b2->size(1));
-    K2 = a2->size(1);
-  }
+  if (a2.has_value()) TORCH_CHECK(b2.has_value() && a2->size(0) == M && b2->size(0) == N && a2->size(1) == b2->size(1));
   if (bias.has_value()) TORCH_CHECK(bias->numel() == N && bias->is_contiguous());
-  CUtensorMap ta = make_tmap_2d(a, GBM), tb = make_tmap_2d(b, GBN);
-  CUtensorMap ta2 = ext ? make_tmap_2d(*a2, GBM) : ta, tb2 = ext ? make_tmap_2d(*b2, GBN) : tb;
-  int dev = a.get_device();
+  TmapSet ta;
+  ta.m[0] = make_tmap_2d(a, GBM);
+  CUtensorMap tb = make_tmap_2d(b, GBN);
+  CUtensorMap ta2 = a2.has_value() ? make_tmap_2d(*a2, GBM) : ta.m[0];
+  CUtensorMap tb2 = a2.has_value() ? make_tmap_2d(*b2, GBN) : tb;
   GemmArgs p;
-  p.M = (int)M;
-  p.N = (int)N;
-  p.K2 = K2;
-  p.nk1 = (int)((K + GBK - 1) / GBK);
-  p.nk2 = ext ? (K2 + GBK - 1) / GBK : 0;
+  fill_common(p, M, K, N, a2, bias, accumulate);
   p.C = reinterpret_cast<__nv_bfloat16*>(c.data_ptr());
   p.ldc = c.stride(0);
-  p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
-  p.accumulate_c = accumulate ? 1 : 0;
-  p.err = error_word(dev).data_ptr<int>();
-  static int num_sms = 0;
-  if (!num_sms) ART_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev));
-  const int tiles = (int)(((M + GBM - 1) / GBM) * ((N + GBN - 1) / GBN));
-  const int grid = tiles < num_sms ? tiles : num_sms;
-  static bool attr = false;
-  if (!attr) {
-    ART_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM));
-    attr = true;
-  }
-  gemm_tc_kernel<<<grid, GEMM_THREADS, GEMM_SMEM, at::cuda::getCurrentCUDAStream()>>>(ta, tb, ta2, tb2, p);
-  ART_CUDA_CHECK(cudaGetLastError());
+  launch_gemm(ta, tb, ta2, tb2, p, a.get_device());
   return c;
+}
+
+// All-gather fused into the GEMM: A = concat_s(shard_s) where shard s is a
+// [rows, K] bf16 matrix at address a_ptrs[s] (peer memory allowed: plain TMA
+// loads, no multicast).  rows must be a multiple of 128.
+torch::Tensor gemm_tc_ag(std::vector<int64_t> a_ptrs, int64_t rows, int64_t K, int64_t lda, torch::Tensor b,
+                         c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2,
+                         c10::optional<torch::Tensor> bias) {
+  const int nsrc = (int)a_ptrs.size();
+  TORCH_CHECK(nsrc >= 1 && nsrc <= MAX_SRC && rows % GBM == 0);
+  const int64_t M = rows * nsrc, N = b.size(0);
+  TORCH_CHECK(b.size(1) == K && N % 32 == 0);
+  auto opts = b.options();
+  auto c = torch::empty({M, N}, opts);
+  TmapSet ta;
+  for (int q = 0; q < nsrc; ++q) {
+    auto view = torch::from_blob(reinterpret_cast<void*>(a_ptrs[q]), {rows, K}, {lda, 1}, opts);
+    ta.m[q] = make_tmap_2d(view, GBM);
+  }
+  for (int q = nsrc; q < MAX_SRC; ++q) ta.m[q] = ta.m[0];
+  CUtensorMap tb = make_tmap_2d(b, GBN);
+  if (a2.has_value()) TORCH_CHECK(b2.has_value() && a2->size(0) == M && b2->size(0) == N);
+  CUtensorMap ta2 = a2.has_value() ? make_tmap_2d(*a2, GBM) : ta.m[0];
+  CUtensorMap tb2 = a2.has_value() ? make_tmap_2d(*b2, GBN) : tb;
+  GemmArgs p;
+  fill_common(p, M, K, N, a2, bias, false);
+  p.a_src_rows = (int)rows;
+  p.C = reinterpret_cast<__nv_bfloat16*>(c.data_ptr());
+  p.ldc = c.stride(0);
+  launch_gemm(ta, tb, ta2, tb2, p, b.get_device());
+  return c;
+}
+
+// Reduce-scatter fused into the epilogue: C rows [r*rows, (r+1)*rows) are
+// stored into the staging buffer of rank r (c_ptrs[r], peer memory) at slot
+// `slot`: staging_r[slot*rows + i, :].  The owner sums the slots afterwards.
+void gemm_tc_rs(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2,
+                std::vector<int64_t> c_ptrs, int64_t rows, int64_t ldc, int64_t slot) {
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+  const int ndst = (int)c_ptrs.size();
+  TORCH_CHECK(ndst >= 1 && ndst <= MAX_SRC && rows * ndst == M && N % 32 == 0 && ldc % 8 == 0);
+  TmapSet ta;
+  ta.m[0] = make_tmap_2d(a, GBM);
+  for (int q = 1; q < MAX_SRC; ++q) ta.m[q] = ta.m[0];
+  CUtensorMap tb = make_tmap_2d(b, GBN);
+  if (a2.has_value()) TORCH_CHECK(b2.has_value() && a2->size(0) == M && b2->size(0) == N);
+  CUtensorMap ta2 = a2.has_value() ? make_tmap_2d(*a2, GBM) : ta.m[0];
+  CUtensorMap tb2 = a2.has_value() ? make_tmap_2d(*b2, GBN) : tb;
+  GemmArgs p;
+  fill_common(p, M, K, N, a2, c10::nullopt, false);
+  p.C = nullptr;
+  p.ldc = ldc;
+  p.c_dst_rows = (int)rows;
+  p.c_slot = (int)slot;
+  for (int q = 0; q < ndst; ++q) p.c_bases[q] = c_ptrs[q];
+  launch_gemm(ta, tb, ta2, tb2, p, a.get_device());
+}
+
+// Owner side of the fused reduce-scatter: out[i] = sum_s staging[s*rows + i] (+ residual).
+__global__ void slot_sum_kernel(const __nv_bfloat16* __restrict__ staging, int nslots, int64_t rows, int N,
+                                const __nv_bfloat16* __restrict__ res, __nv_bfloat16* __restrict__ out) {
+  const int64_t nv = rows * (N / 8);
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = v / (N / 8);
+    const int c = (v % (N / 8)) * 8;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int s = 0; s < nslots; ++s) {
+      uint4 x = *reinterpret_cast<const uint4*>(staging + ((int64_t)s * rows + i) * N + c);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&x);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += bf2f(e[k]);
+    }
+    if (res) {
+      uint4 x = *reinterpret_cast<const uint4*>(res + i * N + c);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&x);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += bf2f(e[k]);
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + i * N + c) = o;
+  }
+}
+
+torch::Tensor slot_sum(torch::Tensor staging, int64_t nslots, int64_t rows, c10::optional<torch::Tensor> res) {
+  const int N = staging.size(1);
+  TORCH_CHECK(staging.is_contiguous() && N % 8 == 0 && staging.size(0) >= nslots * rows);
+  auto out = torch::empty({rows, N}, staging.options());
+  int64_t blocks = (rows * N / 8 + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (rows > 0)
+    slot_sum_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(staging.data_ptr()), (int)nslots, rows, N,
+        res.has_value() ? reinterpret_cast<const __nv_bfloat16*>(res->data_ptr()) : nullptr,
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  ART_CUDA_CHECK(cudaGetLastError());
+  return out;
 }
 
 }  // namespace art

@@ -187,6 +187,7 @@ class GRPOTrainer:
         logprob_chunk: int = 4096,
         fused_dp: bool = True,
         max_tokens_per_rank: int = 16384,
+        tp_size: int = 1,
     ) -> None:
         self.device = torch.device(device)
         self.group = group
@@ -206,12 +207,23 @@ class GRPOTrainer:
                               grad_buf=self.grad_sync.grad)
             store.init_(seed + 1)
         self.ep = None
+        self.tp = None
+        self.tp_size = tp_size if self.world > 1 else 1
+        if self.tp_size > 1:
+            assert self.tp_size == self.world, "tensor parallelism spans all ranks (tp = world)"
+            from ..models.tp_decoder import TPDecoderLM
+            from ..parallel.tp import TPContext
+
+            self.tp = TPContext(group, self.device, max_tokens_per_rank, cfg.hidden_size)
         if cfg.is_moe and self.world > 1:
             from ..parallel.ep import EPContext
 
             cap = 2 * max_tokens_per_rank * cfg.num_experts_per_tok
             self.ep = EPContext(group, cfg.num_experts, cfg.hidden_size, self.device, cap)
-        self.model = DecoderLM(cfg, lora, self.device, seed=seed, store=store, ep=self.ep)
+        if self.tp is not None:
+            self.model = TPDecoderLM(cfg, lora, self.device, self.tp, seed=seed, store=store)
+        else:
+            self.model = DecoderLM(cfg, lora, self.device, seed=seed, store=store, ep=self.ep)
         self.store = self.model.store
         self.optim = FlatAdamW(self.store, adamw)
         self.logprob_chunk = logprob_chunk
@@ -263,6 +275,8 @@ class GRPOTrainer:
 
     # ------------------------------------------------------------------
     def _logprobs(self, mb: MicroBatch, ctx: dict[str, Any], entropy: bool) -> tuple[torch.Tensor, torch.Tensor | None]:
+        if self.tp is not None:
+            return self.model.token_logprobs(mb.tokens, mb.meta, mb.sel, mb.targets, ctx, entropy)
         h = self.model.forward(mb.tokens, mb.meta, ctx)
         hs = h.index_select(0, mb.sel)
         return fused.lm_head_logprobs(hs, self.model.lm_head, mb.targets, self.logprob_chunk, entropy)
@@ -326,9 +340,12 @@ class GRPOTrainer:
         mask = packed["assistant_mask"]
         total = float(mask[:, 1:].sum().item())  # trainable (scored) tokens of the whole step
         n_rows = int(mask.shape[0])
-        rows = list(range(n_rows))[self.rank :: self.world]
+        dp_world = self.world // self.tp_size
+        dp_rank = self.rank // self.tp_size
+        rows = list(range(n_rows))[dp_rank::dp_world]
+        pad_to = 128 * self.tp_size if self.tp is not None else 64
         if micro_batches is None:
-            micro_batches = [stage_row(packed, r, self.device) for r in rows]
+            micro_batches = [stage_row(packed, r, self.device, pad_to=pad_to) for r in rows]
         if self.ep is not None:
             # expert-parallel layers are collective: every rank runs the same
             # number of micro steps; missing ones are zero-weight copies
@@ -346,7 +363,10 @@ class GRPOTrainer:
         acc["probs_corr"] /= nmb
         acc["kl"] /= nmb
         if self.world > 1:
-            stats = torch.stack([acc["loss"], acc["entropy"], acc["probs_corr"] / self.world, acc["kl"] / self.world])
+            # tensor-parallel ranks hold identical copies of the loss statistics
+            rep = float(self.tp_size)
+            stats = torch.stack([acc["loss"] / rep, acc["entropy"] / rep, acc["probs_corr"] / self.world,
+                                 acc["kl"] / self.world])
             if self.grad_sync is not None:
                 self.grad_sync.reduce_and_step(self.optim, learning_rate, stats)
             else:

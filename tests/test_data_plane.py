@@ -168,3 +168,25 @@ def test_group_aggregate_matches_naive(reduce):
                 var = torch.clamp((sel * sel).sum() / (n + 1e-8) - mean * mean, min=0)
                 e = var if reduce == "var" else torch.sqrt(var + 1e-8)
             assert torch.allclose(out[b][by[b] == g], e.expand(n), atol=1e-5)
+
+
+def test_pad_groups_aligns_each_group():
+    from art_mlx_b200.models.moe import pad_groups
+
+    x = torch.arange(11, dtype=torch.float32).view(11, 1)
+    out, pc = pad_groups(x, [3, 0, 8])
+    assert pc == [8, 0, 8]
+    assert out.shape[0] == 16
+    assert out[:3, 0].tolist() == [0, 1, 2] and out[3:8].abs().sum() == 0
+    assert out[8:, 0].tolist() == list(range(3, 11))
+    # weight-gradient of padded groups equals the unpadded per-group products
+    a = torch.randn(11, 4)
+    b = torch.randn(11, 5)
+    ap, pcs = pad_groups(a, [3, 0, 8])
+    bp, _ = pad_groups(b, [3, 0, 8])
+    s0 = 0
+    for e, (c, p) in enumerate(zip([3, 0, 8], pcs)):
+        ref = a[sum([3, 0, 8][:e]) : sum([3, 0, 8][:e]) + c].t() @ b[sum([3, 0, 8][:e]) : sum([3, 0, 8][:e]) + c]
+        got = ap[s0 : s0 + p].t() @ bp[s0 : s0 + p]
+        assert torch.allclose(ref, got)
+        s0 += p

@@ -30,7 +30,16 @@ MOE_GPU = ModelConfig(
     num_attention_heads=2, num_key_value_heads=1, head_dim=128, intermediate_size=0, qk_norm=True,
     num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
 )
-CONFIGS = {"moe-tiny": MOE_CPU, "moe-small": MOE_GPU}
+TP_CPU = ModelConfig(
+    name="tp-tiny", family="qwen3", vocab_size=512, hidden_size=64, num_hidden_layers=2,
+    num_attention_heads=4, num_key_value_heads=2, head_dim=16, intermediate_size=96, qk_norm=True,
+    attention_bias=True,
+)
+TP_GPU = ModelConfig(
+    name="tp-small", family="qwen3", vocab_size=2048, hidden_size=512, num_hidden_layers=2,
+    num_attention_heads=4, num_key_value_heads=2, head_dim=128, intermediate_size=1024, qk_norm=True,
+)
+CONFIGS = {"moe-tiny": MOE_CPU, "moe-small": MOE_GPU, "tp-tiny": TP_CPU, "tp-small": TP_GPU}
 
 GPU_CFG = ModelConfig(
     name="dp-small", family="qwen2", vocab_size=2048, hidden_size=256, num_hidden_layers=2,
@@ -45,7 +54,7 @@ def _packed(vocab: int, prompt: int, comp: int, seq_len: int):
     return packed_tensors_from_tokenized_results(res, seq_len, rng=random.Random(0))
 
 
-def _worker(rank, world, init_file, out_path, backend, cfg_name):
+def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1):
     if backend == "nccl":
         torch.cuda.set_device(rank)
         device = torch.device("cuda", rank)
@@ -59,7 +68,7 @@ def _worker(rank, world, init_file, out_path, backend, cfg_name):
         cfg = {"dp-small": GPU_CFG, **CONFIGS}.get(cfg_name) or get_config(cfg_name)
         packed = _packed(cfg.vocab_size, 24 if backend == "gloo" else 96, 12 if backend == "gloo" else 48,
                          128 if backend == "gloo" else 512)
-        tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), device, seed=0, group=dist.group.WORLD)
+        tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), device, seed=0, group=dist.group.WORLD, tp_size=tp_size)
         assert (tr.grad_sync is not None) == (backend == "nccl")
         assert (tr.ep is not None) == cfg.is_moe
         for _ in range(2):
@@ -83,11 +92,12 @@ def _single(device, cfg, backend):
     return tr.store.master.cpu(), m.to_host(), packed
 
 
-def _run(world, backend, cfg_name):
+def _run(world, backend, cfg_name, tp_size=1):
     d = tempfile.mkdtemp()
     init = os.path.join(d, "init")
     out = os.path.join(d, "out.pt")
-    mp.start_processes(_worker, args=(world, init, out, backend, cfg_name), nprocs=world, start_method="spawn")
+    mp.start_processes(_worker, args=(world, init, out, backend, cfg_name, tp_size), nprocs=world,
+                       start_method="spawn")
     return torch.load(out)
 
 
@@ -127,5 +137,25 @@ def test_ep_moe_p2p_two_gpus_matches_single_gpu():
     master, metrics, _ = _single(torch.device("cuda", 0), MOE_GPU, "nccl")
     err = (res["master"] - master).norm() / master.norm()
     # bf16 expert outputs are combined in a different order than on one GPU
+    assert err < 1e-2, err
+    assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-2 * max(1.0, abs(metrics["loss/train"]))
+
+
+def test_tp_gloo_matches_single_process():
+    """Tensor + sequence parallel dense model (2 CPU ranks) vs one process."""
+    res = _run(2, "gloo", "tp-tiny", tp_size=2)
+    master, metrics, _ = _single(torch.device("cpu"), TP_CPU, "gloo")
+    err = (res["master"] - master).norm() / master.norm()
+    assert err < 1e-5, err
+    assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-5
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_fused_two_gpus_matches_single_gpu():
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    res = _run(2, "nccl", "tp-small", tp_size=2)
+    master, metrics, _ = _single(torch.device("cuda", 0), TP_GPU, "nccl")
+    err = (res["master"] - master).norm() / master.norm()
     assert err < 1e-2, err
     assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-2 * max(1.0, abs(metrics["loss/train"]))
