@@ -535,3 +535,75 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::
 }
 
 }  // namespace art
+
+// ============================================================================
+// Allocation-free C entry point of the attention backward.
+//
+// No counterpart in the reference: this entry point exists for callers that
+// cannot allocate device memory themselves -- for example code running inside
+// a host application that owns the whole device memory budget (a plugin given
+// fixed buffers), or a latency-critical loop that must never enter the CUDA
+// allocator, which can synchronise the device.  The caller passes every input
+// and output; the only extra memory, the per-(head, query) `delta = sum(dO*O)`
+// vector, lives in a fixed file-scope device array.
+//
+// Limits and behaviour:
+//  * scratch: kNoAllocDeltaMax floats (4 MiB) per device, held by every GPU
+//    that loads this library until the process exits; calls with
+//    T * Hq > kNoAllocDeltaMax are rejected (return 2);
+//  * head_dim must be 128 (return 3 otherwise); other bad arguments return 4;
+//  * the first call on a device looks up the array's device address
+//    (cudaGetSymbolAddress) with that device current; make that first call
+//    before any stream capture;
+//  * all calls on a device share the scratch array, so calls that overlap on
+//    the GPU (different streams, no ordering) race; order them on one stream;
+//  * the fp32 outputs dq [T, Hq, 128], dk and dv [T, Hkv, 128] are cleared
+//    (cudaMemsetAsync) by the entry point before accumulation;
+//  * no cudaMalloc, cudaFree or allocating library call is made.
+// Returns 0 on success, 1 on a CUDA error, 2-4 on rejected arguments.
+// ============================================================================
+namespace {
+constexpr int64_t kNoAllocDeltaMax = int64_t(1) << 20;
+static __device__ __align__(256) float g_noalloc_delta[kNoAllocDeltaMax];
+static float* g_noalloc_delta_ptr[64] = {nullptr};
+}  // namespace
+
+extern "C" int art_attn_bwd_noalloc(const void* dout, int64_t lddo, const void* q, int64_t ldq, const void* k,
+                                    int64_t ldk, const void* v, int64_t ldv, const void* out, int64_t ldo,
+                                    const float* lse, const int* kend, const int* units, int n_units, float* dq,
+                                    float* dk, float* dv, int T, int Hq, int Hkv, int D, float scale,
+                                    cudaStream_t stream) {
+  using namespace art;
+  if (D != 128) return 3;
+  if (T < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || n_units < 0) return 4;
+  if ((int64_t)T * Hq > kNoAllocDeltaMax) return 2;
+  if (!dout || !q || !k || !v || !out || !lse || !kend || !dq || !dk || !dv || (n_units > 0 && !units)) return 4;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  if (!g_noalloc_delta_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_delta) != cudaSuccess || !p) return 1;
+    g_noalloc_delta_ptr[dev] = static_cast<float*>(p);
+  }
+  float* delta = g_noalloc_delta_ptr[dev];
+  const size_t nq = (size_t)T * Hq * D * sizeof(float), nk = (size_t)T * Hkv * D * sizeof(float);
+  if (cudaMemsetAsync(dq, 0, nq, stream) != cudaSuccess) return 1;
+  if (cudaMemsetAsync(dk, 0, nk, stream) != cudaSuccess) return 1;
+  if (cudaMemsetAsync(dv, 0, nk, stream) != cudaSuccess) return 1;
+  if (T == 0 || n_units == 0) return cudaGetLastError() == cudaSuccess ? 0 : 1;
+  const int64_t warps = (int64_t)T * Hq;
+  attn_bwd_pre_kernel<128><<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout), lddo, reinterpret_cast<const __nv_bfloat16*>(out), ldo, delta,
+      T, Hq);
+  const size_t smem = (2 * BWD_KEYS * 128 + 4 * BWD_Q * 128 + BWD_KEYS * DS_LD) * sizeof(__nv_bfloat16) +
+                      4 * BWD_Q * sizeof(float);
+  if (cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return 1;
+  dim3 grid((unsigned)n_units, (unsigned)Hkv);
+  attn_bwd_kernel<128><<<grid, 256, smem, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(q), ldq, reinterpret_cast<const __nv_bfloat16*>(k), ldk,
+      reinterpret_cast<const __nv_bfloat16*>(v), ldv, reinterpret_cast<const __nv_bfloat16*>(dout), lddo, lse, delta,
+      kend, units, dq, dk, dv, T, Hq, Hkv, scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
