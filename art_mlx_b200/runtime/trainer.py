@@ -55,6 +55,8 @@ class MicroBatch:
     n_tokens: int = 0  # valid (non-padding) tokens in the row
     n_train: int = 0
     h2d_bytes: int = 0  # bytes copied host -> device to stage this row
+    group_ids: torch.Tensor | None = None  # [L] host copies (tree-structured layers)
+    parent_ids: torch.Tensor | None = None
 
     @property
     def L(self) -> int:
@@ -119,6 +121,8 @@ def stage_row(
         n_tokens=n_valid,
         n_train=int(sel.numel()),
         h2d_bytes=moved[0],
+        group_ids=packed["group_ids"][row, :L].clone(),
+        parent_ids=packed["parent_ids"][row, :L].clone(),
     )
 
 
@@ -286,7 +290,7 @@ class GRPOTrainer:
     ) -> dict[str, torch.Tensor]:
         """Forward + backward of one packed row; gradients accumulate into the
         store.  Returns device scalars (loss contribution, entropy sum, ...)."""
-        ctx: dict[str, Any] = {}
+        ctx: dict[str, Any] = {"group_ids": mb.group_ids, "parent_ids": mb.parent_ids}
         if mb.routes is not None:
             ctx["replay_routes"] = mb.routes
         ref = None
