@@ -141,6 +141,30 @@ def delta_rule_reference(q, k, v, g, beta, S0=None):
 # ---------------------------------------------------------------------------
 
 
+def sequence_predecessors(segs: list[tuple[int, int, int]], T: int, width: int) -> torch.Tensor:
+    """Conv predecessor table of a packed tree row: ``prev[i, m]`` is the
+    packed index of the token ``m+1`` positions before ``i`` in its sequence
+    (walking from a segment's start into its ancestors), -1 before the
+    sequence start.  ``segs`` = (start, end, parent segment or -1)."""
+    prev = torch.full((T, width - 1), -1, dtype=torch.int64)
+    for n, (s, e, p) in enumerate(segs):
+        for m in range(1, width):
+            if e - s > m:  # inside the segment
+                prev[s + m : e, m - 1] = torch.arange(s, e - m)
+            for i in range(s, min(e, s + m)):  # first m tokens: into the ancestors
+                need = m - (i - s)
+                anc, pos = p, None
+                while anc >= 0:
+                    a_s, a_e, a_p = segs[anc]
+                    if a_e - a_s >= need:
+                        pos = a_e - need
+                        break
+                    need -= a_e - a_s
+                    anc = a_p
+                prev[i, m - 1] = pos if pos is not None else -1
+    return prev
+
+
 class TreePlan:
     """Segments of one packed row grouped by depth, plus the conv
     predecessor table (``prev[i, m]`` = packed index of the token ``m+1``
@@ -168,24 +192,7 @@ class TreePlan:
             while len(self.levels) <= d:
                 self.levels.append([])
             self.levels[d].append(n)
-        prev = torch.full((T, width - 1), -1, dtype=torch.int64)
-        for n, (s, e, p) in enumerate(segs):
-            for m in range(1, width):
-                # inside the segment
-                if e - s > m:
-                    prev[s + m : e, m - 1] = torch.arange(s, e - m)
-                # first m tokens: walk into the ancestors
-                for i in range(s, min(e, s + m)):
-                    need = m - (i - s)  # tokens to go back before the segment start
-                    anc, pos = p, None
-                    while anc >= 0:
-                        a_s, a_e, a_p = segs[anc]
-                        if a_e - a_s >= need:
-                            pos = a_e - need
-                            break
-                        need -= a_e - a_s
-                        anc = a_p
-                    prev[i, m - 1] = pos if pos is not None else -1
+        prev = sequence_predecessors(segs, T, width)
         self.prev = prev.to(meta.kend.device, non_blocking=True)
 
 

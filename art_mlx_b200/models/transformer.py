@@ -215,7 +215,7 @@ class DecoderLM:
         return layer
 
     # ------------------------------------------------------------------
-    def attention(self, layer: Layer, h: torch.Tensor, meta: AttnMeta) -> torch.Tensor:
+    def attention(self, layer: Layer, h: torch.Tensor, meta: AttnMeta, ctx: dict[str, Any] | None = None) -> torch.Tensor:
         cfg = self.cfg
         v = self.store.version
         en = self.lora_enabled
@@ -228,9 +228,15 @@ class DecoderLM:
             qg = qkv[:, : 2 * cfg.q_size].view(T, nq, 2 * D)
             gate = qg[..., D:].reshape(T, cfg.q_size)
             qkv = torch.cat([qg[..., :D].reshape(T, cfg.q_size), qkv[:, 2 * cfg.q_size :]], dim=1)
-        o = fused.rope_attention(
-            qkv, meta, self.inv_freq, nq, nkv, D, layer.q_norm, layer.k_norm, cfg.rms_norm_eps
-        )
+        if ctx is not None and ctx.get("cp_plan") is not None:
+            from ..parallel.cp import cp_rope_attention
+
+            o = cp_rope_attention(qkv, ctx["cp_plan"], ctx["cp"], self.inv_freq, nq, nkv, D,
+                                  layer.q_norm, layer.k_norm, cfg.rms_norm_eps)
+        else:
+            o = fused.rope_attention(
+                qkv, meta, self.inv_freq, nq, nkv, D, layer.q_norm, layer.k_norm, cfg.rms_norm_eps
+            )
         if gate is not None:
             o = o * torch.sigmoid(gate)
         return fused.lora_linear(o, layer.o_w, None, layer.o_lora, v, en)
@@ -258,7 +264,11 @@ class DecoderLM:
         for layer in self.layers:
             h, resid = fused.add_rmsnorm(out, resid, layer.in_norm, eps)
             if layer.kind == "attention":
-                a = self.attention(layer, h, meta)
+                a = self.attention(layer, h, meta, ctx)
+            elif ctx.get("cp_plan") is not None:
+                from ..parallel.cp import cp_gdn
+
+                a = cp_gdn(layer.gdn, h, ctx["cp_plan"], ctx["cp"], self.store.version, self.lora_enabled)
             else:
                 a = layer.gdn(h, meta, self.store.version, self.lora_enabled, ctx)
             h, resid = fused.add_rmsnorm(a, resid, layer.post_norm, eps)

@@ -26,8 +26,10 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(
     const __nv_bfloat16* __restrict__ q, int64_t ldq, const __nv_bfloat16* __restrict__ k,
     int64_t ldk, const __nv_bfloat16* __restrict__ v, int64_t ldv, const int* __restrict__ kend,
     const int* __restrict__ tile_kmax, __nv_bfloat16* __restrict__ o, int64_t ldo,
-    float* __restrict__ lse, int T, int Hq, int Hkv, float scale_log2) {
+    float* __restrict__ lse, int Tq, int Tk, int q_off, int Hq, int Hkv, float scale_log2) {
   static_assert(D == 128, "head_dim 128");
+  // queries are local rows [0, Tq) at global positions q_off + row; keys are
+  // global rows [0, Tk) (Tq == Tk, q_off == 0 without context parallelism)
   constexpr int CH = D / 8;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);
@@ -42,15 +44,16 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(
   for (int c = tid; c < 64 * CH; c += 128) {
     const int r = c / CH, ch = c % CH;
     const int t = q0 + r;
-    const int tt = t < T ? t : T - 1;
-    cp_async16(smem_u32(sQ + swz<D>(r, ch)), q + (int64_t)tt * ldq + h * D + ch * 8, t < T ? 16 : 0);
+    const int tt = t < Tq ? t : Tq - 1;
+    cp_async16(smem_u32(sQ + swz<D>(r, ch)), q + (int64_t)tt * ldq + h * D + ch * 8, t < Tq ? 16 : 0);
   }
   cp_async_commit();
 
-  const int q_last = min(q0 + 63, T - 1);
-  const int ntiles = q_last / 64 + 1;
+  const int gq0 = q_off + q0;  // global position of the first query of the block
+  const int q_last = min(gq0 + 63, q_off + Tq - 1);
+  const int ntiles = min(q_last / 64 + 1, (Tk + 63) / 64);
   auto next_needed = [&](int t) {
-    while (t < ntiles && __ldg(tile_kmax + t) <= q0) ++t;
+    while (t < ntiles && __ldg(tile_kmax + t) <= gq0) ++t;
     return t;
   };
   auto load_kv = [&](int tile, int stage) {
@@ -58,8 +61,8 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(
     for (int c = tid; c < 64 * CH; c += 128) {
       const int r = c / CH, ch = c % CH;
       const int j = j0 + r;
-      const int jj = j < T ? j : T - 1;
-      const int nb = j < T ? 16 : 0;
+      const int jj = j < Tk ? j : Tk - 1;
+      const int nb = j < Tk ? 16 : 0;
       cp_async16(smem_u32(sK + stage * 64 * D + swz<D>(r, ch)), k + (int64_t)jj * ldk + hk * D + ch * 8, nb);
       cp_async16(smem_u32(sV + stage * 64 * D + swz<D>(r, ch)), v + (int64_t)jj * ldv + hk * D + ch * 8, nb);
     }
@@ -80,8 +83,9 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-  const int row_a = q0 + warp * 16 + (lane >> 2);
+  const int row_a = q0 + warp * 16 + (lane >> 2);  // local query rows
   const int row_b = row_a + 8;
+  const int grow_a = q_off + row_a, grow_b = q_off + row_b;  // global positions
 
   int stage = 0;
   while (tile < ntiles) {
@@ -114,9 +118,9 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int j = j0 + nt * 8 + 2 * (lane & 3) + e;
-        const int ke = j < T ? __ldg(kend + j) : -1;
-        const bool va = j <= row_a && row_a < ke;
-        const bool vb = j <= row_b && row_b < ke;
+        const int ke = j < Tk ? __ldg(kend + j) : -1;
+        const bool va = row_a < Tq && j <= grow_a && grow_a < ke;
+        const bool vb = row_b < Tq && j <= grow_b && grow_b < ke;
         s[nt][e] = va ? s[nt][e] * scale_log2 : -INFINITY;
         s[nt][2 + e] = vb ? s[nt][2 + e] * scale_log2 : -INFINITY;
         mx_a = fmaxf(mx_a, s[nt][e]);
@@ -182,16 +186,16 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(
 #pragma unroll
   for (int nd = 0; nd < D / 8; ++nd) {
     const int col = h * D + nd * 8 + 2 * (lane & 3);
-    if (row_a < T)
+    if (row_a < Tq)
       *reinterpret_cast<uint32_t*>(o + (int64_t)row_a * ldo + col) =
           pack_bf16x2(oacc[nd][0] * inv_a, oacc[nd][1] * inv_a);
-    if (row_b < T)
+    if (row_b < Tq)
       *reinterpret_cast<uint32_t*>(o + (int64_t)row_b * ldo + col) =
           pack_bf16x2(oacc[nd][2] * inv_b, oacc[nd][3] * inv_b);
   }
   if ((lane & 3) == 0) {
-    if (row_a < T) lse[(int64_t)h * T + row_a] = l_a > 0.f ? (m_a + log2f(l_a)) / kLog2e : -INFINITY;
-    if (row_b < T) lse[(int64_t)h * T + row_b] = l_b > 0.f ? (m_b + log2f(l_b)) / kLog2e : -INFINITY;
+    if (row_a < Tq) lse[(int64_t)h * Tq + row_a] = l_a > 0.f ? (m_a + log2f(l_a)) / kLog2e : -INFINITY;
+    if (row_b < Tq) lse[(int64_t)h * Tq + row_b] = l_b > 0.f ? (m_b + log2f(l_b)) / kLog2e : -INFINITY;
   }
 }
 
@@ -236,7 +240,8 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
     const __nv_bfloat16* __restrict__ dout, int64_t lddo, const float* __restrict__ lse,
     const float* __restrict__ delta, const int* __restrict__ kend,
     const int* __restrict__ units, float* __restrict__ dq_acc, float* __restrict__ dk_acc,
-    float* __restrict__ dv_acc, int T, int Hq, int Hkv, float scale) {
+    float* __restrict__ dv_acc, int Tq, int Tk, int q_off, int Hq, int Hkv, float scale) {
+  // q tiles of the work units are local query tiles (global position q_off + row)
   static_assert(D == 128, "head_dim 128");
   constexpr int CH = D / 8;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -261,8 +266,8 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
   for (int c = tid; c < BWD_KEYS * CH; c += 256) {
     const int r = c / CH, ch = c % CH;
     const int j = j0 + r;
-    const int jj = j < T ? j : T - 1;
-    const int nb = j < T ? 16 : 0;
+    const int jj = j < Tk ? j : Tk - 1;
+    const int nb = j < Tk ? 16 : 0;
     cp_async16(smem_u32(sK + swz<D>(r, ch)), k + (int64_t)jj * ldk + hk * D + ch * 8, nb);
     cp_async16(smem_u32(sV + swz<D>(r, ch)), v + (int64_t)jj * ldv + hk * D + ch * 8, nb);
   }
@@ -279,15 +284,15 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
     for (int c = tid; c < BWD_Q * CH; c += 256) {
       const int r = c / CH, ch = c % CH;
       const int i = i0 + r;
-      const int ii = i < T ? i : T - 1;
-      const int nb = i < T ? 16 : 0;
+      const int ii = i < Tq ? i : Tq - 1;
+      const int nb = i < Tq ? 16 : 0;
       cp_async16(smem_u32(sQ + st * BWD_Q * D + swz<D>(r, ch)), q + (int64_t)ii * ldq + h * D + ch * 8, nb);
       cp_async16(smem_u32(sdO + st * BWD_Q * D + swz<D>(r, ch)), dout + (int64_t)ii * lddo + h * D + ch * 8, nb);
     }
     if (tid < BWD_Q) {
       const int i = i0 + tid;
-      sL[st * BWD_Q + tid] = i < T ? lse[(int64_t)h * T + i] * kLog2e : INFINITY;
-      sDl[st * BWD_Q + tid] = i < T ? delta[(int64_t)h * T + i] : 0.f;
+      sL[st * BWD_Q + tid] = i < Tq ? lse[(int64_t)h * Tq + i] * kLog2e : INFINITY;
+      sDl[st * BWD_Q + tid] = i < Tq ? delta[(int64_t)h * Tq + i] : 0.f;
     }
   };
 
@@ -304,8 +309,8 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
 
   const int kr0 = warp * 16 + (lane >> 2);  // local key rows owned by this thread
   const int kr1 = kr0 + 8;
-  const int ke0 = (j0 + kr0 < T) ? __ldg(kend + j0 + kr0) : -1;
-  const int ke1 = (j0 + kr1 < T) ? __ldg(kend + j0 + kr1) : -1;
+  const int ke0 = (j0 + kr0 < Tk) ? __ldg(kend + j0 + kr0) : -1;
+  const int ke1 = (j0 + kr1 < Tk) ? __ldg(kend + j0 + kr1) : -1;
 
   for (int n = 0; n < n_items; ++n) {
     const int st = n & 1;
@@ -349,11 +354,12 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int ql = nt * 8 + 2 * (lane & 3) + e;
-        const int i = i0 + ql;
+        const int i = i0 + ql;  // local query row
+        const int gi = q_off + i;  // its global position
         const float L = cL[ql], dl = cDl[ql];
         const int jj0 = j0 + kr0, jj1 = j0 + kr1;
-        const bool v0 = i < T && jj0 <= i && i < ke0;
-        const bool v1 = i < T && jj1 <= i && i < ke1;
+        const bool v0 = i < Tq && jj0 <= gi && gi < ke0;
+        const bool v1 = i < Tq && jj1 <= gi && gi < ke1;
         const float p0 = v0 ? exp2f(sT[nt][e] * scale_log2 - L) : 0.f;
         const float p1 = v1 ? exp2f(sT[nt][2 + e] * scale_log2 - L) : 0.f;
         sT[nt][e] = p0;
@@ -429,8 +435,8 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         const int col = h * D + warp * 16 + nt * 8 + 2 * (lane & 3);
-        if (ia < T) red_add_v2(dq_acc + (int64_t)ia * Hq * D + col, dqa[mq][nt][0] * scale, dqa[mq][nt][1] * scale);
-        if (ib < T) red_add_v2(dq_acc + (int64_t)ib * Hq * D + col, dqa[mq][nt][2] * scale, dqa[mq][nt][3] * scale);
+        if (ia < Tq) red_add_v2(dq_acc + (int64_t)ia * Hq * D + col, dqa[mq][nt][0] * scale, dqa[mq][nt][1] * scale);
+        if (ib < Tq) red_add_v2(dq_acc + (int64_t)ib * Hq * D + col, dqa[mq][nt][2] * scale, dqa[mq][nt][3] * scale);
       }
     }
   }
@@ -442,11 +448,11 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
 #pragma unroll
   for (int nd = 0; nd < D / 8; ++nd) {
     const int col = hk * D + nd * 8 + 2 * (lane & 3);
-    if (ja < T) {
+    if (ja < Tk) {
       red_add_v2(dk_acc + (int64_t)ja * Hkv * D + col, dkacc[nd][0] * scale, dkacc[nd][1] * scale);
       red_add_v2(dv_acc + (int64_t)ja * Hkv * D + col, dvacc[nd][0], dvacc[nd][1]);
     }
-    if (jb < T) {
+    if (jb < Tk) {
       red_add_v2(dk_acc + (int64_t)jb * Hkv * D + col, dkacc[nd][2] * scale, dkacc[nd][3] * scale);
       red_add_v2(dv_acc + (int64_t)jb * Hkv * D + col, dvacc[nd][2], dvacc[nd][3]);
     }
@@ -461,62 +467,66 @@ static void check_view(const torch::Tensor& t, int64_t T, int64_t H, int64_t D, 
               name, ": rows must be 16-byte aligned");
 }
 
-// q [T, Hq, D], k/v [T, Hkv, D] (row-strided views allowed); kend [T] int32;
-// tile_kmax [ceil(T/64)] int32.  Returns o [T, Hq, D], lse [Hq, T].
+// q [Tq, Hq, D] (local queries at global positions q_off + row), k/v [Tk, Hkv, D]
+// (row-strided views allowed); kend [Tk] int32; tile_kmax [ceil(Tk/64)] int32.
+// Returns o [Tq, Hq, D], lse [Hq, Tq].
 std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v,
-                                    torch::Tensor kend, torch::Tensor tile_kmax, double scale) {
-  const int64_t T = q.size(0), Hq = q.size(1), D = q.size(2), Hkv = k.size(1);
+                                    torch::Tensor kend, torch::Tensor tile_kmax, double scale, int64_t q_off) {
+  const int64_t Tq = q.size(0), Hq = q.size(1), D = q.size(2), Tk = k.size(0), Hkv = k.size(1);
   TORCH_CHECK(D == 128, "attention kernel supports head_dim 128");
   TORCH_CHECK(Hq % Hkv == 0);
-  check_view(q, T, Hq, D, "q");
-  check_view(k, T, Hkv, D, "k");
-  check_view(v, T, Hkv, D, "v");
-  TORCH_CHECK(kend.scalar_type() == at::kInt && kend.numel() == T && kend.is_contiguous());
-  TORCH_CHECK(tile_kmax.scalar_type() == at::kInt && tile_kmax.numel() >= (T + 63) / 64);
-  auto o = torch::empty({T, Hq, D}, q.options());
-  auto lse = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
-  if (T == 0) return {o, lse};
+  TORCH_CHECK(q_off >= 0 && q_off + Tq <= Tk, "query range must lie inside the key range");
+  check_view(q, Tq, Hq, D, "q");
+  check_view(k, Tk, Hkv, D, "k");
+  check_view(v, Tk, Hkv, D, "v");
+  TORCH_CHECK(kend.scalar_type() == at::kInt && kend.numel() == Tk && kend.is_contiguous());
+  TORCH_CHECK(tile_kmax.scalar_type() == at::kInt && tile_kmax.numel() >= (Tk + 63) / 64);
+  auto o = torch::empty({Tq, Hq, D}, q.options());
+  auto lse = torch::empty({Hq, Tq}, q.options().dtype(at::kFloat));
+  if (Tq == 0) return {o, lse};
   const size_t smem = (64 + 4 * 64) * D * sizeof(__nv_bfloat16);
   auto kern = attn_fwd_kernel<128>;
   ART_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  dim3 grid((T + 63) / 64, Hq);
+  dim3 grid((Tq + 63) / 64, Hq);
   kern<<<grid, 128, smem, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()), k.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), v.stride(0), kend.data_ptr<int>(),
       tile_kmax.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), o.stride(0),
-      lse.data_ptr<float>(), (int)T, (int)Hq, (int)Hkv, (float)(scale * kLog2e));
+      lse.data_ptr<float>(), (int)Tq, (int)Tk, (int)q_off, (int)Hq, (int)Hkv, (float)(scale * kLog2e));
   ART_CUDA_CHECK(cudaGetLastError());
   return {o, lse};
 }
 
-// Backward.  units [n, 3] int32 = (key block of 128, q tile lo, q tile hi) in
-// 32-query tiles.  Returns {dq, dk, dv} fp32 accumulators [T, H, D].
+// Backward.  units [n, 3] int32 = (key block of 128, local q tile lo, local q tile hi)
+// in 32-query tiles.  Returns {dq [Tq,Hq,D], dk [Tk,Hkv,D], dv [Tk,Hkv,D]} fp32.
 std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k,
                                     torch::Tensor v, torch::Tensor out, torch::Tensor lse,
-                                    torch::Tensor kend, torch::Tensor units, double scale) {
-  const int64_t T = q.size(0), Hq = q.size(1), D = q.size(2), Hkv = k.size(1);
+                                    torch::Tensor kend, torch::Tensor units, double scale, int64_t q_off) {
+  const int64_t Tq = q.size(0), Hq = q.size(1), D = q.size(2), Tk = k.size(0), Hkv = k.size(1);
   TORCH_CHECK(D == 128);
-  check_view(q, T, Hq, D, "q");
-  check_view(k, T, Hkv, D, "k");
-  check_view(v, T, Hkv, D, "v");
-  check_view(dout, T, Hq, D, "dout");
-  check_view(out, T, Hq, D, "out");
+  TORCH_CHECK(q_off >= 0 && q_off + Tq <= Tk);
+  check_view(q, Tq, Hq, D, "q");
+  check_view(k, Tk, Hkv, D, "k");
+  check_view(v, Tk, Hkv, D, "v");
+  check_view(dout, Tq, Hq, D, "dout");
+  check_view(out, Tq, Hq, D, "out");
+  TORCH_CHECK(kend.numel() == Tk && lse.numel() == Hq * Tq);
   TORCH_CHECK(units.scalar_type() == at::kInt && units.is_contiguous() && units.dim() == 2 && units.size(1) == 3);
   auto f32 = q.options().dtype(at::kFloat);
-  auto dq_acc = torch::zeros({T, Hq, D}, f32);
-  auto dk_acc = torch::zeros({T, Hkv, D}, f32);
-  auto dv_acc = torch::zeros({T, Hkv, D}, f32);
+  auto dq_acc = torch::zeros({Tq, Hq, D}, f32);
+  auto dk_acc = torch::zeros({Tk, Hkv, D}, f32);
+  auto dv_acc = torch::zeros({Tk, Hkv, D}, f32);
   const int64_t n_units = units.size(0);
-  if (T == 0 || n_units == 0) return {dq_acc, dk_acc, dv_acc};
-  auto delta = torch::empty({Hq, T}, f32);
+  if (Tq == 0 || n_units == 0) return {dq_acc, dk_acc, dv_acc};
+  auto delta = torch::empty({Hq, Tq}, f32);
   auto stream = at::cuda::getCurrentCUDAStream();
   {
-    const int64_t warps = T * Hq;
+    const int64_t warps = Tq * Hq;
     attn_bwd_pre_kernel<128><<<(warps + 7) / 8, 256, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
         reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), out.stride(0),
-        delta.data_ptr<float>(), (int)T, (int)Hq);
+        delta.data_ptr<float>(), (int)Tq, (int)Hq);
   }
   const size_t smem = (2 * BWD_KEYS * D + 4 * BWD_Q * D + BWD_KEYS * DS_LD) * sizeof(__nv_bfloat16) +
                       4 * BWD_Q * sizeof(float);
@@ -529,7 +539,8 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::
       reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), v.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0), lse.data_ptr<float>(),
       delta.data_ptr<float>(), kend.data_ptr<int>(), units.data_ptr<int>(), dq_acc.data_ptr<float>(),
-      dk_acc.data_ptr<float>(), dv_acc.data_ptr<float>(), (int)T, (int)Hq, (int)Hkv, (float)scale);
+      dk_acc.data_ptr<float>(), dv_acc.data_ptr<float>(), (int)Tq, (int)Tk, (int)q_off, (int)Hq, (int)Hkv,
+      (float)scale);
   ART_CUDA_CHECK(cudaGetLastError());
   return {dq_acc, dk_acc, dv_acc};
 }
@@ -604,6 +615,6 @@ extern "C" int art_attn_bwd_noalloc(const void* dout, int64_t lddo, const void* 
   attn_bwd_kernel<128><<<grid, 256, smem, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(q), ldq, reinterpret_cast<const __nv_bfloat16*>(k), ldk,
       reinterpret_cast<const __nv_bfloat16*>(v), ldv, reinterpret_cast<const __nv_bfloat16*>(dout), lddo, lse, delta,
-      kend, units, dq, dk, dv, T, Hq, Hkv, scale);
+      kend, units, dq, dk, dv, T, T, 0, Hq, Hkv, scale);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

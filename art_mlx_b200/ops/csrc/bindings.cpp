@@ -26,10 +26,10 @@ torch::Tensor grad_sumsq(torch::Tensor g);
 void adamw_step(torch::Tensor p, torch::Tensor p16, torch::Tensor g, torch::Tensor m,
                 torch::Tensor v, torch::Tensor hp, torch::Tensor norm_sq, torch::Tensor norm_out);
 std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v,
-                                    torch::Tensor kend, torch::Tensor tile_kmax, double scale);
+                                    torch::Tensor kend, torch::Tensor tile_kmax, double scale, int64_t q_off);
 std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k,
                                     torch::Tensor v, torch::Tensor out, torch::Tensor lse,
-                                    torch::Tensor kend, torch::Tensor units, double scale);
+                                    torch::Tensor kend, torch::Tensor units, double scale, int64_t q_off);
 std::vector<torch::Tensor> ipc_alloc(int64_t nbytes);
 int64_t ipc_open(torch::Tensor handle);
 void ipc_close(int64_t ptr);
@@ -75,8 +75,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grpo_token_loss", &art::grpo_token_loss);
   m.def("grad_sumsq", &art::grad_sumsq);
   m.def("adamw_step", &art::adamw_step);
-  m.def("attn_fwd", &art::attn_fwd);
-  m.def("attn_bwd", &art::attn_bwd);
+  m.def("attn_fwd", &art::attn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("kend"), py::arg("tile_kmax"),
+        py::arg("scale"), py::arg("q_off") = 0);
+  m.def("attn_bwd", &art::attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
+        py::arg("lse"), py::arg("kend"), py::arg("units"), py::arg("scale"), py::arg("q_off") = 0);
   m.def("gemm_tc", &art::gemm_tc);
   m.def("tc_error_code", &art::tc_error_code);
   m.def("gemm_tc_ag", &art::gemm_tc_ag);

@@ -57,6 +57,7 @@ class MicroBatch:
     h2d_bytes: int = 0  # bytes copied host -> device to stage this row
     group_ids: torch.Tensor | None = None  # [L] host copies (tree-structured layers)
     parent_ids: torch.Tensor | None = None
+    cp_plan: Any = None  # context-parallel plan (parallel/cp.py) when the row is split across ranks
 
     @property
     def L(self) -> int:
@@ -74,9 +75,16 @@ def stage_row(
     device: torch.device,
     pad_to: int = 64,
     pin: bool = True,
+    cp: Any = None,
+    conv_width: int = 4,
+    linear_layers: bool = False,
 ) -> MicroBatch:
     """Slice one row of CPU packed tensors, trim trailing padding (rounded up
-    to ``pad_to``), build the attention metadata and copy it to ``device``."""
+    to ``pad_to``), build the attention metadata and copy it to ``device``.
+
+    With a context-parallel group ``cp`` every rank of the group stages the
+    same row but keeps only its contiguous token slice (plus the plan that
+    the attention and gated DeltaNet layers use to exchange the rest)."""
     gids = packed["group_ids"][row]
     n_valid = max(_valid_length(gids), 1)
     L = min(int(gids.numel()), (n_valid + pad_to - 1) // pad_to * pad_to)
@@ -90,6 +98,8 @@ def stage_row(
     nxt = sel + 1
     kend = visibility_ends(packed["group_ids"][row : row + 1, :L], packed["parent_ids"][row : row + 1, :L])[0]
     pos = packed["input_pos"][row, :L]
+    if cp is not None and cp.world > 1:
+        return _stage_row_cp(packed, row, device, L, kend, pos, sel, n_valid, cp, pin, conv_width, linear_layers)
 
     moved = [0]
 
@@ -123,6 +133,53 @@ def stage_row(
         h2d_bytes=moved[0],
         group_ids=packed["group_ids"][row, :L].clone(),
         parent_ids=packed["parent_ids"][row, :L].clone(),
+    )
+
+
+def _stage_row_cp(packed, row, device, L, kend, pos, sel, n_valid, cp, pin, conv_width, linear_layers) -> MicroBatch:
+    from ..parallel.cp import CPPlan
+
+    assert L % (cp.world * 64) == 0, "context-parallel rows must split into 64-token multiples"
+    gids = packed["group_ids"][row, :L]
+    pids = packed["parent_ids"][row, :L]
+    plan = CPPlan(cp, kend, pos, gids, pids, conv_width, linear_layers)
+    a, b = plan.a, plan.b
+    moved = [sum(t.numel() * t.element_size() for t in (plan.meta.positions, plan.meta.kend,
+                                                         plan.meta.tile_kmax, plan.meta.bwd_units))]
+
+    def dev(t: torch.Tensor) -> torch.Tensor:
+        t = t.contiguous()
+        moved[0] += t.numel() * t.element_size()
+        if pin and device.type == "cuda":
+            t = t.pin_memory()
+        return t.to(device, non_blocking=True)
+
+    tokens = packed["tokens"][row, a:b].clone()
+    tokens[tokens < 0] = 0
+    sel = sel[(sel >= a) & (sel < b)]
+    nxt = sel + 1
+    routes = None
+    rr = packed.get("moe_routing_replay")
+    if rr is not None:
+        routes = dev(rr.expert_indices[row, a:b])
+    orig = packed.get("original_logprobs")
+    return MicroBatch(
+        tokens=dev(tokens),
+        meta=plan.meta,
+        sel=dev(sel - a),
+        targets=dev(packed["tokens"][row, nxt]),
+        old=dev(packed["logprobs"][row, nxt].float()),
+        adv=dev(packed["advantages"][row, nxt].float()),
+        w=dev(packed["weights"][row, nxt].float()),
+        group=dev(packed["group_ids"][row, nxt]),
+        original=dev(orig[row, nxt].float()) if orig is not None else None,
+        routes=routes,
+        n_tokens=max(0, min(n_valid, b) - a),
+        n_train=int(sel.numel()),
+        h2d_bytes=moved[0],
+        group_ids=gids.clone(),
+        parent_ids=pids.clone(),
+        cp_plan=plan,
     )
 
 
@@ -192,6 +249,7 @@ class GRPOTrainer:
         fused_dp: bool = True,
         max_tokens_per_rank: int = 16384,
         tp_size: int = 1,
+        cp_size: int = 1,
     ) -> None:
         self.device = torch.device(device)
         self.group = group
@@ -219,6 +277,15 @@ class GRPOTrainer:
             from ..parallel.tp import TPContext
 
             self.tp = TPContext(group, self.device, max_tokens_per_rank, cfg.hidden_size)
+        self.cp = None
+        self.cp_size = cp_size if self.world > 1 else 1
+        if self.cp_size > 1:
+            # context parallelism: every rank takes a contiguous slice of each
+            # packed row; it spans all ranks and is exclusive with TP
+            assert self.cp_size == self.world and self.tp_size == 1, "context parallelism spans all ranks"
+            from ..parallel.cp import CPContext
+
+            self.cp = CPContext(group, self.device)
         if cfg.is_moe and self.world > 1:
             from ..parallel.ep import EPContext
 
@@ -291,6 +358,8 @@ class GRPOTrainer:
         """Forward + backward of one packed row; gradients accumulate into the
         store.  Returns device scalars (loss contribution, entropy sum, ...)."""
         ctx: dict[str, Any] = {"group_ids": mb.group_ids, "parent_ids": mb.parent_ids}
+        if mb.cp_plan is not None:
+            ctx["cp_plan"], ctx["cp"] = mb.cp_plan, self.cp
         if mb.routes is not None:
             ctx["replay_routes"] = mb.routes
         ref = None
@@ -344,16 +413,21 @@ class GRPOTrainer:
         mask = packed["assistant_mask"]
         total = float(mask[:, 1:].sum().item())  # trainable (scored) tokens of the whole step
         n_rows = int(mask.shape[0])
-        dp_world = self.world // self.tp_size
-        dp_rank = self.rank // self.tp_size
+        shard = self.tp_size * self.cp_size  # ranks that split one row
+        dp_world = self.world // shard
+        dp_rank = self.rank // shard
         rows = list(range(n_rows))[dp_rank::dp_world]
-        pad_to = 128 * self.tp_size if self.tp is not None else 64
+        pad_to = 128 * shard if shard > 1 else 64
+        cfgm = self.model.cfg
+        linear = any(cfgm.layer_kind(i) != "attention" for i in range(cfgm.num_hidden_layers))
         if micro_batches is None:
-            micro_batches = [stage_row(packed, r, self.device, pad_to=pad_to) for r in rows]
-        if self.ep is not None:
+            micro_batches = [stage_row(packed, r, self.device, pad_to=pad_to, cp=self.cp,
+                                       conv_width=cfgm.linear_conv_kernel_dim, linear_layers=linear)
+                             for r in rows]
+        if self.ep is not None and self.cp is None:
             # expert-parallel layers are collective: every rank runs the same
             # number of micro steps; missing ones are zero-weight copies
-            per_rank = (n_rows + self.world - 1) // self.world
+            per_rank = (n_rows + dp_world - 1) // dp_world
             while len(micro_batches) < per_rank:
                 micro_batches.append(zero_weight(stage_row(packed, self.rank % n_rows, self.device)))
         acc = {k: torch.zeros((), device=self.device) for k in ("loss", "entropy", "probs_corr", "kl")}

@@ -39,7 +39,22 @@ TP_GPU = ModelConfig(
     name="tp-small", family="qwen3", vocab_size=2048, hidden_size=512, num_hidden_layers=2,
     num_attention_heads=4, num_key_value_heads=2, head_dim=128, intermediate_size=1024, qk_norm=True,
 )
-CONFIGS = {"moe-tiny": MOE_CPU, "moe-small": MOE_GPU, "tp-tiny": TP_CPU, "tp-small": TP_GPU}
+HYBRID_CPU = ModelConfig(
+    name="hybrid-tiny", family="qwen3_next", vocab_size=512, hidden_size=64, num_hidden_layers=4,
+    num_attention_heads=2, num_key_value_heads=1, head_dim=32, intermediate_size=0, qk_norm=True,
+    full_attention_interval=2, num_experts=4, num_experts_per_tok=2, moe_intermediate_size=32,
+    shared_expert_intermediate_size=32, linear_num_key_heads=2, linear_num_value_heads=2,
+    linear_key_head_dim=16, linear_value_head_dim=16, attn_output_gate=True,
+)
+HYBRID_GPU = ModelConfig(
+    name="hybrid-small", family="qwen3_next", vocab_size=2048, hidden_size=256, num_hidden_layers=4,
+    num_attention_heads=2, num_key_value_heads=1, head_dim=128, intermediate_size=0, qk_norm=True,
+    full_attention_interval=2, num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
+    shared_expert_intermediate_size=128, linear_num_key_heads=2, linear_num_value_heads=2,
+    linear_key_head_dim=64, linear_value_head_dim=64, attn_output_gate=True,
+)
+CONFIGS = {"moe-tiny": MOE_CPU, "moe-small": MOE_GPU, "tp-tiny": TP_CPU, "tp-small": TP_GPU,
+           "hybrid-tiny": HYBRID_CPU, "hybrid-small": HYBRID_GPU}
 
 GPU_CFG = ModelConfig(
     name="dp-small", family="qwen2", vocab_size=2048, hidden_size=256, num_hidden_layers=2,
@@ -54,7 +69,17 @@ def _packed(vocab: int, prompt: int, comp: int, seq_len: int):
     return packed_tensors_from_tokenized_results(res, seq_len, rng=random.Random(0))
 
 
-def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1):
+def _shape(backend: str, cfg: ModelConfig) -> tuple[int, int, int, int]:
+    """(vocab, prompt, completion, packed row length) of the synthetic batch."""
+    if cfg.family == "qwen3_next":
+        # tree segments straddle the context-parallel split
+        return (cfg.vocab_size, 100, 30, 256) if backend == "gloo" else (cfg.vocab_size, 200, 60, 512)
+    if backend == "gloo":
+        return cfg.vocab_size, 24, 12, 128
+    return cfg.vocab_size, 96, 48, 512
+
+
+def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1, cp_size=1):
     if backend == "nccl":
         torch.cuda.set_device(rank)
         device = torch.device("cuda", rank)
@@ -66,9 +91,9 @@ def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1):
                             timeout=timedelta(seconds=120))
     try:
         cfg = {"dp-small": GPU_CFG, **CONFIGS}.get(cfg_name) or get_config(cfg_name)
-        packed = _packed(cfg.vocab_size, 24 if backend == "gloo" else 96, 12 if backend == "gloo" else 48,
-                         128 if backend == "gloo" else 512)
-        tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), device, seed=0, group=dist.group.WORLD, tp_size=tp_size)
+        packed = _packed(*_shape(backend, cfg))
+        tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), device, seed=0, group=dist.group.WORLD, tp_size=tp_size,
+                         cp_size=cp_size)
         assert (tr.grad_sync is not None) == (backend == "nccl")
         assert (tr.ep is not None) == cfg.is_moe
         for _ in range(2):
@@ -84,19 +109,18 @@ def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1):
 
 
 def _single(device, cfg, backend):
-    packed = _packed(cfg.vocab_size, 24 if backend == "gloo" else 96, 12 if backend == "gloo" else 48,
-                     128 if backend == "gloo" else 512)
+    packed = _packed(*_shape(backend, cfg))
     tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), device, seed=0)
     for _ in range(2):
         m = tr.train_step(packed, 1e-3, {})
     return tr.store.master.cpu(), m.to_host(), packed
 
 
-def _run(world, backend, cfg_name, tp_size=1):
+def _run(world, backend, cfg_name, tp_size=1, cp_size=1):
     d = tempfile.mkdtemp()
     init = os.path.join(d, "init")
     out = os.path.join(d, "out.pt")
-    mp.start_processes(_worker, args=(world, init, out, backend, cfg_name, tp_size), nprocs=world,
+    mp.start_processes(_worker, args=(world, init, out, backend, cfg_name, tp_size, cp_size), nprocs=world,
                        start_method="spawn")
     return torch.load(out)
 
@@ -159,3 +183,24 @@ def test_tp_fused_two_gpus_matches_single_gpu():
     err = (res["master"] - master).norm() / master.norm()
     assert err < 1e-2, err
     assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-2 * max(1.0, abs(metrics["loss/train"]))
+
+
+def test_cp_hybrid_gloo_matches_single_process():
+    """Context parallelism (2 CPU ranks) on the hybrid gated-DeltaNet / MoE
+    model: every packed row is split in two, tree segments cross the split."""
+    res = _run(2, "gloo", "hybrid-tiny", cp_size=2)
+    master, metrics, packed = _single(torch.device("cpu"), HYBRID_CPU, "gloo")
+    err = (res["master"] - master).norm() / master.norm()
+    assert err < 1e-4, err
+    assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-5
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_cp_hybrid_two_gpus_matches_single_gpu():
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    res = _run(2, "nccl", "hybrid-small", cp_size=2)
+    master, metrics, _ = _single(torch.device("cuda", 0), HYBRID_GPU, "nccl")
+    err = (res["master"] - master).norm() / master.norm()
+    assert err < 2e-2, err
+    assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 2e-2 * max(1.0, abs(metrics["loss/train"]))
