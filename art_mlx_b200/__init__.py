@@ -38,10 +38,14 @@ def __getattr__(name: str):
         from .backends.local import LocalBackend
 
         return LocalBackend
-    if name == "MultiGPUBackend":
+    if name in ("MultiGPUBackend", "MegatronBackend"):
         from .backends.multigpu import MultiGPUBackend
 
         return MultiGPUBackend
+    if name in ("init_runtime_config", "init_megatron_runtime_config"):
+        from .backends.multigpu import init_runtime_config
+
+        return init_runtime_config
     if name == "PipelineTrainer":
         from .pipeline_trainer.trainer import PipelineTrainer
 
@@ -59,6 +63,7 @@ __all__ = [
     "Messages",
     "MessagesAndChoices",
     "Model",
+    "MegatronBackend",
     "MultiGPUBackend",
     "PipelineTrainer",
     "RuntimeConfig",
@@ -74,5 +79,7 @@ __all__ = [
     "dev",
     "gather_trajectories",
     "gather_trajectory_groups",
+    "init_megatron_runtime_config",
+    "init_runtime_config",
     "trajectory_group_batches",
 ]

@@ -39,7 +39,7 @@ from ..preprocessing.pack import packed_tensors_from_tokenized_results, packed_t
 from ..preprocessing.prefix_tree import estimate_prefix_tree_packed_tokens
 from ..preprocessing.tokenize import TokenizedResult, tokenize_trajectory_groups
 from ..runtime.checkpoint import load_adapter, save_adapter
-from ..runtime.trainer import GRPOTrainer, stage_row
+from ..runtime.trainer import GRPOTrainer
 from ..trajectories import Trajectory, TrajectoryGroup
 from ..types import LocalTrainResult, TrainSFTConfig
 from ..utils.output_dirs import get_model_dir, get_step_checkpoint_dir, get_step_from_dir
@@ -155,6 +155,10 @@ class LocalBackend:
             )
             group = dist.group.WORLD if dist.is_available() and dist.is_initialized() else None
             tr = GRPOTrainer(cfg, self._lora_spec(model), self._device, seed=self._seed, adamw=adamw, group=group)
+            from ..models.weights import maybe_load_base_weights
+
+            if hasattr(tr.model, "load_hf_state_dict"):
+                maybe_load_base_weights(tr.model, model.base_model)
         self._trainers[key] = tr
         return tr
 
@@ -268,7 +272,6 @@ class LocalBackend:
             num_trajectories_learning_rate_multiplier_power=num_trajectories_learning_rate_multiplier_power,
             kl_ref_adapter_path=kl_ref_adapter_path,
         )
-        tr = self._get_trainer(model)
         step = get_step_from_dir(d)
         results = list(
             tokenize_trajectory_groups(
@@ -291,7 +294,14 @@ class LocalBackend:
             new_step = step + 1
             ck = get_step_checkpoint_dir(d, new_step)
             if save_checkpoint and _rank() == 0:
-                save_adapter(ck, tr.store, model.base_model, tr.model.lora_spec, tr.optim.state_dict())
+                prev = get_step_checkpoint_dir(d, step)
+                if os.path.exists(ck):
+                    shutil.rmtree(ck)
+                if os.path.exists(prev):
+                    shutil.copytree(prev, ck)
+                else:
+                    tr = self._get_trainer(model)
+                    save_adapter(ck, tr.store, model.base_model, tr.model.lora_spec, tr.optim.state_dict())
             _barrier()
             base_metrics.update({"data/step_num_groups_trainable": 0.0, "data/step_trainer_tokens": 0.0})
             return LocalTrainResult(step=new_step, metrics=base_metrics, checkpoint_path=ck if save_checkpoint else None)
@@ -299,26 +309,12 @@ class LocalBackend:
         packed = self._pack(results, packed_sequence_length, advantage_balance)
         if plot_tensors and _rank() == 0:
             packed_tensors_to_dir(packed, os.path.join(d, "tensors"))
-        # reference adapter for the KL penalty (default: the frozen base)
-        ref_state = None
-        if kl_penalty_coef > 0 and kl_ref_adapter_path:
-            from safetensors.torch import load_file
-
-            ref_state = load_file(os.path.join(kl_ref_adapter_path, "adapter_model.safetensors"))
-        tr.set_reference_adapter(ref_state)
-        tr.logprob_chunk = logprob_calculation_chunk_size
-        rows = list(range(int(packed["tokens"].shape[0])))[tr.rank :: tr.world]
-        mbs = [stage_row(packed, r, tr.device) for r in rows]
-        self.last_h2d_bytes = sum(mb.h2d_bytes for mb in mbs)
-        metrics = tr.train_step(packed, lr, dev_config, micro_batches=mbs).to_host()
-        self.last_d2h_bytes = 5 * 4
         new_step = step + 1
         ck = get_step_checkpoint_dir(d, new_step)
-        if save_checkpoint:
-            tr.prepare_checkpoint()
-            if _rank() == 0:
-                save_adapter(ck, tr.store, model.base_model, tr.model.lora_spec, tr.optim.state_dict())
-        _barrier()
+        metrics = await self._train_packed(
+            model, packed, lr, dev_config, kl_ref_adapter_path if kl_penalty_coef > 0 else None,
+            logprob_calculation_chunk_size, ck if save_checkpoint else None,
+        )
         metrics["time/step_trainer_s"] = time.monotonic() - started
         metrics[("data/step_num_gradient_steps")] = 1.0
         builder = self._metrics.setdefault(model.name, MetricsBuilder())
@@ -327,6 +323,37 @@ class LocalBackend:
         if self._inference == "vllm" and model.name in self._servers and _rank() == 0:
             self._servers[model.name].load_adapter(self._model_inference_name(model, new_step), ck)
         return LocalTrainResult(step=new_step, metrics=metrics, checkpoint_path=ck if save_checkpoint else None)
+
+    async def _train_packed(
+        self,
+        model: Any,
+        packed: dict[str, Any],
+        lr: float,
+        dev_config: dict[str, Any],
+        kl_ref_adapter_path: str | None,
+        logprob_chunk: int,
+        out_dir: str | None,
+    ) -> dict[str, float]:
+        """One GRPO step on packed rows; publishes the adapter to ``out_dir``."""
+        tr = self._get_trainer(model)
+        # reference adapter for the KL penalty (default: the frozen base)
+        ref_state = None
+        if kl_ref_adapter_path:
+            from safetensors.torch import load_file
+
+            ref_state = load_file(os.path.join(kl_ref_adapter_path, "adapter_model.safetensors"))
+        tr.set_reference_adapter(ref_state)
+        tr.logprob_chunk = logprob_chunk
+        mbs = tr.stage(packed)
+        self.last_h2d_bytes = sum(mb.h2d_bytes for mb in mbs)
+        metrics = tr.train_step(packed, lr, dev_config, micro_batches=mbs).to_host()
+        self.last_d2h_bytes = 5 * 4
+        if out_dir is not None:
+            tr.prepare_checkpoint()
+            if _rank() == 0:
+                save_adapter(out_dir, tr.store, model.base_model, tr.model.lora_spec, tr.optim.state_dict())
+        _barrier()
+        return metrics
 
     # ------------------------------------------------------------------
     async def _train_sft(

@@ -9,6 +9,8 @@ follow the Hugging Face config keys so an HF ``config.json`` maps directly
 
 from __future__ import annotations
 
+import json
+import os
 from dataclasses import asdict, dataclass, replace
 from typing import Any, Literal
 
@@ -117,6 +119,19 @@ PRESETS: dict[str, ModelConfig] = {
         intermediate_size=704,
         qk_norm=True,
     ),
+    # head_dim 128 (the GPU attention kernels' head size) at test scale
+    "small-qwen3": ModelConfig(
+        name="small-qwen3",
+        family="qwen3",
+        vocab_size=2048,
+        hidden_size=512,
+        num_hidden_layers=4,
+        num_attention_heads=4,
+        num_key_value_heads=2,
+        head_dim=128,
+        intermediate_size=1024,
+        qk_norm=True,
+    ),
     "qwen2.5-7b": ModelConfig(
         name="qwen2.5-7b",
         family="qwen2",
@@ -192,6 +207,12 @@ HF_ALIASES = {
 
 
 def get_config(name: str) -> ModelConfig:
+    """A preset by name or Hugging Face id, or the ``config.json`` of a local
+    checkpoint directory."""
+    cj = os.path.join(name, "config.json")
+    if os.path.isdir(name) and os.path.exists(cj):
+        with open(cj) as f:
+            return ModelConfig.from_hf_dict(json.load(f), name=os.path.basename(os.path.normpath(name)))
     key = HF_ALIASES.get(name, name)
     if key not in PRESETS:
         raise KeyError(f"unknown model preset {name!r}; known: {sorted(PRESETS)}")

@@ -17,6 +17,7 @@ Format and normalisations follow the reference
 
 from __future__ import annotations
 
+import dataclasses
 import math
 import os
 import random
@@ -277,6 +278,9 @@ def packed_tensors_from_dir(**kwargs: Any) -> PackedTensors:
     out["pixel_values"] = [None] * n
     out["image_grid_thw"] = [None] * n
     out["moe_routing_replay"] = None
+    rp = f"{d}/moe_routing_replay.pt"
+    if os.path.exists(rp):
+        out["moe_routing_replay"] = PackedMoeRoutingReplay(**torch.load(rp))
     return out  # type: ignore[return-value]
 
 
@@ -289,4 +293,10 @@ def packed_tensors_to_dir(tensors: PackedTensors, dir: str) -> DiskPackedTensors
     mapped = packed_tensors_from_dir(**disk)
     for key in DISK_DTYPES:
         mapped[key].copy_(tensors[key])  # type: ignore[literal-required]
+    rr = tensors.get("moe_routing_replay")  # type: ignore[attr-defined]
+    rp = f"{dir}/moe_routing_replay.pt"
+    if rr is not None:
+        torch.save(dataclasses.asdict(rr), rp)
+    elif os.path.exists(rp):
+        os.remove(rp)
     return disk

@@ -271,27 +271,33 @@ class GRPOTrainer:
         self.ep = None
         self.tp = None
         self.tp_size = tp_size if self.world > 1 else 1
+        self.cp_size = cp_size if self.world > 1 else 1
+        if self.tp_size > 1 and self.cp_size > 1:
+            raise ValueError("tensor and context parallelism are not combined")
+        if self.world % (self.tp_size * self.cp_size) != 0:
+            raise ValueError(f"tp={self.tp_size} x cp={self.cp_size} does not divide world={self.world}")
         if self.tp_size > 1:
-            assert self.tp_size == self.world, "tensor parallelism spans all ranks (tp = world)"
-            from ..models.tp_decoder import TPDecoderLM
+            from ..parallel.topology import shard_subgroup
             from ..parallel.tp import TPContext
 
-            self.tp = TPContext(group, self.device, max_tokens_per_rank, cfg.hidden_size)
+            self.tp = TPContext(shard_subgroup(group, self.tp_size), self.device, max_tokens_per_rank,
+                                cfg.hidden_size)
         self.cp = None
-        self.cp_size = cp_size if self.world > 1 else 1
         if self.cp_size > 1:
-            # context parallelism: every rank takes a contiguous slice of each
-            # packed row; it spans all ranks and is exclusive with TP
-            assert self.cp_size == self.world and self.tp_size == 1, "context parallelism spans all ranks"
+            # context parallelism: every rank of a CP group takes a contiguous
+            # slice of the group's packed rows
             from ..parallel.cp import CPContext
+            from ..parallel.topology import shard_subgroup
 
-            self.cp = CPContext(group, self.device)
+            self.cp = CPContext(shard_subgroup(group, self.cp_size), self.device)
         if cfg.is_moe and self.world > 1:
             from ..parallel.ep import EPContext
 
             cap = 2 * max_tokens_per_rank * cfg.num_experts_per_tok
             self.ep = EPContext(group, cfg.num_experts, cfg.hidden_size, self.device, cap)
         if self.tp is not None:
+            from ..models.tp_decoder import TPDecoderLM
+
             self.model = TPDecoderLM(cfg, lora, self.device, self.tp, seed=seed, store=store)
         else:
             self.model = DecoderLM(cfg, lora, self.device, seed=seed, store=store, ep=self.ep)
@@ -397,6 +403,34 @@ class GRPOTrainer:
             "kl": kl.detach() if torch.is_tensor(kl) else lp.new_tensor(float(kl)),
         }
 
+    def stage(self, packed: Mapping[str, Any]) -> list[MicroBatch]:
+        """Stage this rank's rows of ``packed`` on the device.
+
+        Rows are interleaved over the data-parallel groups; the ranks of one
+        tensor- or context-parallel group stage the same rows (TP: whole
+        rows, CP: each its slice).  With expert parallelism every rank runs
+        the same number of micro steps (the expert exchange is collective),
+        so short ranks get zero-weight copies.
+        """
+        n_rows = int(packed["tokens"].shape[0])
+        shard = self.tp_size * self.cp_size  # ranks that split one row
+        dp_world = self.world // shard
+        dp_rank = self.rank // shard
+        pad_to = 128 * shard if shard > 1 else 64
+        cfgm = self.model.cfg
+        linear = any(cfgm.layer_kind(i) != "attention" for i in range(cfgm.num_hidden_layers))
+
+        def one(r: int) -> MicroBatch:
+            return stage_row(packed, r, self.device, pad_to=pad_to, cp=self.cp,
+                             conv_width=cfgm.linear_conv_kernel_dim, linear_layers=linear)
+
+        mbs = [one(r) for r in list(range(n_rows))[dp_rank::dp_world]]
+        if self.ep is not None:
+            per_rank = (n_rows + dp_world - 1) // dp_world
+            while len(mbs) < per_rank:
+                mbs.append(zero_weight(one(dp_rank % n_rows)))
+        return mbs
+
     def train_step(
         self,
         packed: Mapping[str, Any],
@@ -412,24 +446,8 @@ class GRPOTrainer:
         cfg = dict(cfg or {})
         mask = packed["assistant_mask"]
         total = float(mask[:, 1:].sum().item())  # trainable (scored) tokens of the whole step
-        n_rows = int(mask.shape[0])
-        shard = self.tp_size * self.cp_size  # ranks that split one row
-        dp_world = self.world // shard
-        dp_rank = self.rank // shard
-        rows = list(range(n_rows))[dp_rank::dp_world]
-        pad_to = 128 * shard if shard > 1 else 64
-        cfgm = self.model.cfg
-        linear = any(cfgm.layer_kind(i) != "attention" for i in range(cfgm.num_hidden_layers))
         if micro_batches is None:
-            micro_batches = [stage_row(packed, r, self.device, pad_to=pad_to, cp=self.cp,
-                                       conv_width=cfgm.linear_conv_kernel_dim, linear_layers=linear)
-                             for r in rows]
-        if self.ep is not None and self.cp is None:
-            # expert-parallel layers are collective: every rank runs the same
-            # number of micro steps; missing ones are zero-weight copies
-            per_rank = (n_rows + dp_world - 1) // dp_world
-            while len(micro_batches) < per_rank:
-                micro_batches.append(zero_weight(stage_row(packed, self.rank % n_rows, self.device)))
+            micro_batches = self.stage(packed)
         acc = {k: torch.zeros((), device=self.device) for k in ("loss", "entropy", "probs_corr", "kl")}
         n_tokens = 0
         for mb in micro_batches:

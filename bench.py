@@ -162,7 +162,7 @@ def main() -> None:
     from art_mlx_b200.preprocessing.pack import packed_tensors_from_tokenized_results
     from art_mlx_b200.preprocessing.synthetic import synthetic_groups
     from art_mlx_b200.preprocessing.tokenize import tokenize_trajectory_groups
-    from art_mlx_b200.runtime.trainer import GRPOTrainer, stage_row
+    from art_mlx_b200.runtime.trainer import GRPOTrainer
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -197,8 +197,7 @@ def main() -> None:
     trainer = GRPOTrainer(cfg, lora, device, seed=0, group=dist.group.WORLD if world > 1 else None)
     lr = 1e-5
     loss_cfg: dict = {}
-    my_rows = list(range(n_rows))[rank::world]
-    staged = [stage_row(packed, r, device) for r in my_rows]
+    staged = trainer.stage(packed)
     l2_flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
 
     def step() -> None:
