@@ -63,7 +63,7 @@ class LocalBackend:
         trainer: GRPOTrainer | None = None,
         device: str | torch.device | None = None,
         seed: int = 0,
-        inference: Literal["none", "vllm"] = "none",
+        inference: Literal["none", "native"] = "none",
     ) -> None:
         self._path = path or os.path.join(os.getcwd(), ".art")
         os.makedirs(self._path, exist_ok=True)
@@ -74,6 +74,7 @@ class LocalBackend:
         self._seed = seed
         self._inference = inference
         self._servers: dict[str, Any] = {}
+        self._engines: dict[str, Any] = {}
         self._metrics: dict[str, MetricsBuilder] = {}
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
@@ -179,13 +180,67 @@ class LocalBackend:
         cfg = config or {}
         host = cfg.get("host", "127.0.0.1")
         port = int(cfg.get("port", 8000))
-        if self._inference == "vllm" and _rank() == 0 and model.name not in self._servers:
+        api_key = cfg.get("server_args", {}).get("api_key", "default")
+        if self._inference == "native" and _rank() == 0 and model.name not in self._servers:
             from .inference import RolloutServer
 
-            server = RolloutServer(model=model, checkpoint_dir=ck, host=host, port=port, config=cfg)
+            server = RolloutServer(self._engine(model), self._tokenizer(model), served_name=model.name,
+                                   resolve_adapter=lambda name: self._resolve_adapter(model, name),
+                                   host=host, port=port, api_key=api_key)
             server.start()
             self._servers[model.name] = server
-        return f"http://{host}:{port}/v1", cfg.get("server_args", {}).get("api_key", "default")
+        return f"http://{host}:{port}/v1", api_key
+
+    # ------------------------------------------------------------------ generation
+    def _engine(self, model: Any):
+        """Generation engine on the trainer's own model: rollouts sample from
+        the live adapter the trainer updates (no weight transfer)."""
+        eng = self._engines.get(model.name)
+        if eng is None:
+            from ..runtime.generate import GenerationEngine
+
+            eng = GenerationEngine(self._get_trainer(model).model)
+            self._engines[model.name] = eng
+        return eng
+
+    def _tokenizer(self, model: Any):
+        from ..tokenizer import get_tokenizer
+
+        return get_tokenizer(model.base_model)
+
+    def _resolve_adapter(self, model: Any, name: str) -> str | None:
+        """Served model name -> engine adapter: the base model, a saved step
+        ``{name}@{step}`` other than the current one (loaded on first use), or
+        the live policy (``None``)."""
+        if name == model.base_model:
+            return "base"
+        if "@" in name:
+            _, step = name.rsplit("@", 1)
+            d = self._model_dir(model)
+            if step.isdigit() and int(step) != get_step_from_dir(d):
+                eng = self._engine(model)
+                if name not in eng.adapters:
+                    eng.add_adapter(name, get_step_checkpoint_dir(d, int(step)))
+                return name
+        return None
+
+    async def create_chat_completion(self, model: Any, messages: list[dict[str, Any]], **kwargs: Any) -> dict[str, Any]:
+        """One chat completion from the in-process engine, without HTTP
+        (the MLX fork's ``MLXBackend.create_chat_completion``); the response is
+        the OpenAI JSON the rollout server returns, token ids included."""
+        from .inference import RolloutServer
+
+        server = self._servers.get(model.name)
+        if server is None:
+            server = RolloutServer(self._engine(model), self._tokenizer(model), served_name=model.name,
+                                   resolve_adapter=lambda name: self._resolve_adapter(model, name))
+            import threading
+
+            server._worker = threading.Thread(target=server._work, name="rollout-engine", daemon=True)
+            server._worker.start()
+            self._servers[f"{model.name}#inproc"] = server
+        body = {"model": kwargs.pop("model", model.name), "messages": messages, **kwargs}
+        return await server.chat_completions(body)
 
     # ------------------------------------------------------------------
     def _pack(
@@ -320,8 +375,6 @@ class LocalBackend:
         builder = self._metrics.setdefault(model.name, MetricsBuilder())
         metrics = builder.update(metrics)
         metrics = aggregate_rl_training_metrics([metrics], groups)
-        if self._inference == "vllm" and model.name in self._servers and _rank() == 0:
-            self._servers[model.name].load_adapter(self._model_inference_name(model, new_step), ck)
         return LocalTrainResult(step=new_step, metrics=metrics, checkpoint_path=ck if save_checkpoint else None)
 
     async def _train_packed(
@@ -346,7 +399,12 @@ class LocalBackend:
         tr.logprob_chunk = logprob_chunk
         mbs = tr.stage(packed)
         self.last_h2d_bytes = sum(mb.h2d_bytes for mb in mbs)
-        metrics = tr.train_step(packed, lr, dev_config, micro_batches=mbs).to_host()
+        server = self._servers.get(model.name) or self._servers.get(f"{model.name}#inproc")
+        if server is not None:  # colocated rollouts: no generation batch during the update
+            with server.engine_lock:
+                metrics = tr.train_step(packed, lr, dev_config, micro_batches=mbs).to_host()
+        else:
+            metrics = tr.train_step(packed, lr, dev_config, micro_batches=mbs).to_host()
         self.last_d2h_bytes = 5 * 4
         if out_dir is not None:
             tr.prepare_checkpoint()
