@@ -21,6 +21,7 @@ for one process per GPU:
 
 from __future__ import annotations
 
+import contextlib
 import json
 import os
 import random
@@ -297,6 +298,7 @@ class LocalBackend:
         scale_learning_rate_by_reward_std_dev: bool = False,
         logprob_calculation_chunk_size: int = 4096,
         packed_sequence_length: int | None = None,
+        grad_accumulation_sequences: int | None = None,
         num_trajectories_learning_rate_multiplier_power: float = 0.0,
         save_checkpoint: bool = True,
         verbose: bool = False,
@@ -368,10 +370,10 @@ class LocalBackend:
         ck = get_step_checkpoint_dir(d, new_step)
         metrics = await self._train_packed(
             model, packed, lr, dev_config, kl_ref_adapter_path if kl_penalty_coef > 0 else None,
-            logprob_calculation_chunk_size, ck if save_checkpoint else None,
+            logprob_calculation_chunk_size, ck if save_checkpoint else None, grad_accumulation_sequences,
         )
         metrics["time/step_trainer_s"] = time.monotonic() - started
-        metrics[("data/step_num_gradient_steps")] = 1.0
+        metrics.setdefault("data/step_num_gradient_steps", 1.0)
         builder = self._metrics.setdefault(model.name, MetricsBuilder())
         metrics = builder.update(metrics)
         metrics = aggregate_rl_training_metrics([metrics], groups)
@@ -386,8 +388,10 @@ class LocalBackend:
         kl_ref_adapter_path: str | None,
         logprob_chunk: int,
         out_dir: str | None,
+        grad_accumulation_sequences: int | None = None,
     ) -> dict[str, float]:
-        """One GRPO step on packed rows; publishes the adapter to ``out_dir``."""
+        """GRPO optimizer step(s) on packed rows (one, or one per
+        ``grad_accumulation_sequences`` rows); publishes the adapter to ``out_dir``."""
         tr = self._get_trainer(model)
         # reference adapter for the KL penalty (default: the frozen base)
         ref_state = None
@@ -397,14 +401,21 @@ class LocalBackend:
             ref_state = load_file(os.path.join(kl_ref_adapter_path, "adapter_model.safetensors"))
         tr.set_reference_adapter(ref_state)
         tr.logprob_chunk = logprob_chunk
-        mbs = tr.stage(packed)
-        self.last_h2d_bytes = sum(mb.h2d_bytes for mb in mbs)
         server = self._servers.get(model.name) or self._servers.get(f"{model.name}#inproc")
-        if server is not None:  # colocated rollouts: no generation batch during the update
-            with server.engine_lock:
+        lock = server.engine_lock if server is not None else contextlib.nullcontext()
+        n_rows = int(packed["tokens"].shape[0])
+        with lock:  # colocated rollouts: no generation batch during the update
+            if grad_accumulation_sequences is not None and grad_accumulation_sequences < n_rows:
+                steps = [m.to_host() for m in tr.train_steps(packed, lr, dev_config, grad_accumulation_sequences)]
+                metrics = {k: sum(m[k] for m in steps) / len(steps) for k in steps[0]}
+                for k in ("data/step_trainer_tokens", "data/step_packed_tokens"):
+                    metrics[k] = sum(m[k] for m in steps)
+                metrics["data/step_num_gradient_steps"] = float(len(steps))
+                self.last_h2d_bytes = 0
+            else:
+                mbs = tr.stage(packed)
+                self.last_h2d_bytes = sum(mb.h2d_bytes for mb in mbs)
                 metrics = tr.train_step(packed, lr, dev_config, micro_batches=mbs).to_host()
-        else:
-            metrics = tr.train_step(packed, lr, dev_config, micro_batches=mbs).to_host()
         self.last_d2h_bytes = 5 * 4
         if out_dir is not None:
             tr.prepare_checkpoint()

@@ -205,7 +205,8 @@ class MultiGPUBackend(LocalBackend):
     def _pack(self, results, packed_sequence_length, advantage_balance):
         return super()._pack(results, packed_sequence_length or self._packed_len, advantage_balance)
 
-    async def _train_packed(self, model, packed, lr, dev_config, kl_ref_adapter_path, logprob_chunk, out_dir):
+    async def _train_packed(self, model, packed, lr, dev_config, kl_ref_adapter_path, logprob_chunk, out_dir,
+                            grad_accumulation_sequences=None):
         from ..preprocessing.pack import packed_tensors_to_dir
 
         d = self._model_dir(model)
@@ -221,7 +222,7 @@ class MultiGPUBackend(LocalBackend):
             packed_dir=pdir, num_sequences=disk["num_sequences"], sequence_length=disk["sequence_length"],
             checkpoint_dir=get_step_checkpoint_dir(d, step), output_dir=out_dir, base_model=model.base_model,
             learning_rate=lr, config=dict(dev_config), kl_ref_adapter_path=kl_ref_adapter_path,
-            logprob_chunk=logprob_chunk, log_path=log,
+            logprob_chunk=logprob_chunk, grad_accumulation_sequences=grad_accumulation_sequences, log_path=log,
         )):
             out = rec
         if out is None:

@@ -267,6 +267,24 @@ def tensorize_routes(rows: list[list[Any]], seq_len: int) -> PackedMoeRoutingRep
     return PackedMoeRoutingReplay(idx, have, L, K, max(K, int(idx.max().item()) + 1))
 
 
+def select_rows(packed: PackedTensors, rows: list[int]) -> PackedTensors:
+    """The packed rows ``rows`` as a new PackedTensors (one optimizer step's
+    share when a train call is split into several gradient steps)."""
+    idx = torch.tensor(rows, dtype=torch.long)
+    out: dict[str, Any] = {}
+    for key, val in packed.items():
+        if isinstance(val, torch.Tensor):
+            out[key] = val.index_select(0, idx)
+        elif isinstance(val, list):
+            out[key] = [val[r] for r in rows]
+        elif isinstance(val, PackedMoeRoutingReplay):
+            out[key] = dataclasses.replace(val, expert_indices=val.expert_indices.index_select(0, idx),
+                                           token_mask=val.token_mask.index_select(0, idx))
+        else:
+            out[key] = val
+    return out  # type: ignore[return-value]
+
+
 def packed_tensors_from_dir(**kwargs: Any) -> PackedTensors:
     d = kwargs["dir"]
     n, s = kwargs["num_sequences"], kwargs["sequence_length"]

@@ -43,6 +43,7 @@ class TrainJob(BaseModel):
     config: dict[str, Any] = Field(default_factory=dict)  # loss knobs (dev.TrainConfig)
     kl_ref_adapter_path: str | None = None
     logprob_chunk: int = 4096
+    grad_accumulation_sequences: int | None = None
     log_path: str
 
 

@@ -477,6 +477,28 @@ class GRPOTrainer:
             grad_norm=self.optim.grad_norm, n_train=int(total), n_tokens=n_tokens,
         )
 
+    def train_steps(
+        self,
+        packed: Mapping[str, Any],
+        learning_rate: float,
+        cfg: Mapping[str, Any] | None = None,
+        grad_accumulation_sequences: int | None = None,
+    ) -> list[StepMetrics]:
+        """Optimizer steps over ``packed``: one over every row when
+        ``grad_accumulation_sequences`` is ``None``, else one per consecutive
+        block of that many rows (reference ``megatron/training/microbatches.py:
+        115-170``: ``ceil(rows / sequences)`` gradient steps, each normalised by
+        its own trainable tokens; its blocks are spread over the data-parallel
+        ranks like a whole call)."""
+        from ..preprocessing.pack import select_rows
+
+        n = int(packed["tokens"].shape[0])
+        g = grad_accumulation_sequences
+        if g is None or g >= n:
+            return [self.train_step(packed, learning_rate, cfg)]
+        return [self.train_step(select_rows(packed, list(range(a, min(n, a + g)))), learning_rate, cfg)
+                for a in range(0, n, g)]
+
     # ------------------------------------------------------------------
     def sft_step(self, batch: list[tuple[list[int], list[int]]], learning_rate: float) -> dict[str, float]:
         """One supervised step: mean negative log-likelihood of the label

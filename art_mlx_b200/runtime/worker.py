@@ -89,8 +89,12 @@ def run_job(tr, job, state: dict) -> list[dict]:
         tr.set_reference_adapter(ref)
         tr.logprob_chunk = job.logprob_chunk
         t0 = time.monotonic()
-        mbs = tr.stage(packed)
-        metrics = tr.train_step(packed, job.learning_rate, job.config, micro_batches=mbs).to_host()
+        steps = [m.to_host() for m in tr.train_steps(packed, job.learning_rate, job.config,
+                                                     job.grad_accumulation_sequences)]
+        metrics = {k: sum(m[k] for m in steps) / len(steps) for k in steps[0]}
+        for k in ("data/step_trainer_tokens", "data/step_packed_tokens"):
+            metrics[k] = sum(m[k] for m in steps)
+        metrics["data/step_num_gradient_steps"] = float(len(steps))
         metrics["time/step_trainer_s"] = time.monotonic() - t0
         if job.output_dir is not None:
             _save(tr, job.output_dir, job.base_model, rank)

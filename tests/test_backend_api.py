@@ -98,3 +98,33 @@ def test_openai_client_requests_token_ids(tmp_path):
         assert client._extra == {"return_token_ids": True, "return_tokens_as_token_ids": True}
 
     asyncio.run(go())
+
+
+def test_grad_accumulation_sequences_splits_the_call(tmp_path):
+    """grad_accumulation_sequences=1: one optimizer step per packed row,
+    equal to calling train once per row."""
+    import random
+
+    from art_mlx_b200.preprocessing.pack import packed_tensors_from_tokenized_results, select_rows
+    from art_mlx_b200.preprocessing.tokenize import tokenize_trajectory_groups
+
+    async def go():
+        backend = LocalBackend(path=str(tmp_path), device="cpu")
+        model = _model()
+        await model.register(backend)
+        res = await backend.train(model, _groups(), learning_rate=1e-4, grad_accumulation_sequences=1,
+                                  packed_sequence_length=128)
+        return backend._get_trainer(model).store.master.clone(), res.metrics["data/step_num_gradient_steps"]
+
+    multi, nsteps = asyncio.run(go())
+    # the same rows, one train_step each, on a fresh trainer
+    from art_mlx_b200.models.config import LoRASpec, get_config
+    from art_mlx_b200.runtime.trainer import GRPOTrainer
+
+    res = list(tokenize_trajectory_groups(None, _groups(), False, True, rng=random.Random(0)))
+    packed = packed_tensors_from_tokenized_results(res, 128, rng=random.Random(7))
+    tr = GRPOTrainer(get_config("tiny-qwen3"), LoRASpec(r=8, alpha=16), "cpu", seed=0)
+    for r in range(int(packed["tokens"].shape[0])):
+        tr.train_step(select_rows(packed, [r]), 1e-4, {})
+    assert nsteps == packed["tokens"].shape[0] > 1
+    assert torch.allclose(multi, tr.store.master, atol=1e-6)
