@@ -10,6 +10,8 @@ Public API (same names and call shapes as OpenPipe ART):
 """
 
 from . import dev
+from .auto_trajectory import auto_trajectory, capture_auto_trajectory
+from .yield_trajectory import capture_yielded_trajectory, yield_trajectory
 from .backend import Backend
 from .gather import gather_trajectories, gather_trajectory_groups, trajectory_group_batches
 from .model import Model, TrainableModel
@@ -54,6 +56,10 @@ def __getattr__(name: str):
 
 
 __all__ = [
+    "auto_trajectory",
+    "capture_auto_trajectory",
+    "capture_yielded_trajectory",
+    "yield_trajectory",
     "Backend",
     "History",
     "LocalBackend",

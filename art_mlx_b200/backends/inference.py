@@ -151,6 +151,22 @@ class RolloutServer:
             "usage": {"prompt_tokens": len(prompt), "completion_tokens": comp, "total_tokens": len(prompt) + comp},
         }
 
+    @staticmethod
+    async def sse_chunks(out: dict[str, Any]):
+        """A finished completion as server-sent chat.completion.chunk events:
+        one content delta per choice (with its token ids and logprobs), then
+        the finish reasons (generation here is not incremental)."""
+        import json
+
+        base = {"id": out["id"], "object": "chat.completion.chunk", "created": out["created"], "model": out["model"]}
+        for ch in out["choices"]:
+            delta = {"index": ch["index"], "delta": {"role": "assistant", "content": ch["message"]["content"]},
+                     "logprobs": ch["logprobs"], "finish_reason": None, "token_ids": ch["token_ids"]}
+            yield f"data: {json.dumps({**base, 'choices': [delta], 'prompt_token_ids': out['prompt_token_ids']})}\n\n"
+        fin = [{"index": ch["index"], "delta": {}, "finish_reason": ch["finish_reason"]} for ch in out["choices"]]
+        yield f"data: {json.dumps({**base, 'choices': fin, 'usage': out['usage']})}\n\n"
+        yield "data: [DONE]\n\n"
+
     async def completions(self, body: dict[str, Any]) -> dict[str, Any]:
         p = body.get("prompt") or ""
         prompt = list(p) if isinstance(p, list) else self.tokenizer.encode(p)
@@ -184,7 +200,13 @@ class RolloutServer:
         @app.post("/v1/chat/completions")
         async def chat(req: Request):
             check(req)
-            return await server.chat_completions(await req.json())
+            body = await req.json()
+            out = await server.chat_completions(body)
+            if not body.get("stream"):
+                return out
+            from fastapi.responses import StreamingResponse
+
+            return StreamingResponse(server.sse_chunks(out), media_type="text/event-stream")
 
         @app.post("/v1/completions")
         async def completions(req: Request):
