@@ -76,6 +76,7 @@ class LocalBackend:
         self._inference = inference
         self._servers: dict[str, Any] = {}
         self._engines: dict[str, Any] = {}
+        self._leases: dict[str, Any] = {}
         self._metrics: dict[str, MetricsBuilder] = {}
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
@@ -102,6 +103,10 @@ class LocalBackend:
         return get_model_dir(model, self._path)
 
     def _model_inference_name(self, model: Any, step: int | None = None) -> str:
+        from ..adapter_leases import pinned_inference_step
+
+        if step is None:
+            step = pinned_inference_step(model.name)
         if step is None:
             step = get_step_from_dir(self._model_dir(model)) if getattr(model, "trainable", False) else None
         base = model.name
@@ -119,7 +124,14 @@ class LocalBackend:
     async def _get_step(self, model: Any) -> int:
         return get_step_from_dir(self._model_dir(model))
 
+    def adapter_leases(self, model: Any):
+        """Lease manager of the model's checkpoints: leased steps survive cleanup."""
+        from ..adapter_leases import AdapterLeaseManager
+
+        return self._leases.setdefault(model.name, AdapterLeaseManager())
+
     async def _delete_checkpoint_files(self, model: Any, steps_to_keep: list[int]) -> None:
+        steps_to_keep = sorted(set(steps_to_keep) | self.adapter_leases(model).active_steps())
         if _rank() != 0:
             return
         ck = os.path.join(self._model_dir(model), "checkpoints")

@@ -291,6 +291,35 @@ class DecoderLM:
                 n += layer.gdn.num_parameters()
         return n
 
+    def hf_state_dict(self) -> dict[str, torch.Tensor]:
+        """Base weights under Hugging Face names (the fused q/k/v and gate/up
+        projections split back), inverse of :meth:`load_hf_state_dict`."""
+        cfg = self.cfg
+        out: dict[str, torch.Tensor] = {"model.embed_tokens.weight": self.embed, "model.norm.weight": self.final_norm}
+        if not cfg.tie_word_embeddings:
+            out["lm_head.weight"] = self.lm_head
+        q, kv = cfg.q_size * (2 if cfg.attn_output_gate else 1), cfg.kv_size
+        for i, layer in enumerate(self.layers):
+            p = f"model.layers.{i}."
+            out[p + "input_layernorm.weight"] = layer.in_norm
+            out[p + "post_attention_layernorm.weight"] = layer.post_norm
+            if layer.kind == "attention":
+                a = p + "self_attn."
+                out[a + "q_proj.weight"], out[a + "k_proj.weight"], out[a + "v_proj.weight"] = (
+                    layer.qkv_w[:q], layer.qkv_w[q : q + kv], layer.qkv_w[q + kv :])
+                if layer.qkv_b is not None:
+                    out[a + "q_proj.bias"], out[a + "k_proj.bias"], out[a + "v_proj.bias"] = (
+                        layer.qkv_b[:q], layer.qkv_b[q : q + kv], layer.qkv_b[q + kv :])
+                if layer.q_norm is not None:
+                    out[a + "q_norm.weight"], out[a + "k_norm.weight"] = layer.q_norm, layer.k_norm
+                out[a + "o_proj.weight"] = layer.o_w
+            if layer.mlp is not None:
+                m = p + "mlp."
+                F = cfg.intermediate_size
+                out[m + "gate_proj.weight"], out[m + "up_proj.weight"] = layer.mlp.gu_w[:F], layer.mlp.gu_w[F:]
+                out[m + "down_proj.weight"] = layer.mlp.down_w
+        return out
+
     def load_hf_state_dict(self, sd: dict[str, torch.Tensor]) -> None:
         """Copy Hugging Face weights (``model.layers.{i}.self_attn.q_proj.weight``
         etc.) into the fused layout."""

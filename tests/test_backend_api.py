@@ -128,3 +128,24 @@ def test_grad_accumulation_sequences_splits_the_call(tmp_path):
         tr.train_step(select_rows(packed, [r]), 1e-4, {})
     assert nsteps == packed["tokens"].shape[0] > 1
     assert torch.allclose(multi, tr.store.master, atol=1e-6)
+
+
+def test_pinned_inference_step_and_leases(tmp_path):
+    from art_mlx_b200.adapter_leases import pin_inference_step
+
+    async def go():
+        backend = LocalBackend(path=str(tmp_path), device="cpu")
+        model = _model()
+        await model.register(backend)
+        for s in range(3):
+            await backend.train(model, _groups(s), learning_rate=1e-4)
+        assert model.get_inference_name() == "tiny@3"
+        async with pin_inference_step("tiny", 1):
+            assert model.get_inference_name() == "tiny@1"
+            async with backend.adapter_leases(model).lease(1):
+                await backend._delete_checkpoint_files(model, [3])
+        assert model.get_inference_name() == "tiny@3"
+        ck = os.path.join(str(tmp_path), "p", "models", "tiny", "checkpoints")
+        assert sorted(os.listdir(ck)) == ["0001", "0003"]
+
+    asyncio.run(go())
