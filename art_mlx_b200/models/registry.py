@@ -1,0 +1,67 @@
+"""Model-support registry: which architectures the trainer knows, their
+default LoRA targets and which parallel modes and features they support.
+
+Role of the reference ``src/art/megatron/model_support/spec.py:92``
+(``ModelSupportSpec``), ``registry.py`` and the per-family handlers: the
+backend resolves ``base_model`` (a preset name, a Hugging Face id or a local
+checkpoint directory) to a family, refuses unknown families unless
+``allow_unvalidated_arch`` is set, and takes the family's default LoRA
+targets.  Families are described by data here, since every supported family
+runs through the same :class:`DecoderLM` layers.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+from .config import ModelConfig, get_config
+
+
+@dataclass(frozen=True)
+class ModelSupportSpec:
+    key: str  # family name (ModelConfig.family)
+    hf_model_types: tuple[str, ...]
+    default_target_modules: tuple[str, ...]
+    is_moe: bool = False
+    linear_attention: bool = False
+    supports: frozenset[str] = field(default_factory=frozenset)  # "dp", "tp", "cp", "ep", "generate"
+
+
+_DENSE = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+_REGISTRY: dict[str, ModelSupportSpec] = {}
+
+
+def register_model_support(spec: ModelSupportSpec) -> None:
+    _REGISTRY[spec.key] = spec
+
+
+for _spec in (
+    ModelSupportSpec("qwen2", ("qwen2",), _DENSE, supports=frozenset({"dp", "tp", "cp", "generate"})),
+    ModelSupportSpec("qwen3", ("qwen3",), _DENSE, supports=frozenset({"dp", "tp", "cp", "generate"})),
+    ModelSupportSpec("qwen3_moe", ("qwen3_moe",), _DENSE, is_moe=True,
+                     supports=frozenset({"dp", "ep", "cp", "generate"})),
+    ModelSupportSpec("qwen3_next", ("qwen3_next",), _DENSE + ("in_proj_qkvz", "out_proj"), is_moe=True,
+                     linear_attention=True, supports=frozenset({"dp", "ep", "cp"})),
+):
+    register_model_support(_spec)
+
+
+def registered_families() -> list[str]:
+    return sorted(_REGISTRY)
+
+
+def get_model_support(base_model: str | ModelConfig, allow_unvalidated_arch: bool = False) -> ModelSupportSpec:
+    cfg = base_model if isinstance(base_model, ModelConfig) else get_config(base_model)
+    spec = _REGISTRY.get(cfg.family)
+    if spec is None:
+        if not allow_unvalidated_arch:
+            raise ValueError(f"model family {cfg.family!r} is not supported (known: {registered_families()}); "
+                             "pass allow_unvalidated_arch=True to try it anyway")
+        return ModelSupportSpec(cfg.family, (cfg.family,), _DENSE)
+    return spec
+
+
+def check_parallelism(spec: ModelSupportSpec, *, tp: int = 1, cp: int = 1, ep: bool = False) -> None:
+    for mode, on in (("tp", tp > 1), ("cp", cp > 1), ("ep", ep)):
+        if on and mode not in spec.supports:
+            raise ValueError(f"{spec.key} does not support {mode} parallelism (supported: {sorted(spec.supports)})")

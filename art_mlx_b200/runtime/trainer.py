@@ -250,7 +250,11 @@ class GRPOTrainer:
         max_tokens_per_rank: int = 16384,
         tp_size: int = 1,
         cp_size: int = 1,
+        allow_unvalidated_arch: bool = False,
     ) -> None:
+        from ..models.registry import check_parallelism, get_model_support
+
+        self.support = get_model_support(cfg, allow_unvalidated_arch)
         self.device = torch.device(device)
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -290,6 +294,7 @@ class GRPOTrainer:
             from ..parallel.topology import shard_subgroup
 
             self.cp = CPContext(shard_subgroup(group, self.cp_size), self.device)
+        check_parallelism(self.support, tp=self.tp_size, cp=self.cp_size)
         if cfg.is_moe and self.world > 1:
             from ..parallel.ep import EPContext
 

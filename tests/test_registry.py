@@ -1,0 +1,18 @@
+import pytest
+
+from art_mlx_b200.models.config import get_config
+from art_mlx_b200.models.registry import check_parallelism, get_model_support, registered_families
+
+
+def test_registry_resolves_presets_and_hf_ids():
+    assert get_model_support("Qwen/Qwen2.5-7B-Instruct").key == "qwen2"
+    s = get_model_support("qwen3-30b-a3b")
+    assert s.is_moe and "ep" in s.supports
+    assert get_model_support("qwen3-next-hybrid").linear_attention
+    assert set(registered_families()) >= {"qwen2", "qwen3", "qwen3_moe", "qwen3_next"}
+    with pytest.raises(ValueError, match="does not support tp"):
+        check_parallelism(get_model_support("qwen3-30b-a3b"), tp=2)
+    cfg = get_config("tiny-qwen3").scaled(family="llama")
+    with pytest.raises(ValueError, match="not supported"):
+        get_model_support(cfg)
+    assert get_model_support(cfg, allow_unvalidated_arch=True).key == "llama"
