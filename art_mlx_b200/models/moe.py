@@ -131,9 +131,56 @@ class ExpertParams:
         self.scale = scale
 
 
+def _tc_grouped(x: torch.Tensor, p: ExpertParams) -> bool:
+    """Whether the experts run on the tcgen05 grouped GEMM (base product and
+    LoRA in one kernel, ops/csrc/gemm_tc.cu ``gemm_tc_grouped``)."""
+    if x.device.type != "cuda" or x.dtype != torch.bfloat16 or x.shape[0] == 0:
+        return False
+    H, F2 = p.gu_w_t.shape[1], p.gu_w_t.shape[2]
+    return H % 64 == 0 and F2 % 128 == 0 and p.gu_w_t.is_contiguous() and p.down_w_t.is_contiguous()
+
+
+def _offs(counts: list[int]) -> list[int]:
+    out = [0]
+    for c in counts:
+        out.append(out[-1] + int(c))
+    return out
+
+
+def _experts_forward_tc(xs, counts, p: ExpertParams, lora: bool):
+    """Gate/up and down as grouped tcgen05 GEMMs with the LoRA products as a
+    K-extension of each (x A^T is the small library grouped GEMM)."""
+    from ..ops import native
+
+    C = native.lib()
+    s = p.scale
+    E, H, F2 = p.gu_w_t.shape
+    Fh = F2 // 2
+    offs = _offs(counts)
+    a2 = b2 = u_gu = u_d = None
+    if lora and p.A_gu is not None:
+        r = p.B_gu.shape[-1]
+        u_gu = grouped_mm(xs, p.A_gu.transpose(1, 2), counts)  # [N, 2r]
+        bd = xs.new_zeros(E, F2, 2 * r)  # per expert: block-diagonal s*[B_gate, B_up]
+        bd[:, :Fh, :r] = s * p.B_gu[:, 0]
+        bd[:, Fh:, r:] = s * p.B_gu[:, 1]
+        a2, b2 = u_gu.contiguous(), bd.view(E * F2, 2 * r)
+    gu = C.gemm_tc_grouped(xs.contiguous(), p.gu_w_t.view(E * H, F2), offs, F2, a2, b2, True)
+    g, up = gu[:, :Fh], gu[:, Fh:]
+    act = ((g.float() * torch.sigmoid(g.float())).to(gu.dtype) * up).contiguous()
+    a2 = b2 = None
+    if lora and p.A_d is not None:
+        u_d = grouped_mm(act, p.A_d.transpose(1, 2), counts).contiguous()  # [N, r]
+        a2, b2 = u_d, (s * p.B_d).reshape(E * H, -1).contiguous()
+    out = C.gemm_tc_grouped(act, p.down_w_t.view(E * Fh, H), offs, H, a2, b2, True)
+    return out, (xs, gu, act, u_gu, u_d, counts, lora)
+
+
 def experts_forward(xs: torch.Tensor, counts: list[int], p: ExpertParams, lora: bool):
     """Grouped SwiGLU experts with LoRA on gate/up and down.  Returns
     ``(out, saved)`` where ``saved`` feeds :func:`experts_backward`."""
+    if _tc_grouped(xs, p):
+        return _experts_forward_tc(xs, counts, p, lora)
     s = p.scale
     gu = grouped_mm(xs, p.gu_w_t, counts)
     u_gu = u_d = None
@@ -157,8 +204,24 @@ def experts_backward(dout: torch.Tensor, saved, p: ExpertParams) -> torch.Tensor
     xs, gu, act, u_gu, u_d, counts, lora = saved
     s = p.scale
     dout = dout.contiguous()
-    dact = grouped_mm(dout, p.down_w_t.transpose(1, 2), counts)
-    if lora and p.A_d is not None:
+    tc = _tc_grouped(xs, p)
+    E, H, F2 = p.gu_w_t.shape
+    if tc:
+        from ..ops import native
+
+        C = native.lib()
+        offs = _offs(counts)
+    if tc:
+        a2 = b2 = None
+        if lora and p.A_d is not None:
+            dyB = grouped_mm(dout, p.B_d, counts).contiguous()  # [N, r]
+            grouped_wgrad(dout, u_d, counts, p.g_B_d, s)
+            grouped_wgrad(dyB, act, counts, p.g_A_d, s)
+            a2, b2 = dyB, (s * p.A_d.transpose(1, 2)).reshape(E * (F2 // 2), -1).contiguous()
+        dact = C.gemm_tc_grouped(dout, p.down_w_t.view(E * (F2 // 2), H), offs, F2 // 2, a2, b2, False)
+    else:
+        dact = grouped_mm(dout, p.down_w_t.transpose(1, 2), counts)
+    if not tc and lora and p.A_d is not None:
         dyB = grouped_mm(dout, p.B_d, counts)  # [N, r]
         grouped_wgrad(dout, u_d, counts, p.g_B_d, s)
         grouped_wgrad(dyB, act, counts, p.g_A_d, s)
@@ -168,6 +231,18 @@ def experts_backward(dout: torch.Tensor, saved, p: ExpertParams) -> torch.Tensor
     sg = torch.sigmoid(g)
     da = dact.float()
     dgu = torch.cat([da * up * sg * (1 + g * (1 - sg)), da * g * sg], dim=1).to(gu.dtype)
+    if tc:
+        a2 = b2 = None
+        if lora and p.A_gu is not None:
+            r = p.B_gu.shape[-1]
+            dyB = torch.cat(
+                [grouped_mm(dgu[:, :Fh].contiguous(), p.B_gu[:, 0], counts),
+                 grouped_mm(dgu[:, Fh:].contiguous(), p.B_gu[:, 1], counts)], dim=1).contiguous()
+            grouped_wgrad(dgu[:, :Fh], u_gu[:, :r], counts, p.g_B_gu[:, 0], s)
+            grouped_wgrad(dgu[:, Fh:], u_gu[:, r:], counts, p.g_B_gu[:, 1], s)
+            grouped_wgrad(dyB, xs, counts, p.g_A_gu, s)
+            a2, b2 = dyB, (s * p.A_gu.transpose(1, 2)).reshape(E * H, -1).contiguous()
+        return C.gemm_tc_grouped(dgu, p.gu_w_t.view(E * H, F2), offs, H, a2, b2, False)
     dxs = grouped_mm(dgu, p.gu_w_t.transpose(1, 2), counts)
     if lora and p.A_gu is not None:
         r = p.B_gu.shape[-1]

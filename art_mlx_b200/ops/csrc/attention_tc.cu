@@ -1,0 +1,771 @@
+// Prefix-tree attention forward on the 5th-generation tensor cores (sm_100a):
+// tcgen05.mma with TMEM accumulators, TMA-fed shared memory, one elected
+// thread issuing the MMAs.  Same contract as the warp-level kernel in
+// attention.cu (GQA, head_dim 128, bf16 in, natural-log LSE out, mask
+// "key j visible to query i iff j <= i < kend[j]", queries at global
+// positions q_off + row).
+//
+// CTA = 128 queries x one q head; key tiles of 128, only the tiles whose
+// largest kend reaches the query block are visited.
+//   warp 0      TMA producer: Q once (2 boxes of 64 columns), then K and V of
+//               every visited key tile into separate 2-stage rings (128-byte
+//               swizzle): a K slot is released when S of its tile completes,
+//               a V slot when P V completes, so the loads run ahead of the
+//               tensor cores instead of sitting on the per-tile critical path
+//   warp 1      TMEM allocation (512 columns) and the MMA issuer:
+//                 S[b] = Q K^T         (M=128, N=128, K=128; both K-major)
+//                 O   += P V           (P K-major from shared memory, V
+//                                       MN-major straight from its TMA tile)
+//               S of tile n+1 is issued before P V of tile n, so the tensor
+//               cores compute the next scores while the softmax runs
+//   warps 2..5  softmax, one query row per thread (TMEM lane = row): read the
+//               S row (tcgen05.ld), mask, online max with lazy rescaling of O
+//               (only when the running max grows by more than 2^8), exp2,
+//               row sum, P row as bf16 into swizzled shared memory; finally
+//               O / l to global memory and the LSE.
+// TMEM columns: S[0] 0..127, S[1] 128..255, O 256..383.
+// All mbarrier waits are bounded (tc_common.cuh): on timeout the kernel
+// records an error code, every role leaves its loop and TMEM is freed.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <cudaTypedefs.h>
+#include "common.cuh"
+#include "tc_common.cuh"
+
+namespace art {
+using namespace tc;
+
+namespace {
+
+constexpr int FB = 128;                      // queries per CTA = keys per tile = head_dim
+constexpr int CHUNK_BYTES = FB * 64 * 2;     // 128 rows x 64 bf16 (one 128-byte swizzle span)
+constexpr int TILE_BYTES = 2 * CHUNK_BYTES;  // 128 x 128 bf16
+constexpr int KV_STAGES = 2;
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = TILE_BYTES;                       // K stage s at OFF_K + s*T
+constexpr int OFF_V = OFF_K + KV_STAGES * TILE_BYTES;  // V stage s at OFF_V + s*T
+constexpr int OFF_P = OFF_V + KV_STAGES * TILE_BYTES;
+constexpr int OFF_BAR = OFF_P + TILE_BYTES;
+constexpr int MAX_KT = 1024;                 // key tiles per row the tile list holds (131072 keys)
+constexpr int OFF_TL = OFF_BAR + 256;        // visible key-tile list (+ count)
+constexpr int FA_SMEM = OFF_TL + MAX_KT * 4 + 16 + 1024;  // + alignment slack
+constexpr int TILE_FULL = 1 << 30;           // list flag: every (query, key) pair of the tile is visible
+constexpr int FA_THREADS = 192;
+constexpr float kLog2eF = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct FaArgs {
+  const int* kend;
+  const int* tile_kmax;  // max kend over 64-key tiles
+  const int* tile_kmin;  // min kend over 64-key tiles
+  __nv_bfloat16* o;
+  int64_t ldo;
+  float* lse;
+  int Tq, Tk, q_off, Hq, Hkv;
+  float scale_log2;
+  int* err;
+};
+
+// Visibility of key tile kt (128 keys) for the query block starting at global
+// position g0: some key of the tile has kend > g0.
+__device__ __forceinline__ bool tile_visible(const FaArgs& p, int kt, int g0) {
+  const int a = 2 * kt, b = 2 * kt + 1;
+  int km = __ldg(p.tile_kmax + a);
+  if (b * 64 < p.Tk) km = max(km, __ldg(p.tile_kmax + b));
+  return km > g0;
+}
+
+// Every pair of the (query block [g0, g_last], key tile kt) is visible: all
+// keys precede the first query and every key's kend exceeds the last query.
+__device__ __forceinline__ bool tile_full(const FaArgs& p, int kt, int g0, int g_last) {
+  const int k_last = kt * FB + FB - 1;
+  if (k_last >= p.Tk || k_last > g0) return false;
+  const int km = min(__ldg(p.tile_kmin + 2 * kt), __ldg(p.tile_kmin + 2 * kt + 1));
+  return km > g_last;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(FA_THREADS, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const FaArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* s_empty = bars + 11;  // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* pv_done = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * FB;  // local query row of the block
+  const int h = blockIdx.y;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int g0 = p.q_off + q0;  // global position of the first query
+  const int g_last = min(g0 + FB - 1, p.q_off + p.Tq - 1);
+  const int kt_last = min(g_last / FB, (p.Tk - 1) / FB);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  // visible key tiles of this query block, computed once (entries: kt | TILE_FULL)
+  int* tlist = reinterpret_cast<int*>(smem + OFF_TL);
+  int* tcount = tlist + MAX_KT;
+  if (warp == 0) {
+    int count = 0;
+    for (int base = 0; base <= kt_last; base += 32) {
+      const int kt = base + lane;
+      const bool vis = kt <= kt_last && tile_visible(p, kt, g0);
+      const bool full = vis && tile_full(p, kt, g0, g_last);
+      const unsigned m = __ballot_sync(0xffffffffu, vis);
+      const int pos = count + __popc(m & ((1u << lane) - 1u));
+      if (vis && pos < MAX_KT) tlist[pos] = kt | (full ? TILE_FULL : 0);
+      count += __popc(m);
+    }
+    if (lane == 0) *tcount = min(count, MAX_KT);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_o = tmem + 256;
+  const int ntl = *tcount;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_2d(smem + OFF_Q, &tmQ, q_full, h * FB, q0);
+      tma_load_2d(smem + OFF_Q + CHUNK_BYTES, &tmQ, q_full, h * FB + 64, q0);
+      for (int n = 0; n < ntl; ++n) {
+        const int kt = tlist[n] & (TILE_FULL - 1);
+        const int s = n & 1;
+        const uint32_t ph = ((n >> 1) & 1) ^ 1;
+        if (!mbar_wait(&k_empty[s], ph, abort_flag, p.err, 11)) break;
+        uint8_t* kb = smem + OFF_K + s * TILE_BYTES;
+        mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
+        tma_load_2d(kb, &tmK, &k_full[s], hk * FB, kt * FB);
+        tma_load_2d(kb + CHUNK_BYTES, &tmK, &k_full[s], hk * FB + 64, kt * FB);
+        if (!mbar_wait(&v_empty[s], ph, abort_flag, p.err, 19)) break;
+        uint8_t* vb = smem + OFF_V + s * TILE_BYTES;
+        mbar_arrive_expect_tx(&v_full[s], TILE_BYTES);
+        tma_load_2d(vb, &tmV, &v_full[s], hk * FB, kt * FB);
+        tma_load_2d(vb + CHUNK_BYTES, &tmV, &v_full[s], hk * FB + 64, kt * FB);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(FB, FB);
+      constexpr uint32_t idO = idesc_bf16_bmn(FB, FB);
+      const uint32_t qa = smem_addr(smem + OFF_Q);
+      const uint32_t pa = smem_addr(smem + OFF_P);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.err, 12);
+      tc_fence_after();
+      auto issue_pv = [&](int n) -> bool {  // O += P_n V_n
+        const int s = n & 1;
+        if (!mbar_wait(p_full, n & 1, abort_flag, p.err, 13)) return false;
+        if (!mbar_wait(&v_full[s], (n >> 1) & 1, abort_flag, p.err, 10)) return false;
+        tc_fence_after();
+        const uint32_t va = smem_addr(smem + OFF_V + s * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < FB / 16; ++kk)
+          mma_bf16(tmem_o, desc_k_sw128(pa + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32),
+                   desc_mn_sw128(va + kk * 2048, CHUNK_BYTES), idO, (n > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&v_empty[s]);
+        mma_commit(pv_done);
+        return true;
+      };
+      int n = 0;
+      if (ok) {
+        for (; n < ntl; ++n) {
+          const int s = n & 1, b = n & 1;
+          if (!mbar_wait(&k_full[s], (n >> 1) & 1, abort_flag, p.err, 14)) { ok = false; break; }
+          if (!mbar_wait(&s_empty[b], ((n >> 1) & 1) ^ 1, abort_flag, p.err, 15)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t ka = smem_addr(smem + OFF_K + s * TILE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < FB / 16; ++kk)
+            mma_bf16(tmem + b * FB, desc_k_sw128(qa + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32),
+                     desc_k_sw128(ka + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32), idS, kk > 0 ? 1u : 0u);
+          mma_commit(&s_full[b]);
+          mma_commit(&k_empty[s]);
+          if (n > 0 && !issue_pv(n - 1)) { ok = false; break; }
+        }
+        if (ok && n > 0) issue_pv(n - 1);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const int gi = g0 + row;  // global query position of this thread's row
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    uint8_t* prow = smem + OFF_P + row * 128;
+    const int sw = row & 7;
+    float m_ref = -INFINITY, l = 0.f;
+    int n = 0;
+    bool ok = true;
+    for (; n < ntl; ++n) {
+      const int kt = tlist[n] & (TILE_FULL - 1);
+      const bool full_tile = (tlist[n] & TILE_FULL) != 0;
+      const int b = n & 1;
+      if (!mbar_wait_warp(&s_full[b], (n >> 1) & 1, abort_flag, p.err, 16)) { ok = false; break; }
+      tc_fence_after();
+      float sv[FB];
+      {
+        uint32_t r[FB / 32][32];
+#pragma unroll
+        for (int c = 0; c < FB / 32; ++c) tmem_ld32(tmem + lane_base + b * FB + c * 32, r[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < FB / 32; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(r[c][e]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[b]);
+      // mask + scale, running max (fully visible tiles skip the mask)
+      const int k0 = kt * FB;
+      float mx = -INFINITY;
+      if (full_tile) {
+#pragma unroll
+        for (int c = 0; c < FB; ++c) {
+          sv[c] *= p.scale_log2;
+          mx = fmaxf(mx, sv[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < FB; c += 4) {
+          int4 ke = make_int4(0, 0, 0, 0);
+          if (k0 + c + 3 < p.Tk) {
+            ke = __ldg(reinterpret_cast<const int4*>(p.kend + k0 + c));
+          } else {
+            ke.x = k0 + c + 0 < p.Tk ? __ldg(p.kend + k0 + c + 0) : 0;
+            ke.y = k0 + c + 1 < p.Tk ? __ldg(p.kend + k0 + c + 1) : 0;
+            ke.z = k0 + c + 2 < p.Tk ? __ldg(p.kend + k0 + c + 2) : 0;
+            ke.w = k0 + c + 3 < p.Tk ? __ldg(p.kend + k0 + c + 3) : 0;
+          }
+          const int kv[4] = {ke.x, ke.y, ke.z, ke.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = k0 + c + e;
+            const bool vis = (j <= gi) && (gi < kv[e]);
+            const float x = vis ? sv[c + e] * p.scale_log2 : -INFINITY;
+            sv[c + e] = x;
+            mx = fmaxf(mx, x);
+          }
+        }
+      }
+      // P buffer and O are free once P V of the previous tile completed
+      if (n > 0) {
+        if (!mbar_wait_warp(pv_done, (n - 1) & 1, abort_flag, p.err, 17)) { ok = false; break; }
+        tc_fence_after();
+      }
+      // lazy rescale: a row moves its reference max only when the tile max
+      // exceeds it by more than 2^8.  tcgen05.ld/st are warp-collective, so
+      // the O rows are rescaled by the whole warp when any of its rows needs
+      // it (alpha = 1 for the others).
+      const bool move = mx > m_ref + kRescaleThreshold || (m_ref == -INFINITY && mx > -INFINITY);
+      const bool scale_o = move && n > 0 && m_ref > -INFINITY;
+      if (__any_sync(0xffffffffu, scale_o)) {
+        const float alpha = scale_o ? exp2f(m_ref - mx) : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < FB / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem_o + lane_base + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+          tmem_st32(tmem_o + lane_base + c * 32, r);
+        }
+        tmem_wait_st();
+        l *= alpha;
+      }
+      if (move) m_ref = mx;
+      // P = exp2(s - m_ref) as bf16 into the swizzled K-major tile
+      float rs = 0.f;
+#pragma unroll
+      for (int u = 0; u < FB / 8; ++u) {
+        float e8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float x = sv[u * 8 + e];
+          e8[e] = (x == -INFINITY) ? 0.f : exp2f(x - m_ref);
+          rs += e8[e];
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(e8[0], e8[1]);
+        pk.y = pack_bf16x2(e8[2], e8[3]);
+        pk.z = pack_bf16x2(e8[4], e8[5]);
+        pk.w = pack_bf16x2(e8[6], e8[7]);
+        const int chunk = u >> 3, unit = u & 7;
+        *reinterpret_cast<uint4*>(prow + chunk * CHUNK_BYTES + ((unit ^ sw) << 4)) = pk;
+      }
+      l += rs;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // epilogue: O / l and the LSE
+    const int qrow = q0 + row;
+    if (ok && n > 0) {
+      if (mbar_wait_warp(pv_done, (n - 1) & 1, abort_flag, p.err, 18)) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __nv_bfloat16* dst = p.o + (int64_t)qrow * p.ldo + (int64_t)h * FB;
+#pragma unroll 1
+        for (int c = 0; c < FB / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem_o + lane_base + c * 32, r);
+          tmem_wait_ld();
+          if (qrow < p.Tq) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 o;
+              o.x = pack_bf16x2(__uint_as_float(r[j + 0]) * inv, __uint_as_float(r[j + 1]) * inv);
+              o.y = pack_bf16x2(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+              o.z = pack_bf16x2(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
+              o.w = pack_bf16x2(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
+              *reinterpret_cast<uint4*>(dst + c * 32 + j) = o;
+            }
+          }
+        }
+        if (qrow < p.Tq)
+          p.lse[(int64_t)h * p.Tq + qrow] = l > 0.f ? (m_ref + log2f(l)) / kLog2eF : -INFINITY;
+      }
+    } else if (ok && qrow < p.Tq) {  // no visible key
+      __nv_bfloat16* dst = p.o + (int64_t)qrow * p.ldo + (int64_t)h * FB;
+      for (int j = 0; j < FB; j += 8) *reinterpret_cast<uint4*>(dst + j) = make_uint4(0, 0, 0, 0);
+      p.lse[(int64_t)h * p.Tq + qrow] = -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// q [Tq, Hq, 128] (rows at global positions q_off + row), k/v [Tk, Hkv, 128];
+// heads packed, rows 16-byte aligned.  Returns {o [Tq, Hq, 128] bf16, lse [Hq, Tq] fp32}.
+std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kend,
+                                       torch::Tensor tile_kmax, torch::Tensor tile_kmin, double scale, int64_t q_off) {
+  const int64_t Tq = q.size(0), Hq = q.size(1), D = q.size(2), Tk = k.size(0), Hkv = k.size(1);
+  TORCH_CHECK(D == 128, "attention kernel supports head_dim 128");
+  TORCH_CHECK(Hq % Hkv == 0, "GQA: q heads must be a multiple of kv heads");
+  TORCH_CHECK(q_off >= 0 && q_off + Tq <= Tk, "query range must lie inside the key range");
+  for (auto* t : {&q, &k, &v}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 3, "bf16 CUDA [T, H, 128]");
+    TORCH_CHECK(t->stride(2) == 1 && t->stride(1) == 128, "heads must be packed");
+    TORCH_CHECK(t->stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(t->data_ptr()) % 16) == 0,
+                "rows must be 16-byte aligned");
+  }
+  TORCH_CHECK(v.size(0) == Tk && v.size(1) == Hkv, "v shape");
+  TORCH_CHECK(kend.scalar_type() == at::kInt && kend.numel() == Tk && kend.is_contiguous());
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(kend.data_ptr()) % 16) == 0, "kend must be 16-byte aligned");
+  TORCH_CHECK(tile_kmax.scalar_type() == at::kInt && tile_kmax.numel() >= (Tk + 63) / 64);
+  TORCH_CHECK(tile_kmin.scalar_type() == at::kInt && tile_kmin.numel() >= (Tk + 63) / 64);
+  TORCH_CHECK((Tk + FB - 1) / FB <= MAX_KT, "attention rows longer than ", MAX_KT * FB, " keys");
+  auto o = torch::empty({Tq, Hq, D}, q.options());
+  auto lse = torch::empty({Hq, Tq}, q.options().dtype(at::kFloat));
+  if (Tq == 0) return {o, lse};
+  // 2-D views [rows, heads*128] for the tensor maps
+  auto q2 = q.as_strided({Tq, Hq * D}, {q.stride(0), 1});
+  auto k2 = k.as_strided({Tk, Hkv * D}, {k.stride(0), 1});
+  auto v2 = v.as_strided({Tk, Hkv * D}, {v.stride(0), 1});
+  const CUtensorMap mq = make_tmap_bf16(q2, FB), mk = make_tmap_bf16(k2, FB), mv = make_tmap_bf16(v2, FB);
+  int dev = 0;
+  ART_CUDA_CHECK(cudaGetDevice(&dev));
+  FaArgs a;
+  a.kend = kend.data_ptr<int>();
+  a.tile_kmax = tile_kmax.data_ptr<int>();
+  a.tile_kmin = tile_kmin.data_ptr<int>();
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.ldo = o.stride(0);
+  a.lse = lse.data_ptr<float>();
+  a.Tq = (int)Tq;
+  a.Tk = (int)Tk;
+  a.q_off = (int)q_off;
+  a.Hq = (int)Hq;
+  a.Hkv = (int)Hkv;
+  a.scale_log2 = (float)(scale * kLog2eF);
+  a.err = tc_error_ptr(dev);
+  static bool attr = false;
+  if (!attr) {
+    ART_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM));
+    attr = true;
+  }
+  dim3 grid((unsigned)((Tq + FB - 1) / FB), (unsigned)Hq);
+  attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, at::cuda::getCurrentCUDAStream()>>>(mq, mk, mv, a);
+  ART_CUDA_CHECK(cudaGetLastError());
+  return {o, lse};
+}
+
+
+// ============================================================================
+// Backward on the tensor cores.
+//
+// CTA = one work unit (128-key block kb, local 128-query tiles [t_lo, t_hi))
+// x one kv head; it loops over the G q heads of that kv head and the query
+// tiles, with K and V of the block resident in shared memory:
+//   S^T  = K Q^T          (TMEM cols   0..127, lanes = keys)
+//   dP^T = V dO^T         (TMEM cols 128..255)
+//   softmax warps: P^T = exp2(S^T*scale*log2e - lse*log2e) under the mask,
+//                  dS^T = P^T (dP^T - delta)  -> bf16 tiles in shared memory
+//   dV  += P^T dO         (TMEM cols 256..383, dO as an MN-major B operand)
+//   dK  += dS^T Q         (TMEM cols 384..511)
+//   dQ   = dS K           (TMEM cols 0..127, dS^T read as an MN-major A
+//                          operand, K as an MN-major B operand; lanes = queries)
+// then dQ*scale is added to global memory (red.global.add.v4.f32) and, after
+// the last tile, dK*scale and dV are added for the block (several units may
+// share a key block).  delta = rowsum(dO * O) comes from attn_bwd_delta.
+// ============================================================================
+
+namespace {
+
+constexpr int B_OFF_K = 0;
+constexpr int B_OFF_V = TILE_BYTES;
+constexpr int B_OFF_Q = 2 * TILE_BYTES;
+constexpr int B_OFF_DO = 3 * TILE_BYTES;
+constexpr int B_OFF_P = 4 * TILE_BYTES;
+constexpr int B_OFF_DS = 5 * TILE_BYTES;
+constexpr int B_OFF_BAR = 6 * TILE_BYTES;
+constexpr int FB_SMEM = B_OFF_BAR + 256 + 1024;
+
+struct FbArgs {
+  const int* kend;
+  const int* units;  // [n, 3]
+  const float* lse;    // [Hq, Tq] natural log
+  const float* delta;  // [Hq, Tq]
+  float* dq;           // [Tq, Hq, 128]
+  float* dk;           // [Tk, Hkv, 128]
+  float* dv;
+  int Tq, Tk, q_off, Hq, Hkv;
+  float scale, scale_log2;
+  int* err;
+};
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+}  // namespace
+
+__global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ o,
+                                      int64_t ldo, float* __restrict__ delta, int Tq, int Hq) {
+  const int w = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (w >= Tq * Hq) return;
+  const int t = w / Hq, h = w % Hq;
+  const uint2 a = *reinterpret_cast<const uint2*>(dout + ((int64_t)t * Hq + h) * FB + lane * 4);
+  const uint2 b = *reinterpret_cast<const uint2*>(o + (int64_t)t * ldo + (int64_t)h * FB + lane * 4);
+  const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&a);
+  const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(&b);
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) s += bf2f(x[e]) * bf2f(y[e]);
+  s = warp_sum(s);
+  if (lane == 0) delta[(int64_t)h * Tq + t] = s;
+}
+
+__global__ void __launch_bounds__(FA_THREADS, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                       const FbArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + B_OFF_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* qdo_empty = bars + 2;
+  uint64_t* sdp_full = bars + 3;
+  uint64_t* ds_full = bars + 4;
+  uint64_t* dq_full = bars + 5;
+  uint64_t* dq_free = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kb = p.units[blockIdx.x * 3 + 0];
+  const int t_lo = p.units[blockIdx.x * 3 + 1], t_hi = p.units[blockIdx.x * 3 + 2];
+  const int hk = blockIdx.y;
+  const int G = p.Hq / p.Hkv;
+  const int ntiles = t_hi - t_lo;
+  const int iters = G * ntiles;  // iteration i: head hk*G + i / ntiles, tile t_lo + i % ntiles
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qdo_full, 1);
+    mbar_init(qdo_empty, 1);
+    mbar_init(sdp_full, 1);
+    mbar_init(ds_full, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      prefetch_tmap(&tmDO);
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_2d(smem + B_OFF_K, &tmK, kv_full, hk * FB, kb * FB);
+      tma_load_2d(smem + B_OFF_K + CHUNK_BYTES, &tmK, kv_full, hk * FB + 64, kb * FB);
+      tma_load_2d(smem + B_OFF_V, &tmV, kv_full, hk * FB, kb * FB);
+      tma_load_2d(smem + B_OFF_V + CHUNK_BYTES, &tmV, kv_full, hk * FB + 64, kb * FB);
+      for (int i = 0; i < iters; ++i) {
+        const int h = hk * G + i / ntiles, t = t_lo + i % ntiles;
+        if (!mbar_wait(qdo_empty, (i & 1) ^ 1, abort_flag, p.err, 21)) break;
+        mbar_arrive_expect_tx(qdo_full, 2 * TILE_BYTES);
+        tma_load_2d(smem + B_OFF_Q, &tmQ, qdo_full, h * FB, t * FB);
+        tma_load_2d(smem + B_OFF_Q + CHUNK_BYTES, &tmQ, qdo_full, h * FB + 64, t * FB);
+        tma_load_2d(smem + B_OFF_DO, &tmDO, qdo_full, h * FB, t * FB);
+        tma_load_2d(smem + B_OFF_DO + CHUNK_BYTES, &tmDO, qdo_full, h * FB + 64, t * FB);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idKK = idesc_bf16(FB, FB);                  // both K-major
+      constexpr uint32_t idKM = idesc_bf16_bmn(FB, FB);              // B MN-major
+      constexpr uint32_t idMM = idesc_bf16_bmn(FB, FB) | (1u << 15);  // A and B MN-major
+      const uint32_t ka = smem_addr(smem + B_OFF_K), va = smem_addr(smem + B_OFF_V);
+      const uint32_t qa = smem_addr(smem + B_OFF_Q), doa = smem_addr(smem + B_OFF_DO);
+      const uint32_t pa = smem_addr(smem + B_OFF_P), dsa = smem_addr(smem + B_OFF_DS);
+      if (mbar_wait(kv_full, 0, abort_flag, p.err, 22)) {
+        for (int i = 0; i < iters; ++i) {
+          if (!mbar_wait(qdo_full, i & 1, abort_flag, p.err, 23)) break;
+          if (!mbar_wait(dq_free, (i & 1) ^ 1, abort_flag, p.err, 24)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < FB / 16; ++kk) {
+            const uint32_t ko = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
+            mma_bf16(tmem + 0, desc_k_sw128(ka + ko), desc_k_sw128(qa + ko), idKK, kk > 0 ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < FB / 16; ++kk) {
+            const uint32_t ko = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
+            mma_bf16(tmem + 128, desc_k_sw128(va + ko), desc_k_sw128(doa + ko), idKK, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(sdp_full);
+          if (!mbar_wait(ds_full, i & 1, abort_flag, p.err, 25)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < FB / 16; ++kk) {
+            const uint32_t ko = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
+            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+            mma_bf16(tmem + 256, desc_k_sw128(pa + ko), desc_mn_sw128(doa + kk * 2048, CHUNK_BYTES), idKM, acc);
+            mma_bf16(tmem + 384, desc_k_sw128(dsa + ko), desc_mn_sw128(qa + kk * 2048, CHUNK_BYTES), idKM, acc);
+          }
+          mma_commit(qdo_empty);
+#pragma unroll
+          for (int kk = 0; kk < FB / 16; ++kk)
+            mma_bf16(tmem + 0, desc_mn_sw128(dsa + kk * 2048, CHUNK_BYTES),
+                     desc_mn_sw128(ka + kk * 2048, CHUNK_BYTES), idMM, kk > 0 ? 1u : 0u);
+          mma_commit(dq_full);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogues
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;  // TMEM lane: key row (S^T, dP^T, dK, dV) or query row (dQ)
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const int j = kb * FB + row;  // this thread's key
+    const int kend_j = j < p.Tk ? __ldg(p.kend + j) : 0;
+    const int sw = row & 7;
+    bool ok = true;
+    for (int i = 0; i < iters && ok; ++i) {
+      const int h = hk * G + i / ntiles, t = t_lo + i % ntiles;
+      if (!mbar_wait_warp(sdp_full, i & 1, abort_flag, p.err, 26)) { ok = false; break; }
+      tc_fence_after();
+      const float* lse_h = p.lse + (int64_t)h * p.Tq;
+      const float* del_h = p.delta + (int64_t)h * p.Tq;
+#pragma unroll 1
+      for (int c = 0; c < FB / 32; ++c) {
+        uint32_t rs[32], rd[32];
+        tmem_ld32(tmem + lane_base + c * 32, rs);
+        tmem_ld32(tmem + lane_base + 128 + c * 32, rd);
+        // lane e fetches the LSE / delta of query c*32+e; shared by shuffles
+        const int ql_mine = t * FB + c * 32 + lane;
+        const float lse_mine = ql_mine < p.Tq ? lse_h[ql_mine] * kLog2eF : INFINITY;
+        const float del_mine = ql_mine < p.Tq ? del_h[ql_mine] : 0.f;
+        tmem_wait_ld();
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], dv2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int ql = t * FB + c * 32 + e + u;
+            const int qg = p.q_off + ql;
+            const float l2 = __shfl_sync(0xffffffffu, lse_mine, e + u);
+            const float de = __shfl_sync(0xffffffffu, del_mine, e + u);
+            const bool vis = (j <= qg) && (qg < kend_j) && (ql < p.Tq);
+            const float pr = vis ? exp2f(__uint_as_float(rs[e + u]) * p.scale_log2 - l2) : 0.f;
+            pv[u] = pr;
+            dv2[u] = pr * (__uint_as_float(rd[e + u]) - de);
+          }
+          pp[e >> 1] = pack_bf16x2(pv[0], pv[1]);
+          dd[e >> 1] = pack_bf16x2(dv2[0], dv2[1]);
+        }
+        // 32 queries = 4 units of 16 bytes of this key's row
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const int u = c * 4 + w;  // unit along the 128-query row
+          const uint32_t off = (u >> 3) * CHUNK_BYTES + row * 128 + (((u & 7) ^ sw) << 4);
+          *reinterpret_cast<uint4*>(smem + B_OFF_P + off) = make_uint4(pp[4 * w], pp[4 * w + 1], pp[4 * w + 2], pp[4 * w + 3]);
+          *reinterpret_cast<uint4*>(smem + B_OFF_DS + off) = make_uint4(dd[4 * w], dd[4 * w + 1], dd[4 * w + 2], dd[4 * w + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+      // dQ tile: lanes are queries now
+      if (!mbar_wait_warp(dq_full, i & 1, abort_flag, p.err, 27)) { ok = false; break; }
+      tc_fence_after();
+      const int ql = t * FB + row;
+#pragma unroll 1
+      for (int c = 0; c < FB / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + c * 32, r);
+        tmem_wait_ld();
+        if (ql < p.Tq) {
+          float* dst = p.dq + ((int64_t)ql * p.Hq + h) * FB + c * 32;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            red_add_v4(dst + e, __uint_as_float(r[e]) * p.scale, __uint_as_float(r[e + 1]) * p.scale,
+                       __uint_as_float(r[e + 2]) * p.scale, __uint_as_float(r[e + 3]) * p.scale);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+    // dK, dV of the block (all MMAs completed: the last dq_full covered them).
+    // Every lane runs the warp-collective TMEM loads; rows past Tk skip the stores.
+    if (ok && iters > 0) {
+      float* dkr = p.dk + ((int64_t)j * p.Hkv + hk) * FB;
+      float* dvr = p.dv + ((int64_t)j * p.Hkv + hk) * FB;
+#pragma unroll 1
+      for (int c = 0; c < FB / 32; ++c) {
+        uint32_t a[32], b[32];
+        tmem_ld32(tmem + lane_base + 384 + c * 32, a);
+        tmem_ld32(tmem + lane_base + 256 + c * 32, b);
+        tmem_wait_ld();
+        if (j >= p.Tk) continue;
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          red_add_v4(dkr + c * 32 + e, __uint_as_float(a[e]) * p.scale, __uint_as_float(a[e + 1]) * p.scale,
+                     __uint_as_float(a[e + 2]) * p.scale, __uint_as_float(a[e + 3]) * p.scale);
+          red_add_v4(dvr + c * 32 + e, __uint_as_float(b[e]), __uint_as_float(b[e + 1]), __uint_as_float(b[e + 2]),
+                     __uint_as_float(b[e + 3]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Backward.  units [n, 3] int32 = (128-key block, first and end local
+// 128-query tile).  Returns {dq [Tq,Hq,128], dk [Tk,Hkv,128], dv} fp32.
+std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                       torch::Tensor out, torch::Tensor lse, torch::Tensor kend, torch::Tensor units,
+                                       double scale, int64_t q_off) {
+  const int64_t Tq = q.size(0), Hq = q.size(1), D = q.size(2), Tk = k.size(0), Hkv = k.size(1);
+  TORCH_CHECK(D == 128 && Hq % Hkv == 0 && q_off >= 0 && q_off + Tq <= Tk);
+  for (auto* t : {&q, &k, &v, &out}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 3, "bf16 CUDA [T, H, 128]");
+    TORCH_CHECK(t->stride(2) == 1 && t->stride(1) == 128, "heads must be packed");
+    TORCH_CHECK(t->stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(t->data_ptr()) % 16) == 0,
+                "rows must be 16-byte aligned");
+  }
+  TORCH_CHECK(dout.is_contiguous() && dout.sizes() == q.sizes() && dout.scalar_type() == at::kBFloat16);
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() == Hq * Tq);
+  TORCH_CHECK(kend.scalar_type() == at::kInt && kend.numel() == Tk && kend.is_contiguous());
+  TORCH_CHECK(units.scalar_type() == at::kInt && units.is_contiguous() && units.dim() == 2 && units.size(1) == 3);
+  auto f32 = q.options().dtype(at::kFloat);
+  auto dq = torch::zeros({Tq, Hq, D}, f32);
+  auto dk = torch::zeros({Tk, Hkv, D}, f32);
+  auto dv = torch::zeros({Tk, Hkv, D}, f32);
+  const int64_t n = units.size(0);
+  if (Tq == 0 || n == 0) return {dq, dk, dv};
+  auto delta = torch::empty({Hq, Tq}, f32);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  attn_bwd_delta_kernel<<<(unsigned)((Tq * Hq + 3) / 4), 128, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
+      out.stride(0), delta.data_ptr<float>(), (int)Tq, (int)Hq);
+  ART_CUDA_CHECK(cudaGetLastError());
+  auto q2 = q.as_strided({Tq, Hq * D}, {q.stride(0), 1});
+  auto do2 = dout.view({Tq, Hq * D});
+  auto k2 = k.as_strided({Tk, Hkv * D}, {k.stride(0), 1});
+  auto v2 = v.as_strided({Tk, Hkv * D}, {v.stride(0), 1});
+  const CUtensorMap mq = make_tmap_bf16(q2, FB), mk = make_tmap_bf16(k2, FB), mv = make_tmap_bf16(v2, FB),
+                    mdo = make_tmap_bf16(do2, FB);
+  int dev = 0;
+  ART_CUDA_CHECK(cudaGetDevice(&dev));
+  FbArgs a;
+  a.kend = kend.data_ptr<int>();
+  a.units = units.data_ptr<int>();
+  a.lse = lse.data_ptr<float>();
+  a.delta = delta.data_ptr<float>();
+  a.dq = dq.data_ptr<float>();
+  a.dk = dk.data_ptr<float>();
+  a.dv = dv.data_ptr<float>();
+  a.Tq = (int)Tq;
+  a.Tk = (int)Tk;
+  a.q_off = (int)q_off;
+  a.Hq = (int)Hq;
+  a.Hkv = (int)Hkv;
+  a.scale = (float)scale;
+  a.scale_log2 = (float)(scale * kLog2eF);
+  a.err = tc_error_ptr(dev);
+  static bool attr = false;
+  if (!attr) {
+    ART_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM));
+    attr = true;
+  }
+  attn_bwd_tc_kernel<<<dim3((unsigned)n, (unsigned)Hkv), FA_THREADS, FB_SMEM, stream>>>(mq, mk, mv, mdo, a);
+  ART_CUDA_CHECK(cudaGetLastError());
+  return {dq, dk, dv};
+}
+
+}  // namespace art

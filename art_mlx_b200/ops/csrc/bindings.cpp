@@ -27,6 +27,17 @@ void adamw_step(torch::Tensor p, torch::Tensor p16, torch::Tensor g, torch::Tens
                 torch::Tensor v, torch::Tensor hp, torch::Tensor norm_sq, torch::Tensor norm_out);
 std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                     torch::Tensor kend, torch::Tensor tile_kmax, double scale, int64_t q_off);
+std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kend,
+                                       torch::Tensor tile_kmax, torch::Tensor tile_kmin, double scale, int64_t q_off);
+std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                       torch::Tensor out, torch::Tensor lse, torch::Tensor kend, torch::Tensor units,
+                                       double scale, int64_t q_off);
+torch::Tensor gemm_tc_grouped(torch::Tensor x, torch::Tensor w, std::vector<int64_t> offs, int64_t N,
+                              c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, bool w_transposed);
+torch::Tensor decode_attn(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
+                          double scale);
+void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor slot, torch::Tensor pos, torch::Tensor k_cache,
+               torch::Tensor v_cache);
 std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k,
                                     torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                                     torch::Tensor kend, torch::Tensor units, double scale, int64_t q_off);
@@ -77,6 +88,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &art::adamw_step);
   m.def("attn_fwd", &art::attn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("kend"), py::arg("tile_kmax"),
         py::arg("scale"), py::arg("q_off") = 0);
+  m.def("attn_fwd_tc", &art::attn_fwd_tc, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("kend"),
+        py::arg("tile_kmax"), py::arg("tile_kmin"), py::arg("scale"), py::arg("q_off") = 0);
+  m.def("attn_bwd_tc", &art::attn_bwd_tc, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("out"), py::arg("lse"), py::arg("kend"), py::arg("units"), py::arg("scale"), py::arg("q_off") = 0);
+  m.def("gemm_tc_grouped", &art::gemm_tc_grouped, py::arg("x"), py::arg("w"), py::arg("offs"), py::arg("N"),
+        py::arg("a2") = py::none(), py::arg("b2") = py::none(), py::arg("w_transposed") = false);
+  m.def("decode_attn", &art::decode_attn);
+  m.def("kv_append", &art::kv_append);
   m.def("attn_bwd", &art::attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
         py::arg("lse"), py::arg("kend"), py::arg("units"), py::arg("scale"), py::arg("q_off") = 0);
   m.def("gemm_tc", &art::gemm_tc);

@@ -54,6 +54,16 @@ struct GemmArgs {
   int c_dst_rows;
   int c_slot;
   long long c_bases[MAX_SRC];
+  // grouped mode (MoE experts): tile list of (m0, n0, first B row, row end);
+  // B and B2 are the experts' matrices stacked along rows, A rows of tile t
+  // are valid up to row end (the next expert's rows are computed, not stored)
+  const int4* tiles;
+  int num_tiles;
+  // B of the main product given transposed, as [K, N] row-major (MN-major
+  // operand: four 64-column TMA boxes per k-block, read with an MN-major
+  // descriptor); the tile's B row is then the first K row of its matrix
+  int b_mn;
+  int kmain;  // K of the main product (transposed-B tiles: B2 row = (brow / K) * N + n0)
 };
 
 struct TmapSet {
@@ -76,7 +86,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (p.M + GBM - 1) / GBM;
   const int num_n = (p.N + GBN - 1) / GBN;
-  const int num_tiles = num_m * num_n;
+  const int num_tiles = p.tiles ? p.num_tiles : num_m * num_n;
+  // tile -> (m0, n0, row of B, end of valid A rows)
+  auto coords = [&](int tile) -> int4 {
+    if (p.tiles) return __ldg(p.tiles + tile);
+    const int m0 = (tile % num_m) * GBM, n0 = (tile / num_m) * GBN;
+    return make_int4(m0, n0, n0, p.M);
+  };
   const int nk = p.nk1 + p.nk2;
 
   if (threadIdx.x == 0) {
@@ -108,7 +124,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       int it = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int m0 = (tile % num_m) * GBM, n0 = (tile / num_m) * GBN;
+        const int4 tc4 = coords(tile);
+        const int m0 = tc4.x, n0 = tc4.y, brow = tc4.z;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % GSTAGES;
           const uint32_t ph = (it / GSTAGES) & 1;
@@ -123,11 +140,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             } else {
               tma_load_2d(a, &tmA.m[0], &full[s], kb * GBK, m0);
             }
-            tma_load_2d(b, &tmB, &full[s], kb * GBK, n0);
+            if (p.b_mn) {
+#pragma unroll
+              for (int j = 0; j < GBN / 64; ++j)
+                tma_load_2d(b + j * (GBK * 128), &tmB, &full[s], n0 + 64 * j, brow + kb * GBK);
+            } else {
+              tma_load_2d(b, &tmB, &full[s], kb * GBK, brow);
+            }
           } else {
             const int k2 = (kb - p.nk1) * GBK;
+            const int b2row = p.b_mn ? (brow / p.kmain) * p.N + n0 : brow;
             tma_load_2d(a, &tmA2, &full[s], k2, m0);
-            tma_load_2d(b, &tmB2, &full[s], k2, n0);
+            tma_load_2d(b, &tmB2, &full[s], k2, b2row);
           }
         }
       }
@@ -158,9 +182,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const int rem = p.K2 - (kb - p.nk1) * GBK;
             ksteps = min(ksteps, (rem + 15) / 16);
           }
+          const bool bmn = p.b_mn && kb < p.nk1;
           for (int kk = 0; kk < ksteps; ++kk)
-            mma_bf16(d, desc_k_sw128(a_addr + kk * 32), desc_k_sw128(b_addr + kk * 32), idesc,
-                     (kb > 0 || kk > 0) ? 1u : 0u);
+            mma_bf16(d, desc_k_sw128(a_addr + kk * 32),
+                     bmn ? desc_mn_sw128(b_addr + kk * 2048, GBK * 128) : desc_k_sw128(b_addr + kk * 32),
+                     bmn ? (idesc | (1u << 16)) : idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&empty[s]);
         }
         if (!ok) break;
@@ -174,9 +200,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int buf = t & 1;
       const uint32_t use = (uint32_t)(t >> 1);
-      if (!mbar_wait(&acc_full[buf], use & 1, abort_flag, p.err, 4)) break;
+      if (!mbar_wait_warp(&acc_full[buf], use & 1, abort_flag, p.err, 4)) break;
       tc_fence_after();
-      const int m0 = (tile % num_m) * GBM, n0 = (tile / num_m) * GBN;
+      const int4 tc4 = coords(tile);
+      const int m0 = tc4.x, n0 = tc4.y, row_end = tc4.w;
       const int row = m0 + q * 32 + lane;
 #pragma unroll 1
       for (int c = 0; c < GBN / 32; ++c) {
@@ -184,7 +211,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * GBN + c * 32, r);
         tmem_wait_ld();
         const int col0 = n0 + c * 32;
-        if (row < p.M && col0 < p.N) {
+        if (row < row_end && col0 < p.N) {
           __nv_bfloat16* dst;
           if (p.c_dst_rows) {
             const int rr = row / p.c_dst_rows;
@@ -268,12 +295,16 @@ static CUtensorMap make_tmap_2d(const torch::Tensor& t, int box_rows) {
   return m;
 }
 
+CUtensorMap make_tmap_bf16(const at::Tensor& t, int box_rows) { return make_tmap_2d(t, box_rows); }
+
 static torch::Tensor& error_word(int dev) {
   static std::vector<torch::Tensor> words(64);
   if (!words[dev].defined())
     words[dev] = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt).device(torch::kCUDA, dev));
   return words[dev];
 }
+
+int* tc_error_ptr(int dev) { return error_word(dev).data_ptr<int>(); }
 
 // Returns and clears the device error word of the tensor-core kernels
 // (0 = ok; 1..4 = which pipeline wait timed out).
@@ -291,7 +322,7 @@ static void launch_gemm(const TmapSet& ta, const CUtensorMap& tb, const CUtensor
   p.err = error_word(dev).data_ptr<int>();
   static int num_sms = 0;
   if (!num_sms) ART_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev));
-  const int tiles = ((p.M + GBM - 1) / GBM) * ((p.N + GBN - 1) / GBN);
+  const int tiles = p.tiles ? p.num_tiles : ((p.M + GBM - 1) / GBM) * ((p.N + GBN - 1) / GBN);
   const int grid = tiles < num_sms ? tiles : num_sms;
   static bool attr = false;
   if (!attr) {
@@ -316,6 +347,10 @@ static void fill_common(GemmArgs& p, int64_t M, int64_t K, int64_t N, const c10:
   p.c_dst_rows = 0;
   p.c_slot = 0;
   for (int i = 0; i < MAX_SRC; ++i) p.c_bases[i] = 0;
+  p.tiles = nullptr;
+  p.num_tiles = 0;
+  p.b_mn = 0;
+  p.kmain = (int)K;
 }
 
 // out = a @ b^T (+ a2 @ b2^T) (+ bias) (+ out if accumulate)
@@ -347,6 +382,58 @@ torch::Tensor gemm_tc(torch::Tensor a, torch::Tensor b, c10::optional<torch::Ten
   p.C = reinterpret_cast<__nv_bfloat16*>(c.data_ptr());
   p.ldc = c.stride(0);
   launch_gemm(ta, tb, ta2, tb2, p, a.get_device());
+  return c;
+}
+
+// Grouped GEMM for MoE experts: rows [offs[e], offs[e+1]) of x belong to
+// expert e;  out[rows_e] = x[rows_e] W_e^T (+ a2[rows_e] B2_e^T), W = w viewed
+// as [E*N, K] (expert-major), or, with w_transposed, w = the stacked W_e^T as
+// [E*K, N]; B2 = b2 as [E*N, K2].  offs are host ints (the routing plan is
+// built on the host).  N must be a multiple of 32 (of 64 when transposed).
+torch::Tensor gemm_tc_grouped(torch::Tensor x, torch::Tensor w, std::vector<int64_t> offs, int64_t N,
+                              c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2,
+                              bool w_transposed) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.dim() == 2 && w.dim() == 2);
+  const int64_t M = x.size(0), K = x.size(1);
+  const int64_t E = (int64_t)offs.size() - 1;
+  TORCH_CHECK(E >= 1 && offs[0] == 0 && offs[E] == M, "offsets must span the rows");
+  if (w_transposed) {
+    TORCH_CHECK(w.size(0) == E * K && w.size(1) == N && N % 64 == 0, "w must be [E*K, N]");
+  } else {
+    TORCH_CHECK(w.size(0) == E * N && w.size(1) == K && N % 32 == 0, "w must be [E*N, K]");
+  }
+  if (a2.has_value())
+    TORCH_CHECK(b2.has_value() && a2->size(0) == M && b2->size(0) == E * N && a2->size(1) == b2->size(1));
+  auto c = torch::empty({M, N}, x.options());
+  if (M == 0) return c;
+  std::vector<int32_t> tab;
+  for (int64_t e = 0; e < E; ++e) {
+    TORCH_CHECK(offs[e + 1] >= offs[e], "offsets must be non-decreasing");
+    for (int64_t n0 = 0; n0 < N; n0 += GBN)
+      for (int64_t m0 = offs[e]; m0 < offs[e + 1]; m0 += GBM) {
+        tab.push_back((int32_t)m0);
+        tab.push_back((int32_t)n0);
+        tab.push_back((int32_t)(w_transposed ? e * K : e * N + n0));
+        tab.push_back((int32_t)offs[e + 1]);
+      }
+  }
+  const int ntiles = (int)(tab.size() / 4);
+  if (ntiles == 0) return c;
+  auto tiles = torch::from_blob(tab.data(), {(int64_t)tab.size()}, torch::kInt32).pin_memory().to(x.device(), true);
+  TmapSet ta;
+  ta.m[0] = make_tmap_2d(x, GBM);
+  for (int q = 1; q < MAX_SRC; ++q) ta.m[q] = ta.m[0];
+  CUtensorMap tb = make_tmap_2d(w, w_transposed ? GBK : GBN);
+  CUtensorMap ta2 = a2.has_value() ? make_tmap_2d(*a2, GBM) : ta.m[0];
+  CUtensorMap tb2 = a2.has_value() ? make_tmap_2d(*b2, GBN) : tb;
+  GemmArgs p;
+  fill_common(p, M, K, N, a2, c10::nullopt, false);
+  p.C = reinterpret_cast<__nv_bfloat16*>(c.data_ptr());
+  p.ldc = c.stride(0);
+  p.b_mn = w_transposed ? 1 : 0;
+  p.tiles = reinterpret_cast<const int4*>(tiles.data_ptr<int>());
+  p.num_tiles = ntiles;
+  launch_gemm(ta, tb, ta2, tb2, p, x.get_device());
   return c;
 }
 

@@ -63,6 +63,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait by a whole warp, with a warp-uniform result: warps that go on
+// to warp-collective instructions (tcgen05.ld/st, shuffles) must not split
+// on the error path.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               int* err, int code) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, err, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
@@ -115,6 +124,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 32 lanes x 32 columns store (thread l writes row l).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Generic-proxy shared-memory writes -> visible to the async proxy (tensor core).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle (rows of 64 bf16,
 // 8-row atoms of 1024 bytes): start>>4 | LBO(16B)>>4 << 16 | SBO(1024B)>>4 << 32
 // | version 1 << 46 | layout SWIZZLE_128B (2) << 61.
@@ -123,10 +150,29 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t saddr) {
          ((uint64_t)2 << 61);
 }
 
+// Shared-memory matrix descriptor, MN-major, 128-byte swizzle: rows along K
+// of 64 contiguous MN elements (128 B), 8-row atoms of 1024 bytes (SBO), the
+// next 64 MN elements `lbo_bytes` further on.
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)64 << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
 // Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// B operand MN-major (bit 16) for the same instruction.
+__host__ __device__ constexpr uint32_t idesc_bf16_bmn(int M, int N) { return idesc_bf16(M, N) | (1u << 16); }
+
 }  // namespace tc
+
+// Host helpers shared by the tensor-core kernels (defined in gemm_tc.cu;
+// includers include <torch/extension.h> first).
+// 2-D bf16 row-major tensor map, 128-byte swizzle, box = 64 columns x box_rows.
+CUtensorMap make_tmap_bf16(const at::Tensor& t, int box_rows);
+// Device error word of the tensor-core kernels (read and cleared by tc_error_code).
+int* tc_error_ptr(int dev);
+
 }  // namespace art

@@ -44,13 +44,15 @@ def _acc(t: torch.Tensor) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 
 
-BWD_KEYS = 128  # key block of the attention backward kernel
-BWD_Q = 32  # query tile of the attention backward kernel
-BWD_MAX_QTILES = 8  # query tiles per backward work unit
+BWD_KEYS = 128  # key block of the warp-level attention backward kernel
+BWD_Q = 32  # query tile of the warp-level attention backward kernel
+BWD_MAX_QTILES = 8  # query tiles per warp-level backward work unit
 
 
 def attention_bwd_units(kend: torch.Tensor, max_qtiles: int = BWD_MAX_QTILES) -> torch.Tensor:
-    """Backward work units ``[n, 3]`` = (key block, q tile lo, q tile hi).
+    """Work units ``[n, 3]`` = (key block, q tile lo, q tile hi) of the
+    warp-level backward (``attn_bwd`` and its allocation-free C entry point;
+    training runs the tensor-core backward, :func:`attention_bwd_units_tc`).
 
     Key block ``kb`` (128 keys) is seen by queries ``[128 kb, max kend)``;
     that range (in 32-query tiles) is split into units of at most
@@ -72,13 +74,45 @@ def attention_bwd_units(kend: torch.Tensor, max_qtiles: int = BWD_MAX_QTILES) ->
     return torch.tensor(units, dtype=torch.int32).view(-1, 3)
 
 
+TC_TILE = 128  # key block and query tile of the tensor-core backward
+TC_MAX_QTILES = 4  # query tiles per tensor-core backward work unit
+
+
+def attention_bwd_units_tc(kend: torch.Tensor, q_off: int = 0, Tq: int | None = None,
+                           max_qtiles: int = TC_MAX_QTILES) -> torch.Tensor:
+    """Work units ``[n, 3]`` = (128-key block, first, end local 128-query
+    tile) of the tensor-core backward for local queries ``[q_off, q_off+Tq)``
+    (global positions) against every key.  A key block is seen by the
+    queries ``[128 kb, max kend)``; that range is cut into units of at most
+    ``max_qtiles`` tiles so shared-prompt blocks spread over many CTAs."""
+    T = int(kend.numel())
+    Tq = T - q_off if Tq is None else Tq
+    if T == 0 or Tq <= 0:
+        return torch.zeros(0, 3, dtype=torch.int32)
+    nkb = (T + TC_TILE - 1) // TC_TILE
+    kp = torch.nn.functional.pad(kend.to(torch.int64), (0, nkb * TC_TILE - T), value=0)
+    kmax = kp.view(nkb, TC_TILE).amax(1).clamp(max=T).tolist()
+    units = []
+    for kb in range(nkb):
+        lo = max(kb * TC_TILE, q_off) - q_off
+        hi = min(kmax[kb], q_off + Tq) - q_off
+        if hi <= lo:
+            continue
+        t_lo, t_hi = lo // TC_TILE, (hi + TC_TILE - 1) // TC_TILE
+        for a in range(t_lo, t_hi, max_qtiles):
+            units.append((kb, a, min(t_hi, a + max_qtiles)))
+    return torch.tensor(units, dtype=torch.int32).view(-1, 3)
+
+
 @dataclass
 class AttnMeta:
     """Per-row attention metadata shared by every layer of one micro step.
 
     ``kend[j]``: query ``i`` may attend key ``j`` iff ``j <= i < kend[j]``.
-    ``tile_kmax[t]``: max of ``kend`` over keys ``[64t, 64t+64)`` (tile skip).
-    ``bwd_units``: load-balanced work list of the attention backward.
+    ``tile_kmax[t]`` / ``tile_kmin[t]``: max / min of ``kend`` over keys
+    ``[64t, 64t+64)`` (tile skipping, and tiles that need no mask).
+    ``bwd_units``: load-balanced work list of the tensor-core attention
+    backward (128-key blocks x 128-query tiles).
     """
 
     positions: torch.Tensor  # int32 [T]
@@ -86,6 +120,7 @@ class AttnMeta:
     tile_kmax: torch.Tensor  # int32 [ceil(T/64)]
     T: int
     bwd_units: torch.Tensor | None = None  # int32 [n, 3]
+    tile_kmin: torch.Tensor | None = None  # int32 [ceil(T/64)]
 
     @staticmethod
     def build(positions: torch.Tensor, kend: torch.Tensor, device: torch.device) -> "AttnMeta":
@@ -95,7 +130,9 @@ class AttnMeta:
         k_cpu = kend.detach().to("cpu", torch.int32)
         kp = torch.nn.functional.pad(k_cpu, (0, pad), value=0)
         tile = kp.view(-1, 64).amax(dim=1).to(torch.int32)
-        units = attention_bwd_units(k_cpu)
+        kq = torch.nn.functional.pad(k_cpu, (0, pad), value=torch.iinfo(torch.int32).max)
+        tile_min = kq.view(-1, 64).amin(dim=1).to(torch.int32)
+        units = attention_bwd_units_tc(k_cpu)
         pin = device.type == "cuda"
         mv = lambda t: (t.pin_memory() if pin else t).to(device, non_blocking=True)  # noqa: E731
         return AttnMeta(
@@ -104,6 +141,7 @@ class AttnMeta:
             tile_kmax=mv(tile),
             T=T,
             bwd_units=mv(units),
+            tile_kmin=mv(tile_min),
         )
 
 
@@ -195,7 +233,7 @@ class _RopeAttention(torch.autograd.Function):
         q = qk[:, : nq * D].view(T, nq, D)
         k = qk[:, nq * D :].view(T, nkv, D)
         v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
-        o, lse = C.attn_fwd(q, k, v, meta.kend, meta.tile_kmax, scale)
+        o, lse = C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, scale)
         ctx.save_for_backward(qkv, qk, o, lse, inv_freq, qn_w if qn_w is not None else qkv.new_empty(0),
                               kn_w if kn_w is not None else qkv.new_empty(0),
                               rstd if rstd is not None and rstd.numel() else qkv.new_empty(0, dtype=torch.float32))
@@ -216,7 +254,7 @@ class _RopeAttention(torch.autograd.Function):
         v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
         dqkv = torch.empty_like(qkv)
         dqk = torch.empty_like(qk)
-        dq_acc, dk_acc, dv_acc = C.attn_bwd(do, q, k, v, o, lse, meta.kend, meta.bwd_units, scale)
+        dq_acc, dk_acc, dv_acc = C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, meta.bwd_units, scale)
         dqk[:, : nq * D].copy_(dq_acc.view(T, nq * D))
         dqk[:, nq * D :].copy_(dk_acc.view(T, nkv * D))
         dqkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].copy_(dv_acc.view(T, nkv * D))

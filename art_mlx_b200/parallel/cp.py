@@ -33,7 +33,6 @@ import torch
 import torch.distributed as dist
 
 from ..ops import fused, native
-from ..ops.fused import BWD_KEYS, BWD_MAX_QTILES, BWD_Q
 
 
 class CPContext:
@@ -79,25 +78,6 @@ def gather(x: torch.Tensor, cp: CPContext) -> torch.Tensor:
     return _Gather.apply(x, cp)
 
 
-def local_bwd_units(kend: torch.Tensor, q_off: int, Tq: int, max_qtiles: int = BWD_MAX_QTILES) -> torch.Tensor:
-    """Attention-backward work units for local queries ``[q_off, q_off+Tq)``
-    against all keys (q tiles are local)."""
-    T = int(kend.numel())
-    nkb = (T + BWD_KEYS - 1) // BWD_KEYS
-    kp = torch.nn.functional.pad(kend.to(torch.int64), (0, nkb * BWD_KEYS - T), value=0)
-    kmax = kp.view(nkb, BWD_KEYS).amax(1).clamp(max=T).tolist()
-    units = []
-    for kb in range(nkb):
-        lo = max(kb * BWD_KEYS, q_off) - q_off
-        hi = min(kmax[kb], q_off + Tq) - q_off
-        if hi <= lo:
-            continue
-        t_lo, t_hi = lo // BWD_Q, (hi + BWD_Q - 1) // BWD_Q
-        for s in range(t_lo, t_hi, max_qtiles):
-            units.append((kb, s, min(t_hi, s + max_qtiles)))
-    return torch.tensor(units, dtype=torch.int32).view(-1, 3)
-
-
 @dataclass
 class Piece:
     seg: int
@@ -124,7 +104,7 @@ class CPPlan:
         k_cpu = kend_full.to("cpu", torch.int32)
         self.meta = fused.AttnMeta.build(positions_full[self.a : self.b], k_cpu, dev)
         pin = dev.type == "cuda"
-        units = local_bwd_units(k_cpu, self.a, self.rows)
+        units = fused.attention_bwd_units_tc(k_cpu, self.a, self.rows)
         self.meta.bwd_units = (units.pin_memory() if pin else units).to(dev, non_blocking=True)
         self.K = conv_width - 1
         if linear_layers:
@@ -210,7 +190,7 @@ class _CPRopeAttention(torch.autograd.Function):
         v_loc = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].reshape(T, nkv, D)
         k_full = cp.all_gather(k_loc)
         v_full = cp.all_gather(v_loc)
-        o, lse = C.attn_fwd(q, k_full, v_full, meta.kend, meta.tile_kmax, scale, plan.a)
+        o, lse = C.attn_fwd_tc(q, k_full, v_full, meta.kend, meta.tile_kmax, meta.tile_kmin, scale, plan.a)
         ctx.save_for_backward(qkv, qk, k_full, v_full, o, lse, inv_freq,
                               qn_w if qn_w is not None else qkv.new_empty(0),
                               kn_w if kn_w is not None else qkv.new_empty(0),
@@ -227,8 +207,8 @@ class _CPRopeAttention(torch.autograd.Function):
         T = qkv.shape[0]
         do = do.contiguous().view(T, nq, D)
         q = qk[:, : nq * D].view(T, nq, D)
-        dq, dk_full, dv_full = C.attn_bwd(do, q, k_full, v_full, o, lse, plan.meta.kend, plan.meta.bwd_units,
-                                          scale, plan.a)
+        dq, dk_full, dv_full = C.attn_bwd_tc(do, q, k_full, v_full, o, lse, plan.meta.kend, plan.meta.bwd_units,
+                                             scale, plan.a)
         dk = cp.reduce_scatter(dk_full)
         dv = cp.reduce_scatter(dv_full)
         dqkv = torch.empty_like(qkv)

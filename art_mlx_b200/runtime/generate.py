@@ -237,7 +237,7 @@ class GenerationEngine:
             vs = v.index_select(0, fill_rows)
             if q.is_cuda:
                 C = native.lib()
-                o, _ = C.attn_fwd(q, k, v, meta.kend, meta.tile_kmax, scale)
+                o, _ = C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, scale)
                 C.kv_append(ks.reshape(ks.shape[0], -1), vs.reshape(vs.shape[0], -1), fill_slot, fill_pos,
                             kc[li], vc[li])
                 return o
@@ -296,4 +296,6 @@ def _decode_ref(q, kc, vc, lens, scale):
     s = torch.einsum("bhd,blhd->bhl", q.float(), k) * scale
     mask = torch.arange(kc.shape[1], device=q.device).view(1, 1, -1) < lens.view(B, 1, 1).to(q.device)
     s = s.masked_fill(~mask, float("-inf"))
+    # cache rows past each length are unwritten memory: keep them out of the sum
+    v = v.masked_fill(~mask.view(B, 1, -1).transpose(1, 2).unsqueeze(-1), 0.0)
     return torch.einsum("bhl,blhd->bhd", torch.softmax(s, -1), v).to(q.dtype)

@@ -116,7 +116,7 @@ def stage_row(
         routes = dev(rr.expert_indices[row, :L])
     orig = packed.get("original_logprobs")
     meta = AttnMeta.build(dev(pos), kend, device)
-    moved[0] += sum(t.numel() * t.element_size() for t in (meta.kend, meta.tile_kmax, meta.bwd_units))
+    moved[0] += sum(t.numel() * t.element_size() for t in (meta.kend, meta.tile_kmax, meta.tile_kmin, meta.bwd_units))
     return MicroBatch(
         tokens=dev(tokens),
         meta=meta,
@@ -145,7 +145,8 @@ def _stage_row_cp(packed, row, device, L, kend, pos, sel, n_valid, cp, pin, conv
     plan = CPPlan(cp, kend, pos, gids, pids, conv_width, linear_layers)
     a, b = plan.a, plan.b
     moved = [sum(t.numel() * t.element_size() for t in (plan.meta.positions, plan.meta.kend,
-                                                         plan.meta.tile_kmax, plan.meta.bwd_units))]
+                                                         plan.meta.tile_kmax, plan.meta.tile_kmin,
+                                                         plan.meta.bwd_units))]
 
     def dev(t: torch.Tensor) -> torch.Tensor:
         t = t.contiguous()

@@ -54,3 +54,35 @@ def test_gemm_tc_repeated_calls_stable(cuda):
         r = C.gemm_tc(a, b, None, None, None, None, False)
         assert torch.equal(r, r0)
     assert C.tc_error_code() == 0
+
+
+@pytest.mark.parametrize("E,K,N,K2,wt", [(8, 256, 512, 0, False), (16, 2048, 1536, 16, False), (4, 512, 96, 8, False),
+                                         (8, 256, 512, 0, True), (16, 2048, 1536, 32, True), (4, 200, 64, 8, True)])
+def test_gemm_tc_grouped_matches_fp32(cuda, E, K, N, K2, wt):
+    """Per-expert rows (some experts empty, counts not multiples of 128)."""
+    C = native.lib()
+    g = torch.Generator().manual_seed(E * K)
+    counts = [int(c) for c in torch.randint(0, 300, (E,), generator=g)]
+    counts[1] = 0
+    offs = [0]
+    for c in counts:
+        offs.append(offs[-1] + c)
+    M = offs[-1]
+    x = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+    w = torch.randn(E * N, K, device=cuda, dtype=torch.bfloat16) * 0.05
+    a2 = torch.randn(M, K2, device=cuda, dtype=torch.bfloat16) if K2 else None
+    b2 = torch.randn(E * N, K2, device=cuda, dtype=torch.bfloat16) * 0.05 if K2 else None
+    if wt:  # the same matrices handed over transposed, stacked as [E*K, N]
+        wt_ = w.view(E, N, K).transpose(1, 2).contiguous().view(E * K, N)
+        out = C.gemm_tc_grouped(x, wt_, offs, N, a2, b2, True)
+    else:
+        out = C.gemm_tc_grouped(x, w, offs, N, a2, b2)
+    torch.cuda.synchronize()
+    assert C.tc_error_code() == 0
+    ref = torch.empty(M, N, device=cuda)
+    for e in range(E):
+        r = slice(offs[e], offs[e + 1])
+        ref[r] = x[r].float() @ w[e * N : (e + 1) * N].float().t()
+        if K2:
+            ref[r] += a2[r].float() @ b2[e * N : (e + 1) * N].float().t()
+    assert rel_err(out, ref) < 1e-2

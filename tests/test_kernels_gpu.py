@@ -106,7 +106,7 @@ def test_attention_fwd_bwd(cuda, shape):
     assert rel_err(o, orf) < 1e-2
     assert torch.allclose(lse, lser.float(), atol=2e-2, rtol=1e-3)
     do = torch.randn_like(o)
-    dq, dk, dv = C.attn_bwd(do, q, k, v, o, lse, meta.kend, meta.bwd_units, scale)
+    dq, dk, dv = C.attn_bwd(do, q, k, v, o, lse, meta.kend, fused.attention_bwd_units(kend).to(cuda), scale)
     orf.backward(do.float())
     assert rel_err(dq, qr.grad) < 2e-2
     assert rel_err(dk, kr.grad) < 2e-2

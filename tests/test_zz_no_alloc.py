@@ -48,13 +48,13 @@ def test_attn_bwd_noalloc_matches_entry_point(cuda):
     scale = 1 / math.sqrt(D)
     o, lse = C.attn_fwd(q, k, v, meta.kend, meta.tile_kmax, scale)
     do = torch.randn_like(o)
-    ref_dq, ref_dk, ref_dv = C.attn_bwd(do, q, k, v, o, lse, meta.kend, meta.bwd_units, scale)
+    units = fused.attention_bwd_units(kend).to(cuda)  # work units of the warp-level backward
+    ref_dq, ref_dk, ref_dv = C.attn_bwd(do, q, k, v, o, lse, meta.kend, units, scale)
 
     dq = torch.full((T, Hq, D), 123.0, device=cuda)  # garbage: the entry point must clear it
     dk = torch.full((T, Hkv, D), -7.0, device=cuda)
     dv = torch.full((T, Hkv, D), 5.0, device=cuda)
     stream = torch.cuda.current_stream().cuda_stream
-    units = meta.bwd_units
     for call in range(2):
         rc = fn(do.data_ptr(), do.stride(0), q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0),
                 v.data_ptr(), v.stride(0), o.data_ptr(), o.stride(0), lse.data_ptr(), meta.kend.data_ptr(),
