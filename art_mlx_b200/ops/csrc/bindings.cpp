@@ -34,6 +34,7 @@ std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torc
                                        double scale, int64_t q_off);
 torch::Tensor gemm_tc_grouped(torch::Tensor x, torch::Tensor w, std::vector<int64_t> offs, int64_t N,
                               c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, bool w_transposed);
+void peer_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes);
 torch::Tensor decode_attn(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
                           double scale);
 void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor slot, torch::Tensor pos, torch::Tensor k_cache,
@@ -94,6 +95,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out"), py::arg("lse"), py::arg("kend"), py::arg("units"), py::arg("scale"), py::arg("q_off") = 0);
   m.def("gemm_tc_grouped", &art::gemm_tc_grouped, py::arg("x"), py::arg("w"), py::arg("offs"), py::arg("N"),
         py::arg("a2") = py::none(), py::arg("b2") = py::none(), py::arg("w_transposed") = false);
+  m.def("peer_copy", &art::peer_copy);
   m.def("decode_attn", &art::decode_attn);
   m.def("kv_append", &art::kv_append);
   m.def("attn_bwd", &art::attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),

@@ -215,3 +215,16 @@ void dp_adamw_allgather(torch::Tensor compute_bases, int64_t world, int64_t off,
 }
 
 }  // namespace art
+
+namespace art {
+
+// Copy nbytes from a peer's mapped buffer (CUDA-IPC address, reached over
+// NVLink) into a local tensor, on the current stream (one copy-engine
+// transfer; the SMs stay free for the GEMM that overlaps it).
+void peer_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes) {
+  TORCH_CHECK(dst.is_cuda() && dst.is_contiguous() && dst.numel() * dst.element_size() >= nbytes);
+  ART_CUDA_CHECK(cudaMemcpyAsync(dst.data_ptr(), reinterpret_cast<const void*>(src_ptr), (size_t)nbytes,
+                                 cudaMemcpyDeviceToDevice, at::cuda::getCurrentCUDAStream()));
+}
+
+}  // namespace art

@@ -112,19 +112,59 @@ class TPContext:
 
     def ag_gemm(self, x_sh: torch.Tensor, W: torch.Tensor, a2: torch.Tensor | None = None,
                 b2: torch.Tensor | None = None, bias: torch.Tensor | None = None) -> torch.Tensor:
-        """``AG(x_sh) @ W^T (+ a2 @ b2^T) (+ bias)`` with the gather inside the GEMM."""
+        """``AG(x_sh) @ W^T (+ a2 @ b2^T) (+ bias)`` with the gather overlapped.
+
+        Every rank publishes its shard into its peer arena; then each peer
+        shard crosses NVLink exactly once, pulled by the copy engine into a
+        local buffer on a side stream, while the tcgen05 GEMM runs on the
+        shard that arrived before it (the own shard first).  Reading the peer
+        rows straight from the GEMM's TMA would fetch every remote A tile
+        once per output column band."""
         rows, H = x_sh.shape
         if self.transport != "p2p":
             y = self.all_gather(x_sh) @ W.t()
             if a2 is not None:
                 y = y + a2 @ b2.t()
             return y if bias is None else y + bias
+        C = native.lib()
         off = self._ag_slot()
         slot = self.arena.view(off, rows * H, x_sh.dtype).view(rows, H)
         slot.copy_(x_sh)
         self.barrier()  # every rank's shard is published
-        ptrs = [b + off for b in self.arena.bases]
-        return native.lib().gemm_tc_ag(ptrs, rows, H, H, W, a2, b2, bias)
+        T, N = rows * self.world, W.shape[0]
+        out = torch.empty(T, N, device=x_sh.device, dtype=x_sh.dtype)
+        gathered = self._gather_buffer(T, H, x_sh.dtype)
+        main = torch.cuda.current_stream()
+        side = self._side_stream()
+        side.wait_stream(main)
+        order = [(self.rank + i) % self.world for i in range(self.world)]
+        events = {}
+        with torch.cuda.stream(side):
+            for q in order[1:]:
+                C.peer_copy(gathered[q * rows : (q + 1) * rows], self.arena.bases[q] + off, rows * H * x_sh.element_size())
+                ev = torch.cuda.Event()
+                ev.record(side)
+                events[q] = ev
+        for q in order:
+            src = x_sh if q == self.rank else gathered[q * rows : (q + 1) * rows]
+            if q != self.rank:
+                main.wait_event(events[q])
+            r = slice(q * rows, (q + 1) * rows)
+            C.gemm_tc(src, W, None if a2 is None else a2[r], b2, bias, out[r], False)
+        gathered.record_stream(side)
+        return out
+
+    def _side_stream(self) -> torch.cuda.Stream:
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        return self._side
+
+    def _gather_buffer(self, T: int, H: int, dtype: torch.dtype) -> torch.Tensor:
+        buf = getattr(self, "_gbuf", None)
+        if buf is None or buf.numel() < T * H or buf.dtype != dtype:
+            buf = torch.empty(T * H, device=self.device, dtype=dtype)
+            self._gbuf = buf
+        return buf[: T * H].view(T, H)
 
     def gemm_rs(self, x: torch.Tensor, W: torch.Tensor, a2: torch.Tensor | None = None,
                 b2: torch.Tensor | None = None) -> torch.Tensor:

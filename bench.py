@@ -46,6 +46,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--completion-len", type=int, default=512)
     p.add_argument("--lora-rank", type=int, default=16)
     p.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the headline)")
+    p.add_argument("--tp", type=int, default=1, help="tensor-parallel size (dense models)")
+    p.add_argument("--cp", type=int, default=1, help="context-parallel size")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=2)
     return p.parse_args()
@@ -194,10 +196,21 @@ def main() -> None:
     train_tokens = float(packed["assistant_mask"][:, 1:].sum())
     packed_tokens = int((packed["group_ids"] >= 0).sum())
 
-    trainer = GRPOTrainer(cfg, lora, device, seed=0, group=dist.group.WORLD if world > 1 else None)
+    trainer = GRPOTrainer(cfg, lora, device, seed=0, group=dist.group.WORLD if world > 1 else None,
+                          tp_size=args.tp, cp_size=args.cp, max_tokens_per_rank=max(16384, seq_len))
     lr = 1e-5
     loss_cfg: dict = {}
     staged = trainer.stage(packed)
+    if cfg.is_moe:
+        # routing replay: the top-k experts of every token and layer are
+        # recorded in a seeded forward pass and replayed by the training pass
+        for mb in staged:
+            rec: dict = {}
+            with torch.no_grad():
+                trainer.model.forward(mb.tokens, mb.meta, {"record_routes": rec, "group_ids": mb.group_ids,
+                                                           "parent_ids": mb.parent_ids, "cp_plan": mb.cp_plan,
+                                                           "cp": trainer.cp})
+            mb.routes = torch.stack([rec[i] for i in sorted(rec)], dim=1)
     l2_flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
 
     def step() -> None:
@@ -226,6 +239,8 @@ def main() -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    parallelism = f"dp{world // (args.tp * args.cp)}" + (f"_tp{args.tp}" if args.tp > 1 else "") + (
+        f"_cp{args.cp}" if args.cp > 1 else "") + (f"_ep{world}" if cfg.is_moe and world > 1 else "")
     ms = start.elapsed_time(end) / args.steps
     t = torch.tensor([ms], device=device)
     if world > 1:
@@ -276,7 +291,7 @@ def main() -> None:
                 "prompt_len": args.prompt_len,
                 "completion_len": args.completion_len,
                 "lora_rank": args.lora_rank,
-                "parallelism": f"dp{world}",
+                "parallelism": parallelism,
                 "rows_per_step": n_rows,
                 "trained_tokens_per_step": int(train_tokens),
                 "packed_tokens_per_step": packed_tokens,
