@@ -39,7 +39,7 @@ from ..models.config import LoRASpec, get_config
 from ..preprocessing.pack import packed_tensors_from_tokenized_results, packed_tensors_to_dir
 from ..preprocessing.prefix_tree import estimate_prefix_tree_packed_tokens
 from ..preprocessing.tokenize import TokenizedResult, tokenize_trajectory_groups
-from ..runtime.checkpoint import load_adapter, save_adapter
+from ..runtime.checkpoint import AsyncCheckpointWriter, load_adapter, save_adapter
 from ..runtime.trainer import GRPOTrainer
 from ..trajectories import Trajectory, TrajectoryGroup
 from ..types import LocalTrainResult, TrainSFTConfig
@@ -76,6 +76,9 @@ class LocalBackend:
         self._inference = inference
         self._servers: dict[str, Any] = {}
         self._engines: dict[str, Any] = {}
+        # step checkpoints are written in the background (the write of step n
+        # overlaps step n+1); everything that reads checkpoints waits first
+        self._writer = AsyncCheckpointWriter()
         self._leases: dict[str, Any] = {}
         self._metrics: dict[str, MetricsBuilder] = {}
         self.last_h2d_bytes = 0
@@ -93,7 +96,12 @@ class LocalBackend:
     async def __aexit__(self, *exc: Any) -> None:
         await self.close()
 
+    def _flush(self) -> None:
+        """Wait until every submitted checkpoint is published."""
+        self._writer.wait()
+
     async def close(self) -> None:
+        self._flush()
         for server in self._servers.values():
             server.stop()
         self._servers.clear()
@@ -105,6 +113,7 @@ class LocalBackend:
     def _model_inference_name(self, model: Any, step: int | None = None) -> str:
         from ..adapter_leases import pinned_inference_step
 
+        self._flush()
         if step is None:
             step = pinned_inference_step(model.name)
         if step is None:
@@ -122,6 +131,7 @@ class LocalBackend:
                 json.dump(model.model_dump(mode="json"), f, indent=2, default=str)
 
     async def _get_step(self, model: Any) -> int:
+        self._flush()
         return get_step_from_dir(self._model_dir(model))
 
     def adapter_leases(self, model: Any):
@@ -131,6 +141,7 @@ class LocalBackend:
         return self._leases.setdefault(model.name, AdapterLeaseManager())
 
     async def _delete_checkpoint_files(self, model: Any, steps_to_keep: list[int]) -> None:
+        self._flush()
         steps_to_keep = sorted(set(steps_to_keep) | self.adapter_leases(model).active_steps())
         if _rank() != 0:
             return
@@ -179,6 +190,7 @@ class LocalBackend:
     async def _prepare_backend_for_training(
         self, model: Any, config: dev.OpenAIServerConfig | None = None
     ) -> tuple[str, str]:
+        self._flush()
         tr = self._get_trainer(model)
         d = self._model_dir(model)
         step = get_step_from_dir(d)
@@ -227,6 +239,7 @@ class LocalBackend:
         the live policy (``None``)."""
         if name == model.base_model:
             return "base"
+        self._flush()
         if "@" in name:
             _, step = name.rsplit("@", 1)
             d = self._model_dir(model)
@@ -341,6 +354,7 @@ class LocalBackend:
             num_trajectories_learning_rate_multiplier_power=num_trajectories_learning_rate_multiplier_power,
             kl_ref_adapter_path=kl_ref_adapter_path,
         )
+        self._flush()
         step = get_step_from_dir(d)
         results = list(
             tokenize_trajectory_groups(
@@ -432,7 +446,7 @@ class LocalBackend:
         if out_dir is not None:
             tr.prepare_checkpoint()
             if _rank() == 0:
-                save_adapter(out_dir, tr.store, model.base_model, tr.model.lora_spec, tr.optim.state_dict())
+                self._writer.submit(out_dir, tr.store, model.base_model, tr.model.lora_spec, tr.optim.state_dict())
         _barrier()
         return metrics
 
@@ -459,6 +473,7 @@ class LocalBackend:
             lr = lrs[i] if isinstance(lrs, list) else lrs
             m = tr.sft_step(batch, lr)
             yield m
+        self._flush()
         step = get_step_from_dir(d) + 1
         if _rank() == 0:
             save_adapter(get_step_checkpoint_dir(d, step), tr.store, model.base_model, tr.model.lora_spec,
@@ -472,6 +487,7 @@ class LocalBackend:
         as its current step (reference ``local/backend.py:1540``)."""
         from ..utils.output_dirs import get_output_dir_from_model_properties, list_checkpoint_steps
 
+        self._flush()
         src = get_output_dir_from_model_properties(from_project or model.project, from_model, self._path)
         steps = [s for s in list_checkpoint_steps(src) if not_after_step is None or s <= not_after_step]
         if not steps:

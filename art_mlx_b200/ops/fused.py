@@ -79,12 +79,14 @@ TC_MAX_QTILES = 4  # query tiles per tensor-core backward work unit
 
 
 def attention_bwd_units_tc(kend: torch.Tensor, q_off: int = 0, Tq: int | None = None,
-                           max_qtiles: int = TC_MAX_QTILES) -> torch.Tensor:
+                           max_qtiles: int = TC_MAX_QTILES, kv_heads: int = 4, min_ctas: int = 2 * 148) -> torch.Tensor:
     """Work units ``[n, 3]`` = (128-key block, first, end local 128-query
     tile) of the tensor-core backward for local queries ``[q_off, q_off+Tq)``
     (global positions) against every key.  A key block is seen by the
     queries ``[128 kb, max kend)``; that range is cut into units of at most
-    ``max_qtiles`` tiles so shared-prompt blocks spread over many CTAs."""
+    ``max_qtiles`` tiles so shared-prompt blocks spread over many CTAs, and
+    the cut is made finer (down to one tile) while the launch
+    (units x ``kv_heads``) would not fill ``min_ctas`` CTAs."""
     T = int(kend.numel())
     Tq = T - q_off if Tq is None else Tq
     if T == 0 or Tq <= 0:
@@ -92,15 +94,16 @@ def attention_bwd_units_tc(kend: torch.Tensor, q_off: int = 0, Tq: int | None = 
     nkb = (T + TC_TILE - 1) // TC_TILE
     kp = torch.nn.functional.pad(kend.to(torch.int64), (0, nkb * TC_TILE - T), value=0)
     kmax = kp.view(nkb, TC_TILE).amax(1).clamp(max=T).tolist()
-    units = []
+    spans = []
     for kb in range(nkb):
         lo = max(kb * TC_TILE, q_off) - q_off
         hi = min(kmax[kb], q_off + Tq) - q_off
-        if hi <= lo:
-            continue
-        t_lo, t_hi = lo // TC_TILE, (hi + TC_TILE - 1) // TC_TILE
-        for a in range(t_lo, t_hi, max_qtiles):
-            units.append((kb, a, min(t_hi, a + max_qtiles)))
+        if hi > lo:
+            spans.append((kb, lo // TC_TILE, (hi + TC_TILE - 1) // TC_TILE))
+    m = max_qtiles
+    while m > 1 and sum((b - a + m - 1) // m for _, a, b in spans) * kv_heads < min_ctas:
+        m //= 2
+    units = [(kb, a, min(b, a + m)) for kb, lo, b in spans for a in range(lo, b, m)]
     return torch.tensor(units, dtype=torch.int32).view(-1, 3)
 
 

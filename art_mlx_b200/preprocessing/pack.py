@@ -24,6 +24,7 @@ import random
 from dataclasses import dataclass
 from typing import Any, NamedTuple, TypedDict
 
+import numpy as np
 import torch
 from typing_extensions import NotRequired
 
@@ -98,10 +99,10 @@ def _first_trainable(r: TokenizedResult) -> int:
 def _item(r: TokenizedResult, seq_len: int) -> _Item:
     share = min(int(r.prompt_length), max(_first_trainable(r) - 1, 0))
     it = _Item(
-        tuple(int(v) for v in r.token_ids),
-        tuple(int(v) for v in r.input_pos),
-        tuple(int(v) for v in r.assistant_mask),
-        tuple(float(v) for v in r.logprobs),
+        tuple(map(int, r.token_ids)),
+        tuple(map(int, r.input_pos)),
+        tuple(map(int, r.assistant_mask)),
+        tuple(map(float, r.logprobs)),
         float(r.advantage),
         float(r.weight),
         int(r.prompt_id),
@@ -125,13 +126,13 @@ def _truncate(it: _Item, seq_len: int) -> _Item:
 
 
 def _row_len(row: list[_Item], seq_len: int) -> int:
-    n = estimate_prefix_tree_packed_tokens(
-        (torch.tensor(i.token_ids, dtype=torch.long) for i in row),
-        max_depth=seq_len,
-        shareable_lengths=(i.shareable for i in row),
-    )
-    assert n is not None
-    return n
+    """Packed length of a candidate row, planned on the token tuples directly
+    (same plan as ``estimate_prefix_tree_packed_tokens``, no tensor round trip)."""
+    from .prefix_tree import _plan_segments
+
+    segs = _plan_segments([i.token_ids for i in row], seq_len,
+                          [max(0, min(i.shareable, len(i.token_ids))) for i in row])
+    return sum(s.end - s.start for s in segs)
 
 
 def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
@@ -142,37 +143,48 @@ def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
         max_depth=seq_len if share else 0,
         shareable_lengths=(i.shareable if share else 0 for i in row),
     )
-    toks = tree.tokens.reshape(-1).tolist()
+    # every packed slot belongs to the first sequence that reaches it; later
+    # sequences sharing the slot must agree on it (vectorised per sequence)
+    toks = tree.tokens.reshape(-1).numpy()
     n = len(toks)
-    owned = [False] * n
-    pos = [0] * n
-    mask = [0] * n
-    lps = [float("nan")] * n
-    adv = [0.0] * n
-    w = [0.0] * n
+    owned = np.zeros(n, dtype=bool)
+    pos = np.zeros(n, dtype=np.int64)
+    mask = np.zeros(n, dtype=np.int64)
+    lps = np.full(n, np.nan, dtype=np.float64)
+    adv = np.zeros(n, dtype=np.float64)
+    w = np.zeros(n, dtype=np.float64)
     routes: list[Any] = [None] * n
     for k, it in enumerate(row):
-        for src, dst in enumerate(tree.positions_by_sequence[k].tolist()):
-            if toks[dst] != it.token_ids[src]:
-                raise RuntimeError("Prefix-tree pack token assignment mismatch")
-            if owned[dst]:
-                if pos[dst] != it.input_pos[src]:
-                    raise RuntimeError("Prefix-tree pack cannot share mismatched input positions")
-                if it.assistant_mask[src] or not math.isnan(it.logprobs[src]):
-                    raise RuntimeError("Prefix-tree pack attempted to share a trainable token")
-                continue
-            owned[dst] = True
-            pos[dst] = it.input_pos[src]
-            mask[dst] = it.assistant_mask[src]
-            lps[dst] = it.logprobs[src]
-            adv[dst] = it.advantage
-            w[dst] = it.weight
-            if it.routes is not None and src < len(it.routes):
-                routes[dst] = it.routes[src]
+        dst = tree.positions_by_sequence[k].numpy()
+        m = len(dst)
+        tk = np.asarray(it.token_ids[:m], dtype=np.int64)
+        if (toks[dst] != tk).any():
+            raise RuntimeError("Prefix-tree pack token assignment mismatch")
+        ip = np.asarray(it.input_pos[:m], dtype=np.int64)
+        am = np.asarray(it.assistant_mask[:m], dtype=np.int64)
+        lp = np.asarray(it.logprobs[:m], dtype=np.float64)
+        shared = owned[dst]
+        if shared.any():
+            if (pos[dst[shared]] != ip[shared]).any():
+                raise RuntimeError("Prefix-tree pack cannot share mismatched input positions")
+            if (am[shared] != 0).any() or (~np.isnan(lp[shared])).any():
+                raise RuntimeError("Prefix-tree pack attempted to share a trainable token")
+        fresh = ~shared
+        d = dst[fresh]
+        owned[d] = True
+        pos[d] = ip[fresh]
+        mask[d] = am[fresh]
+        lps[d] = lp[fresh]
+        adv[d] = it.advantage
+        w[d] = it.weight
+        if it.routes is not None:
+            for src in np.nonzero(fresh)[0].tolist():
+                if src < len(it.routes):
+                    routes[int(dst[src])] = it.routes[src]
     return {
         "tokens": toks[:seq_len],
-        "group_ids": tree.group_ids.reshape(-1).tolist()[:seq_len],
-        "parent_ids": tree.parent_ids.reshape(-1).tolist()[:seq_len],
+        "group_ids": tree.group_ids.reshape(-1).numpy()[:seq_len],
+        "parent_ids": tree.parent_ids.reshape(-1).numpy()[:seq_len],
         "input_pos": pos[:seq_len],
         "assistant_mask": mask[:seq_len],
         "logprobs": lps[:seq_len],
@@ -182,11 +194,11 @@ def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
     }
 
 
-def _padded(rows: list[list], seq_len: int, value: Any, dtype: torch.dtype) -> torch.Tensor:
+def _padded(rows: list, seq_len: int, value: Any, dtype: torch.dtype) -> torch.Tensor:
     out = torch.full((len(rows), seq_len), value, dtype=dtype)
     for r, vals in enumerate(rows):
-        if vals:
-            out[r, : len(vals)] = torch.tensor(vals, dtype=dtype)
+        if len(vals):
+            out[r, : len(vals)] = torch.as_tensor(np.asarray(vals)).to(dtype)
     return out
 
 

@@ -49,22 +49,29 @@ def adapter_config(base_model: str, spec: LoRASpec, **extra: Any) -> dict[str, A
     return cfg
 
 
-def save_adapter(
-    path: str,
-    store: LoRAStore,
-    base_model: str,
-    spec: LoRASpec,
-    optimizer_state: dict | None = None,
-    dtype: torch.dtype = torch.float32,
-) -> str:
-    """Write a checkpoint to ``path`` atomically (stage + rename)."""
+def snapshot_adapter(store: LoRAStore, optimizer_state: dict | None = None,
+                     dtype: torch.dtype = torch.float32) -> tuple[dict[str, torch.Tensor], dict | None]:
+    """Host copies of the adapter (and optimizer state) that later training
+    steps do not touch, for writing now or in the background."""
+    sd = store.state_dict(dtype)
+    on_cpu = store.master.device.type == "cpu"
+    if on_cpu:  # .cpu() of a host tensor is the tensor itself: copy
+        sd = {k: v.clone() for k, v in sd.items()}
+    opt = None
+    if optimizer_state is not None:
+        opt = {k: (v.detach().cpu().clone() if isinstance(v, torch.Tensor) else v) for k, v in optimizer_state.items()}
+    return sd, opt
+
+
+def write_adapter(path: str, sd: dict[str, torch.Tensor], base_model: str, spec: LoRASpec,
+                  optimizer_state: dict | None = None) -> str:
+    """Write a snapshot to ``path`` atomically (stage + rename)."""
     parent = os.path.dirname(os.path.abspath(path))
     os.makedirs(parent, exist_ok=True)
     stage = os.path.join(parent, f".staging-{uuid.uuid4().hex[:8]}")
     os.makedirs(stage)
     try:
-        save_file(store.state_dict(dtype), os.path.join(stage, "adapter_model.safetensors"),
-                  metadata={"format": "pt"})
+        save_file(sd, os.path.join(stage, "adapter_model.safetensors"), metadata={"format": "pt"})
         with open(os.path.join(stage, "adapter_config.json"), "w") as f:
             json.dump(adapter_config(base_model, spec), f, indent=2)
         if optimizer_state is not None:
@@ -76,6 +83,56 @@ def save_adapter(
         shutil.rmtree(stage, ignore_errors=True)
         raise
     return path
+
+
+def save_adapter(
+    path: str,
+    store: LoRAStore,
+    base_model: str,
+    spec: LoRASpec,
+    optimizer_state: dict | None = None,
+    dtype: torch.dtype = torch.float32,
+) -> str:
+    """Write a checkpoint to ``path`` atomically (stage + rename)."""
+    sd = store.state_dict(dtype)
+    return write_adapter(path, sd, base_model, spec, optimizer_state)
+
+
+def _write_optimizer(path: str, optimizer_state: dict) -> None:
+    tmp = os.path.join(path, f".optimizer-{uuid.uuid4().hex[:8]}.tmp")
+    torch.save(optimizer_state, tmp)
+    os.replace(tmp, os.path.join(path, "optimizer.pt"))
+
+
+class AsyncCheckpointWriter:
+    """Publishes the adapter of a step at once (the rollout side may load it
+    immediately) and writes the optimizer state, which only a resume reads,
+    on one background thread so that its file I/O overlaps the next step.
+    Both files appear atomically (stage + rename); ``wait()`` returns once
+    every submitted write is on disk and re-raises a write error."""
+
+    def __init__(self) -> None:
+        from concurrent.futures import ThreadPoolExecutor
+
+        self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="ckpt-writer")
+        self._pending: list = []
+
+    def submit(self, path: str, store: LoRAStore, base_model: str, spec: LoRASpec,
+               optimizer_state: dict | None = None) -> str:
+        sd, opt = snapshot_adapter(store, optimizer_state)
+        write_adapter(path, sd, base_model, spec, None)
+        if opt is not None:
+            self._pending.append(self._pool.submit(_write_optimizer, path, opt))
+        return path
+
+    def wait(self) -> None:
+        pending, self._pending = self._pending, []
+        for f in pending:
+            f.result()
+
+    def close(self) -> None:
+        self.wait()
+        self._pool.shutdown(wait=True)
 
 
 def load_adapter(path: str, store: LoRAStore, strict: bool = True) -> dict | None:

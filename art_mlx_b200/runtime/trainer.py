@@ -319,6 +319,22 @@ class GRPOTrainer:
         if self.grad_sync is not None:
             self.grad_sync.gather_full_state(self.store)
 
+    def offload(self) -> int:
+        """Move the model, LoRA store and optimizer state to pinned host
+        memory (the GPU is free for other work until :meth:`reload`)."""
+        if self.grad_sync is not None or self.tp is not None or self.ep is not None:
+            raise RuntimeError("offload applies to a single-GPU trainer (peer-mapped buffers stay resident)")
+        from .offload import OffloadState
+
+        self._offload = OffloadState(self.model, self.store, self.optim)
+        return self._offload.offload()
+
+    def reload(self) -> None:
+        st = getattr(self, "_offload", None)
+        if st is not None:
+            st.reload()
+            self._offload = None
+
     def check_health(self) -> None:
         if self.grad_sync is not None:
             self.grad_sync.check()
