@@ -207,8 +207,9 @@ def causal_conv(x: torch.Tensor, w: torch.Tensor, prev: torch.Tensor) -> torch.T
     return y
 
 
-def tree_delta_rule(q, k, v, g, beta, plan: TreePlan):
-    """Delta rule over a packed prefix-tree row: ``[T, H, d]`` inputs."""
+def tree_delta_rule(q, k, v, g, beta, plan: TreePlan, finals_out: dict | None = None):
+    """Delta rule over a packed prefix-tree row: ``[T, H, d]`` inputs.
+    ``finals_out`` (optional) receives each segment's final state."""
     T, Hh, dk = k.shape
     dv = v.shape[-1]
     out = q.new_zeros(T, Hh, dv)
@@ -234,6 +235,8 @@ def tree_delta_rule(q, k, v, g, beta, plan: TreePlan):
     for idx, valid, o in outs:
         sel = valid.reshape(-1)
         out = out.index_copy(0, idx.reshape(-1)[sel], o.reshape(-1, Hh, dv)[sel])
+    if finals_out is not None:
+        finals_out.update(finals)
     return out
 
 
@@ -276,8 +279,11 @@ class GatedDeltaNet:
         return qkvz[:, : 2 * kd + vd], qkvz[:, 2 * kd + vd :], g, beta
 
     def core_inputs(self, qkv, plan_prev):
-        kd, T = self.kd, qkv.shape[0]
-        x = causal_conv(qkv, self.conv_w, plan_prev)
+        return self.post_conv(causal_conv(qkv, self.conv_w, plan_prev))
+
+    def post_conv(self, x):
+        """SiLU after the causal conv, split into q, k, v heads, L2-normalised q / k."""
+        kd, T = self.kd, x.shape[0]
         x = torch.nn.functional.silu(x.float())
         q = x[:, :kd].view(T, self.nk, self.dk)
         k = x[:, kd : 2 * kd].view(T, self.nk, self.dk)
@@ -285,6 +291,32 @@ class GatedDeltaNet:
         q = torch.nn.functional.normalize(q, dim=-1) / math.sqrt(self.dk)
         k = torch.nn.functional.normalize(k, dim=-1)
         return q, k, v
+
+    def expand_heads(self, q, k):
+        if self.nv != self.nk:  # grouped value heads
+            rep = self.nv // self.nk
+            q = q.repeat_interleave(rep, dim=1)
+            k = k.repeat_interleave(rep, dim=1)
+        return q, k
+
+    def decode_step(self, h: torch.Tensor, state: dict[str, torch.Tensor], version: int, enabled: bool) -> torch.Tensor:
+        """One token per sequence: ``h`` [B, hidden]; ``state`` holds the
+        delta-rule state ``S`` [B, H, dk, dv] and the conv tail ``tail``
+        [B, width-1, C] (oldest first), both updated in place."""
+        qkv, z, g, beta = self.mix(h, version, enabled)
+        tail = state["tail"]
+        K = tail.shape[1]
+        w = self.conv_w
+        y = qkv * w[:, -1]
+        for m in range(K):  # the token m+1 positions back sits at tail[:, K-1-m]
+            y = y + tail[:, K - 1 - m].to(qkv.dtype) * w[:, -2 - m]
+        state["tail"] = torch.cat([tail[:, 1:], qkv.unsqueeze(1).to(tail.dtype)], dim=1)
+        q, k, v = self.post_conv(y)
+        q, k = self.expand_heads(q, k)
+        o, S = delta_rule_reference(q.unsqueeze(1), k.unsqueeze(1), v.float().unsqueeze(1), g.unsqueeze(1),
+                                    beta.unsqueeze(1), state["S"])
+        state["S"] = S
+        return self.finish(o[:, 0], z, version, enabled, h.dtype)
 
     def finish(self, o, z, version: int, enabled: bool, out_dtype):
         T = o.shape[0]
@@ -303,9 +335,10 @@ class GatedDeltaNet:
             ctx["gdn_plan"] = plan
         qkv, z, g, beta = self.mix(h, version, enabled)
         q, k, v = self.core_inputs(qkv, plan.prev)
-        if self.nv != self.nk:  # grouped value heads
-            rep = self.nv // self.nk
-            q = q.repeat_interleave(rep, dim=1)
-            k = k.repeat_interleave(rep, dim=1)
-        o = tree_delta_rule(q, k, v.float(), g, beta, plan)
+        q, k = self.expand_heads(q, k)
+        finals = ctx.get("gdn_finals")
+        out_finals = {} if finals is not None else None
+        o = tree_delta_rule(q, k, v.float(), g, beta, plan, out_finals)
+        if finals is not None:  # generation prefill: per-segment final states and conv inputs
+            finals[self.index] = (out_finals, qkv)
         return self.finish(o, z, version, enabled, h.dtype)

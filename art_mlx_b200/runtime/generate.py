@@ -21,8 +21,11 @@ store) the trainer updates, so a colocated policy needs no weight sync:
   compute buffer for the call and restored afterwards); ``"base"`` disables
   LoRA.
 
-On CPU the same loop runs the PyTorch reference ops (tests).  Gated DeltaNet
-layers are not supported for generation yet.
+Gated DeltaNet layers (hybrid models) run recurrently: the prefill runs the
+chunked delta rule over each prompt and keeps its final state and the last
+conv inputs per sequence; every decode step updates them with one token.
+
+On CPU the same loop runs the PyTorch reference ops (tests).
 """
 
 from __future__ import annotations
@@ -56,8 +59,6 @@ class GenerationResult:
 class GenerationEngine:
     def __init__(self, model, max_len: int = 8192) -> None:
         cfg = model.cfg
-        if any(layer.kind != "attention" for layer in model.layers):
-            raise NotImplementedError("generation with gated DeltaNet layers is not supported yet")
         self.model, self.cfg = model, cfg
         self.device = model.device
         self.max_len = max_len
@@ -116,13 +117,18 @@ class GenerationEngine:
             k = fused._rmsnorm_ref(k, layer.k_norm, cfg.rms_norm_eps)
         return fused._rope_ref(q, positions, m.inv_freq), fused._rope_ref(k, positions, m.inv_freq), v
 
-    def _layers(self, tokens: torch.Tensor, positions: torch.Tensor, attend) -> torch.Tensor:
+    def _layers(self, tokens: torch.Tensor, positions: torch.Tensor, attend, linear=None) -> torch.Tensor:
         m, cfg = self.model, self.cfg
         eps = cfg.rms_norm_eps
         out = m.embed[tokens]
         resid = None
         for li, layer in enumerate(m.layers):
             h, resid = fused.add_rmsnorm(out, resid, layer.in_norm, eps)
+            if layer.kind != "attention":  # gated DeltaNet
+                a = linear(li, layer, h)
+                h, resid = fused.add_rmsnorm(a, resid, layer.post_norm, eps)
+                out = m.mlp(layer, h, {})
+                continue
             qkv, gate = self._qkv(layer, h)
             q, k, v = self._rope(layer, qkv, positions)
             o = attend(li, q, k, v).reshape(q.shape[0], -1)
@@ -156,12 +162,14 @@ class GenerationEngine:
     # ------------------------------------------------------------------ cache
     def _kv(self, B: int, L: int):
         cfg = self.cfg
-        if self._cache is None or self._cache[0][0].shape[0] < B or self._cache[0][0].shape[1] < L:
+        first = None if self._cache is None else next((c for c in self._cache[0] if c is not None), None)
+        if self._cache is None or (first is not None and (first.shape[0] < B or first.shape[1] < L)):
             shape = (B, L, cfg.num_key_value_heads, cfg.head_dim)
             n = len(self.model.layers)
             dt = self.model.embed.dtype
-            self._cache = ([torch.empty(shape, device=self.device, dtype=dt) for _ in range(n)],
-                           [torch.empty(shape, device=self.device, dtype=dt) for _ in range(n)])
+            att = [layer.kind == "attention" for layer in self.model.layers]  # gated DeltaNet layers keep no KV
+            self._cache = ([torch.empty(shape, device=self.device, dtype=dt) if a else None for a in att],
+                           [torch.empty(shape, device=self.device, dtype=dt) if a else None for a in att])
         return self._cache
 
     # ------------------------------------------------------------------ generate
@@ -246,7 +254,29 @@ class GenerationEngine:
             vc[li][fill_slot.long(), fill_pos.long()] = vs.to(vc[li].dtype)
             return o
 
-        h = self._layers(tok_t, pos_t, attend_prefill)
+        # gated DeltaNet prefill: each distinct prompt is a root segment
+        seg = torch.tensor([u + 1 for u, x in enumerate(order) for _ in x], dtype=torch.long)
+        gdn_ctx = {"group_ids": seg, "parent_ids": seg, "gdn_finals": {}}
+        K = cfg.linear_conv_kernel_dim - 1
+        states: dict[int, dict[str, torch.Tensor]] = {}
+        seq_u = [uniq[tuple(x)] for x in prompts]
+
+        def linear_prefill(li, layer, h):
+            a = layer.gdn(h, meta, self.model.store.version, self.model.lora_enabled, gdn_ctx)
+            finals, qkv = gdn_ctx["gdn_finals"][layer.gdn.index]
+            S = torch.stack([finals[u] for u in seq_u])
+            tail = qkv.new_zeros(B, K, qkv.shape[1])
+            for b, u in enumerate(seq_u):
+                e = starts[u] + len(order[u])
+                lo = max(starts[u], e - K)
+                tail[b, K - (e - lo):] = qkv[lo:e]
+            states[li] = {"S": S, "tail": tail}
+            return a
+
+        def linear_decode(li, layer, h):
+            return layer.gdn.decode_step(h, states[li], self.model.store.version, self.model.lora_enabled)
+
+        h = self._layers(tok_t, pos_t, attend_prefill, linear_prefill)
         last = torch.tensor([starts[uniq[tuple(x)]] + len(x) - 1 for x in prompts]).to(dev)
         tok, lp = self._sample(self._logits(h.index_select(0, last)), p, gen)
         lens = torch.tensor([len(x) for x in prompts], dtype=torch.int32, device=dev)
@@ -281,7 +311,7 @@ class GenerationEngine:
                 vc[li][slots.long(), positions.long()] = v.to(vc[li].dtype)
                 return _decode_ref(q, kc[li][:B], vc[li][:B], lens, scale)
 
-            h = self._layers(tok, positions, attend_decode)
+            h = self._layers(tok, positions, attend_decode, linear_decode)
             tok, lp = self._sample(self._logits(h), p, gen)
         return results
 

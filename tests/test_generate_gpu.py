@@ -59,3 +59,30 @@ def test_engine_greedy_matches_full_recompute(cuda):
         got = torch.tensor(r.logprobs, device=cuda)
         want = lp[P - 1 : T - 1].gather(1, torch.tensor(r.token_ids, device=cuda)[:, None])[:, 0]
         assert torch.allclose(got, want, atol=5e-2), (got, want)
+
+
+def test_engine_hybrid_gated_deltanet_on_gpu(cuda):
+    from art_mlx_b200.models.config import ModelConfig
+
+    cfg = ModelConfig(
+        name="hybrid-small", family="qwen3_next", vocab_size=2048, hidden_size=256, num_hidden_layers=4,
+        num_attention_heads=2, num_key_value_heads=1, head_dim=128, intermediate_size=0, qk_norm=True,
+        full_attention_interval=2, num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
+        shared_expert_intermediate_size=128, linear_num_key_heads=2, linear_num_value_heads=2,
+        linear_key_head_dim=64, linear_value_head_dim=64, attn_output_gate=True,
+    )
+    m = DecoderLM(cfg, LoRASpec(r=8, alpha=16), cuda, seed=0)
+    eng = GenerationEngine(m, max_len=512)
+    prompts = [[1, 2, 3, 4, 5, 6, 7, 8, 9], [9, 8, 7]]
+    res = eng.generate(prompts, SamplingParams(max_tokens=6, temperature=0.0))
+    for r in res:
+        seq = r.prompt_token_ids + r.token_ids
+        T = len(seq)
+        meta = fused.AttnMeta.build(torch.arange(T), torch.full((T,), T, dtype=torch.int32), cuda)
+        with torch.no_grad():
+            h = m.forward(torch.tensor(seq, device=cuda), meta, {})
+            lp = torch.log_softmax((h @ m.lm_head.t()).float(), -1)
+        P = len(r.prompt_token_ids)
+        got = torch.tensor(r.logprobs, device=cuda)
+        want = lp[P - 1 : T - 1].gather(1, torch.tensor(r.token_ids, device=cuda)[:, None])[:, 0]
+        assert torch.allclose(got, want, atol=5e-2), (got, want)
