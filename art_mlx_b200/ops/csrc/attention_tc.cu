@@ -48,9 +48,13 @@ constexpr int OFF_P = OFF_V + KV_STAGES * TILE_BYTES;
 constexpr int OFF_BAR = OFF_P + TILE_BYTES;
 constexpr int MAX_KT = 1024;                 // key tiles per row the tile list holds (131072 keys)
 constexpr int OFF_TL = OFF_BAR + 256;        // visible key-tile list (+ count)
-constexpr int FA_SMEM = OFF_TL + MAX_KT * 4 + 16 + 1024;  // + alignment slack
+constexpr int OFF_X = OFF_TL + MAX_KT * 4 + 16;  // exchange [3][2 half][128]: row max (2 parities), row sum
+constexpr int FA_SMEM = OFF_X + 3 * 2 * FB * 4 + 1024;  // + alignment slack
 constexpr int TILE_FULL = 1 << 30;           // list flag: every (query, key) pair of the tile is visible
-constexpr int FA_THREADS = 192;
+// 2 control warps + 8 softmax warps: two warps per TMEM lane quadrant, each
+// owning 64 of a row's 128 key columns (and 64 of its 128 output columns)
+constexpr int FA_THREADS = 320;
+constexpr int FA_SOFT = 256;
 constexpr float kLog2eF = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -103,6 +107,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   uint64_t* pv_done = bars + 14;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* xbar = bars + 18;  // [4]: the two softmax warps of a lane quadrant exchange row max / sum
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * FB;  // local query row of the block
@@ -120,10 +125,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 128);
+      mbar_init(&s_empty[s], FA_SOFT);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, FA_SOFT);
     mbar_init(pv_done, 1);
+    for (int qd = 0; qd < 4; ++qd) mbar_init(&xbar[qd], 64);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -220,13 +226,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int quad = warp & 3;         // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;  // key columns (S) and output columns (O) [64*half, 64*half+64)
     const int row = quad * 32 + lane;
     const int gi = g0 + row;  // global query position of this thread's row
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    uint8_t* prow = smem + OFF_P + row * 128;
+    uint8_t* prow = smem + OFF_P + half * CHUNK_BYTES + row * 128;
+    float* xch = reinterpret_cast<float*>(smem + OFF_X);  // [slot][half][row]; slots 0/1 max, 2 sum
     const int sw = row & 7;
-    float m_ref = -INFINITY, l = 0.f;
+    float m_ref = -INFINITY, l = 0.f;  // l: this half's share of the row sum
     int n = 0;
     bool ok = true;
     for (; n < ntl; ++n) {
@@ -235,31 +243,31 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       const int b = n & 1;
       if (!mbar_wait_warp(&s_full[b], (n >> 1) & 1, abort_flag, p.err, 16)) { ok = false; break; }
       tc_fence_after();
-      float sv[FB];
+      float sv[64];
       {
-        uint32_t r[FB / 32][32];
+        uint32_t r[2][32];
 #pragma unroll
-        for (int c = 0; c < FB / 32; ++c) tmem_ld32(tmem + lane_base + b * FB + c * 32, r[c]);
+        for (int c = 0; c < 2; ++c) tmem_ld32(tmem + lane_base + b * FB + half * 64 + c * 32, r[c]);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < FB / 32; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(r[c][e]);
       }
       tc_fence_before();
       mbar_arrive(&s_empty[b]);
       // mask + scale, running max (fully visible tiles skip the mask)
-      const int k0 = kt * FB;
+      const int k0 = kt * FB + half * 64;
       float mx = -INFINITY;
       if (full_tile) {
 #pragma unroll
-        for (int c = 0; c < FB; ++c) {
+        for (int c = 0; c < 64; ++c) {
           sv[c] *= p.scale_log2;
           mx = fmaxf(mx, sv[c]);
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < FB; c += 4) {
+        for (int c = 0; c < 64; c += 4) {
           int4 ke = make_int4(0, 0, 0, 0);
           if (k0 + c + 3 < p.Tk) {
             ke = __ldg(reinterpret_cast<const int4*>(p.kend + k0 + c));
@@ -280,36 +288,41 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           }
         }
       }
+      // row max over both halves (bounded mbarrier exchange between the two warps)
+      xch[(b * 2 + half) * FB + row] = mx;
+      mbar_arrive(&xbar[quad]);
+      if (!mbar_wait_warp(&xbar[quad], n & 1, abort_flag, p.err, 19)) { ok = false; break; }
+      mx = fmaxf(mx, xch[(b * 2 + (half ^ 1)) * FB + row]);
       // P buffer and O are free once P V of the previous tile completed
       if (n > 0) {
         if (!mbar_wait_warp(pv_done, (n - 1) & 1, abort_flag, p.err, 17)) { ok = false; break; }
         tc_fence_after();
       }
       // lazy rescale: a row moves its reference max only when the tile max
-      // exceeds it by more than 2^8.  tcgen05.ld/st are warp-collective, so
-      // the O rows are rescaled by the whole warp when any of its rows needs
-      // it (alpha = 1 for the others).
+      // exceeds it by more than 2^8 (both halves decide alike: same max).
+      // tcgen05.ld/st are warp-collective, so the warp rescales its O columns
+      // when any of its rows needs it (alpha = 1 for the others).
       const bool move = mx > m_ref + kRescaleThreshold || (m_ref == -INFINITY && mx > -INFINITY);
       const bool scale_o = move && n > 0 && m_ref > -INFINITY;
       if (__any_sync(0xffffffffu, scale_o)) {
         const float alpha = scale_o ? exp2f(m_ref - mx) : 1.f;
 #pragma unroll 1
-        for (int c = 0; c < FB / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem_o + lane_base + c * 32, r);
+          tmem_ld32(tmem_o + lane_base + half * 64 + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-          tmem_st32(tmem_o + lane_base + c * 32, r);
+          tmem_st32(tmem_o + lane_base + half * 64 + c * 32, r);
         }
         tmem_wait_st();
         l *= alpha;
       }
       if (move) m_ref = mx;
-      // P = exp2(s - m_ref) as bf16 into the swizzled K-major tile
+      // P = exp2(s - m_ref) as bf16: this half's 64 keys are one swizzled K chunk
       float rs = 0.f;
 #pragma unroll
-      for (int u = 0; u < FB / 8; ++u) {
+      for (int u = 0; u < 8; ++u) {
         float e8[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -322,25 +335,31 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         pk.y = pack_bf16x2(e8[2], e8[3]);
         pk.z = pack_bf16x2(e8[4], e8[5]);
         pk.w = pack_bf16x2(e8[6], e8[7]);
-        const int chunk = u >> 3, unit = u & 7;
-        *reinterpret_cast<uint4*>(prow + chunk * CHUNK_BYTES + ((unit ^ sw) << 4)) = pk;
+        *reinterpret_cast<uint4*>(prow + ((u ^ sw) << 4)) = pk;
       }
       l += rs;
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    // epilogue: O / l and the LSE
+    // epilogue: O / l and the LSE (the two halves' sums are exchanged once more)
     const int qrow = q0 + row;
     if (ok && n > 0) {
+      xch[(4 + half) * FB + row] = l;  // own slot: the max slots may still be read by the partner
+      bool got = false;
       if (mbar_wait_warp(pv_done, (n - 1) & 1, abort_flag, p.err, 18)) {
+        mbar_arrive(&xbar[quad]);
+        got = mbar_wait_warp(&xbar[quad], n & 1, abort_flag, p.err, 20);
+      }
+      if (got) {
         tc_fence_after();
+        l += xch[(4 + (half ^ 1)) * FB + row];
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        __nv_bfloat16* dst = p.o + (int64_t)qrow * p.ldo + (int64_t)h * FB;
+        __nv_bfloat16* dst = p.o + (int64_t)qrow * p.ldo + (int64_t)h * FB + half * 64;
 #pragma unroll 1
-        for (int c = 0; c < FB / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem_o + lane_base + c * 32, r);
+          tmem_ld32(tmem_o + lane_base + half * 64 + c * 32, r);
           tmem_wait_ld();
           if (qrow < p.Tq) {
 #pragma unroll
@@ -354,13 +373,13 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             }
           }
         }
-        if (qrow < p.Tq)
+        if (qrow < p.Tq && half == 0)
           p.lse[(int64_t)h * p.Tq + qrow] = l > 0.f ? (m_ref + log2f(l)) / kLog2eF : -INFINITY;
       }
     } else if (ok && qrow < p.Tq) {  // no visible key
-      __nv_bfloat16* dst = p.o + (int64_t)qrow * p.ldo + (int64_t)h * FB;
-      for (int j = 0; j < FB; j += 8) *reinterpret_cast<uint4*>(dst + j) = make_uint4(0, 0, 0, 0);
-      p.lse[(int64_t)h * p.Tq + qrow] = -INFINITY;
+      __nv_bfloat16* dst = p.o + (int64_t)qrow * p.ldo + (int64_t)h * FB + half * 64;
+      for (int j = 0; j < 64; j += 8) *reinterpret_cast<uint4*>(dst + j) = make_uint4(0, 0, 0, 0);
+      if (half == 0) p.lse[(int64_t)h * p.Tq + qrow] = -INFINITY;
     }
   }
   tc_fence_before();
@@ -456,6 +475,10 @@ constexpr int B_OFF_P = 4 * TILE_BYTES;
 constexpr int B_OFF_DS = 5 * TILE_BYTES;
 constexpr int B_OFF_BAR = 6 * TILE_BYTES;
 constexpr int FB_SMEM = B_OFF_BAR + 256 + 1024;
+// 2 control warps + 8 softmax warps: two warps per TMEM lane quadrant, each
+// taking 64 of the 128 query columns (the backward needs no row reduction)
+constexpr int FB_THREADS = 320;
+constexpr int FB_SOFT = 256;
 
 struct FbArgs {
   const int* kend;
@@ -493,7 +516,7 @@ __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ dout, co
   if (lane == 0) delta[(int64_t)h * Tq + t] = s;
 }
 
-__global__ void __launch_bounds__(FA_THREADS, 1)
+__global__ void __launch_bounds__(FB_THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                        const FbArgs p) {
@@ -523,9 +546,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     mbar_init(qdo_full, 1);
     mbar_init(qdo_empty, 1);
     mbar_init(sdp_full, 1);
-    mbar_init(ds_full, 128);
+    mbar_init(ds_full, FB_SOFT);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 128);
+    mbar_init(dq_free, FB_SOFT);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -603,6 +626,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   } else {
     // ------------------------------------------------------------ softmax + epilogues
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // query / head-dim columns [64*half, 64*half + 64)
     const int row = quad * 32 + lane;  // TMEM lane: key row (S^T, dP^T, dK, dV) or query row (dQ)
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const int j = kb * FB + row;  // this thread's key
@@ -611,19 +635,27 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     bool ok = true;
     for (int i = 0; i < iters && ok; ++i) {
       const int h = hk * G + i / ntiles, t = t_lo + i % ntiles;
-      if (!mbar_wait_warp(sdp_full, i & 1, abort_flag, p.err, 26)) { ok = false; break; }
-      tc_fence_after();
+      // lane e fetches the LSE / delta of query column c*32+e (shared by
+      // shuffles); issued before the MMA wait so the loads overlap it
       const float* lse_h = p.lse + (int64_t)h * p.Tq;
       const float* del_h = p.delta + (int64_t)h * p.Tq;
-#pragma unroll 1
-      for (int c = 0; c < FB / 32; ++c) {
+      float lse_pf[2], del_pf[2];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int ql_mine = t * FB + (2 * half + cc) * 32 + lane;
+        lse_pf[cc] = ql_mine < p.Tq ? __ldg(lse_h + ql_mine) * kLog2eF : INFINITY;
+        del_pf[cc] = ql_mine < p.Tq ? __ldg(del_h + ql_mine) : 0.f;
+      }
+      if (!mbar_wait_warp(sdp_full, i & 1, abort_flag, p.err, 26)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * half + cc;
         uint32_t rs[32], rd[32];
         tmem_ld32(tmem + lane_base + c * 32, rs);
         tmem_ld32(tmem + lane_base + 128 + c * 32, rd);
-        // lane e fetches the LSE / delta of query c*32+e; shared by shuffles
-        const int ql_mine = t * FB + c * 32 + lane;
-        const float lse_mine = ql_mine < p.Tq ? lse_h[ql_mine] * kLog2eF : INFINITY;
-        const float del_mine = ql_mine < p.Tq ? del_h[ql_mine] : 0.f;
+        const float lse_mine = lse_pf[cc];
+        const float del_mine = del_pf[cc];
         tmem_wait_ld();
         uint32_t pp[16], dd[16];
 #pragma unroll
@@ -660,7 +692,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       tc_fence_after();
       const int ql = t * FB + row;
 #pragma unroll 1
-      for (int c = 0; c < FB / 32; ++c) {
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_base + c * 32, r);
         tmem_wait_ld();
@@ -681,7 +713,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       float* dkr = p.dk + ((int64_t)j * p.Hkv + hk) * FB;
       float* dvr = p.dv + ((int64_t)j * p.Hkv + hk) * FB;
 #pragma unroll 1
-      for (int c = 0; c < FB / 32; ++c) {
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
         uint32_t a[32], b[32];
         tmem_ld32(tmem + lane_base + 384 + c * 32, a);
         tmem_ld32(tmem + lane_base + 256 + c * 32, b);
@@ -763,7 +795,7 @@ std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torc
     ART_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM));
     attr = true;
   }
-  attn_bwd_tc_kernel<<<dim3((unsigned)n, (unsigned)Hkv), FA_THREADS, FB_SMEM, stream>>>(mq, mk, mv, mdo, a);
+  attn_bwd_tc_kernel<<<dim3((unsigned)n, (unsigned)Hkv), FB_THREADS, FB_SMEM, stream>>>(mq, mk, mv, mdo, a);
   ART_CUDA_CHECK(cudaGetLastError());
   return {dq, dk, dv};
 }
