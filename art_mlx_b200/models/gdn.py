@@ -36,6 +36,7 @@ from typing import Any
 import torch
 
 from ..ops import fused
+from ..ops import gdn as gdn_ops
 from ..ops.fused import AttnMeta, LoRABinding
 from .config import LoRASpec, ModelConfig
 from .lora import LoRAStore, peft_key
@@ -65,11 +66,11 @@ def gdn_lora_specs(cfg: ModelConfig, i: int, spec: LoRASpec) -> list[tuple[str, 
 # ---------------------------------------------------------------------------
 
 
-def chunk_summaries(q, k, v, g, beta, C: int = CHUNK):
-    """Intra-chunk quantities for sequences ``[N, L, H, d]`` (L multiple of C).
-
-    Returns per chunk (shapes ``[N, H, nc, ...]``): gq = gamma*Q, W, U0,
-    QKM = (Q K^T)*M, A = gamma_C I - Kd^T W, B = Kd^T U0."""
+def chunk_parts(q, k, v, g, beta, C: int = CHUNK):
+    """Intra-chunk operands of the scan for sequences ``[N, L, H, d]`` (L a
+    multiple of C), all batched over chunks.  Returns (shapes ``[N, H, nc,
+    ...]``) gq = gamma*Q, W, U0, QKM = (Q K^T)*M, Kd = exp(G_C - G)*K and
+    gC = gamma_C ``[N, H, nc]``."""
     N, L, Hh, dk = k.shape
     dv = v.shape[-1]
     nc = L // C
@@ -89,33 +90,36 @@ def chunk_summaries(q, k, v, g, beta, C: int = CHUNK):
     W = Tinv @ ((bt * gamma).unsqueeze(-1) * K)
     U0 = Tinv @ (bt.unsqueeze(-1) * V)
     QKM = (Q @ K.transpose(-1, -2)) * decay
-    gC = gamma[..., -1:]  # [N,H,nc,1]
     Kd = torch.exp(G[..., -1:] - G).unsqueeze(-1) * K  # [N,H,nc,C,dk]
-    A = gC.unsqueeze(-1) * torch.eye(dk, dtype=k.dtype, device=k.device) - Kd.transpose(-1, -2) @ W
+    return gamma.unsqueeze(-1) * Q, W, U0, QKM, Kd, gamma[..., -1]
+
+
+def chunk_summaries(q, k, v, g, beta, C: int = CHUNK):
+    """:func:`chunk_parts` with each chunk's affine map instead of (Kd, gC):
+    returns gq, W, U0, QKM, A = gamma_C I - Kd^T W, B = Kd^T U0."""
+    gq, W, U0, QKM, Kd, gC = chunk_parts(q, k, v, g, beta, C)
+    dk = W.shape[-1]
+    A = gC[..., None, None] * torch.eye(dk, dtype=W.dtype, device=W.device) - Kd.transpose(-1, -2) @ W
     B = Kd.transpose(-1, -2) @ U0
-    return gamma.unsqueeze(-1) * Q, W, U0, QKM, A, B
+    return gq, W, U0, QKM, A, B
 
 
 def delta_rule(q, k, v, g, beta, S0=None, C: int = CHUNK):
     """Chunked gated delta rule.  Inputs ``[N, L, H, d]``, ``g``/``beta``
     ``[N, L, H]``, optional initial state ``[N, H, dk, dv]``.  Returns
     ``(o [N, L, H, dv], S_end)``.  Lengths are padded to ``C`` internally
-    (padded steps: g=0, beta=0, k=0, which leave the state unchanged)."""
+    (padded steps: g=0, beta=0, k=0, which leave the state unchanged).  The
+    intra-chunk operands are batched GEMMs; the chunk recurrence is the
+    ``gdn_scan`` kernel on CUDA."""
     N, L, Hh, dk = k.shape
     dv = v.shape[-1]
     pad = (-L) % C
     if pad:
         P = lambda t: torch.nn.functional.pad(t, (0, 0, 0, 0, 0, pad)) if t.dim() == 4 else torch.nn.functional.pad(t, (0, 0, 0, pad))  # noqa: E731
         q, k, v, g, beta = P(q), P(k), P(v), P(g), P(beta)
-    gq, W, U0, QKM, A, B = chunk_summaries(q, k, v, g, beta, C)
+    gq, W, U0, QKM, Kd, gC = chunk_parts(q, k, v, g, beta, C)
     nc = gq.shape[2]
-    S = S0 if S0 is not None else q.new_zeros(N, Hh, dk, dv)
-    outs = []
-    for c in range(nc):
-        U = U0[:, :, c] - W[:, :, c] @ S
-        outs.append(gq[:, :, c] @ S + QKM[:, :, c] @ U)
-        S = A[:, :, c] @ S + B[:, :, c]
-    o = torch.stack(outs, dim=2)  # [N,H,nc,C,dv]
+    o, S = gdn_ops.scan(gq, W, U0, QKM, Kd, gC, S0)
     o = o.permute(0, 2, 3, 1, 4).reshape(N, nc * C, Hh, dv)[:, :L]
     return o, S
 
@@ -193,7 +197,10 @@ class TreePlan:
                 self.levels.append([])
             self.levels[d].append(n)
         prev = sequence_predecessors(segs, T, width)
-        self.prev = prev.to(meta.kend.device, non_blocking=True)
+        dev = meta.kend.device
+        self.prev = prev.to(dev, non_blocking=True)
+        # inverse table for the conv backward kernel (CUDA only)
+        self.succ = gdn_ops.successors(prev, dev) if dev.type == "cuda" else None
 
 
 def causal_conv(x: torch.Tensor, w: torch.Tensor, prev: torch.Tensor) -> torch.Tensor:
@@ -278,13 +285,17 @@ class GatedDeltaNet:
         g = -torch.exp(self.A_log) * torch.nn.functional.softplus(a + self.dt_bias)
         return qkvz[:, : 2 * kd + vd], qkvz[:, 2 * kd + vd :], g, beta
 
-    def core_inputs(self, qkv, plan_prev):
-        return self.post_conv(causal_conv(qkv, self.conv_w, plan_prev))
+    def core_inputs(self, qkv, plan_prev, succ=None):
+        """Tree causal conv + SiLU (one kernel on CUDA), then the head split."""
+        return self.split_heads(gdn_ops.conv_silu(qkv, self.conv_w, plan_prev, succ))
 
     def post_conv(self, x):
         """SiLU after the causal conv, split into q, k, v heads, L2-normalised q / k."""
+        return self.split_heads(torch.nn.functional.silu(x.float()))
+
+    def split_heads(self, x):
+        """Split the activated conv output into q, k, v heads; L2-normalised q / k."""
         kd, T = self.kd, x.shape[0]
-        x = torch.nn.functional.silu(x.float())
         q = x[:, :kd].view(T, self.nk, self.dk)
         k = x[:, kd : 2 * kd].view(T, self.nk, self.dk)
         v = x[:, 2 * kd :].view(T, self.nv, self.dv)
@@ -334,7 +345,7 @@ class GatedDeltaNet:
                             self.cfg.linear_conv_kernel_dim)
             ctx["gdn_plan"] = plan
         qkv, z, g, beta = self.mix(h, version, enabled)
-        q, k, v = self.core_inputs(qkv, plan.prev)
+        q, k, v = self.core_inputs(qkv, plan.prev, plan.succ)
         q, k = self.expand_heads(q, k)
         finals = ctx.get("gdn_finals")
         out_finals = {} if finals is not None else None

@@ -72,6 +72,15 @@ void scatter_rows_idx(torch::Tensor src, torch::Tensor src_idx, torch::Tensor ds
 void gather_rows(torch::Tensor dst, c10::optional<torch::Tensor> src_rank, torch::Tensor src_row,
                  c10::optional<torch::Tensor> scale, torch::Tensor bases, int64_t ld_src);
 torch::Tensor combine_rows(torch::Tensor slots, c10::optional<torch::Tensor> w, int64_t k);
+std::vector<torch::Tensor> gdn_scan_fwd(torch::Tensor gq, torch::Tensor W, torch::Tensor U0, torch::Tensor QKM,
+                                        torch::Tensor Kd, torch::Tensor gC, c10::optional<torch::Tensor> S0,
+                                        bool want_out, bool save, c10::optional<torch::Tensor> peer_out);
+std::vector<torch::Tensor> gdn_scan_bwd(c10::optional<torch::Tensor> dO, c10::optional<torch::Tensor> dS_end,
+                                        torch::Tensor gq, torch::Tensor W, torch::Tensor QKM, torch::Tensor Kd,
+                                        torch::Tensor gC, int64_t DV);
+torch::Tensor gdn_conv_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor prev);
+std::vector<torch::Tensor> gdn_conv_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor prev,
+                                        torch::Tensor succ_ptr, torch::Tensor succ_idx, torch::Tensor succ_tap);
 }  // namespace art
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -116,4 +125,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_reduce_sumsq", &art::dp_reduce_sumsq);
   m.def("dp_publish_norm", &art::dp_publish_norm);
   m.def("dp_adamw_allgather", &art::dp_adamw_allgather);
+  m.def("gdn_scan_fwd", &art::gdn_scan_fwd, py::arg("gq"), py::arg("W"), py::arg("U0"), py::arg("QKM"),
+        py::arg("Kd"), py::arg("gC"), py::arg("S0") = py::none(), py::arg("want_out") = true,
+        py::arg("save") = false, py::arg("peer_out") = py::none());
+  m.def("gdn_scan_bwd", &art::gdn_scan_bwd, py::arg("dO"), py::arg("dS_end"), py::arg("gq"), py::arg("W"),
+        py::arg("QKM"), py::arg("Kd"), py::arg("gC"), py::arg("DV"));
+  m.def("gdn_conv_fwd", &art::gdn_conv_fwd);
+  m.def("gdn_conv_bwd", &art::gdn_conv_bwd);
 }

@@ -35,12 +35,60 @@ import torch.distributed as dist
 from ..ops import fused, native
 
 
+CP_BARRIER_TIMEOUT_NS = 60 * 10**9
+
+
 class CPContext:
-    def __init__(self, group: dist.ProcessGroup | None, device: torch.device) -> None:
+    """Context-parallel group.  Transport ``"p2p"`` (CUDA, world > 1): the
+    gated DeltaNet summary exchange is fused into the summary scan, whose
+    epilogue stores each piece's ``[A | B]`` into every rank's peer-mapped
+    receive slot; ``"nccl"``: an all-gather (also the gloo CPU path)."""
+
+    def __init__(self, group: dist.ProcessGroup | None, device: torch.device, transport: str | None = None) -> None:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         self.device = device
+        if transport is None:
+            transport = "p2p" if device.type == "cuda" and self.world > 1 else "nccl"
+        self.transport = transport
+        self.arena = None
+        self._turn_bytes = 0
+        self._turn = 0
+        self.epoch = 0
+        self.status = torch.zeros(1, dtype=torch.int32, device=device) if transport == "p2p" else None
+
+    def exchange_region(self, nbytes: int) -> int:
+        """Byte offset of this call's receive region (two regions alternate, so
+        a fast rank never overwrites data a slow rank has yet to read: it
+        must pass the barrier of the call in between first).  Collective:
+        every rank calls it in the same order with the same size."""
+        from .dp import PeerArena, _round
+
+        need = _round(nbytes)
+        if self.arena is None or need > self._turn_bytes:
+            if self.arena is not None:
+                torch.cuda.current_stream(self.device).synchronize()
+                dist.barrier(group=self.group)
+                self.arena.close()
+            self._turn_bytes = need
+            self.arena = PeerArena(2 * need + 256, self.group, self.device)
+            self.flag_tab = self.arena.table(2 * need)
+            self.arena.buf[2 * need :].zero_()
+            self.epoch = 0
+            dist.barrier(group=self.group)
+        off = self._turn * self._turn_bytes
+        self._turn ^= 1
+        return off
+
+    def barrier(self) -> None:
+        self.epoch += 1
+        native.lib().peer_barrier(self.flag_tab, self.rank, self.world, self.epoch, CP_BARRIER_TIMEOUT_NS,
+                                  self.status)
+
+    def check(self) -> None:
+        if self.status is not None and int(self.status.item()) != 0:
+            raise RuntimeError("context-parallel peer barrier timed out")
 
     def all_gather(self, x: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
@@ -76,6 +124,24 @@ class _Gather(torch.autograd.Function):
 def gather(x: torch.Tensor, cp: CPContext) -> torch.Tensor:
     """Differentiable all-gather along dim 0 (backward: reduce-scatter)."""
     return _Gather.apply(x, cp)
+
+
+class _ArenaGather(torch.autograd.Function):
+    """The receive side of the fused summary exchange: the scan epilogues have
+    already stored every rank's rows into this rank's arena region; after the
+    peer barrier the region is the all-gathered stack.  Backward: the
+    reduce-scatter of the gathered gradient, as for :func:`gather`."""
+
+    @staticmethod
+    def forward(ctx, local, cp, off):
+        ctx.cp = cp
+        cp.barrier()
+        n = local.numel() * cp.world
+        return cp.arena.view(off, n, torch.float32).view(-1, *local.shape[1:]).clone()
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.cp.reduce_scatter(g.contiguous()), None, None
 
 
 @dataclass
@@ -171,6 +237,15 @@ class CPPlan:
         prev = torch.where(loc < 0, torch.full_like(loc, -1), prev)
         assert bool((prev[(loc >= 0) & ~inside] >= self.rows).all()), "conv predecessor outside every piece tail"
         self.conv_prev = prev.to(dev)
+        # predecessor table of [local rows | gathered tails] and its inverse
+        ext_prev = torch.cat([prev, torch.full((W * self.max_local * K, K), -1, dtype=torch.int64)])
+        self.ext_prev = ext_prev.to(dev)
+        if dev.type == "cuda":
+            from ..ops.gdn import successors
+
+            self.ext_succ = successors(ext_prev, dev)
+        else:
+            self.ext_succ = None
 
 
 # ---------------------------------------------------------------------------
@@ -264,7 +339,8 @@ def _dense_cp_attention(q, k, v, kend, q_off, scale):
 
 
 def compose(A: torch.Tensor, B: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Compose per-chunk maps ``S -> A_c S + B_c`` over the chunk axis (dim 2)."""
+    """Compose per-chunk maps ``S -> A_c S + B_c`` over the chunk axis (dim 2)
+    (a plain-PyTorch oracle of :func:`art_mlx_b200.ops.gdn.summary_scan`)."""
     Acc, Bcc = A[:, :, 0], B[:, :, 0]
     for c in range(1, A.shape[2]):
         Acc = A[:, :, c] @ Acc
@@ -273,27 +349,34 @@ def compose(A: torch.Tensor, B: torch.Tensor) -> tuple[torch.Tensor, torch.Tenso
 
 
 def cp_gdn(layer, h: torch.Tensor, plan: CPPlan, cp: CPContext, version: int, enabled: bool) -> torch.Tensor:
-    from ..models.gdn import CHUNK, chunk_summaries
+    """Gated DeltaNet over this rank's slice of a packed row (reference
+    ``src/art/megatron/gdn/fla_cp.py:315-580``): local pieces of every tree
+    segment collapse into affine summaries ``[A | B]`` (the summary scan),
+    the summaries are exchanged (fused into the scan epilogue over NVLink on
+    the p2p transport), the tree recurrence is resolved in pre-order, and
+    each local piece is scanned from its true initial state."""
+    from ..models.gdn import CHUNK, chunk_parts
+    from ..ops import gdn as gdn_ops
 
     qkv, z, g, beta = layer.mix(h, version, enabled)
     T = qkv.shape[0]
-    K = plan.K
     # cross-rank conv predecessors: every rank publishes its pieces' last tokens
     tr = plan.tail_rows
     tails = qkv.index_select(0, tr.clamp_min(0)) * (tr >= 0).unsqueeze(1).to(qkv.dtype)
     ext = torch.cat([qkv, gather(tails.contiguous(), cp)], dim=0)
-    ext_prev = torch.cat([plan.conv_prev, torch.full((ext.shape[0] - T, K), -1, dtype=torch.int64,
-                                                     device=qkv.device)])
-    q, k, v = layer.core_inputs(ext, ext_prev)
+    q, k, v = layer.core_inputs(ext, plan.ext_prev, plan.ext_succ)
     q, k, v = q[:T], k[:T], v[:T].float()
     if layer.nv != layer.nk:
         rep = layer.nv // layer.nk
         q, k = q.repeat_interleave(rep, dim=1), k.repeat_interleave(rep, dim=1)
     Hh, dk, dv = k.shape[1], k.shape[2], v.shape[2]
-    # local pieces: intra-chunk quantities and their composite affine maps
+    fused_x = cp.transport == "p2p"
+    slot_numel = Hh * dk * (dk + dv)
+    off = cp.exchange_region(cp.world * plan.max_local * slot_numel * 4) if fused_x else 0
+    # local pieces: intra-chunk operands and their affine summaries
     local_data = []
-    As, Bs = [], []
-    for gi in plan.local:
+    summs = []
+    for j, gi in enumerate(plan.local):
         pc = plan.pieces[gi]
         s, e = pc.start - plan.a, pc.end - plan.a
         pad = (-(e - s)) % CHUNK
@@ -303,16 +386,15 @@ def cp_gdn(layer, h: torch.Tensor, plan: CPPlan, cp: CPContext, version: int, en
             t = torch.nn.functional.pad(t, (0, 0) * (t.dim() - 1) + (0, pad))
             return t.unsqueeze(0)
 
-        parts = chunk_summaries(cut(q), cut(k), cut(v), cut(g), cut(beta), CHUNK)
-        A, B = compose(parts[4], parts[5])
-        As.append(A[0])
-        Bs.append(B[0])
+        parts = chunk_parts(cut(q), cut(k), cut(v), cut(g), cut(beta), CHUNK)
+        _, Wm, U0, _, Kd, gC = parts
+        peer_out = cp.arena.table(off + (cp.rank * plan.max_local + j) * slot_numel * 4) if fused_x else None
+        summs.append(gdn_ops.summary_scan(Wm, U0, Kd, gC, peer_out)[0])
         local_data.append((s, e, parts))
-    while len(As) < plan.max_local:  # padding slots (never read)
-        As.append(torch.eye(dk, device=q.device, dtype=q.dtype).expand(Hh, dk, dk))
-        Bs.append(q.new_zeros(Hh, dk, dv))
-    summ = torch.cat([torch.stack(As), torch.stack(Bs)], dim=-1)  # [P, H, dk, dk+dv]
-    allsumm = gather(summ.contiguous(), cp)
+    while len(summs) < plan.max_local:  # padding slots (never read)
+        summs.append(q.new_zeros(Hh, dk, dk + dv))
+    summ = torch.stack(summs)  # [P, H, dk, dk+dv]
+    allsumm = _ArenaGather.apply(summ, cp, off) if fused_x else gather(summ.contiguous(), cp)
     # resolve the tree recurrence over all pieces in pre-order
     S_out: list[torch.Tensor] = []
     S_in: list[torch.Tensor] = []
@@ -324,13 +406,7 @@ def cp_gdn(layer, h: torch.Tensor, plan: CPPlan, cp: CPContext, version: int, en
     # local outputs
     out = q.new_zeros(T, Hh, dv)
     for (s, e, parts), gi in zip(local_data, plan.local):
-        gq, Wm, U0, QKM, A, B = parts
-        S = S_in[gi].unsqueeze(0)
-        outs = []
-        for c in range(gq.shape[2]):
-            U = U0[:, :, c] - Wm[:, :, c] @ S
-            outs.append(gq[:, :, c] @ S + QKM[:, :, c] @ U)
-            S = A[:, :, c] @ S + B[:, :, c]
-        o = torch.stack(outs, 2).permute(0, 2, 3, 1, 4).reshape(-1, Hh, dv)[: e - s]
+        o, _ = gdn_ops.scan(*parts, S_in[gi].unsqueeze(0))
+        o = o.permute(0, 2, 3, 1, 4).reshape(-1, Hh, dv)[: e - s]
         out = out.index_copy(0, torch.arange(s, e, device=q.device), o)
     return layer.finish(out, z, version, enabled, h.dtype)

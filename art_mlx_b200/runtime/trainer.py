@@ -338,6 +338,8 @@ class GRPOTrainer:
     def check_health(self) -> None:
         if self.grad_sync is not None:
             self.grad_sync.check()
+        if self.cp is not None:
+            self.cp.check()
 
     def set_reference_adapter(self, state: Mapping[str, torch.Tensor] | None) -> None:
         """Use a saved adapter (PEFT state dict) as the KL reference; ``None``

@@ -97,3 +97,37 @@ def test_hybrid_model_packed_matches_independent():
         ref = torch.log_softmax(hi @ m.lm_head.t(), -1)
         pos = pack.positions_by_sequence[n]
         assert torch.allclose(logp[pos[:-1], s[1:]], ref[torch.arange(L - 1), s[1:]], atol=1e-9)
+
+
+def test_summary_scan_matches_composed_chunk_maps():
+    from art_mlx_b200.models.gdn import chunk_parts, chunk_summaries
+    from art_mlx_b200.ops.gdn import summary_scan
+    from art_mlx_b200.parallel.cp import compose
+
+    q, k, v, g, b = _inputs(2, 96, 3, 16, 8)
+    _, W, U0, _, Kd, gC = chunk_parts(q, k, v, g, b, C=32)
+    AB = summary_scan(W, U0, Kd, gC)
+    parts = chunk_summaries(q, k, v, g, b, C=32)
+    A, B = compose(parts[4], parts[5])
+    assert torch.allclose(AB[..., :16], A, atol=1e-10)
+    assert torch.allclose(AB[..., 16:], B, atol=1e-10)
+
+
+def test_conv_successor_table_inverts_predecessors():
+    from art_mlx_b200.models.gdn import sequence_predecessors
+    from art_mlx_b200.ops.gdn import successors
+
+    segs = [(0, 10, -1), (10, 12, 0), (12, 20, 0), (20, 23, 1)]
+    prev = sequence_predecessors(segs, 23, 4)
+    ptr, idx, tap = successors(prev, torch.device("cpu"))
+    seen = set()
+    for j in range(23):
+        for e in range(int(ptr[j]), int(ptr[j + 1])):
+            i, t = int(idx[e]), int(tap[e])
+            if t == 0:
+                assert i == j
+            else:
+                assert int(prev[i, t - 1]) == j
+            seen.add((i, t))
+    want = {(i, 0) for i in range(23)} | {(i, m + 1) for i in range(23) for m in range(3) if prev[i, m] >= 0}
+    assert seen == want
