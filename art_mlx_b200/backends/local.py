@@ -37,7 +37,6 @@ from ..backend import aggregate_rl_training_metrics, build_rl_train_configs
 from ..metrics import MetricsBuilder
 from ..models.config import LoRASpec, get_config
 from ..preprocessing.pack import packed_tensors_from_tokenized_results, packed_tensors_to_dir
-from ..preprocessing.prefix_tree import estimate_prefix_tree_packed_tokens
 from ..preprocessing.tokenize import TokenizedResult, tokenize_trajectory_groups
 from ..runtime.checkpoint import AsyncCheckpointWriter, load_adapter, save_adapter
 from ..runtime.trainer import GRPOTrainer
@@ -276,6 +275,8 @@ class LocalBackend:
         advantage_balance: float,
     ) -> dict[str, Any]:
         if packed_sequence_length is None:
+            from ..preprocessing.prefix_tree import _plan_segments
+
             # one prompt group per row at least: the row length is the largest
             # prefix-tree-packed group, rounded up to 128
             by_prompt: dict[int, list[TokenizedResult]] = {}
@@ -283,11 +284,9 @@ class LocalBackend:
                 by_prompt.setdefault(r.prompt_id, []).append(r)
             longest = 0
             for rs in by_prompt.values():
-                n = estimate_prefix_tree_packed_tokens(
-                    (torch.tensor(r.token_ids) for r in rs), max_depth=1 << 30,
-                    shareable_lengths=[r.prompt_length for r in rs],
-                )
-                longest = max(longest, int(n or 0))
+                segs = _plan_segments([r.token_ids for r in rs], 1 << 30,
+                                      [max(0, min(r.prompt_length, len(r.token_ids))) for r in rs])
+                longest = max(longest, sum(s.end - s.start for s in segs))
             packed_sequence_length = max(128, (longest + 127) // 128 * 128)
         return packed_tensors_from_tokenized_results(
             results, packed_sequence_length, advantage_balance=advantage_balance,
@@ -390,6 +389,7 @@ class LocalBackend:
             return LocalTrainResult(step=new_step, metrics=base_metrics, checkpoint_path=ck if save_checkpoint else None)
 
         packed = self._pack(results, packed_sequence_length, advantage_balance)
+        t_prepared = time.monotonic()
         if plot_tensors and _rank() == 0:
             packed_tensors_to_dir(packed, os.path.join(d, "tensors"))
         new_step = step + 1
@@ -399,6 +399,7 @@ class LocalBackend:
             logprob_calculation_chunk_size, ck if save_checkpoint else None, grad_accumulation_sequences,
         )
         metrics["time/step_trainer_s"] = time.monotonic() - started
+        metrics["time/step_prepare_s"] = t_prepared - started
         metrics.setdefault("data/step_num_gradient_steps", 1.0)
         builder = self._metrics.setdefault(model.name, MetricsBuilder())
         metrics = builder.update(metrics)
@@ -439,15 +440,21 @@ class LocalBackend:
                 metrics["data/step_num_gradient_steps"] = float(len(steps))
                 self.last_h2d_bytes = 0
             else:
+                t0 = time.monotonic()
                 mbs = tr.stage(packed)
                 self.last_h2d_bytes = sum(mb.h2d_bytes for mb in mbs)
+                t1 = time.monotonic()
                 metrics = tr.train_step(packed, lr, dev_config, micro_batches=mbs).to_host()
+                metrics["time/step_stage_s"] = t1 - t0
+                metrics["time/step_compute_s"] = time.monotonic() - t1
         self.last_d2h_bytes = 5 * 4
+        t2 = time.monotonic()
         if out_dir is not None:
             tr.prepare_checkpoint()
             if _rank() == 0:
-                self._writer.submit(out_dir, tr.store, model.base_model, tr.model.lora_spec, tr.optim.state_dict())
+                self._writer.submit(out_dir, tr.store, model.base_model, tr.model.lora_spec)
         _barrier()
+        metrics["time/step_checkpoint_s"] = time.monotonic() - t2
         return metrics
 
     # ------------------------------------------------------------------

@@ -28,7 +28,7 @@ import numpy as np
 import torch
 from typing_extensions import NotRequired
 
-from .prefix_tree import estimate_prefix_tree_packed_tokens, prefix_tree_pack
+from .prefix_tree import estimate_prefix_tree_packed_tokens, prefix_tree_layout, prefix_tree_pack
 from .tokenize import TokenizedResult
 
 
@@ -90,19 +90,24 @@ class _Item(NamedTuple):
 
 
 def _first_trainable(r: TokenizedResult) -> int:
-    for i, (m, lp) in enumerate(zip(r.assistant_mask, r.logprobs)):
-        if m or not math.isnan(float(lp)):
-            return i
-    return len(r.token_ids)
+    n = min(len(r.assistant_mask), len(r.logprobs))
+    m = np.asarray(r.assistant_mask[:n], dtype=bool)
+    lp = np.asarray(r.logprobs[:n], dtype=np.float64)
+    hit = np.flatnonzero(m | ~np.isnan(lp))
+    return int(hit[0]) if hit.size else len(r.token_ids)
+
+
+def _ints(v: Any) -> tuple:
+    return tuple(v.tolist()) if isinstance(v, np.ndarray) else tuple(v)
 
 
 def _item(r: TokenizedResult, seq_len: int) -> _Item:
     share = min(int(r.prompt_length), max(_first_trainable(r) - 1, 0))
     it = _Item(
-        tuple(map(int, r.token_ids)),
-        tuple(map(int, r.input_pos)),
-        tuple(map(int, r.assistant_mask)),
-        tuple(map(float, r.logprobs)),
+        _ints(r.token_ids),
+        _ints(r.input_pos),
+        _ints(r.assistant_mask),
+        _ints(r.logprobs),
         float(r.advantage),
         float(r.weight),
         int(r.prompt_id),
@@ -138,14 +143,12 @@ def _row_len(row: list[_Item], seq_len: int) -> int:
 def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
     if not row:
         return {k: [] for k in ("tokens", "group_ids", "parent_ids", "input_pos", "assistant_mask", "logprobs", "advantages", "weights", "routes")}
-    tree = prefix_tree_pack(
-        (torch.tensor(i.token_ids, dtype=torch.long) for i in row),
-        max_depth=seq_len if share else 0,
-        shareable_lengths=(i.shareable if share else 0 for i in row),
+    toks, tree_gids, tree_pids, _, per_seq = prefix_tree_layout(
+        [i.token_ids for i in row], seq_len if share else 0,
+        [max(0, min(i.shareable, len(i.token_ids))) if share else 0 for i in row],
     )
     # every packed slot belongs to the first sequence that reaches it; later
     # sequences sharing the slot must agree on it (vectorised per sequence)
-    toks = tree.tokens.reshape(-1).numpy()
     n = len(toks)
     owned = np.zeros(n, dtype=bool)
     pos = np.zeros(n, dtype=np.int64)
@@ -155,7 +158,7 @@ def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
     w = np.zeros(n, dtype=np.float64)
     routes: list[Any] = [None] * n
     for k, it in enumerate(row):
-        dst = tree.positions_by_sequence[k].numpy()
+        dst = per_seq[k]
         m = len(dst)
         tk = np.asarray(it.token_ids[:m], dtype=np.int64)
         if (toks[dst] != tk).any():
@@ -183,8 +186,8 @@ def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
                     routes[int(dst[src])] = it.routes[src]
     return {
         "tokens": toks[:seq_len],
-        "group_ids": tree.group_ids.reshape(-1).numpy()[:seq_len],
-        "parent_ids": tree.parent_ids.reshape(-1).numpy()[:seq_len],
+        "group_ids": tree_gids[:seq_len],
+        "parent_ids": tree_pids[:seq_len],
         "input_pos": pos[:seq_len],
         "assistant_mask": mask[:seq_len],
         "logprobs": lps[:seq_len],

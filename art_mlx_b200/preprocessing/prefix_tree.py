@@ -18,6 +18,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import Iterable, Sequence
 
+import numpy as np
 import torch
 
 
@@ -118,6 +119,33 @@ def _limits(tensors: Sequence[torch.Tensor], limits: Iterable[int] | None) -> li
     return [max(0, min(v, int(t.numel()))) for v, t in zip(vals, tensors)]
 
 
+def prefix_tree_layout(
+    rows: Sequence[Sequence[int]], max_depth: int, share_limits: Sequence[int]
+) -> tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray, list[np.ndarray]]:
+    """Packed layout of token sequences (lists or tuples) as numpy arrays:
+    ``(tokens, group_ids, parent_ids, position_ids, positions_by_sequence)``."""
+    segs = _plan_segments(rows, max_depth, share_limits)
+    n_total = sum(s.end - s.start for s in segs)
+    toks = np.empty(n_total, np.int64)
+    gids = np.empty(n_total, np.int64)
+    pids = np.empty(n_total, np.int64)
+    pos = np.empty(n_total, np.int64)
+    per_seq: list[list[np.ndarray]] = [[] for _ in rows]
+    base = 0
+    for s in segs:
+        n = s.end - s.start
+        toks[base : base + n] = rows[s.members[0]][s.start : s.end]
+        gids[base : base + n] = s.group_id
+        pids[base : base + n] = s.parent_id
+        pos[base : base + n] = np.arange(s.start, s.end)
+        span = np.arange(base, base + n, dtype=np.int64)
+        for m in s.members:
+            per_seq[m].append(span)
+        base += n
+    seqs = [np.concatenate(p) if p else np.zeros(0, np.int64) for p in per_seq]
+    return toks, gids, pids, pos, seqs
+
+
 def prefix_tree_pack(
     sequences: Iterable[torch.Tensor],
     *,
@@ -136,28 +164,14 @@ def prefix_tree_pack(
         e = torch.empty(1, 0, dtype=torch.long)
         return PrefixTreePack(e, e, e, e, ())
     rows = [t.tolist() for t in tensors]
-    segs = _plan_segments(rows, max_depth, _limits(tensors, shareable_lengths))
-    toks: list[int] = []
-    gids: list[int] = []
-    pids: list[int] = []
-    pos: list[int] = []
-    per_seq: list[list[int]] = [[] for _ in tensors]
-    for s in segs:
-        base = len(toks)
-        n = s.end - s.start
-        toks.extend(rows[s.members[0]][s.start : s.end])
-        gids.extend([s.group_id] * n)
-        pids.extend([s.parent_id] * n)
-        pos.extend(range(s.start, s.end))
-        for m in s.members:
-            per_seq[m].extend(range(base, base + n))
-    as_row = lambda v: torch.tensor(v, dtype=torch.long).unsqueeze(0)  # noqa: E731
+    toks, gids, pids, pos, per_seq = prefix_tree_layout(rows, max_depth, _limits(tensors, shareable_lengths))
+    as_row = lambda v: torch.from_numpy(v).unsqueeze(0)  # noqa: E731
     return PrefixTreePack(
         tokens=as_row(toks),
         group_ids=as_row(gids),
         parent_ids=as_row(pids),
         position_ids=as_row(pos),
-        positions_by_sequence=tuple(torch.tensor(p, dtype=torch.long) for p in per_seq),
+        positions_by_sequence=tuple(torch.from_numpy(p) for p in per_seq),
     )
 
 

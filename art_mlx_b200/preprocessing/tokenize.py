@@ -21,9 +21,9 @@ from __future__ import annotations
 import math
 import random
 from dataclasses import dataclass, field
-from itertools import takewhile
 from typing import Any, Generator, Iterable, Literal
 
+import numpy as np
 import torch
 
 from ..trajectories import History, Trajectory, TrajectoryGroup, get_messages
@@ -216,6 +216,24 @@ def group_advantages(rewards: list[float], scale_rewards: bool) -> list[float]:
     return out
 
 
+def _common_prefix_len(rows: list) -> int:
+    """Length of the prefix shared by every token sequence."""
+    n = min(len(r) for r in rows)
+    first = np.asarray(rows[0][:n], dtype=np.int64)
+    common = n
+    for r in rows[1:]:
+        diff = np.flatnonzero(np.asarray(r[:common], dtype=np.int64) != first[:common])
+        if diff.size:
+            common = int(diff[0])
+    return common
+
+
+def _first_sampled(logprobs) -> int:
+    """Index of the first token with a logprob (the first sampled token)."""
+    hit = np.flatnonzero(~np.isnan(np.asarray(logprobs, dtype=np.float64)))
+    return int(hit[0]) if hit.size else len(logprobs)
+
+
 def tokenize_trajectory_groups(
     tokenizer: Any,
     trajectory_groups: Iterable[TrajectoryGroup],
@@ -255,13 +273,8 @@ def tokenize_trajectory_groups(
         if not results:
             continue
         prompt_id = randint(-(2**63), 2**63 - 1)
-        common = len(
-            list(takewhile(lambda col: len(set(col)) == 1, zip(*(r.token_ids for r in results))))
-        )
-        first_sampled = min(
-            next((i for i, v in enumerate(r.logprobs) if not math.isnan(v)), len(r.logprobs))
-            for r in results
-        )
+        common = _common_prefix_len([r.token_ids for r in results])
+        first_sampled = min(_first_sampled(r.logprobs) for r in results)
         prompt_length = max(min(common, first_sampled) - 1, 0)
         for r in results:
             r.prompt_id = prompt_id

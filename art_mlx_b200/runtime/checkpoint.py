@@ -104,25 +104,102 @@ def _write_optimizer(path: str, optimizer_state: dict) -> None:
     os.replace(tmp, os.path.join(path, "optimizer.pt"))
 
 
+class _PinnedSlot:
+    """Host copy of a store's flat master weights and AdamW moments."""
+
+    def __init__(self, numel: int, pin: bool) -> None:
+        mk = lambda: torch.empty(numel, dtype=torch.float32, pin_memory=pin)  # noqa: E731
+        self.master, self.exp_avg, self.exp_avg_sq = mk(), mk(), mk()
+        self.pending = None  # the optimizer write still reading this slot
+
+
+def write_safetensors_from_flat(path: str, flat: torch.Tensor, entries: dict,
+                                metadata: dict[str, str] | None = None) -> None:
+    """Write the entries of a flat fp32 host buffer as a safetensors file
+    (8-byte little-endian header length, JSON header with dtype / shape /
+    data offsets, then the raw tensor bytes) straight from the buffer: no
+    per-tensor copies.  Tensors are stored in name order."""
+    import struct
+
+    header: dict[str, Any] = {"__metadata__": dict(metadata or {"format": "pt"})}
+    names = sorted(entries)
+    off = 0
+    for name in names:
+        e = entries[name]
+        nbytes = e.numel * 4
+        header[name] = {"dtype": "F32", "shape": list(e.shape), "data_offsets": [off, off + nbytes]}
+        off += nbytes
+    hb = json.dumps(header, separators=(",", ":")).encode()
+    hb += b" " * ((-len(hb)) % 8)
+    arr = flat.numpy()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hb)))
+        f.write(hb)
+        for name in names:
+            e = entries[name]
+            f.write(memoryview(arr[e.offset : e.offset + e.numel]))
+
+
 class AsyncCheckpointWriter:
-    """Publishes the adapter of a step at once (the rollout side may load it
-    immediately) and writes the optimizer state, which only a resume reads,
-    on one background thread so that its file I/O overlaps the next step.
-    Both files appear atomically (stage + rename); ``wait()`` returns once
-    every submitted write is on disk and re-raises a write error."""
+    """Checkpoint publishing with the least work on the training path.
+
+    ``submit`` snapshots the store's flat master weights and AdamW moments
+    with one device-to-host copy each into pinned host memory (two slots
+    alternate), publishes the adapter at once (``adapter_model.safetensors``
+    written straight from the pinned buffer, ``adapter_config.json``, stage +
+    rename), and writes ``optimizer.pt`` (read only by a resume) on one
+    background thread.  ``wait()`` returns once every submitted write is on
+    disk and re-raises a write error."""
 
     def __init__(self) -> None:
         from concurrent.futures import ThreadPoolExecutor
 
         self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="ckpt-writer")
         self._pending: list = []
+        self._slots: list[_PinnedSlot] = []
+        self._turn = 0
+
+    def _slot(self, numel: int, pin: bool) -> _PinnedSlot:
+        if not self._slots or self._slots[0].master.numel() != numel:
+            self.wait()
+            self._slots = [_PinnedSlot(numel, pin), _PinnedSlot(numel, pin)]
+        slot = self._slots[self._turn]
+        self._turn ^= 1
+        if slot.pending is not None:
+            slot.pending.result()
+            slot.pending = None
+        return slot
 
     def submit(self, path: str, store: LoRAStore, base_model: str, spec: LoRASpec,
-               optimizer_state: dict | None = None) -> str:
-        sd, opt = snapshot_adapter(store, optimizer_state)
-        write_adapter(path, sd, base_model, spec, None)
-        if opt is not None:
-            self._pending.append(self._pool.submit(_write_optimizer, path, opt))
+               with_optimizer: bool = True) -> str:
+        cuda = store.master.device.type == "cuda"
+        slot = self._slot(store.numel, cuda)
+        slot.master.copy_(store.master, non_blocking=cuda)
+        if with_optimizer:
+            slot.exp_avg.copy_(store.exp_avg, non_blocking=cuda)
+            slot.exp_avg_sq.copy_(store.exp_avg_sq, non_blocking=cuda)
+        if cuda:
+            torch.cuda.current_stream(store.master.device).synchronize()
+        parent = os.path.dirname(os.path.abspath(path))
+        os.makedirs(parent, exist_ok=True)
+        stage = os.path.join(parent, f".staging-{uuid.uuid4().hex[:8]}")
+        os.makedirs(stage)
+        try:
+            write_safetensors_from_flat(os.path.join(stage, "adapter_model.safetensors"), slot.master,
+                                        store.entries)
+            with open(os.path.join(stage, "adapter_config.json"), "w") as f:
+                json.dump(adapter_config(base_model, spec), f, indent=2)
+            if os.path.exists(path):
+                shutil.rmtree(path)
+            os.replace(stage, path)
+        except BaseException:
+            shutil.rmtree(stage, ignore_errors=True)
+            raise
+        if with_optimizer:
+            opt = {"exp_avg": slot.exp_avg, "exp_avg_sq": slot.exp_avg_sq, "step": store.step}
+            fut = self._pool.submit(_write_optimizer, path, opt)
+            slot.pending = fut
+            self._pending.append(fut)
         return path
 
     def wait(self) -> None:

@@ -338,6 +338,7 @@ def run_e2e(args, cfg, lora, groups, trainer, device, world, rank, train_tokens)
         await model.register(backend)
         times = []
         h2d = d2h = 0
+        breakdown: dict = {}
         for i in range(args.e2e_steps + 1):
             if world > 1:
                 dist.barrier()
@@ -348,11 +349,13 @@ def run_e2e(args, cfg, lora, groups, trainer, device, world, rank, train_tokens)
             dt = time.perf_counter() - t0
             if i > 0:  # first call is warm-up
                 times.append(dt)
+                breakdown = {k.split("/", 1)[1]: round(float(v), 4) for k, v in res.metrics.items()
+                             if k.startswith("time/step_")}
             h2d = backend.last_h2d_bytes
             d2h = backend.last_d2h_bytes
-        return times, h2d, d2h
+        return times, h2d, d2h, breakdown
 
-    times, h2d, d2h = asyncio.run(go())
+    times, h2d, d2h, breakdown = asyncio.run(go())
     dt = max(times) if times else float("nan")
     t = torch.tensor([dt], device=device)
     if world > 1:
@@ -366,6 +369,7 @@ def run_e2e(args, cfg, lora, groups, trainer, device, world, rank, train_tokens)
         "h2d_bytes_per_step": int(h2d),
         "d2h_bytes_per_step": int(d2h),
         "api": "LocalBackend.train(model, groups)",
+        "breakdown_s": breakdown,
     }
 
 
