@@ -96,7 +96,8 @@ class LocalBackend:
         await self.close()
 
     def _flush(self) -> None:
-        """Wait until every submitted checkpoint is published."""
+        """Wait until every submitted optimizer-state write is on disk (adapters
+        are published synchronously by the writer)."""
         self._writer.wait()
 
     async def close(self) -> None:
@@ -130,7 +131,6 @@ class LocalBackend:
                 json.dump(model.model_dump(mode="json"), f, indent=2, default=str)
 
     async def _get_step(self, model: Any) -> int:
-        self._flush()
         return get_step_from_dir(self._model_dir(model))
 
     def adapter_leases(self, model: Any):
@@ -238,7 +238,6 @@ class LocalBackend:
         the live policy (``None``)."""
         if name == model.base_model:
             return "base"
-        self._flush()
         if "@" in name:
             _, step = name.rsplit("@", 1)
             d = self._model_dir(model)
@@ -353,7 +352,8 @@ class LocalBackend:
             num_trajectories_learning_rate_multiplier_power=num_trajectories_learning_rate_multiplier_power,
             kl_ref_adapter_path=kl_ref_adapter_path,
         )
-        self._flush()
+        # adapters are published synchronously; only the optimizer state of
+        # the previous step may still be in flight, and nothing here reads it
         step = get_step_from_dir(d)
         results = list(
             tokenize_trajectory_groups(
@@ -377,6 +377,7 @@ class LocalBackend:
             ck = get_step_checkpoint_dir(d, new_step)
             if save_checkpoint and _rank() == 0:
                 prev = get_step_checkpoint_dir(d, step)
+                self._flush()  # the copy includes the previous optimizer state
                 if os.path.exists(ck):
                     shutil.rmtree(ck)
                 if os.path.exists(prev):
