@@ -112,14 +112,21 @@ def bench_gemm() -> None:
         b = torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02
         fl = 2 * rows * K * N
         t_ours = _timed(lambda: C.gemm_tc(a, b, None, None, None, None, False))
+        t_pair = _timed(lambda: C.gemm_pair(a, b, None, None, None, None, False))
         t_cublas = _timed(lambda: torch.matmul(a, b.t()))
-        row = dict(case=f"gemm_{name}", M=rows, K=K, N=N, ours_ms=round(t_ours, 4), cublas_ms=round(t_cublas, 4),
-                   ours_tflops=round(fl / t_ours / 1e9, 1), cublas_tflops=round(fl / t_cublas / 1e9, 1))
+        row = dict(case=f"gemm_{name}", M=rows, K=K, N=N, ours_1cta_ms=round(t_ours, 4),
+                   ours_pair_ms=round(t_pair, 4), cublas_ms=round(t_cublas, 4),
+                   ours_1cta_tflops=round(fl / t_ours / 1e9, 1), ours_pair_tflops=round(fl / t_pair / 1e9, 1),
+                   cublas_tflops=round(fl / t_cublas / 1e9, 1))
         if r:
             a2 = torch.randn(rows, r, device=dev, dtype=torch.bfloat16)
             b2 = torch.randn(N, r, device=dev, dtype=torch.bfloat16)
-            row["ours_lora_ms"] = round(_timed(lambda: C.gemm_tc(a, b, a2, b2, None, None, False)), 4)
+            row["ours_1cta_lora_ms"] = round(_timed(lambda: C.gemm_tc(a, b, a2, b2, None, None, False)), 4)
+            row["ours_pair_lora_ms"] = round(_timed(lambda: C.gemm_pair(a, b, a2, b2, None, None, False)), 4)
             row["cublas_lora_ms"] = round(_timed(lambda: torch.addmm(torch.matmul(a, b.t()), a2, b2.t())), 4)
+        diff = (C.gemm_pair(a, b, None, None, None, None, False).float() - torch.matmul(a, b.t()).float())
+        row["pair_vs_cublas_rel"] = float(diff.norm() / torch.matmul(a, b.t()).float().norm())
+        row["tc_error"] = int(C.tc_error_code())
         _emit(**row)
 
 

@@ -86,3 +86,37 @@ def test_gemm_tc_grouped_matches_fp32(cuda, E, K, N, K2, wt):
         if K2:
             ref[r] += a2[r].float() @ b2[e * N : (e + 1) * N].float().t()
     assert rel_err(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize(
+    "M,K,N,K2,bias,acc",
+    [
+        (256, 64, 256, 0, False, False),
+        (300, 512, 512, 0, True, False),
+        (1000, 3584, 4608, 48, True, False),
+        (777, 1024, 3584, 16, False, True),
+        (64, 192, 96, 8, False, False),
+        (2048, 2048, 800, 16, False, False),
+    ],
+)
+def test_gemm_pair_matches_fp32(cuda, M, K, N, K2, bias, acc):
+    """The CTA-pair (cta_group::2) tcgen05 GEMM against an fp32 reference."""
+    C = native.lib()
+    torch.manual_seed(M + K + N + 1)
+    a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=cuda, dtype=torch.bfloat16) * 0.05
+    a2 = torch.randn(M, K2, device=cuda, dtype=torch.bfloat16) if K2 else None
+    b2 = torch.randn(N, K2, device=cuda, dtype=torch.bfloat16) * 0.05 if K2 else None
+    bb = torch.randn(N, device=cuda, dtype=torch.bfloat16) if bias else None
+    out = torch.randn(M, N, device=cuda, dtype=torch.bfloat16) if acc else None
+    ref = a.float() @ b.float().t()
+    if K2:
+        ref += a2.float() @ b2.float().t()
+    if bias:
+        ref += bb.float()
+    if acc:
+        ref += out.float()
+    got = C.gemm_pair(a, b, a2, b2, bb, out, acc)
+    torch.cuda.synchronize()
+    assert C.tc_error_code() == 0
+    assert rel_err(got, ref) < 1e-2
