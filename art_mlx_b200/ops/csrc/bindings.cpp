@@ -81,7 +81,8 @@ std::vector<torch::Tensor> gdn_scan_bwd(c10::optional<torch::Tensor> dO, c10::op
 torch::Tensor gdn_conv_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor prev);
 torch::Tensor gemm_pair(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> a2,
                         c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> bias,
-                        c10::optional<torch::Tensor> out, bool accumulate, c10::optional<torch::Tensor> diag);
+                        c10::optional<torch::Tensor> out, bool accumulate, c10::optional<torch::Tensor> diag,
+                        bool b_transposed);
 std::vector<torch::Tensor> gdn_conv_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor prev,
                                         torch::Tensor succ_ptr, torch::Tensor succ_idx, torch::Tensor succ_tap);
 }  // namespace art
@@ -136,6 +137,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_conv_fwd", &art::gdn_conv_fwd);
   m.def("gemm_pair", &art::gemm_pair, py::arg("a"), py::arg("b"), py::arg("a2") = py::none(),
         py::arg("b2") = py::none(), py::arg("bias") = py::none(), py::arg("out") = py::none(),
-        py::arg("accumulate") = false, py::arg("diag") = py::none());
+        py::arg("accumulate") = false, py::arg("diag") = py::none(), py::arg("b_transposed") = false);
   m.def("gdn_conv_bwd", &art::gdn_conv_bwd);
 }

@@ -49,6 +49,7 @@ struct PairArgs {
   const __nv_bfloat16* bias;
   int accumulate_c;
   int group_m;  // pair rows of A per raster group
+  int b_mn;     // B of the main product given as [K, N] row-major (MN-major operand)
   int* err;
   // optional pipeline counters (null: off), summed over the leader CTAs:
   // [0] ns the MMA thread waited for operands, [1] ns it waited for a free
@@ -135,7 +136,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * P_STAGE);  // both CTAs' bytes
           if (kb < p.nk1) {
             tma_load_2d_pair(a, &tmA, fb, kb * PBK, am);
-            tma_load_2d_pair(b, &tmB, fb, kb * PBK, bn);
+            if (p.b_mn) {  // two 64-column boxes of the [K, N] matrix: 64 K rows each
+              tma_load_2d_pair(b, &tmB, fb, bn, kb * PBK);
+              tma_load_2d_pair(b + P_HALF / 2, &tmB, fb, bn + 64, kb * PBK);
+            } else {
+              tma_load_2d_pair(b, &tmB, fb, kb * PBK, bn);
+            }
           } else {
             const int k2 = (kb - p.nk1) * PBK;
             tma_load_2d_pair(a, &tmA2, fb, k2, am);
@@ -183,7 +189,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           // orders them for the MMA: no thread-sync fence per k-block
           const uint32_t a_addr = smem_addr(smem + s * P_STAGE);
           const uint64_t da = desc_k_sw128(a_addr), db = desc_k_sw128(a_addr + P_HALF);
-          if (kb < p.nk1) {
+          if (kb < p.nk1 && p.b_mn) {
+            // MN-major B: 16 K rows of 128 B per step (+2048 B), 64-column chunks 8 KB apart
+            const uint64_t dbm = desc_mn_sw128(a_addr + P_HALF, P_HALF / 2);
+#pragma unroll
+            for (int kk = 0; kk < PBK / 16; ++kk)
+              mma_bf16_pair(d, da + 2 * kk, dbm + 128 * kk, idesc | (1u << 16), (kb > 0 || kk > 0) ? 1u : 0u);
+          } else if (kb < p.nk1) {
 #pragma unroll
             for (int kk = 0; kk < PBK / 16; ++kk)  // +32 bytes per K=16 step (descriptor units of 16 B)
               mma_bf16_pair(d, da + 2 * kk, db + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
@@ -277,13 +289,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
 
 }  // namespace
 
-// out = a @ b^T (+ a2 @ b2^T) (+ bias) (+ out if accumulate), on CTA pairs.
+// out = a @ b^T (+ a2 @ b2^T) (+ bias) (+ out if accumulate), on CTA pairs;
+// with b_transposed, b is given as [K, N] (out = a @ b): the frozen weight of
+// a linear layer in its stored layout for the input-gradient GEMM.
 torch::Tensor gemm_pair(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> a2,
                         c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> bias,
-                        c10::optional<torch::Tensor> out, bool accumulate, c10::optional<torch::Tensor> diag) {
+                        c10::optional<torch::Tensor> out, bool accumulate, c10::optional<torch::Tensor> diag,
+                        bool b_transposed) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda());
-  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
-  TORCH_CHECK(b.size(1) == K, "inner dimensions differ");
+  const int64_t M = a.size(0), K = a.size(1), N = b_transposed ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_transposed ? b.size(0) : b.size(1)) == K, "inner dimensions differ");
+  if (b_transposed) TORCH_CHECK(N % 128 == 0, "transposed B: N must be a multiple of 128");
   TORCH_CHECK(N % 32 == 0, "N must be a multiple of 32");
   torch::Tensor c;
   if (out.has_value()) {
@@ -297,7 +313,7 @@ torch::Tensor gemm_pair(torch::Tensor a, torch::Tensor b, c10::optional<torch::T
   if (a2.has_value())
     TORCH_CHECK(b2.has_value() && a2->size(0) == M && b2->size(0) == N && a2->size(1) == b2->size(1));
   if (bias.has_value()) TORCH_CHECK(bias->numel() == N && bias->is_contiguous());
-  const CUtensorMap ta = make_tmap_bf16(a, 128), tb = make_tmap_bf16(b, 128);
+  const CUtensorMap ta = make_tmap_bf16(a, 128), tb = make_tmap_bf16(b, b_transposed ? 64 : 128);
   const CUtensorMap ta2 = a2.has_value() ? make_tmap_bf16(*a2, 128) : ta;
   const CUtensorMap tb2 = a2.has_value() ? make_tmap_bf16(*b2, 128) : tb;
   PairArgs p;
@@ -310,6 +326,7 @@ torch::Tensor gemm_pair(torch::Tensor a, torch::Tensor b, c10::optional<torch::T
   p.ldc = c.stride(0);
   p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
   p.accumulate_c = accumulate ? 1 : 0;
+  p.b_mn = b_transposed ? 1 : 0;
   p.diag = nullptr;
   if (diag.has_value()) {
     TORCH_CHECK(diag->is_cuda() && diag->scalar_type() == torch::kInt64 && diag->numel() >= 5, "diag: int64[5]");

@@ -21,6 +21,7 @@ Ops:
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Any, Sequence
 
@@ -347,6 +348,20 @@ class LoRABinding:
     _bd: torch.Tensor | None = None
     _bd_version: int = -1
 
+    _bd_s: torch.Tensor | None = None
+    _at_s: torch.Tensor | None = None
+    _fused_version: int = -1
+
+    def fused_factors(self, version: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """``(scale * B_blockdiag [out, n*r], scale * A^T [in, n*r])``: the
+        K-extension operands of the forward and input-gradient GEMMs (cached
+        until the parameters change)."""
+        if self._fused_version != version or self._bd_s is None:
+            self._bd_s = (self.block_diag(version) * self.scale).contiguous()
+            self._at_s = (self.A.t() * self.scale).contiguous()
+            self._fused_version = version
+        return self._bd_s, self._at_s
+
     def block_diag(self, version: int) -> torch.Tensor:
         """Dense ``[out, n*r]`` B with the slice blocks on its diagonal (cached
         until the parameters change)."""
@@ -385,17 +400,42 @@ def grad_anchor(device: torch.device) -> torch.Tensor:
     return a
 
 
+PAIR_GEMM = os.environ.get("ART_B200_PAIR_GEMM", "1") != "0"
+PAIR_MIN_ROWS = 1024
+PAIR_MAX_CONTRACTION = 8192
+
+
+def _pair_ok(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None, contraction: int) -> bool:
+    """Calls the CTA-pair tcgen05 GEMM takes: bf16, 16-byte rows, out and in
+    features multiples of 128, enough rows to fill the GPU (decode-sized
+    calls stay on cuBLAS) and a contraction of at most 8192 (on longer ones
+    cuBLAS's base GEMM is faster than the fused LoRA pass saves)."""
+    return (PAIR_GEMM and _cuda(x) and x.dim() == 2 and x.dtype == torch.bfloat16 and W.dtype == torch.bfloat16
+            and x.shape[0] >= PAIR_MIN_ROWS and W.shape[0] % 128 == 0 and W.shape[1] % 128 == 0
+            and contraction <= PAIR_MAX_CONTRACTION
+            and x.is_contiguous() and W.is_contiguous() and (bias is None or bias.dtype == torch.bfloat16))
+
+
 class _LoRALinear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, W, bias, lora, version, enabled, anchor):
-        y = torch.nn.functional.linear(x, W, bias)
         u = None
-        if enabled and lora is not None:
+        on = enabled and lora is not None
+        pair = _pair_ok(x, W, bias, W.shape[1])
+        if on:
             u = x @ lora.A.t()  # [T, n*r]
-            y.addmm_(u, lora.block_diag(version).t(), alpha=lora.scale)
+        if pair:
+            # base GEMM + LoRA as one more k-block of the same accumulator
+            bd_s = lora.fused_factors(version)[0] if on else None
+            y = native.lib().gemm_pair(x, W, u, bd_s, bias)
+        else:
+            y = torch.nn.functional.linear(x, W, bias)
+            if on:
+                y.addmm_(u, lora.block_diag(version).t(), alpha=lora.scale)
         ctx.save_for_backward(x, W, u if u is not None else x.new_empty(0))
-        ctx.lora = lora if enabled else None
+        ctx.lora = lora if on else None
         ctx.version = version
+        ctx.pair_dgrad = _pair_ok(x, W, None, W.shape[0])
         return y
 
     @staticmethod
@@ -403,7 +443,7 @@ class _LoRALinear(torch.autograd.Function):
         x, W, u = ctx.saved_tensors
         lora = ctx.lora
         dy = dy.contiguous()
-        dx = dy @ W
+        dyB = None
         if lora is not None:
             bd = lora.block_diag(ctx.version)
             dyB = dy @ bd  # [T, n*r]
@@ -415,7 +455,14 @@ class _LoRALinear(torch.autograd.Function):
                 if gB is None:
                     continue
                 _accum_mm(gB, dy[:, a:b].t(), u[:, k * lora.r : (k + 1) * lora.r], s)
-            dx.addmm_(dyB, lora.A, alpha=s)
+        if ctx.pair_dgrad:
+            # dx = dy W + (dy B) (s A): W read in its stored [out, in] layout
+            at_s = lora.fused_factors(ctx.version)[1] if lora is not None else None
+            dx = native.lib().gemm_pair(dy, W, dyB, at_s, None, None, False, None, True)
+        else:
+            dx = dy @ W
+            if lora is not None:
+                dx.addmm_(dyB, lora.A, alpha=lora.scale)
         return dx, None, None, None, None, None, None
 
 

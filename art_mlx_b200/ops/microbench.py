@@ -124,6 +124,16 @@ def bench_gemm() -> None:
             row["ours_1cta_lora_ms"] = round(_timed(lambda: C.gemm_tc(a, b, a2, b2, None, None, False)), 4)
             row["ours_pair_lora_ms"] = round(_timed(lambda: C.gemm_pair(a, b, a2, b2, None, None, False)), 4)
             row["cublas_lora_ms"] = round(_timed(lambda: torch.addmm(torch.matmul(a, b.t()), a2, b2.t())), 4)
+        if r:
+            # input-gradient form: dx = dy W (+ (dy B) (s A)), W in its stored [N, K] layout
+            dy = torch.randn(rows, N, device=dev, dtype=torch.bfloat16)
+            dyb = torch.randn(rows, r, device=dev, dtype=torch.bfloat16)
+            at = torch.randn(K, r, device=dev, dtype=torch.bfloat16)
+            A = at.t().contiguous()
+            row["dgrad_pair_ms"] = round(_timed(lambda: C.gemm_pair(dy, b, None, None, None, None, False, None, True)), 4)
+            row["dgrad_cublas_ms"] = round(_timed(lambda: torch.matmul(dy, b)), 4)
+            row["dgrad_pair_lora_ms"] = round(_timed(lambda: C.gemm_pair(dy, b, dyb, at, None, None, False, None, True)), 4)
+            row["dgrad_cublas_lora_ms"] = round(_timed(lambda: torch.matmul(dy, b).addmm_(dyb, A)), 4)
         diff = (C.gemm_pair(a, b, None, None, None, None, False).float() - torch.matmul(a, b.t()).float())
         row["pair_vs_cublas_rel"] = float(diff.norm() / torch.matmul(a, b.t()).float().norm())
         row["tc_error"] = int(C.tc_error_code())

@@ -120,3 +120,21 @@ def test_gemm_pair_matches_fp32(cuda, M, K, N, K2, bias, acc):
     torch.cuda.synchronize()
     assert C.tc_error_code() == 0
     assert rel_err(got, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,K,N,K2", [(300, 512, 256, 0), (1000, 3584, 3584, 48), (2048, 4608, 3584, 16)])
+def test_gemm_pair_transposed_b_matches_fp32(cuda, M, K, N, K2):
+    """Input-gradient form: out = a @ bt (+ a2 @ b2^T) with bt = [K, N] row-major."""
+    C = native.lib()
+    torch.manual_seed(M + K + N + 2)
+    a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+    bt = torch.randn(K, N, device=cuda, dtype=torch.bfloat16) * 0.05
+    a2 = torch.randn(M, K2, device=cuda, dtype=torch.bfloat16) if K2 else None
+    b2 = torch.randn(N, K2, device=cuda, dtype=torch.bfloat16) * 0.05 if K2 else None
+    ref = a.float() @ bt.float()
+    if K2:
+        ref += a2.float() @ b2.float().t()
+    got = C.gemm_pair(a, bt, a2, b2, None, None, False, None, True)
+    torch.cuda.synchronize()
+    assert C.tc_error_code() == 0
+    assert rel_err(got, ref) < 1e-2
