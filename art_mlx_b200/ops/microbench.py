@@ -2,6 +2,7 @@
 
     python -m art_mlx_b200.ops.microbench attn [--small]   # tcgen05 vs warp-level prefix-tree attention
     python -m art_mlx_b200.ops.microbench gemm             # tcgen05 GEMM (+ fused LoRA) vs cuBLAS
+    python -m art_mlx_b200.ops.microbench gemm_one         # 3 pair-GEMM calls, gate_up shape (ncu target)
     python -m art_mlx_b200.ops.microbench gdn              # gated DeltaNet scan / conv kernels vs PyTorch
     python -m torch.distributed.run --nnodes 1 --nproc-per-node 2 --master-addr 127.0.0.1 \\
         --master-port 29533 -m art_mlx_b200.ops.microbench comm   # fused comm paths vs NCCL
@@ -138,6 +139,21 @@ def bench_gemm() -> None:
         row["pair_vs_cublas_rel"] = float(diff.norm() / torch.matmul(a, b.t()).float().norm())
         row["tc_error"] = int(C.tc_error_code())
         _emit(**row)
+
+
+def gemm_one() -> None:
+    """Three CTA-pair GEMM calls on the gate_up shape: a small, self-ending
+    target for a one-launch profiler capture."""
+    from . import native
+
+    C = native.lib()
+    dev = torch.device("cuda")
+    a = torch.randn(9280, 3584, device=dev, dtype=torch.bfloat16)
+    b = torch.randn(37888, 3584, device=dev, dtype=torch.bfloat16) * 0.02
+    for _ in range(3):
+        C.gemm_pair(a, b)
+    torch.cuda.synchronize()
+    _emit(case="gemm_one", tc_error=int(C.tc_error_code()))
 
 
 # ---------------------------------------------------------------------------
@@ -351,12 +367,14 @@ def main(argv: list[str]) -> None:
         bench_attn(small="--small" in argv)
     elif which == "gemm":
         bench_gemm()
+    elif which == "gemm_one":
+        gemm_one()
     elif which == "gdn":
         bench_gdn()
     elif which == "comm":
         bench_comm()
     else:
-        raise SystemExit(f"unknown case {which!r}: attn | gemm | gdn | comm")
+        raise SystemExit(f"unknown case {which!r}: attn | gemm | gemm_one | gdn | comm")
 
 
 if __name__ == "__main__":
