@@ -139,12 +139,14 @@ class MultiGPUBackend(LocalBackend):
         topo = self._topology
         tp = topo.tp if topo.tp > 1 else 1
         cp = topo.cp if (topo.cp > 1 and topo.cp <= self._world and tp == 1) else 1
+        etp = topo.etp if (topo.etp > 1 and self._world % topo.etp == 0) else 1
         cmd = [
             sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", str(self._world),
             "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
             "-m", "art_mlx_b200.runtime.worker", "--jobs-dir", jobs_dir, "--model", preset,
             "--base-model", model.base_model, "--lora", json.dumps(peft), "--adamw", json.dumps(adamw),
-            "--tp", str(tp), "--cp", str(cp), "--seed", str(self._seed), "--device", self._dev_type,
+            "--tp", str(tp), "--cp", str(cp), "--etp", str(etp), "--seed", str(self._seed),
+            "--device", self._dev_type,
             "--init-checkpoint", init_ck, "--timeout-s", str(self._worker_timeout),
         ]
         log_path = os.path.join(d, "logs", "workers.log")

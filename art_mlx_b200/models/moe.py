@@ -130,6 +130,17 @@ class ExpertParams:
         self.g_A_gu, self.g_B_gu, self.g_A_d, self.g_B_d = g_A_gu, g_B_gu, g_A_d, g_B_d
         self.scale = scale
 
+    def for_compute(self) -> "ExpertParams":
+        """Contiguous copies of the factors the products read (slices under
+        expert tensor parallelism are strided views of the flat store); the
+        gradient views stay the store's."""
+        facs = (self.A_gu, self.B_gu, self.A_d, self.B_d)
+        if all(t is None or t.is_contiguous() for t in facs):
+            return self
+        c = lambda t: None if t is None else t.contiguous()  # noqa: E731
+        return ExpertParams(self.gu_w_t, self.down_w_t, c(self.A_gu), c(self.B_gu), c(self.A_d), c(self.B_d),
+                            self.g_A_gu, self.g_B_gu, self.g_A_d, self.g_B_d, self.scale)
+
 
 def _tc_grouped(x: torch.Tensor, p: ExpertParams) -> bool:
     """Whether the experts run on the tcgen05 grouped GEMM (base product and
@@ -321,20 +332,26 @@ class _EPExperts(torch.autograd.Function):
 
 class MoEBlock:
     def __init__(self, cfg: ModelConfig, i: int, gen, dev, dt, store: LoRAStore, spec: LoRASpec,
-                 ep: Any = None) -> None:
+                 ep: Any = None, etp: Any = None) -> None:
         from .transformer import _randn
 
-        self.cfg, self.index, self.ep = cfg, i, ep
+        self.cfg, self.index, self.ep, self.etp = cfg, i, ep, etp
         E, H, F = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size
         self.router_w = _randn((E, H), gen, dev, dt)
         e0 = ep.first_expert if ep is not None else 0
         El = ep.E_local if ep is not None else E
+        f0, Fl = etp.slice(F) if etp is not None else (0, F)
+        self.f0, self.F_local = f0, Fl
         # the expert weights are drawn in one piece so the random init does not
-        # depend on the expert-parallel degree; each rank keeps its slice
-        gu = _randn((E, H, 2 * F), gen, dev, dt) if El == E else _randn((E, H, 2 * F), gen, dev, dt)[e0 : e0 + El].clone()
-        dn = _randn((E, F, H), gen, dev, dt) if El == E else _randn((E, F, H), gen, dev, dt)[e0 : e0 + El].clone()
-        self.gu_w_t = gu  # [E_local, H, 2F]
-        self.down_w_t = dn  # [E_local, F, H]
+        # depend on the expert- or expert-tensor-parallel degree; each rank
+        # keeps its experts and, under ETP, its intermediate slice
+        gu = _randn((E, H, 2 * F), gen, dev, dt)
+        dn = _randn((E, F, H), gen, dev, dt)
+        if El != E or Fl != F:
+            gu = torch.cat([gu[e0 : e0 + El, :, f0 : f0 + Fl], gu[e0 : e0 + El, :, F + f0 : F + f0 + Fl]], dim=2)
+            dn = dn[e0 : e0 + El, f0 : f0 + Fl].contiguous()
+        self.gu_w_t = gu.contiguous()  # [E_local, H, 2F_local]
+        self.down_w_t = dn  # [E_local, F_local, H]
         self.shared = None
         if cfg.shared_expert_intermediate_size:
             Fs = cfg.shared_expert_intermediate_size
@@ -356,10 +373,13 @@ class MoEBlock:
         A_d, g_A_d = stacked([peft_key(i, "mlp", "down_proj", "A", e) for e in range(E)], (E, r, F))
         B_d, g_B_d = stacked([peft_key(i, "mlp", "down_proj", "B", e) for e in range(E)], (E, H, r))
         sl = slice(e0, e0 + El)
+        fs = slice(f0, f0 + Fl)
         pick = lambda t: None if t is None else t[sl]  # noqa: E731
+        pick_bgu = lambda t: None if t is None else t[sl, :, fs]  # noqa: E731  gate/up B: rows of the F slice
+        pick_ad = lambda t: None if t is None else t[sl, :, fs]  # noqa: E731  down A: columns of the F slice
         self.params = ExpertParams(
-            self.gu_w_t, self.down_w_t, pick(A_gu), pick(B_gu), pick(A_d), pick(B_d),
-            pick(g_A_gu), pick(g_B_gu), pick(g_A_d), pick(g_B_d), spec.scale,
+            self.gu_w_t, self.down_w_t, pick(A_gu), pick_bgu(B_gu), pick_ad(A_d), pick(B_d),
+            pick(g_A_gu), pick_bgu(g_B_gu), pick_ad(g_A_d), pick(g_B_d), spec.scale,
         )
 
     def num_parameters(self) -> int:
@@ -386,21 +406,27 @@ class MoEBlock:
         return idx, wts
 
     def __call__(self, h: torch.Tensor, version: int, enabled: bool, ctx: dict[str, Any]) -> torch.Tensor:
-        T, H = h.shape
         E, k = self.cfg.num_experts, self.cfg.num_experts_per_tok
         idx, wts = self.route(h, ctx)
         anchor = grad_anchor(h.device) if enabled else None
+        hx, wx, ix = h, wts, idx
+        if self.etp is not None:  # the ETP group's whole token set, every member its F slice
+            hx, wx, ix = self.etp.gather(h), self.etp.gather(wts), self.etp.gather_nograd(idx)
+        T, H = hx.shape
+        params = self.params.for_compute()
         if self.ep is not None and self.ep.world > 1:
-            out = _EPExperts.apply(h, wts, idx, self.ep, self.params, enabled, anchor)
+            out = _EPExperts.apply(hx, wx, ix, self.ep, params, enabled, anchor)
         else:
-            flat = idx.reshape(-1)
+            flat = ix.reshape(-1)
             order = torch.argsort(flat, stable=True)
             counts = torch.bincount(flat, minlength=E).tolist()
             tok = order // k
-            xs = h[tok]
-            ys = _LocalExperts.apply(xs, counts, self.params, enabled, anchor)
-            w_sorted = wts.reshape(-1)[order].to(ys.dtype).unsqueeze(1)
-            out = torch.zeros(T, H, device=h.device, dtype=ys.dtype).index_add(0, tok, ys * w_sorted)
+            xs = hx[tok]
+            ys = _LocalExperts.apply(xs, counts, params, enabled, anchor)
+            w_sorted = wx.reshape(-1)[order].to(ys.dtype).unsqueeze(1)
+            out = torch.zeros(T, H, device=hx.device, dtype=ys.dtype).index_add(0, tok, ys * w_sorted)
+        if self.etp is not None:  # sum the F slices, back to this rank's tokens
+            out = self.etp.reduce_scatter(out)
         if self.shared is not None:
             gu_w, down_w, gate_w = self.shared
             gu = h @ gu_w.t()
@@ -412,7 +438,8 @@ class MoEBlock:
     def load_hf(self, sd: dict[str, torch.Tensor], prefix: str, g: Callable[[str], torch.Tensor]) -> None:
         self.router_w.copy_(g(prefix + "gate.weight"))
         e0 = self.ep.first_expert if self.ep is not None else 0
+        fs = slice(self.f0, self.f0 + self.F_local)
         for le in range(self.gu_w_t.shape[0]):
             p = f"{prefix}experts.{e0 + le}."
-            self.gu_w_t[le].copy_(torch.cat([g(p + "gate_proj.weight"), g(p + "up_proj.weight")]).t())
-            self.down_w_t[le].copy_(g(p + "down_proj.weight").t())
+            self.gu_w_t[le].copy_(torch.cat([g(p + "gate_proj.weight")[fs], g(p + "up_proj.weight")[fs]]).t())
+            self.down_w_t[le].copy_(g(p + "down_proj.weight")[:, fs].t())

@@ -61,7 +61,7 @@ def get_model_support(base_model: str | ModelConfig, allow_unvalidated_arch: boo
     return spec
 
 
-def check_parallelism(spec: ModelSupportSpec, *, tp: int = 1, cp: int = 1, ep: bool = False) -> None:
-    for mode, on in (("tp", tp > 1), ("cp", cp > 1), ("ep", ep)):
+def check_parallelism(spec: ModelSupportSpec, *, tp: int = 1, cp: int = 1, ep: bool = False, etp: int = 1) -> None:
+    for mode, on in (("tp", tp > 1), ("cp", cp > 1), ("ep", ep or etp > 1)):
         if on and mode not in spec.supports:
             raise ValueError(f"{spec.key} does not support {mode} parallelism (supported: {sorted(spec.supports)})")

@@ -153,9 +153,11 @@ class DecoderLM:
         store: LoRAStore | None = None,
         init_weights: bool = True,
         ep: Any = None,
+        etp: Any = None,
     ) -> None:
         self.cfg = cfg
         self.ep = ep  # expert-parallel context (MoE models on several ranks)
+        self.etp = etp  # expert-tensor-parallel context (experts' FFN split over ranks)
         self.lora_spec = lora
         self.device = torch.device(device)
         self.dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
@@ -203,7 +205,7 @@ class DecoderLM:
 
             layer.gdn = GatedDeltaNet(cfg, i, gen, dev, dt, st, spec)
         if cfg.is_moe:
-            layer.moe = MoEBlock(cfg, i, gen, dev, dt, st, spec, ep=self.ep)
+            layer.moe = MoEBlock(cfg, i, gen, dev, dt, st, spec, ep=self.ep, etp=self.etp)
         else:
             F = cfg.intermediate_size
             layer.mlp = DenseMLP(

@@ -41,3 +41,23 @@ def shard_subgroup(group: dist.ProcessGroup | None, size: int) -> dist.ProcessGr
         if me in block:
             mine = g
     return mine
+
+
+def strided_subgroup(group: dist.ProcessGroup | None, stride: int) -> dist.ProcessGroup | None:
+    """Collective over ``group``: split it into ``stride`` groups of ranks
+    ``{j, j + stride, j + 2*stride, ...}`` and return the one that holds this
+    rank (the ranks that share a position inside their consecutive block of
+    ``stride``)."""
+    ranks = group_ranks(group)
+    if len(ranks) % stride != 0:
+        raise ValueError(f"stride {stride} does not divide the {len(ranks)} ranks")
+    if stride == 1:
+        return group
+    me = dist.get_rank()
+    mine = None
+    for j in range(stride):
+        members = ranks[j::stride]
+        g = dist.new_group(members)
+        if me in members:
+            mine = g
+    return mine

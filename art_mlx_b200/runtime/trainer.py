@@ -251,6 +251,7 @@ class GRPOTrainer:
         max_tokens_per_rank: int = 16384,
         tp_size: int = 1,
         cp_size: int = 1,
+        etp_size: int = 1,
         allow_unvalidated_arch: bool = False,
     ) -> None:
         from ..models.registry import check_parallelism, get_model_support
@@ -295,18 +296,34 @@ class GRPOTrainer:
             from ..parallel.topology import shard_subgroup
 
             self.cp = CPContext(shard_subgroup(group, self.cp_size), self.device)
-        check_parallelism(self.support, tp=self.tp_size, cp=self.cp_size)
+        check_parallelism(self.support, tp=self.tp_size, cp=self.cp_size, etp=etp_size if self.world > 1 else 1)
+        self.etp = None
+        self.etp_size = etp_size if self.world > 1 else 1
+        if self.etp_size > 1 and not cfg.is_moe:
+            raise ValueError("expert tensor parallelism applies to MoE models")
         if cfg.is_moe and self.world > 1:
             from ..parallel.ep import EPContext
 
-            cap = 2 * max_tokens_per_rank * cfg.num_experts_per_tok
-            self.ep = EPContext(group, cfg.num_experts, cfg.hidden_size, self.device, cap)
+            ep_group = group
+            if self.etp_size > 1:
+                # ETP groups of consecutive ranks; the EP group of a rank holds
+                # the ranks with the same position in their ETP group
+                from ..parallel.etp import ETPContext
+                from ..parallel.topology import strided_subgroup
+
+                if self.world % self.etp_size != 0:
+                    raise ValueError(f"etp={self.etp_size} does not divide world={self.world}")
+                self.etp = ETPContext(group, self.etp_size, self.device)
+                ep_group = strided_subgroup(group, self.etp_size)
+            if self.world // self.etp_size > 1:
+                cap = 2 * max_tokens_per_rank * cfg.num_experts_per_tok * self.etp_size
+                self.ep = EPContext(ep_group, cfg.num_experts, cfg.hidden_size, self.device, cap)
         if self.tp is not None:
             from ..models.tp_decoder import TPDecoderLM
 
             self.model = TPDecoderLM(cfg, lora, self.device, self.tp, seed=seed, store=store)
         else:
-            self.model = DecoderLM(cfg, lora, self.device, seed=seed, store=store, ep=self.ep)
+            self.model = DecoderLM(cfg, lora, self.device, seed=seed, store=store, ep=self.ep, etp=self.etp)
         self.store = self.model.store
         self.optim = FlatAdamW(self.store, adamw)
         self.logprob_chunk = logprob_chunk
@@ -322,7 +339,7 @@ class GRPOTrainer:
     def offload(self) -> int:
         """Move the model, LoRA store and optimizer state to pinned host
         memory (the GPU is free for other work until :meth:`reload`)."""
-        if self.grad_sync is not None or self.tp is not None or self.ep is not None:
+        if self.grad_sync is not None or self.tp is not None or self.ep is not None or self.etp is not None:
             raise RuntimeError("offload applies to a single-GPU trainer (peer-mapped buffers stay resident)")
         from .offload import OffloadState
 
@@ -441,6 +458,10 @@ class GRPOTrainer:
         dp_world = self.world // shard
         dp_rank = self.rank // shard
         pad_to = 128 * shard if shard > 1 else 64
+        if self.etp is not None:
+            # the ETP all-gather wants equal token counts on every member: rows
+            # keep their full packed length
+            pad_to = max(int(packed["tokens"].shape[1]), 1)
         cfgm = self.model.cfg
         linear = any(cfgm.layer_kind(i) != "attention" for i in range(cfgm.num_hidden_layers))
 
@@ -449,7 +470,7 @@ class GRPOTrainer:
                              conv_width=cfgm.linear_conv_kernel_dim, linear_layers=linear)
 
         mbs = [one(r) for r in list(range(n_rows))[dp_rank::dp_world]]
-        if self.ep is not None:
+        if self.ep is not None or self.etp is not None:
             per_rank = (n_rows + dp_world - 1) // dp_world
             while len(mbs) < per_rank:
                 mbs.append(zero_weight(one(dp_rank % n_rows)))

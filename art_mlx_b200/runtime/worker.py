@@ -13,7 +13,7 @@ Usage (what ``MultiGPUBackend`` runs)::
     python -m torch.distributed.run --nnodes 1 --nproc-per-node N \\
         --master-addr 127.0.0.1 --master-port P \\
         -m art_mlx_b200.runtime.worker --jobs-dir D --model qwen2.5-7b \\
-        --lora '{"r": 16, "alpha": 32}' --tp 1 --cp 1 --init-checkpoint C
+        --lora '{"r": 16, "alpha": 32}' --tp 1 --cp 1 --etp 1 --init-checkpoint C
 """
 
 from __future__ import annotations
@@ -124,6 +124,7 @@ def main(argv: list[str] | None = None) -> None:
     ap.add_argument("--adamw", default="{}", help="AdamW settings as JSON")
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--cp", type=int, default=1)
+    ap.add_argument("--etp", type=int, default=1)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--device", choices=["cuda", "cpu"], default="cuda" if torch.cuda.is_available() else "cpu")
     ap.add_argument("--init-checkpoint", required=True, help="adapter to load, written first if missing")
@@ -153,7 +154,7 @@ def main(argv: list[str] | None = None) -> None:
         lora = LoRASpec.from_peft(json.loads(args.lora)) if json.loads(args.lora) else LoRASpec()
         adamw = AdamWConfig(**json.loads(args.adamw))
         tr = GRPOTrainer(cfg, lora, device, seed=args.seed, adamw=adamw, group=dist.group.WORLD,
-                         tp_size=args.tp, cp_size=args.cp)
+                         tp_size=args.tp, cp_size=args.cp, etp_size=args.etp)
         if args.base_model and hasattr(tr.model, "load_hf_state_dict"):
             from ..models.weights import maybe_load_base_weights
 

@@ -79,7 +79,7 @@ def _shape(backend: str, cfg: ModelConfig) -> tuple[int, int, int, int]:
     return cfg.vocab_size, 96, 48, 512
 
 
-def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1, cp_size=1):
+def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1, cp_size=1, etp_size=1):
     if backend == "nccl":
         torch.cuda.set_device(rank)
         device = torch.device("cuda", rank)
@@ -93,9 +93,10 @@ def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1, cp_s
         cfg = {"dp-small": GPU_CFG, **CONFIGS}.get(cfg_name) or get_config(cfg_name)
         packed = _packed(*_shape(backend, cfg))
         tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), device, seed=0, group=dist.group.WORLD, tp_size=tp_size,
-                         cp_size=cp_size)
+                         cp_size=cp_size, etp_size=etp_size)
         assert (tr.grad_sync is not None) == (backend == "nccl")
-        assert (tr.ep is not None) == cfg.is_moe
+        assert (tr.ep is not None) == (cfg.is_moe and world // etp_size > 1)
+        assert (tr.etp is not None) == (etp_size > 1)
         for _ in range(2):
             m = tr.train_step(packed, 1e-3, {})
         host = m.to_host()
@@ -116,12 +117,12 @@ def _single(device, cfg, backend):
     return tr.store.master.cpu(), m.to_host(), packed
 
 
-def _run(world, backend, cfg_name, tp_size=1, cp_size=1):
+def _run(world, backend, cfg_name, tp_size=1, cp_size=1, etp_size=1):
     d = tempfile.mkdtemp()
     init = os.path.join(d, "init")
     out = os.path.join(d, "out.pt")
-    mp.start_processes(_worker, args=(world, init, out, backend, cfg_name, tp_size, cp_size), nprocs=world,
-                       start_method="spawn")
+    mp.start_processes(_worker, args=(world, init, out, backend, cfg_name, tp_size, cp_size, etp_size),
+                       nprocs=world, start_method="spawn")
     return torch.load(out)
 
 
@@ -151,6 +152,28 @@ def test_ep_moe_gloo_matches_single_process():
     err = (res["master"] - master).norm() / master.norm()
     assert err < 1e-5, err
     assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-5
+
+
+@pytest.mark.parametrize("world,etp", [(2, 2), (4, 2)])
+def test_etp_moe_gloo_matches_single_process(world, etp):
+    """Expert tensor parallelism (each expert's FFN split over etp ranks; with
+    world 4 also expert parallelism over the 2 ETP groups) vs one process."""
+    res = _run(world, "gloo", "moe-tiny", etp_size=etp)
+    master, metrics, _ = _single(torch.device("cpu"), MOE_CPU, "gloo")
+    err = (res["master"] - master).norm() / master.norm()
+    assert err < 1e-5, err
+    assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-5
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_etp_moe_two_gpus_matches_single_gpu():
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    res = _run(2, "nccl", "moe-small", etp_size=2)
+    master, metrics, _ = _single(torch.device("cuda", 0), MOE_GPU, "nccl")
+    err = (res["master"] - master).norm() / master.norm()
+    # bf16 partial expert outputs are summed over the two slices in another order than on one GPU
+    assert err < 1e-2, err
 
 
 @pytest.mark.gpu
