@@ -13,16 +13,23 @@
 //               a V slot when P V completes, so the loads run ahead of the
 //               tensor cores instead of sitting on the per-tile critical path
 //   warp 1      TMEM allocation (512 columns) and the MMA issuer:
-//                 S[b] = Q K^T         (M=128, N=128, K=128; both K-major)
-//                 O   += P V           (P K-major from shared memory, V
-//                                       MN-major straight from its TMA tile)
+//                 S[b] = Q K^T         (M=128, N=128, K=128; both K-major,
+//                                       b = tile & 1)
+//                 O   += P V           (P read from TMEM, where the softmax
+//                                       stored it over S[b]; V MN-major
+//                                       straight from its TMA tile)
 //               S of tile n+1 is issued before P V of tile n, so the tensor
-//               cores compute the next scores while the softmax runs
-//   warps 2..5  softmax, one query row per thread (TMEM lane = row): read the
-//               S row (tcgen05.ld), mask, online max with lazy rescaling of O
-//               (only when the running max grows by more than 2^8), exp2,
-//               row sum, P row as bf16 into swizzled shared memory; finally
-//               O / l to global memory and the LSE.
+//               cores compute the next scores while the softmax runs; the
+//               commit after P V releases S[b] and the V slot
+//   warps 2..9  softmax, two warps per TMEM lane quadrant (one query row per
+//               thread, each warp 64 of the 128 key columns and 64 of the
+//               output columns): read the S half-row (tcgen05.ld), mask,
+//               running max (exchanged with the partner warp through a
+//               bounded mbarrier handshake) with lazy rescaling of O (only
+//               when the max grows by more than 2^8, the only time the
+//               softmax waits for the previous P V), exp2, row sum, P as
+//               bf16 pairs into the first 32 columns of the warp's S columns
+//               (tcgen05.st); finally O / l to global memory and the LSE.
 // TMEM columns: S[0] 0..127, S[1] 128..255, O 256..383.
 // All mbarrier waits are bounded (tc_common.cuh): on timeout the kernel
 // records an error code, every role leaves its loop and TMEM is freed.
@@ -104,7 +111,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   uint64_t* s_full = bars + 9;    // [2]
   uint64_t* s_empty = bars + 11;  // [2]
   uint64_t* p_full = bars + 13;
-  uint64_t* pv_done = bars + 14;
+  uint64_t* pv_done = bars + 14;  // [2]: P V of tile m completes phase m>>1 of pv_done[m&1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint64_t* xbar = bars + 18;  // [4]: the two softmax warps of a lane quadrant exchange row max / sum
@@ -125,10 +132,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], FA_SOFT);
+      mbar_init(&s_empty[s], 1);  // committed after the P V that read P from this buffer
+      mbar_init(&pv_done[s], 1);
     }
     mbar_init(p_full, FA_SOFT);
-    mbar_init(pv_done, 1);
     for (int qd = 0; qd < 4; ++qd) mbar_init(&xbar[qd], 64);
     *abort_flag = 0;
     fence_barrier_init();
@@ -188,21 +195,22 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       constexpr uint32_t idS = idesc_bf16(FB, FB);
       constexpr uint32_t idO = idesc_bf16_bmn(FB, FB);
       const uint32_t qa = smem_addr(smem + OFF_Q);
-      const uint32_t pa = smem_addr(smem + OFF_P);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.err, 12);
       tc_fence_after();
-      auto issue_pv = [&](int n) -> bool {  // O += P_n V_n
+      auto issue_pv = [&](int n) -> bool {  // O += P_n V_n, P_n read from TMEM (S buffer n&1)
         const int s = n & 1;
         if (!mbar_wait(p_full, n & 1, abort_flag, p.err, 13)) return false;
         if (!mbar_wait(&v_full[s], (n >> 1) & 1, abort_flag, p.err, 10)) return false;
         tc_fence_after();
         const uint32_t va = smem_addr(smem + OFF_V + s * TILE_BYTES);
+        const uint32_t pt = tmem + s * FB;  // each half's P in the first 32 columns of its S columns
 #pragma unroll
         for (int kk = 0; kk < FB / 16; ++kk)
-          mma_bf16(tmem_o, desc_k_sw128(pa + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32),
-                   desc_mn_sw128(va + kk * 2048, CHUNK_BYTES), idO, (n > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ts(tmem_o, pt + (kk >> 2) * 64 + (kk & 3) * 8, desc_mn_sw128(va + kk * 2048, CHUNK_BYTES), idO,
+                      (n > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&v_empty[s]);
-        mma_commit(pv_done);
+        mma_commit(&s_empty[s]);
+        mma_commit(&pv_done[s]);
         return true;
       };
       int n = 0;
@@ -231,9 +239,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     const int row = quad * 32 + lane;
     const int gi = g0 + row;  // global query position of this thread's row
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    uint8_t* prow = smem + OFF_P + half * CHUNK_BYTES + row * 128;
     float* xch = reinterpret_cast<float*>(smem + OFF_X);  // [slot][half][row]; slots 0/1 max, 2 sum
-    const int sw = row & 7;
     float m_ref = -INFINITY, l = 0.f;  // l: this half's share of the row sum
     int n = 0;
     bool ok = true;
@@ -254,8 +260,6 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(r[c][e]);
       }
-      tc_fence_before();
-      mbar_arrive(&s_empty[b]);
       // mask + scale, running max (fully visible tiles skip the mask)
       const int k0 = kt * FB + half * 64;
       float mx = -INFINITY;
@@ -293,18 +297,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       mbar_arrive(&xbar[quad]);
       if (!mbar_wait_warp(&xbar[quad], n & 1, abort_flag, p.err, 19)) { ok = false; break; }
       mx = fmaxf(mx, xch[(b * 2 + (half ^ 1)) * FB + row]);
-      // P buffer and O are free once P V of the previous tile completed
-      if (n > 0) {
-        if (!mbar_wait_warp(pv_done, (n - 1) & 1, abort_flag, p.err, 17)) { ok = false; break; }
-        tc_fence_after();
-      }
       // lazy rescale: a row moves its reference max only when the tile max
       // exceeds it by more than 2^8 (both halves decide alike: same max).
       // tcgen05.ld/st are warp-collective, so the warp rescales its O columns
-      // when any of its rows needs it (alpha = 1 for the others).
+      // when any of its rows needs it (alpha = 1 for the others).  Only then
+      // does it wait for P V of the previous tile (O is being accumulated);
+      // otherwise the softmax runs ahead of the P V MMAs.  The wait stays
+      // within one phase: s_full of this tile already implies P V of tile
+      // n-2 completed (both were committed by the MMA thread in order).
       const bool move = mx > m_ref + kRescaleThreshold || (m_ref == -INFINITY && mx > -INFINITY);
       const bool scale_o = move && n > 0 && m_ref > -INFINITY;
       if (__any_sync(0xffffffffu, scale_o)) {
+        if (!mbar_wait_warp(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort_flag, p.err, 17)) { ok = false; break; }
+        tc_fence_after();
         const float alpha = scale_o ? exp2f(m_ref - mx) : 1.f;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
@@ -319,26 +324,22 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         l *= alpha;
       }
       if (move) m_ref = mx;
-      // P = exp2(s - m_ref) as bf16: this half's 64 keys are one swizzled K chunk
+      // P = exp2(s - m_ref) as bf16 into tensor memory: this half's 64 keys
+      // as 32 columns of bf16 pairs over the first half of its own S columns
+      // (the P V MMA reads its A operand there)
       float rs = 0.f;
+      uint32_t pk[32];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        float e8[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float x = sv[u * 8 + e];
-          e8[e] = (x == -INFINITY) ? 0.f : exp2f(x - m_ref);
-          rs += e8[e];
-        }
-        uint4 pk;
-        pk.x = pack_bf16x2(e8[0], e8[1]);
-        pk.y = pack_bf16x2(e8[2], e8[3]);
-        pk.z = pack_bf16x2(e8[4], e8[5]);
-        pk.w = pack_bf16x2(e8[6], e8[7]);
-        *reinterpret_cast<uint4*>(prow + ((u ^ sw) << 4)) = pk;
+      for (int c = 0; c < 32; ++c) {
+        const float x0 = sv[2 * c], x1 = sv[2 * c + 1];
+        const float e0 = (x0 == -INFINITY) ? 0.f : exp2f(x0 - m_ref);
+        const float e1 = (x1 == -INFINITY) ? 0.f : exp2f(x1 - m_ref);
+        rs += e0 + e1;
+        pk[c] = pack_bf16x2(e0, e1);
       }
+      tmem_st32(tmem + lane_base + b * FB + half * 64, pk);
+      tmem_wait_st();
       l += rs;
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
@@ -347,7 +348,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     if (ok && n > 0) {
       xch[(4 + half) * FB + row] = l;  // own slot: the max slots may still be read by the partner
       bool got = false;
-      if (mbar_wait_warp(pv_done, (n - 1) & 1, abort_flag, p.err, 18)) {
+      if (mbar_wait_warp(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort_flag, p.err, 18)) {
         mbar_arrive(&xbar[quad]);
         got = mbar_wait_warp(&xbar[quad], n & 1, abort_flag, p.err, 20);
       }
