@@ -452,12 +452,16 @@ std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::
 //
 // CTA = one work unit (128-key block kb, local 128-query tiles [t_lo, t_hi))
 // x one kv head; it loops over the G q heads of that kv head and the query
-// tiles, with K and V of the block resident in shared memory:
+// tiles, with K and V of the block resident in shared memory and Q / dO
+// double-buffered (the next tile's TMA loads run under the current tile):
 //   S^T  = K Q^T          (TMEM cols   0..127, lanes = keys)
 //   dP^T = V dO^T         (TMEM cols 128..255)
 //   softmax warps: P^T = exp2(S^T*scale*log2e - lse*log2e) under the mask,
-//                  dS^T = P^T (dP^T - delta)  -> bf16 tiles in shared memory
-//   dV  += P^T dO         (TMEM cols 256..383, dO as an MN-major B operand)
+//                  dS^T = P^T (dP^T - delta); dS^T as a bf16 tile in shared
+//                  memory, P^T as bf16 pairs in TMEM over the dP^T columns
+//                  each warp has already read (cols 128+64h .. +32)
+//   dV  += P^T dO         (TMEM cols 256..383, P^T a tensor-memory A operand,
+//                          dO an MN-major B operand)
 //   dK  += dS^T Q         (TMEM cols 384..511)
 //   dQ   = dS K           (TMEM cols 0..127, dS^T read as an MN-major A
 //                          operand, K as an MN-major B operand; lanes = queries)
@@ -470,11 +474,10 @@ namespace {
 
 constexpr int B_OFF_K = 0;
 constexpr int B_OFF_V = TILE_BYTES;
-constexpr int B_OFF_Q = 2 * TILE_BYTES;
-constexpr int B_OFF_DO = 3 * TILE_BYTES;
-constexpr int B_OFF_P = 4 * TILE_BYTES;
-constexpr int B_OFF_DS = 5 * TILE_BYTES;
-constexpr int B_OFF_BAR = 6 * TILE_BYTES;
+constexpr int B_OFF_Q = 2 * TILE_BYTES;   // [2] stages
+constexpr int B_OFF_DO = 4 * TILE_BYTES;  // [2] stages
+constexpr int B_OFF_DS = 6 * TILE_BYTES;
+constexpr int B_OFF_BAR = 7 * TILE_BYTES;
 constexpr int FB_SMEM = B_OFF_BAR + 256 + 1024;
 // 2 control warps + 8 softmax warps: two warps per TMEM lane quadrant, each
 // taking 64 of the 128 query columns (the backward needs no row reduction)
@@ -525,13 +528,13 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + B_OFF_BAR);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* qdo_empty = bars + 2;
-  uint64_t* sdp_full = bars + 3;
-  uint64_t* ds_full = bars + 4;
-  uint64_t* dq_full = bars + 5;
-  uint64_t* dq_free = bars + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* sdp_full = bars + 1;
+  uint64_t* ds_full = bars + 2;
+  uint64_t* dq_full = bars + 3;
+  uint64_t* dq_free = bars + 4;
+  uint64_t* qdo_full = bars + 5;   // [2]
+  uint64_t* qdo_empty = bars + 7;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -544,8 +547,10 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qdo_full, 1);
-    mbar_init(qdo_empty, 1);
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(&qdo_full[st], 1);
+      mbar_init(&qdo_empty[st], 1);
+    }
     mbar_init(sdp_full, 1);
     mbar_init(ds_full, FB_SOFT);
     mbar_init(dq_full, 1);
@@ -571,14 +576,17 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       tma_load_2d(smem + B_OFF_K + CHUNK_BYTES, &tmK, kv_full, hk * FB + 64, kb * FB);
       tma_load_2d(smem + B_OFF_V, &tmV, kv_full, hk * FB, kb * FB);
       tma_load_2d(smem + B_OFF_V + CHUNK_BYTES, &tmV, kv_full, hk * FB + 64, kb * FB);
-      for (int i = 0; i < iters; ++i) {
+      for (int i = 0; i < iters; ++i) {  // Q / dO double-buffered: tile i+1 loads while tile i computes
         const int h = hk * G + i / ntiles, t = t_lo + i % ntiles;
-        if (!mbar_wait(qdo_empty, (i & 1) ^ 1, abort_flag, p.err, 21)) break;
-        mbar_arrive_expect_tx(qdo_full, 2 * TILE_BYTES);
-        tma_load_2d(smem + B_OFF_Q, &tmQ, qdo_full, h * FB, t * FB);
-        tma_load_2d(smem + B_OFF_Q + CHUNK_BYTES, &tmQ, qdo_full, h * FB + 64, t * FB);
-        tma_load_2d(smem + B_OFF_DO, &tmDO, qdo_full, h * FB, t * FB);
-        tma_load_2d(smem + B_OFF_DO + CHUNK_BYTES, &tmDO, qdo_full, h * FB + 64, t * FB);
+        const int st = i & 1;
+        if (!mbar_wait(&qdo_empty[st], ((i >> 1) & 1) ^ 1, abort_flag, p.err, 21)) break;
+        uint8_t* qb = smem + B_OFF_Q + st * TILE_BYTES;
+        uint8_t* db = smem + B_OFF_DO + st * TILE_BYTES;
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * TILE_BYTES);
+        tma_load_2d(qb, &tmQ, &qdo_full[st], h * FB, t * FB);
+        tma_load_2d(qb + CHUNK_BYTES, &tmQ, &qdo_full[st], h * FB + 64, t * FB);
+        tma_load_2d(db, &tmDO, &qdo_full[st], h * FB, t * FB);
+        tma_load_2d(db + CHUNK_BYTES, &tmDO, &qdo_full[st], h * FB + 64, t * FB);
       }
     }
   } else if (warp == 1) {
@@ -588,11 +596,13 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       constexpr uint32_t idKM = idesc_bf16_bmn(FB, FB);              // B MN-major
       constexpr uint32_t idMM = idesc_bf16_bmn(FB, FB) | (1u << 15);  // A and B MN-major
       const uint32_t ka = smem_addr(smem + B_OFF_K), va = smem_addr(smem + B_OFF_V);
-      const uint32_t qa = smem_addr(smem + B_OFF_Q), doa = smem_addr(smem + B_OFF_DO);
-      const uint32_t pa = smem_addr(smem + B_OFF_P), dsa = smem_addr(smem + B_OFF_DS);
+      const uint32_t dsa = smem_addr(smem + B_OFF_DS);
       if (mbar_wait(kv_full, 0, abort_flag, p.err, 22)) {
         for (int i = 0; i < iters; ++i) {
-          if (!mbar_wait(qdo_full, i & 1, abort_flag, p.err, 23)) break;
+          const int st = i & 1;
+          const uint32_t qa = smem_addr(smem + B_OFF_Q + st * TILE_BYTES);
+          const uint32_t doa = smem_addr(smem + B_OFF_DO + st * TILE_BYTES);
+          if (!mbar_wait(&qdo_full[st], (i >> 1) & 1, abort_flag, p.err, 23)) break;
           if (!mbar_wait(dq_free, (i & 1) ^ 1, abort_flag, p.err, 24)) break;
           tc_fence_after();
 #pragma unroll
@@ -612,10 +622,13 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
           for (int kk = 0; kk < FB / 16; ++kk) {
             const uint32_t ko = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
             const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-            mma_bf16(tmem + 256, desc_k_sw128(pa + ko), desc_mn_sw128(doa + kk * 2048, CHUNK_BYTES), idKM, acc);
+            // dV += P^T dO with P^T read from TMEM (bf16 pairs over the dP^T columns: queries
+            // [64h, 64h+64) at columns 128 + 64h .. +32)
+            mma_bf16_ts(tmem + 256, tmem + 128 + (kk >> 2) * 64 + (kk & 3) * 8,
+                        desc_mn_sw128(doa + kk * 2048, CHUNK_BYTES), idKM, acc);
             mma_bf16(tmem + 384, desc_k_sw128(dsa + ko), desc_mn_sw128(qa + kk * 2048, CHUNK_BYTES), idKM, acc);
           }
-          mma_commit(qdo_empty);
+          mma_commit(&qdo_empty[st]);
 #pragma unroll
           for (int kk = 0; kk < FB / 16; ++kk)
             mma_bf16(tmem + 0, desc_mn_sw128(dsa + kk * 2048, CHUNK_BYTES),
@@ -653,12 +666,13 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       for (int cc = 0; cc < 2; ++cc) {
         const int c = 2 * half + cc;
         uint32_t rs[32], rd[32];
+        uint32_t pp[16];  // P^T of these 32 queries, bf16 pairs
         tmem_ld32(tmem + lane_base + c * 32, rs);
         tmem_ld32(tmem + lane_base + 128 + c * 32, rd);
         const float lse_mine = lse_pf[cc];
         const float del_mine = del_pf[cc];
         tmem_wait_ld();
-        uint32_t pp[16], dd[16];
+        uint32_t dd[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float pv[2], dv2[2];
@@ -681,10 +695,14 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         for (int w = 0; w < 4; ++w) {
           const int u = c * 4 + w;  // unit along the 128-query row
           const uint32_t off = (u >> 3) * CHUNK_BYTES + row * 128 + (((u & 7) ^ sw) << 4);
-          *reinterpret_cast<uint4*>(smem + B_OFF_P + off) = make_uint4(pp[4 * w], pp[4 * w + 1], pp[4 * w + 2], pp[4 * w + 3]);
           *reinterpret_cast<uint4*>(smem + B_OFF_DS + off) = make_uint4(dd[4 * w], dd[4 * w + 1], dd[4 * w + 2], dd[4 * w + 3]);
         }
+        // P^T of these 32 queries as 16 columns of bf16 pairs at 128 + 64*half
+        // + 16*cc: over dP^T columns of queries 64*half .. +32, which this
+        // warp has already read (chunk cc = 0)
+        tmem_st16(tmem + lane_base + 128 + half * 64 + cc * 16, pp);
       }
+      tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
