@@ -308,7 +308,9 @@ class _EPExperts(torch.autograd.Function):
         out, saved = experts_forward(xs, plan.local_counts, params, lora)
         tr.publish(out, 1)
         slots = tr.pull(plan, 1)
-        y = native_combine(slots, w, plan.k)
+        from ..parallel import mutation
+
+        y = native_combine(slots, None if mutation.active("ep_skip_combine_weights") else w, plan.k)
         ctx.plan, ctx.ep, ctx.params, ctx.saved = plan, ep, params, saved
         ctx.save_for_backward(slots, w)
         return y

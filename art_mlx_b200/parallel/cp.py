@@ -33,6 +33,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops import fused, native
+from . import mutation
 
 
 CP_BARRIER_TIMEOUT_NS = 60 * 10**9
@@ -399,7 +400,8 @@ def cp_gdn(layer, h: torch.Tensor, plan: CPPlan, cp: CPContext, version: int, en
     S_out: list[torch.Tensor] = []
     S_in: list[torch.Tensor] = []
     for i, pc in enumerate(plan.pieces):
-        sin = S_out[pc.pred] if pc.pred >= 0 else q.new_zeros(Hh, dk, dv)
+        handoff = pc.pred >= 0 and not mutation.active("cp_skip_state_handoff")
+        sin = S_out[pc.pred] if handoff else q.new_zeros(Hh, dk, dv)
         row = allsumm[plan.slot_of[i]]
         S_in.append(sin)
         S_out.append(row[..., :dk] @ sin + row[..., dk:])

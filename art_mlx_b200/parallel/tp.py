@@ -31,6 +31,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops import native
+from . import mutation
 
 TP_BARRIER_TIMEOUT_NS = 60 * 10**9
 
@@ -100,7 +101,8 @@ class TPContext:
             dist.reduce_scatter_tensor(out, x.contiguous(), group=self.group)
             return out
         y = x.clone()
-        dist.all_reduce(y, group=self.group)
+        if not mutation.active("tp_skip_reduce_scatter"):
+            dist.all_reduce(y, group=self.group)
         return y[self.rank * rows : (self.rank + 1) * rows].clone()
 
     # ---------------------------------------------------------------- fused

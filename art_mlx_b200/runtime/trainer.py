@@ -34,6 +34,7 @@ from ..models.config import LoRASpec, ModelConfig
 from ..models.transformer import DecoderLM
 from ..ops import fused
 from ..ops.fused import AttnMeta
+from ..parallel import mutation
 from ..preprocessing.prefix_tree import visibility_ends
 from .optimizer import AdamWConfig, FlatAdamW
 
@@ -493,6 +494,8 @@ class GRPOTrainer:
         total = float(mask[:, 1:].sum().item())  # trainable (scored) tokens of the whole step
         if micro_batches is None:
             micro_batches = self.stage(packed)
+        if mutation.active("dp_local_token_normalization"):
+            total = float(sum(int(mb.sel.numel()) for mb in micro_batches))
         acc = {k: torch.zeros((), device=self.device) for k in ("loss", "entropy", "probs_corr", "kl")}
         n_tokens = 0
         for mb in micro_batches:
@@ -511,7 +514,8 @@ class GRPOTrainer:
             if self.grad_sync is not None:
                 self.grad_sync.reduce_and_step(self.optim, learning_rate, stats)
             else:
-                dist.all_reduce(self.store.grad, group=self.group)
+                if not mutation.active("dp_skip_grad_reduce"):
+                    dist.all_reduce(self.store.grad, group=self.group)
                 dist.all_reduce(stats, group=self.group)
                 self.optim.step(learning_rate)
             acc["loss"], acc["entropy"], acc["probs_corr"], acc["kl"] = stats.unbind(0)

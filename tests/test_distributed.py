@@ -145,6 +145,16 @@ def test_fused_dp_two_gpus_matches_single_gpu():
     assert abs(res["metrics"]["loss/grad_norm"] - metrics["loss/grad_norm"]) < 2e-2 * abs(metrics["loss/grad_norm"])
 
 
+@pytest.mark.parametrize("cfg_name,tp,cp", [("tp-tiny", 2, 1), ("hybrid-tiny", 1, 2)])
+def test_dp_times_shard_gloo_matches_single_process(cfg_name, tp, cp):
+    """4 CPU ranks: data parallel x (tensor or context parallel 2) vs one process."""
+    res = _run(4, "gloo", cfg_name, tp_size=tp, cp_size=cp)
+    master, metrics, _ = _single(torch.device("cpu"), CONFIGS[cfg_name], "gloo")
+    err = (res["master"] - master).norm() / master.norm()
+    assert err < 1e-5, err
+    assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-5
+
+
 def test_ep_moe_gloo_matches_single_process():
     """Expert-parallel MoE (all-to-all transport, 2 CPU ranks) vs one process."""
     res = _run(2, "gloo", "moe-tiny")
