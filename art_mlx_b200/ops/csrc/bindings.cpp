@@ -3,9 +3,9 @@
 
 namespace art {
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> res,
-                                       torch::Tensor w, double eps);
+                                       torch::Tensor w, double eps, bool legacy);
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor xs, torch::Tensor w, torch::Tensor rstd,
-                          c10::optional<torch::Tensor> dres);
+                          c10::optional<torch::Tensor> dres, bool legacy);
 std::vector<torch::Tensor> rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
                                     int64_t nq, int64_t nkv, int64_t D,
                                     c10::optional<torch::Tensor> qn_w,
@@ -89,8 +89,11 @@ std::vector<torch::Tensor> gdn_conv_bwd(torch::Tensor dy, torch::Tensor x, torch
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "art_mlx_b200 sm_100a kernels";
-  m.def("rmsnorm_fwd", &art::rmsnorm_fwd);
-  m.def("rmsnorm_bwd", &art::rmsnorm_bwd);
+  // legacy=True: the block-per-row kernels (kept for comparison)
+  m.def("rmsnorm_fwd", &art::rmsnorm_fwd, py::arg("x"), py::arg("res"), py::arg("w"), py::arg("eps"),
+        py::arg("legacy") = false);
+  m.def("rmsnorm_bwd", &art::rmsnorm_bwd, py::arg("dy"), py::arg("xs"), py::arg("w"), py::arg("rstd"),
+        py::arg("dres"), py::arg("legacy") = false);
   m.def("rope_fwd", &art::rope_fwd);
   m.def("rope_bwd", &art::rope_bwd);
   m.def("swiglu_fwd", &art::swiglu_fwd);

@@ -110,6 +110,145 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
   }
 }
 
+// Warp-per-row variants (hidden size = NV * 256): a warp owns one row and
+// each lane NV 16-byte vectors of it (vector v*32 + lane, so a warp's loads are
+// contiguous 512-byte runs), kept in registers as raw bf16 between the two
+// passes (the backward re-reads its row through L2 in the second pass); the
+// row reductions are warp shuffles, so there is no block barrier
+// and a CTA of NORM_WARPS rows retires as soon as its warps do.  Same
+// per-element arithmetic as the kernels above.
+constexpr int NORM_WARPS = 4;
+
+template <int NV>
+__global__ void __launch_bounds__(NORM_WARPS * 32) rmsnorm_fwd_warp_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res, const __nv_bfloat16* __restrict__ w,
+    __nv_bfloat16* __restrict__ y, __nv_bfloat16* __restrict__ xsum, float* __restrict__ rstd, int64_t T, int H,
+    float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * NORM_WARPS + (threadIdx.x >> 5);
+  if (row >= T) return;  // warp-uniform
+  const __nv_bfloat16* xr = x + row * H;
+  uint4 xv[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) xv[v] = *reinterpret_cast<const uint4*>(xr + (v * 32 + lane) * 8);
+  float acc = 0.f;
+  if (res) {
+    const __nv_bfloat16* rr = res + row * H;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(rr + (v * 32 + lane) * 8);
+      __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv[v]);
+      const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        xe[k] = f2bf(bf2f(xe[k]) + bf2f(re[k]));  // residual stream is stored in bf16
+        const float a = bf2f(xe[k]);
+        acc += a * a;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv[v]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float a = bf2f(xe[k]);
+        acc += a * a;
+      }
+    }
+  }
+  const float r = rsqrtf(warp_sum(acc) / H + eps);
+  if (lane == 0) rstd[row] = r;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int64_t off = row * H + (v * 32 + lane) * 8;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + (v * 32 + lane) * 8);
+    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv[v]);
+    uint4 out;
+    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) oe[k] = f2bf(bf2f(f2bf(bf2f(xe[k]) * r)) * bf2f(we[k]));
+    *reinterpret_cast<uint4*>(y + off) = out;
+    if (xsum) *reinterpret_cast<uint4*>(xsum + off) = xv[v];
+  }
+}
+
+// 16-byte load that stays a separate load (L2, not L1): the backward's second
+// pass re-reads the row instead of keeping it in registers.
+__device__ __forceinline__ uint4 ld_cg16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(NORM_WARPS * 32) rmsnorm_bwd_warp_kernel(
+    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ xs, const __nv_bfloat16* __restrict__ w,
+    const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx, int64_t T,
+    int H) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * NORM_WARPS + (threadIdx.x >> 5);
+  if (row >= T) return;  // warp-uniform
+  const float r = rstd[row];
+  // pass 1: mean(w*dy*xhat); the row's dy and x come from HBM here
+  float acc = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int64_t off = row * H + (v * 32 + lane) * 8;
+    const uint4 dv = *reinterpret_cast<const uint4*>(dy + off);
+    const uint4 xv = *reinterpret_cast<const uint4*>(xs + off);
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + (v * 32 + lane) * 8);
+    const __nv_bfloat16* de = reinterpret_cast<const __nv_bfloat16*>(&dv);
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
+    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc += (bf2f(de[k]) * bf2f(we[k])) * (bf2f(xe[k]) * r);
+  }
+  const float mean = warp_sum(acc) / H;
+  // pass 2: dx, re-reading dy and x from L2
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int64_t off = row * H + (v * 32 + lane) * 8;
+    const uint4 dv = ld_cg16(dy + off);
+    const uint4 xv = ld_cg16(xs + off);
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + (v * 32 + lane) * 8);
+    const __nv_bfloat16* de = reinterpret_cast<const __nv_bfloat16*>(&dv);
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
+    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+    uint4 rv;
+    const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv);
+    if (dres) rv = *reinterpret_cast<const uint4*>(dres + off);
+    uint4 out;
+    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float val = r * (bf2f(de[k]) * bf2f(we[k]) - (bf2f(xe[k]) * r) * mean);
+      if (dres) val += bf2f(re[k]);
+      oe[k] = f2bf(val);
+    }
+    *reinterpret_cast<uint4*>(dx + off) = out;
+  }
+}
+
+// Hidden sizes with a warp-per-row instantiation (H = NV * 256).
+#define ART_NORM_NV(X) X(1) X(2) X(4) X(6) X(8) X(10) X(12) X(14) X(16) X(20) X(24)
+#define ART_NORM_NV_BWD(X) ART_NORM_NV(X)
+
+static bool norm_warp_ok(int H, bool bwd) {
+  if (H % 256 != 0) return false;
+  switch (H / 256) {
+#define ART_CASE(n) case n:
+    ART_NORM_NV_BWD(ART_CASE)
+#undef ART_CASE
+    return true;
+    default:
+      return false;
+  }
+}
+
 static int norm_threads(int H) {
   int t = (H / 8 + 7) / 8;  // 8 vectors of 8 per thread at most
   t = ((t + 31) / 32) * 32;
@@ -119,7 +258,7 @@ static int norm_threads(int H) {
 }
 
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> res,
-                                       torch::Tensor w, double eps) {
+                                       torch::Tensor w, double eps, bool legacy) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous());
   const int H = x.size(-1);
   TORCH_CHECK(H % 8 == 0 && H <= 8 * 8 * 1024, "rmsnorm: hidden size must be a multiple of 8");
@@ -137,17 +276,30 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Ten
   } else {
     xs = x;
   }
-  if (T > 0)
-    rmsnorm_fwd_kernel<8><<<T, norm_threads(H), 0, at::cuda::getCurrentCUDAStream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), rp,
-        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
-        reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), xsp, rstd.data_ptr<float>(), H, (float)eps);
+  auto st = at::cuda::getCurrentCUDAStream();
+  const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  const auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  if (T > 0 && !legacy && norm_warp_ok(H, false)) {
+    const unsigned grid = (unsigned)((T + NORM_WARPS - 1) / NORM_WARPS);
+    switch (H / 256) {
+#define ART_CASE(n)                                                                                          \
+  case n:                                                                                                    \
+    rmsnorm_fwd_warp_kernel<n><<<grid, NORM_WARPS * 32, 0, st>>>(xp, rp, wp, yp, xsp, rstd.data_ptr<float>(), T, \
+                                                                 H, (float)eps);                             \
+    break;
+      ART_NORM_NV(ART_CASE)
+#undef ART_CASE
+    }
+  } else if (T > 0) {
+    rmsnorm_fwd_kernel<8><<<T, norm_threads(H), 0, st>>>(xp, rp, wp, yp, xsp, rstd.data_ptr<float>(), H, (float)eps);
+  }
   ART_CUDA_CHECK(cudaGetLastError());
   return {y, xs, rstd};
 }
 
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor xs, torch::Tensor w, torch::Tensor rstd,
-                          c10::optional<torch::Tensor> dres) {
+                          c10::optional<torch::Tensor> dres, bool legacy) {
   TORCH_CHECK(dy.is_contiguous() && xs.is_contiguous());
   const int H = dy.size(-1);
   const int64_t T = dy.numel() / H;
@@ -157,12 +309,24 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor xs, torch::Tensor w, t
     TORCH_CHECK(dres->is_contiguous());
     dr = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
   }
-  if (T > 0)
-    rmsnorm_bwd_kernel<8><<<T, norm_threads(H), 0, at::cuda::getCurrentCUDAStream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
-        reinterpret_cast<const __nv_bfloat16*>(xs.data_ptr()),
-        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), rstd.data_ptr<float>(), dr,
-        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), H);
+  auto st = at::cuda::getCurrentCUDAStream();
+  const auto* dyp = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
+  const auto* xsp = reinterpret_cast<const __nv_bfloat16*>(xs.data_ptr());
+  const auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  auto* dxp = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  if (T > 0 && !legacy && norm_warp_ok(H, true)) {
+    const unsigned grid = (unsigned)((T + NORM_WARPS - 1) / NORM_WARPS);
+    switch (H / 256) {
+#define ART_CASE(n)                                                                                          \
+  case n:                                                                                                    \
+    rmsnorm_bwd_warp_kernel<n><<<grid, NORM_WARPS * 32, 0, st>>>(dyp, xsp, wp, rstd.data_ptr<float>(), dr, dxp, T, H); \
+    break;
+      ART_NORM_NV_BWD(ART_CASE)
+#undef ART_CASE
+    }
+  } else if (T > 0) {
+    rmsnorm_bwd_kernel<8><<<T, norm_threads(H), 0, st>>>(dyp, xsp, wp, rstd.data_ptr<float>(), dr, dxp, H);
+  }
   ART_CUDA_CHECK(cudaGetLastError());
   return dx;
 }

@@ -4,6 +4,7 @@
     python -m art_mlx_b200.ops.microbench gemm             # tcgen05 GEMM (+ fused LoRA) vs cuBLAS
     python -m art_mlx_b200.ops.microbench gemm_one         # 3 pair-GEMM calls, gate_up shape (ncu target)
     python -m art_mlx_b200.ops.microbench gdn              # gated DeltaNet scan / conv kernels vs PyTorch
+    python -m art_mlx_b200.ops.microbench norm             # residual-add RMSNorm: warp-per-row vs block-per-row
     python -m torch.distributed.run --nnodes 1 --nproc-per-node 2 --master-addr 127.0.0.1 \\
         --master-port 29533 -m art_mlx_b200.ops.microbench comm   # fused comm paths vs NCCL
 
@@ -154,6 +155,30 @@ def gemm_one() -> None:
         C.gemm_pair(a, b)
     torch.cuda.synchronize()
     _emit(case="gemm_one", tc_error=int(C.tc_error_code()))
+
+
+def bench_norm() -> None:
+    """Residual add + RMSNorm forward and backward on one packed row of the
+    benchmark (9231 tokens x 3584): warp-per-row kernels vs the block-per-row
+    ones, as achieved HBM bandwidth."""
+    from . import native
+
+    C = native.lib()
+    dev = torch.device("cuda")
+    T, H = 9231, 3584
+    x = torch.randn(T, H, device=dev).bfloat16()
+    res = torch.randn(T, H, device=dev).bfloat16()
+    w = torch.ones(H, device=dev).bfloat16()
+    dy = torch.randn(T, H, device=dev).bfloat16()
+    dres = torch.randn(T, H, device=dev).bfloat16()
+    _, xs, rstd = C.rmsnorm_fwd(x, res, w, 1e-6)
+    row = T * H * 2
+    for legacy in (False, True):
+        tf = _timed(lambda: C.rmsnorm_fwd(x, res, w, 1e-6, legacy))
+        tb = _timed(lambda: C.rmsnorm_bwd(dy, xs, w, rstd, dres, legacy))
+        _emit(case="rmsnorm_block_per_row" if legacy else "rmsnorm_warp_per_row", T=T, H=H,
+              fwd_ms=round(tf, 4), fwd_tbps=round(4 * row / tf / 1e9, 2),  # x, res in; y, sum out
+              bwd_ms=round(tb, 4), bwd_tbps=round(4 * row / tb / 1e9, 2))  # dy, x, dres in; dx out
 
 
 # ---------------------------------------------------------------------------
@@ -371,10 +396,12 @@ def main(argv: list[str]) -> None:
         gemm_one()
     elif which == "gdn":
         bench_gdn()
+    elif which == "norm":
+        bench_norm()
     elif which == "comm":
         bench_comm()
     else:
-        raise SystemExit(f"unknown case {which!r}: attn | gemm | gemm_one | gdn | comm")
+        raise SystemExit(f"unknown case {which!r}: attn | gemm | gemm_one | gdn | norm | comm")
 
 
 if __name__ == "__main__":

@@ -226,3 +226,35 @@ def test_model_step_matches_cpu_fp32(cuda):
         oc = tc.micro_step(stage_row(packed, row, torch.device("cpu")), {}, total)
         assert abs(float(og["loss"]) - float(oc["loss"])) < 2e-2 * max(1.0, abs(float(oc["loss"])))
     assert rel_err(tg.store.grad.cpu(), tc.store.grad) < 5e-2
+
+
+@pytest.mark.parametrize("H", [256, 3584, 5120, 64])
+@pytest.mark.parametrize("with_res", [True, False])
+def test_rmsnorm_warp_kernels_match_block_kernels_and_fp32(H, with_res):
+    """The warp-per-row RMSNorm kernels (hidden sizes = 256 * NV) against the
+    block-per-row kernels and an fp32 reference, forward and backward."""
+    C = native.lib()
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(H)
+    T = 777
+    x = torch.randn(T, H, device=dev, generator=g).bfloat16()
+    res = torch.randn(T, H, device=dev, generator=g).bfloat16() if with_res else None
+    w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).bfloat16()
+    dy = torch.randn(T, H, device=dev, generator=g).bfloat16()
+    dres = torch.randn(T, H, device=dev, generator=g).bfloat16() if with_res else None
+    y, xs, rstd = C.rmsnorm_fwd(x, res, w, 1e-6)
+    y0, xs0, rstd0 = C.rmsnorm_fwd(x, res, w, 1e-6, True)
+    assert torch.equal(xs, xs0)
+    assert float((rstd - rstd0).abs().max() / rstd0.abs().max()) < 1e-5
+    assert float((y.float() - y0.float()).abs().max()) <= 0.02 * float(y0.float().abs().max())
+    s = xs.float()
+    ref = (s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-6)).bfloat16().float() * w.float()
+    assert float((y.float() - ref).norm() / ref.norm()) < 1e-2
+    dx = C.rmsnorm_bwd(dy, xs, w, rstd, dres)
+    dx0 = C.rmsnorm_bwd(dy, xs, w, rstd, dres, True)
+    assert float((dx.float() - dx0.float()).norm() / dx0.float().norm()) < 1e-2
+    sr = s.clone().requires_grad_(True)
+    yr = sr * torch.rsqrt(sr.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    (yr * dy.float()).sum().backward()
+    want = sr.grad + (dres.float() if with_res else 0)
+    assert float((dx.float() - want).norm() / want.norm()) < 2e-2
