@@ -455,6 +455,10 @@ class _LoRALinear(torch.autograd.Function):
                 if gB is None:
                     continue
                 _accum_mm(gB, dy[:, a:b].t(), u[:, k * lora.r : (k + 1) * lora.r], s)
+        if not ctx.needs_input_grad[0]:
+            # the input needs no gradient (e.g. the first layer over the frozen
+            # embedding): the LoRA gradients above are all this pass owes
+            return None, None, None, None, None, None, None
         if ctx.pair_dgrad:
             # dx = dy W + (dy B) (s A): W read in its stored [out, in] layout
             at_s = lora.fused_factors(ctx.version)[1] if lora is not None else None
