@@ -452,8 +452,7 @@ std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::
 //
 // CTA = one work unit (128-key block kb, local 128-query tiles [t_lo, t_hi))
 // x one kv head; it loops over the G q heads of that kv head and the query
-// tiles, with K and V of the block resident in shared memory and Q / dO
-// double-buffered (the next tile's TMA loads run under the current tile):
+// tiles, with K and V of the block resident in shared memory:
 //   S^T  = K Q^T          (TMEM cols   0..127, lanes = keys)
 //   dP^T = V dO^T         (TMEM cols 128..255)
 //   softmax warps: P^T = exp2(S^T*scale*log2e - lse*log2e) under the mask,
@@ -465,19 +464,24 @@ std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::
 //   dK  += dS^T Q         (TMEM cols 384..511)
 //   dQ   = dS K           (TMEM cols 0..127, dS^T read as an MN-major A
 //                          operand, K as an MN-major B operand; lanes = queries)
-// then dQ*scale is added to global memory (red.global.add.v4.f32) and, after
+// then dQ*scale is added to global memory (red.global.add.v4.f32, transposed
+// through a per-warp shared-memory block so each instruction writes whole
+// 128-byte row segments) and, after
 // the last tile, dK*scale and dV are added for the block (several units may
 // share a key block).  delta = rowsum(dO * O) comes from attn_bwd_delta.
 // ============================================================================
 
 namespace {
 
+constexpr int QDO_ST = 1;  // Q / dO stages (shared memory goes to the dQ staging below)
+constexpr int DQ_LD = 36;  // row stride (floats) of a warp's 32x32 dQ staging block: conflict-free both ways
 constexpr int B_OFF_K = 0;
 constexpr int B_OFF_V = TILE_BYTES;
-constexpr int B_OFF_Q = 2 * TILE_BYTES;   // [2] stages
-constexpr int B_OFF_DO = 4 * TILE_BYTES;  // [2] stages
-constexpr int B_OFF_DS = 6 * TILE_BYTES;
-constexpr int B_OFF_BAR = 7 * TILE_BYTES;
+constexpr int B_OFF_Q = 2 * TILE_BYTES;
+constexpr int B_OFF_DO = B_OFF_Q + QDO_ST * TILE_BYTES;
+constexpr int B_OFF_DS = B_OFF_DO + QDO_ST * TILE_BYTES;
+constexpr int B_OFF_DQ = B_OFF_DS + TILE_BYTES;       // 8 warps x [32][DQ_LD] fp32
+constexpr int B_OFF_BAR = B_OFF_DQ + 8 * 32 * DQ_LD * 4;
 constexpr int FB_SMEM = B_OFF_BAR + 256 + 1024;
 // 2 control warps + 8 softmax warps: two warps per TMEM lane quadrant, each
 // taking 64 of the 128 query columns (the backward needs no row reduction)
@@ -578,8 +582,8 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       tma_load_2d(smem + B_OFF_V + CHUNK_BYTES, &tmV, kv_full, hk * FB + 64, kb * FB);
       for (int i = 0; i < iters; ++i) {  // Q / dO double-buffered: tile i+1 loads while tile i computes
         const int h = hk * G + i / ntiles, t = t_lo + i % ntiles;
-        const int st = i & 1;
-        if (!mbar_wait(&qdo_empty[st], ((i >> 1) & 1) ^ 1, abort_flag, p.err, 21)) break;
+        const int st = i % QDO_ST;
+        if (!mbar_wait(&qdo_empty[st], ((i / QDO_ST) & 1) ^ 1, abort_flag, p.err, 21)) break;
         uint8_t* qb = smem + B_OFF_Q + st * TILE_BYTES;
         uint8_t* db = smem + B_OFF_DO + st * TILE_BYTES;
         mbar_arrive_expect_tx(&qdo_full[st], 2 * TILE_BYTES);
@@ -599,10 +603,10 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       const uint32_t dsa = smem_addr(smem + B_OFF_DS);
       if (mbar_wait(kv_full, 0, abort_flag, p.err, 22)) {
         for (int i = 0; i < iters; ++i) {
-          const int st = i & 1;
+          const int st = i % QDO_ST;
           const uint32_t qa = smem_addr(smem + B_OFF_Q + st * TILE_BYTES);
           const uint32_t doa = smem_addr(smem + B_OFF_DO + st * TILE_BYTES);
-          if (!mbar_wait(&qdo_full[st], (i >> 1) & 1, abort_flag, p.err, 23)) break;
+          if (!mbar_wait(&qdo_full[st], (i / QDO_ST) & 1, abort_flag, p.err, 23)) break;
           if (!mbar_wait(dq_free, (i & 1) ^ 1, abort_flag, p.err, 24)) break;
           tc_fence_after();
 #pragma unroll
@@ -709,19 +713,31 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       // dQ tile: lanes are queries now
       if (!mbar_wait_warp(dq_full, i & 1, abort_flag, p.err, 27)) { ok = false; break; }
       tc_fence_after();
-      const int ql = t * FB + row;
+      // Each lane holds one query row of the chunk; the atomic adds go out
+      // transposed through a per-warp staging block so that one warp
+      // instruction covers 4 rows x 128 contiguous bytes (whole L2 sectors)
+      // instead of 32 rows x 16 bytes.
+      float* stg = reinterpret_cast<float*>(smem + B_OFF_DQ) + (warp - 2) * 32 * DQ_LD;
 #pragma unroll 1
       for (int c = 2 * half; c < 2 * half + 2; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_base + c * 32, r);
         tmem_wait_ld();
-        if (ql < p.Tq) {
-          float* dst = p.dq + ((int64_t)ql * p.Hq + h) * FB + c * 32;
 #pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            red_add_v4(dst + e, __uint_as_float(r[e]) * p.scale, __uint_as_float(r[e + 1]) * p.scale,
-                       __uint_as_float(r[e + 2]) * p.scale, __uint_as_float(r[e + 3]) * p.scale);
+        for (int e = 0; e < 32; e += 4)
+          *reinterpret_cast<float4*>(stg + lane * DQ_LD + e) =
+              make_float4(__uint_as_float(r[e]) * p.scale, __uint_as_float(r[e + 1]) * p.scale,
+                          __uint_as_float(r[e + 2]) * p.scale, __uint_as_float(r[e + 3]) * p.scale);
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int rr = 4 * k + (lane >> 3);  // row within the warp's 32
+          const int ql2 = t * FB + quad * 32 + rr;
+          const float4 v = *reinterpret_cast<const float4*>(stg + rr * DQ_LD + (lane & 7) * 4);
+          if (ql2 < p.Tq)
+            red_add_v4(p.dq + ((int64_t)ql2 * p.Hq + h) * FB + c * 32 + (lane & 7) * 4, v.x, v.y, v.z, v.w);
         }
+        __syncwarp();
       }
       tc_fence_before();
       mbar_arrive(dq_free);
@@ -729,21 +745,32 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
     // dK, dV of the block (all MMAs completed: the last dq_full covered them).
     // Every lane runs the warp-collective TMEM loads; rows past Tk skip the stores.
     if (ok && iters > 0) {
-      float* dkr = p.dk + ((int64_t)j * p.Hkv + hk) * FB;
-      float* dvr = p.dv + ((int64_t)j * p.Hkv + hk) * FB;
+      // same transposed atomic adds as dQ: 4 key rows x 128 bytes per instruction
+      float* stg = reinterpret_cast<float*>(smem + B_OFF_DQ) + (warp - 2) * 32 * DQ_LD;
 #pragma unroll 1
       for (int c = 2 * half; c < 2 * half + 2; ++c) {
-        uint32_t a[32], b[32];
-        tmem_ld32(tmem + lane_base + 384 + c * 32, a);
-        tmem_ld32(tmem + lane_base + 256 + c * 32, b);
-        tmem_wait_ld();
-        if (j >= p.Tk) continue;
+#pragma unroll 1
+        for (int which = 0; which < 2; ++which) {  // 0: dK (x scale), 1: dV
+          uint32_t a[32];
+          tmem_ld32(tmem + lane_base + (which ? 256 : 384) + c * 32, a);
+          tmem_wait_ld();
+          const float f = which ? 1.f : p.scale;
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          red_add_v4(dkr + c * 32 + e, __uint_as_float(a[e]) * p.scale, __uint_as_float(a[e + 1]) * p.scale,
-                     __uint_as_float(a[e + 2]) * p.scale, __uint_as_float(a[e + 3]) * p.scale);
-          red_add_v4(dvr + c * 32 + e, __uint_as_float(b[e]), __uint_as_float(b[e + 1]), __uint_as_float(b[e + 2]),
-                     __uint_as_float(b[e + 3]));
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(stg + lane * DQ_LD + e) =
+                make_float4(__uint_as_float(a[e]) * f, __uint_as_float(a[e + 1]) * f, __uint_as_float(a[e + 2]) * f,
+                            __uint_as_float(a[e + 3]) * f);
+          __syncwarp();
+          float* base = which ? p.dv : p.dk;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int rr = 4 * k + (lane >> 3);
+            const int jj = kb * FB + quad * 32 + rr;  // key row
+            const float4 v = *reinterpret_cast<const float4*>(stg + rr * DQ_LD + (lane & 7) * 4);
+            if (jj < p.Tk)
+              red_add_v4(base + ((int64_t)jj * p.Hkv + hk) * FB + c * 32 + (lane & 7) * 4, v.x, v.y, v.z, v.w);
+          }
+          __syncwarp();
         }
       }
     }
