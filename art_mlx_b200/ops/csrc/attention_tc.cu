@@ -139,6 +139,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     for (int qd = 0; qd < 4; ++qd) mbar_init(&xbar[qd], 64);
     *abort_flag = 0;
     fence_barrier_init();
+    // the Q tile depends on nothing below: start its load now, so its latency
+    // runs under the tile-list scan and the TMEM allocation
+    prefetch_tmap(&tmQ);
+    mbar_arrive_expect_tx(q_full, TILE_BYTES);
+    tma_load_2d(smem + OFF_Q, &tmQ, q_full, h * FB, q0);
+    tma_load_2d(smem + OFF_Q + CHUNK_BYTES, &tmQ, q_full, h * FB + 64, q0);
   }
   // visible key tiles of this query block, computed once (entries: kt | TILE_FULL)
   int* tlist = reinterpret_cast<int*>(smem + OFF_TL);
@@ -167,12 +173,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_2d(smem + OFF_Q, &tmQ, q_full, h * FB, q0);
-      tma_load_2d(smem + OFF_Q + CHUNK_BYTES, &tmQ, q_full, h * FB + 64, q0);
       for (int n = 0; n < ntl; ++n) {
         const int kt = tlist[n] & (TILE_FULL - 1);
         const int s = n & 1;
@@ -356,23 +358,35 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         tc_fence_after();
         l += xch[(4 + (half ^ 1)) * FB + row];
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        __nv_bfloat16* dst = p.o + (int64_t)qrow * p.ldo + (int64_t)h * FB + half * 64;
+        // the warp's 32 rows x 64 columns (128 bytes a row) go out through a
+        // per-warp block of the (now unused) P region, 16-byte chunks XOR-
+        // swizzled by row: each store instruction then writes 4 rows x 128
+        // contiguous bytes instead of 32 rows x 16 bytes
+        uint8_t* stg = smem + OFF_P + (warp - 2) * 32 * 128;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           uint32_t r[32];
           tmem_ld32(tmem_o + lane_base + half * 64 + c * 32, r);
           tmem_wait_ld();
-          if (qrow < p.Tq) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint4 o;
-              o.x = pack_bf16x2(__uint_as_float(r[j + 0]) * inv, __uint_as_float(r[j + 1]) * inv);
-              o.y = pack_bf16x2(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
-              o.z = pack_bf16x2(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
-              o.w = pack_bf16x2(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
-              *reinterpret_cast<uint4*>(dst + c * 32 + j) = o;
-            }
+          for (int j = 0; j < 32; j += 8) {
+            uint4 o;
+            o.x = pack_bf16x2(__uint_as_float(r[j + 0]) * inv, __uint_as_float(r[j + 1]) * inv);
+            o.y = pack_bf16x2(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+            o.z = pack_bf16x2(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
+            o.w = pack_bf16x2(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
+            const int u = c * 4 + j / 8;  // 16-byte chunk of the 128-byte row
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((u ^ (lane & 7)) << 4)) = o;
           }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int rr = 4 * k + (lane >> 3), u = lane & 7;
+          const int orow = q0 + quad * 32 + rr;
+          const uint4 o = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((u ^ (rr & 7)) << 4));
+          if (orow < p.Tq)
+            *reinterpret_cast<uint4*>(p.o + (int64_t)orow * p.ldo + (int64_t)h * FB + half * 64 + u * 8) = o;
         }
         if (qrow < p.Tq && half == 0)
           p.lse[(int64_t)h * p.Tq + qrow] = l > 0.f ? (m_ref + log2f(l)) / kLog2eF : -INFINITY;
