@@ -421,7 +421,11 @@ class MoEBlock:
         else:
             flat = ix.reshape(-1)
             order = torch.argsort(flat, stable=True)
-            counts = torch.bincount(flat, minlength=E).tolist()
+            host = ctx.get("replay_counts") if self.etp is None else None
+            if host is not None:  # replayed routes: group sizes known on the host, no device sync
+                counts = list(host[self.index]) + [0] * (E - len(host[self.index]))
+            else:
+                counts = torch.bincount(flat, minlength=E).tolist()
             tok = order // k
             xs = hx[tok]
             ys = _LocalExperts.apply(xs, counts, params, enabled, anchor)

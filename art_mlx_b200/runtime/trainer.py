@@ -26,6 +26,7 @@ import math
 from dataclasses import dataclass, field
 from typing import Any, Mapping
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -53,6 +54,9 @@ class MicroBatch:
     group: torch.Tensor  # [n] group id of the scored token
     original: torch.Tensor | None = None
     routes: torch.Tensor | None = None  # [L, layers, k] replayed MoE routes
+    # per MoE layer, tokens routed to each expert (host lists, from the replayed
+    # routes): the single-GPU MoE path sizes its expert groups without a sync
+    route_counts: list | None = None
     n_tokens: int = 0  # valid (non-padding) tokens in the row
     n_train: int = 0
     h2d_bytes: int = 0  # bytes copied host -> device to stage this row
@@ -63,6 +67,14 @@ class MicroBatch:
     @property
     def L(self) -> int:
         return int(self.tokens.numel())
+
+
+def _route_counts(routes: torch.Tensor) -> list[list[int]]:
+    """Tokens per expert for every MoE layer of a row's replayed routes
+    ``[T, layers, k]`` (host tensor); each list is a bincount over the expert
+    ids seen (the MoE layer pads it to its expert count)."""
+    r = routes.to(torch.int64).numpy()
+    return [np.bincount(r[:, layer, :].reshape(-1)).tolist() for layer in range(r.shape[1])]
 
 
 def _valid_length(group_ids: torch.Tensor) -> int:
@@ -112,9 +124,12 @@ def stage_row(
         return t.to(device, non_blocking=True)
 
     routes = None
+    route_counts = None
     rr = packed.get("moe_routing_replay")
     if rr is not None:
-        routes = dev(rr.expert_indices[row, :L])
+        host_routes = rr.expert_indices[row, :L]
+        routes = dev(host_routes)
+        route_counts = _route_counts(host_routes)
     orig = packed.get("original_logprobs")
     meta = AttnMeta.build(dev(pos), kend, device)
     moved[0] += sum(t.numel() * t.element_size() for t in (meta.kend, meta.tile_kmax, meta.tile_kmin, meta.bwd_units))
@@ -129,6 +144,7 @@ def stage_row(
         group=dev(packed["group_ids"][row, nxt]),
         original=dev(orig[row, nxt].float()) if orig is not None else None,
         routes=routes,
+        route_counts=route_counts,
         n_tokens=n_valid,
         n_train=int(sel.numel()),
         h2d_bytes=moved[0],
@@ -410,6 +426,8 @@ class GRPOTrainer:
             ctx["cp_plan"], ctx["cp"] = mb.cp_plan, self.cp
         if mb.routes is not None:
             ctx["replay_routes"] = mb.routes
+            if mb.route_counts is not None:
+                ctx["replay_counts"] = mb.route_counts
         ref = None
         kl_coef = float(cfg.get("kl_penalty_coef", 0.0) or 0.0)
         if kl_coef > 0:

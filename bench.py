@@ -164,7 +164,7 @@ def main() -> None:
     from art_mlx_b200.preprocessing.pack import packed_tensors_from_tokenized_results
     from art_mlx_b200.preprocessing.synthetic import synthetic_groups
     from art_mlx_b200.preprocessing.tokenize import tokenize_trajectory_groups
-    from art_mlx_b200.runtime.trainer import GRPOTrainer
+    from art_mlx_b200.runtime.trainer import GRPOTrainer, _route_counts
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -211,6 +211,9 @@ def main() -> None:
                                                            "parent_ids": mb.parent_ids, "cp_plan": mb.cp_plan,
                                                            "cp": trainer.cp})
             mb.routes = torch.stack([rec[i] for i in sorted(rec)], dim=1)
+            # as for routes that arrive from the rollout side, the per-layer
+            # expert group sizes are counted on the host while staging
+            mb.route_counts = _route_counts(mb.routes.cpu())
     l2_flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
 
     def step() -> None:
