@@ -52,8 +52,17 @@ def moe_lora_specs(cfg: ModelConfig, i: int, spec: LoRASpec) -> list[tuple[str, 
 # ---------------------------------------------------------------------------
 
 
+def _h2d(t: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """Host -> device without a stream sync: a copy from pageable memory waits
+    for the stream to drain first, one from pinned memory is queued like a
+    kernel (the grouped GEMMs call this for every expert layout)."""
+    if device.type == "cuda":
+        return t.pin_memory().to(device, non_blocking=True)
+    return t.to(device)
+
+
 def _offsets(counts: list[int], device: torch.device) -> torch.Tensor:
-    return torch.tensor(counts, dtype=torch.int64).cumsum(0).to(torch.int32).to(device, non_blocking=True)
+    return _h2d(torch.tensor(counts, dtype=torch.int64).cumsum(0).to(torch.int32), device)
 
 
 def _use_library_grouped(x: torch.Tensor, k: int, m: int) -> bool:
@@ -94,7 +103,7 @@ def pad_groups(x: torch.Tensor, counts: list[int], multiple: int = 8) -> tuple[t
         s += c
         d += pc
     out = x.new_zeros(d, *x.shape[1:])
-    out.index_copy_(0, dst.to(x.device, non_blocking=True), x)
+    out.index_copy_(0, _h2d(dst, x.device), x)
     return out, padded_counts
 
 
@@ -177,8 +186,7 @@ def _experts_forward_tc(xs, counts, p: ExpertParams, lora: bool):
         bd[:, Fh:, r:] = s * p.B_gu[:, 1]
         a2, b2 = u_gu.contiguous(), bd.view(E * F2, 2 * r)
     gu = C.gemm_tc_grouped(xs.contiguous(), p.gu_w_t.view(E * H, F2), offs, F2, a2, b2, True)
-    g, up = gu[:, :Fh], gu[:, Fh:]
-    act = ((g.float() * torch.sigmoid(g.float())).to(gu.dtype) * up).contiguous()
+    act = C.swiglu_fwd(gu)  # fused silu(gate) * up over the [gate | up] halves
     a2 = b2 = None
     if lora and p.A_d is not None:
         u_d = grouped_mm(act, p.A_d.transpose(1, 2), counts).contiguous()  # [N, r]
@@ -238,10 +246,13 @@ def experts_backward(dout: torch.Tensor, saved, p: ExpertParams) -> torch.Tensor
         grouped_wgrad(dyB, act, counts, p.g_A_d, s)
         dact = dact + s * grouped_mm(dyB, p.A_d, counts)
     Fh = gu.shape[1] // 2
-    g, up = gu[:, :Fh].float(), gu[:, Fh:].float()
-    sg = torch.sigmoid(g)
-    da = dact.float()
-    dgu = torch.cat([da * up * sg * (1 + g * (1 - sg)), da * g * sg], dim=1).to(gu.dtype)
+    if tc:
+        dgu = C.swiglu_bwd(dact.contiguous(), gu)  # fused SwiGLU backward into [dgate | dup]
+    else:
+        g, up = gu[:, :Fh].float(), gu[:, Fh:].float()
+        sg = torch.sigmoid(g)
+        da = dact.float()
+        dgu = torch.cat([da * up * sg * (1 + g * (1 - sg)), da * g * sg], dim=1).to(gu.dtype)
     if tc:
         a2 = b2 = None
         if lora and p.A_gu is not None:
