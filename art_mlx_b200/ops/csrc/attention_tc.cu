@@ -552,6 +552,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
   uint64_t* dq_free = bars + 4;
   uint64_t* qdo_full = bars + 5;   // [2]
   uint64_t* qdo_empty = bars + 7;  // [2]
+  uint64_t* dv_done = bars + 9;    // dV / dK of a tile finished (P^T read from the dP^T columns)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -570,6 +571,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       mbar_init(&qdo_empty[st], 1);
     }
     mbar_init(sdp_full, 1);
+    mbar_init(dv_done, 1);
     mbar_init(ds_full, FB_SOFT);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, FB_SOFT);
@@ -621,17 +623,22 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
           const uint32_t qa = smem_addr(smem + B_OFF_Q + st * TILE_BYTES);
           const uint32_t doa = smem_addr(smem + B_OFF_DO + st * TILE_BYTES);
           if (!mbar_wait(&qdo_full[st], (i / QDO_ST) & 1, abort_flag, p.err, 23)) break;
+          // dP^T = V dO^T first: its columns (128..255) only have to be free of
+          // the previous tile's P^T, i.e. its dV MMA done; it then runs while
+          // the softmax warps still read the previous dQ out of columns 0..127
+          if (i > 0 && !mbar_wait(dv_done, (i - 1) & 1, abort_flag, p.err, 28)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < FB / 16; ++kk) {
+            const uint32_t ko = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
+            mma_bf16(tmem + 128, desc_k_sw128(va + ko), desc_k_sw128(doa + ko), idKK, kk > 0 ? 1u : 0u);
+          }
           if (!mbar_wait(dq_free, (i & 1) ^ 1, abort_flag, p.err, 24)) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < FB / 16; ++kk) {
             const uint32_t ko = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
             mma_bf16(tmem + 0, desc_k_sw128(ka + ko), desc_k_sw128(qa + ko), idKK, kk > 0 ? 1u : 0u);
-          }
-#pragma unroll
-          for (int kk = 0; kk < FB / 16; ++kk) {
-            const uint32_t ko = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
-            mma_bf16(tmem + 128, desc_k_sw128(va + ko), desc_k_sw128(doa + ko), idKK, kk > 0 ? 1u : 0u);
           }
           mma_commit(sdp_full);
           if (!mbar_wait(ds_full, i & 1, abort_flag, p.err, 25)) break;
@@ -647,6 +654,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
             mma_bf16(tmem + 384, desc_k_sw128(dsa + ko), desc_mn_sw128(qa + kk * 2048, CHUNK_BYTES), idKM, acc);
           }
           mma_commit(&qdo_empty[st]);
+          mma_commit(dv_done);
 #pragma unroll
           for (int kk = 0; kk < FB / 16; ++kk)
             mma_bf16(tmem + 0, desc_mn_sw128(dsa + kk * 2048, CHUNK_BYTES),
