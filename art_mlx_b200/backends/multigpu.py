@@ -23,7 +23,6 @@ from __future__ import annotations
 
 import json
 import os
-import signal
 import socket
 import subprocess
 import sys
@@ -34,6 +33,7 @@ from .. import dev
 from ..runtime import jobs as J
 from ..trajectories import Trajectory
 from ..types import RuntimeConfig, TopologyConfig, TrainSFTConfig
+from ..utils import managed_process
 from ..utils.output_dirs import get_step_checkpoint_dir, get_step_from_dir
 from .local import LocalBackend
 
@@ -155,7 +155,8 @@ class MultiGPUBackend(LocalBackend):
         pkg_root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         env["PYTHONPATH"] = pkg_root + os.pathsep + env.get("PYTHONPATH", "")
         with open(log_path, "a") as logf:
-            proc = subprocess.Popen(cmd, stdout=logf, stderr=subprocess.STDOUT, env=env, start_new_session=True)
+            # own session + parent-death signal: the worker group never outlives this process
+            proc = managed_process.popen(cmd, stdout=logf, stderr=subprocess.STDOUT, env=env)
         g = _WorkerGroup(jobs_dir, proc, self._world, log_path)
         deadline = time.monotonic() + self._startup_timeout
         while not os.path.exists(os.path.join(jobs_dir, "ready")):
@@ -184,12 +185,7 @@ class MultiGPUBackend(LocalBackend):
                 J.write_job(J.ShutdownJob(log_path=path[:-5] + ".log"), path)
                 g.proc.wait(timeout=grace_s)
             except subprocess.TimeoutExpired:
-                os.killpg(g.proc.pid, signal.SIGTERM)  # the process group this backend started
-                try:
-                    g.proc.wait(timeout=30)
-                except subprocess.TimeoutExpired:
-                    os.killpg(g.proc.pid, signal.SIGKILL)
-                    g.proc.wait()
+                managed_process.stop_group(g.proc)  # the process group this backend started
 
     async def close(self) -> None:
         for g in self._groups.values():
