@@ -41,6 +41,10 @@ class PackedMoeRoutingReplay:
     num_layers: int
     topk: int
     num_experts: int
+    # shared-prefix tokens whose routes a later sibling also carried, and how
+    # many of those disagreed (per-layer expert sets differ; the first kept)
+    shared_route_tokens: int = 0
+    route_conflict_tokens: int = 0
 
 
 class PackedTensors(TypedDict):
@@ -142,7 +146,9 @@ def _row_len(row: list[_Item], seq_len: int) -> int:
 
 def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
     if not row:
-        return {k: [] for k in ("tokens", "group_ids", "parent_ids", "input_pos", "assistant_mask", "logprobs", "advantages", "weights", "routes")}
+        out = {k: [] for k in ("tokens", "group_ids", "parent_ids", "input_pos", "assistant_mask", "logprobs", "advantages", "weights", "routes")}
+        out["route_stats"] = (0, 0)
+        return out
     toks, tree_gids, tree_pids, _, per_seq = prefix_tree_layout(
         [i.token_ids for i in row], seq_len if share else 0,
         [max(0, min(i.shareable, len(i.token_ids))) if share else 0 for i in row],
@@ -157,6 +163,7 @@ def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
     adv = np.zeros(n, dtype=np.float64)
     w = np.zeros(n, dtype=np.float64)
     routes: list[Any] = [None] * n
+    n_shared_routes = n_conflicts = 0
     for k, it in enumerate(row):
         dst = per_seq[k]
         m = len(dst)
@@ -172,6 +179,12 @@ def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
                 raise RuntimeError("Prefix-tree pack cannot share mismatched input positions")
             if (am[shared] != 0).any() or (~np.isnan(lp[shared])).any():
                 raise RuntimeError("Prefix-tree pack attempted to share a trainable token")
+            if it.routes is not None:
+                for src in np.nonzero(shared)[0].tolist():
+                    have = routes[int(dst[src])]
+                    if src < len(it.routes) and have is not None:
+                        n_shared_routes += 1
+                        n_conflicts += int(not _same_routes(have, it.routes[src]))
         fresh = ~shared
         d = dst[fresh]
         owned[d] = True
@@ -194,7 +207,14 @@ def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
         "advantages": adv[:seq_len],
         "weights": w[:seq_len],
         "routes": routes[:seq_len],
+        "route_stats": (n_shared_routes, n_conflicts),
     }
+
+
+def _same_routes(a: Any, b: Any) -> bool:
+    """Same expert set in every layer (top-k order does not matter)."""
+    x, y = np.asarray(a), np.asarray(b)
+    return x.shape == y.shape and bool((np.sort(x, axis=-1) == np.sort(y, axis=-1)).all())
 
 
 def _padded(rows: list, seq_len: int, value: Any, dtype: torch.dtype) -> torch.Tensor:
@@ -259,7 +279,10 @@ def packed_tensors_from_tokenized_results(
         "moe_routing_replay": None,
     }
     if include_moe_routing:
-        out["moe_routing_replay"] = tensorize_routes([p["routes"] for p in packed], seq_len)
+        replay = tensorize_routes([p["routes"] for p in packed], seq_len)
+        replay.shared_route_tokens = sum(p["route_stats"][0] for p in packed)
+        replay.route_conflict_tokens = sum(p["route_stats"][1] for p in packed)
+        out["moe_routing_replay"] = replay
     return out
 
 

@@ -54,3 +54,30 @@ def test_replayed_routes_match_live_routing_and_carry_host_counts():
     m_rep = rep.train_step(replay, 1e-3, {}, micro_batches=mbs).to_host()
     assert torch.allclose(rep.store.master, live.store.master, atol=1e-6)
     assert abs(m_rep["loss/train"] - m_live["loss/train"]) < 1e-6
+
+
+def test_shared_prefix_route_conflicts_are_counted_and_first_routes_kept():
+    from art_mlx_b200.preprocessing.tokenize import TokenizedResult
+
+    nan = float("nan")
+
+    def res(completion, adv, routes):
+        return TokenizedResult(advantage=adv, token_ids=[1, 2, 3, 4, *completion], input_pos=list(range(6)),
+                               assistant_mask=[0, 0, 0, 0, 1, 1], logprobs=[nan] * 4 + [-1.0, -1.0],
+                               weight=1.0, prompt_id=0, prompt_length=4, moe_routed_experts=routes)
+
+    a = [[[0, 1], [2, 3]], [[4, 5], [6, 7]], [[0, 2], [1, 3]], [[5, 6], [7, 0]], [[1, 1], [1, 1]], [[2, 2], [2, 2]]]
+    b = [r for r in a]
+    b[1] = [[4, 6], [6, 7]]  # a different expert set in layer 0: a conflict
+    b[2] = [[2, 0], [3, 1]]  # same sets in another order: no conflict
+    b[4], b[5] = [[3, 3], [3, 3]], [[4, 4], [4, 4]]
+    packed = packed_tensors_from_tokenized_results([res([5, 6], 1.0, a), res([7, 8], -1.0, b)], 16,
+                                                   include_moe_routing=True, rng=random.Random(0))
+    rr = packed["moe_routing_replay"]
+    # the prompt is packed once except its last token, which each branch re-emits (it predicts
+    # the branch's first completion token): [1 2 3 4 5 6 | 4 7 8]
+    assert packed["tokens"][0, :9].tolist() == [1, 2, 3, 4, 5, 6, 4, 7, 8]
+    assert rr.shared_route_tokens == 3 and rr.route_conflict_tokens == 1
+    assert rr.expert_indices[0, 1].tolist() == a[1]  # the first sequence's routes are kept
+    assert rr.expert_indices[0, 6].tolist() == b[3] and rr.expert_indices[0, 7].tolist() == b[4]
+    assert bool(rr.token_mask[0, :9].all())
