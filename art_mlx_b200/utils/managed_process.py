@@ -9,7 +9,7 @@ dies on its own.
 
 * :func:`popen` starts the child in its own session (so its whole process
   tree is one process group) and, on Linux, asks the kernel to send it
-  ``SIGTERM`` when the starting thread exits (``prctl(PR_SET_PDEATHSIG)``).
+  ``SIGTERM`` when the parent's main thread exits (``prctl(PR_SET_PDEATHSIG)``).
   If the parent is already gone by the time the child runs, the child exits
   at once.
 * :func:`stop_group` sends ``SIGTERM`` to the group, waits, then ``SIGKILL``.
@@ -27,6 +27,7 @@ import os
 import signal
 import subprocess
 import sys
+import threading
 from typing import Any, Awaitable, TypeVar
 
 T = TypeVar("T")
@@ -35,12 +36,15 @@ _PR_SET_PDEATHSIG = 1
 
 
 def _pdeathsig_preexec(sig: int, parent_pid: int):
+    # resolved in the parent: between fork and exec the child must not enter the
+    # dynamic loader (another thread of the parent may have held its lock at fork)
+    try:
+        prctl = ctypes.CDLL(None, use_errno=True).prctl
+    except (OSError, AttributeError):
+        return None
+
     def _fn() -> None:
-        try:
-            libc = ctypes.CDLL(None, use_errno=True)
-            libc.prctl(_PR_SET_PDEATHSIG, int(sig), 0, 0, 0)
-        except OSError:
-            return
+        prctl(_PR_SET_PDEATHSIG, int(sig), 0, 0, 0)
         # the parent may have exited between fork and prctl: then nobody sends the signal
         if os.getppid() != parent_pid:
             os._exit(1)
@@ -51,12 +55,18 @@ def _pdeathsig_preexec(sig: int, parent_pid: int):
 def popen(cmd: list[str], *, die_with_parent: bool = True,
           death_signal: int = signal.SIGTERM, **kwargs: Any) -> subprocess.Popen:
     """``subprocess.Popen`` in a new session; with ``die_with_parent`` (Linux)
-    the child gets ``death_signal`` when the calling thread exits."""
+    the child gets ``death_signal`` when this process's main thread exits.
+    The kernel ties the signal to the thread that forks, so it is only
+    requested when called from the main thread (a child started from a
+    short-lived thread would otherwise die with that thread)."""
     kwargs.setdefault("start_new_session", True)
-    if die_with_parent and sys.platform.startswith("linux"):
+    on_main = threading.current_thread() is threading.main_thread()
+    if die_with_parent and on_main and sys.platform.startswith("linux"):
         if "preexec_fn" in kwargs:
             raise ValueError("popen sets preexec_fn itself")
-        kwargs["preexec_fn"] = _pdeathsig_preexec(death_signal, os.getpid())
+        fn = _pdeathsig_preexec(death_signal, os.getpid())
+        if fn is not None:
+            kwargs["preexec_fn"] = fn
     return subprocess.Popen(cmd, **kwargs)
 
 

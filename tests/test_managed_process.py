@@ -126,3 +126,19 @@ def test_watchdog_ignores_an_announced_exit_and_returns_results():
         assert await wd.guard(work()) == 7
 
     asyncio.run(main())
+
+
+def test_child_started_from_a_worker_thread_outlives_that_thread():
+    import threading
+
+    box = {}
+    t = threading.Thread(target=lambda: box.setdefault(
+        "p", mp.popen([sys.executable, "-c", "import time; time.sleep(60)"])))
+    t.start()
+    t.join()
+    p = box["p"]
+    try:
+        time.sleep(0.5)
+        assert p.poll() is None  # no death signal tied to the finished thread
+    finally:
+        mp.stop_group(p, grace_s=10)
