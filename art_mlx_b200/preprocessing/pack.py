@@ -237,6 +237,11 @@ def packed_tensors_from_tokenized_results(
     rng: random.Random | None = None,
 ) -> PackedTensors:
     rows: list[list[_Item]] = [[]]
+    # upper bound of the current row's packed length: an added sequence grows
+    # the prefix tree by at most its own length, so the exact (re-planned)
+    # length is only needed once the bound passes seq_len; same decisions as
+    # planning every candidate row
+    bound = 0
     for r in tokenized_results:
         if len(r.token_ids) > seq_len and not truncate_long_results:
             continue
@@ -245,9 +250,17 @@ def packed_tensors_from_tokenized_results(
         if sum(r.assistant_mask[r.prompt_length :]) == 0:
             continue
         it = _item(r, seq_len)
-        if rows[-1] and (not pack_results or _row_len([*rows[-1], it], seq_len) > seq_len):
-            rows.append([])
+        if rows[-1]:
+            grown = bound + len(it.token_ids)
+            if pack_results and grown > seq_len:
+                grown = _row_len([*rows[-1], it], seq_len)
+            if not pack_results or grown > seq_len:
+                rows.append([])
+                grown = len(it.token_ids)
+        else:
+            grown = len(it.token_ids)
         rows[-1].append(it)
+        bound = grown
     (rng or random).shuffle(rows)
     packed = [_pack_row(row, seq_len, pack_results) for row in rows]
 

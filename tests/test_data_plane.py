@@ -190,3 +190,37 @@ def test_pad_groups_aligns_each_group():
         got = ap[s0 : s0 + p].t() @ bp[s0 : s0 + p]
         assert torch.allclose(ref, got)
         s0 += p
+
+
+def test_row_assignment_matches_planning_every_candidate_row():
+    """The packer's length-bound shortcut takes the same row decisions as
+    re-planning the prefix tree of every candidate row."""
+    import math
+    import random as _random
+
+    from art_mlx_b200.preprocessing import pack as P
+    from art_mlx_b200.preprocessing.tokenize import TokenizedResult
+
+    rng = _random.Random(0)
+    for trial in range(30):
+        seq_len = rng.choice([48, 64, 96])
+        results = []
+        for g in range(rng.randint(1, 6)):
+            prompt = [rng.randrange(2, 50) for _ in range(rng.randint(1, 30))]
+            for _ in range(rng.randint(1, 6)):
+                comp = [rng.randrange(2, 50) for _ in range(rng.randint(1, 40))]
+                n = len(prompt)
+                results.append(TokenizedResult(
+                    advantage=rng.uniform(-1, 1), token_ids=prompt + comp, input_pos=list(range(n + len(comp))),
+                    assistant_mask=[0] * n + [1] * len(comp), logprobs=[math.nan] * n + [-1.0] * len(comp),
+                    weight=1.0, prompt_id=g, prompt_length=n))
+        got = P.packed_tensors_from_tokenized_results(results, seq_len, rng=_random.Random(trial))
+        rows = [[]]
+        for r in results:
+            it = P._item(r, seq_len)
+            if rows[-1] and P._row_len([*rows[-1], it], seq_len) > seq_len:
+                rows.append([])
+            rows[-1].append(it)
+        _random.Random(trial).shuffle(rows)
+        ref = P._padded([P._pack_row(row, seq_len, True)["tokens"] for row in rows], seq_len, -100, torch.long)
+        assert torch.equal(got["tokens"], ref), trial
