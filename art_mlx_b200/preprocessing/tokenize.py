@@ -34,7 +34,7 @@ def _int_list(raw: Any, name: str) -> list[int]:
         raise RuntimeError(f"Missing {name}")
     if not isinstance(raw, list):
         raise RuntimeError(f"Expected {name} list, got {type(raw)}")
-    return [int(v) for v in raw]
+    return list(map(int, raw))
 
 
 def choice_token_ids(choice: Any) -> tuple[list[int], list[int]] | None:
