@@ -13,6 +13,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include "common.cuh"
+#include "art_noalloc.h"
 
 namespace art {
 
@@ -256,6 +257,8 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(
   // work unit: (key block, first q tile, end q tile); the host splits the
   // query range of heavily attended key blocks (shared prompts) into units
   const int kb = units[3 * blockIdx.x], qt_lo = units[3 * blockIdx.x + 1], qt_hi = units[3 * blockIdx.x + 2];
+  // a unit outside the sequence (a malformed work list) is skipped, never read
+  if (kb < 0 || (int64_t)kb * BWD_KEYS >= Tk || qt_lo < 0 || (int64_t)qt_lo * BWD_Q >= Tq) return;
   const int hk = blockIdx.y;
   const int G = Hq / Hkv;
   const int j0 = kb * BWD_KEYS;
@@ -548,35 +551,27 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::
 }  // namespace art
 
 // ============================================================================
-// Allocation-free C entry point of the attention backward.
+// Allocation-free C entry point of the attention backward (declared, with its
+// layouts, limits and return codes, in art_noalloc.h).
 //
-// No counterpart in the reference: this entry point exists for callers that
-// cannot allocate device memory themselves -- for example code running inside
-// a host application that owns the whole device memory budget (a plugin given
-// fixed buffers), or a latency-critical loop that must never enter the CUDA
-// allocator, which can synchronise the device.  The caller passes every input
-// and output; the only extra memory, the per-(head, query) `delta = sum(dO*O)`
-// vector, lives in a fixed file-scope device array.
-//
-// Limits and behaviour:
-//  * scratch: kNoAllocDeltaMax floats (4 MiB) per device, held by every GPU
-//    that loads this library until the process exits; calls with
-//    T * Hq > kNoAllocDeltaMax are rejected (return 2);
-//  * head_dim must be 128 (return 3 otherwise); other bad arguments return 4;
-//  * the first call on a device looks up the array's device address
-//    (cudaGetSymbolAddress) with that device current; make that first call
-//    before any stream capture;
-//  * all calls on a device share the scratch array, so calls that overlap on
-//    the GPU (different streams, no ordering) race; order them on one stream;
-//  * the fp32 outputs dq [T, Hq, 128], dk and dv [T, Hkv, 128] are cleared
-//    (cudaMemsetAsync) by the entry point before accumulation;
-//  * no cudaMalloc, cudaFree or allocating library call is made.
-// Returns 0 on success, 1 on a CUDA error, 2-4 on rejected arguments.
+// No counterpart in the reference: it serves callers that cannot allocate
+// device memory themselves -- code running inside a host application that owns
+// the whole device memory budget (a plugin given fixed buffers), or a
+// latency-critical loop that must never enter the CUDA allocator, which can
+// synchronise the device.  The caller passes every input and output; the only
+// extra memory, the per-(head, query) `delta = sum(dO*O)` vector, lives in the
+// fixed file-scope device array below (4 MiB per device, held until exit).
 // ============================================================================
 namespace {
-constexpr int64_t kNoAllocDeltaMax = int64_t(1) << 20;
-static __device__ __align__(256) float g_noalloc_delta[kNoAllocDeltaMax];
-static float* g_noalloc_delta_ptr[64] = {nullptr};
+static __device__ __align__(256) float g_noalloc_delta[ART_NOALLOC_DELTA_MAX];
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// A bf16 operand of `heads` x 128 columns per row: 16-byte base, row stride a
+// multiple of 8 elements (16 bytes) covering the row.
+bool operand_ok(const void* p, int64_t ld, int heads) {
+  return p && aligned16(p) && ld % 8 == 0 && ld >= (int64_t)heads * 128;
+}
 }  // namespace
 
 extern "C" int art_attn_bwd_noalloc(const void* dout, int64_t lddo, const void* q, int64_t ldq, const void* k,
@@ -585,36 +580,63 @@ extern "C" int art_attn_bwd_noalloc(const void* dout, int64_t lddo, const void* 
                                     float* dk, float* dv, int T, int Hq, int Hkv, int D, float scale,
                                     cudaStream_t stream) {
   using namespace art;
-  if (D != 128) return 3;
-  if (T < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || n_units < 0) return 4;
-  if ((int64_t)T * Hq > kNoAllocDeltaMax) return 2;
-  if (!dout || !q || !k || !v || !out || !lse || !kend || !dq || !dk || !dv || (n_units > 0 && !units)) return 4;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
-  if (!g_noalloc_delta_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_delta) != cudaSuccess || !p) return 1;
-    g_noalloc_delta_ptr[dev] = static_cast<float*>(p);
-  }
-  float* delta = g_noalloc_delta_ptr[dev];
+  if (D != 128) return ART_NOALLOC_BAD_HEAD_DIM;
+  if (T < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || n_units < 0) return ART_NOALLOC_BAD_ARGUMENT;
+  if ((int64_t)T * Hq > ART_NOALLOC_DELTA_MAX) return ART_NOALLOC_TOO_LARGE;
+  // every check below runs before anything touches the device
+  if (!operand_ok(dout, lddo, Hq) || !operand_ok(q, ldq, Hq) || !operand_ok(out, ldo, Hq) ||
+      !operand_ok(k, ldk, Hkv) || !operand_ok(v, ldv, Hkv))
+    return ART_NOALLOC_BAD_ARGUMENT;
+  if (!lse || !kend || !dq || !dk || !dv || (n_units > 0 && !units)) return ART_NOALLOC_BAD_ARGUMENT;
+  if (!aligned16(dq) || !aligned16(dk) || !aligned16(dv)) return ART_NOALLOC_BAD_ARGUMENT;
+  // The array's name is a host-side stand-in in host code: its device address
+  // is looked up here, on the caller's current device, on every call (no
+  // cache that a device reset could leave dangling; no allocation).
+  void* sym = nullptr;
+  if (cudaGetSymbolAddress(&sym, g_noalloc_delta) != cudaSuccess || !sym) return ART_NOALLOC_CUDA_ERROR;
+  float* delta = static_cast<float*>(sym);
   const size_t nq = (size_t)T * Hq * D * sizeof(float), nk = (size_t)T * Hkv * D * sizeof(float);
-  if (cudaMemsetAsync(dq, 0, nq, stream) != cudaSuccess) return 1;
-  if (cudaMemsetAsync(dk, 0, nk, stream) != cudaSuccess) return 1;
-  if (cudaMemsetAsync(dv, 0, nk, stream) != cudaSuccess) return 1;
-  if (T == 0 || n_units == 0) return cudaGetLastError() == cudaSuccess ? 0 : 1;
-  const int64_t warps = (int64_t)T * Hq;
-  attn_bwd_pre_kernel<128><<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(dout), lddo, reinterpret_cast<const __nv_bfloat16*>(out), ldo, delta,
-      T, Hq);
+  if (cudaMemsetAsync(dq, 0, nq, stream) != cudaSuccess) return ART_NOALLOC_CUDA_ERROR;
+  if (cudaMemsetAsync(dk, 0, nk, stream) != cudaSuccess) return ART_NOALLOC_CUDA_ERROR;
+  if (cudaMemsetAsync(dv, 0, nk, stream) != cudaSuccess) return ART_NOALLOC_CUDA_ERROR;
+  if (T == 0 || n_units == 0) return ART_NOALLOC_OK;
+  // launched through cudaLaunchKernel so that each launch's own status is
+  // returned (an earlier, unrelated error pending in the runtime is not
+  // reported as this call's failure)
+  {
+    const int64_t warps = (int64_t)T * Hq;
+    const __nv_bfloat16* a0 = reinterpret_cast<const __nv_bfloat16*>(dout);
+    const __nv_bfloat16* a2 = reinterpret_cast<const __nv_bfloat16*>(out);
+    int64_t a1 = lddo, a3 = ldo;
+    float* a4 = delta;
+    int a5 = T, a6 = Hq;
+    void* args[] = {&a0, &a1, &a2, &a3, &a4, &a5, &a6};
+    if (cudaLaunchKernel(reinterpret_cast<const void*>(&attn_bwd_pre_kernel<128>), dim3((unsigned)((warps + 7) / 8)),
+                         dim3(256), args, 0, stream) != cudaSuccess)
+      return ART_NOALLOC_CUDA_ERROR;
+  }
   const size_t smem = (2 * BWD_KEYS * 128 + 4 * BWD_Q * 128 + BWD_KEYS * DS_LD) * sizeof(__nv_bfloat16) +
                       4 * BWD_Q * sizeof(float);
   if (cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
-    return 1;
-  dim3 grid((unsigned)n_units, (unsigned)Hkv);
-  attn_bwd_kernel<128><<<grid, 256, smem, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(q), ldq, reinterpret_cast<const __nv_bfloat16*>(k), ldk,
-      reinterpret_cast<const __nv_bfloat16*>(v), ldv, reinterpret_cast<const __nv_bfloat16*>(dout), lddo, lse, delta,
-      kend, units, dq, dk, dv, T, T, 0, Hq, Hkv, scale);
-  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+    return ART_NOALLOC_CUDA_ERROR;
+  {
+    const __nv_bfloat16 *pq = reinterpret_cast<const __nv_bfloat16*>(q), *pk = reinterpret_cast<const __nv_bfloat16*>(k),
+                        *pv = reinterpret_cast<const __nv_bfloat16*>(v),
+                        *pdo = reinterpret_cast<const __nv_bfloat16*>(dout);
+    int64_t lq = ldq, lk = ldk, lv = ldv, ld = lddo;
+    const float* plse = lse;
+    const float* pdelta = delta;
+    const int* pkend = kend;
+    const int* punits = units;
+    float *pdq = dq, *pdk = dk, *pdv = dv;
+    int tq = T, tk = T, qoff = 0, hq = Hq, hkv = Hkv;
+    float sc = scale;
+    void* args[] = {&pq, &lq, &pk, &lk, &pv, &lv, &pdo, &ld, &plse, &pdelta, &pkend, &punits,
+                    &pdq, &pdk, &pdv, &tq, &tk, &qoff, &hq, &hkv, &sc};
+    if (cudaLaunchKernel(reinterpret_cast<const void*>(&attn_bwd_kernel<128>), dim3((unsigned)n_units, (unsigned)Hkv),
+                         dim3(256), args, smem, stream) != cudaSuccess)
+      return ART_NOALLOC_CUDA_ERROR;
+  }
+  return ART_NOALLOC_OK;
 }
