@@ -1,9 +1,10 @@
 """GRPO / CISPO / PPO token loss (PyTorch oracle).
 
 This is the fp32 reference of the loss math in the reference's
-``src/art/loss.py:104-225``; the fused CUDA kernel in
-``art_mlx_b200/ops/grpo_loss.py`` computes the same per-token quantities in
-one pass over the vocabulary and is tested against this module.
+``src/art/loss.py:104-225``; the fused CUDA kernels in
+``art_mlx_b200/ops/csrc/loss.cu`` (called through ``ops/fused.py``:
+``grpo_token_loss``, ``lm_head_logprobs``) compute the same per-token
+quantities and are tested against this module.
 
 Per token ``t`` (inputs are shifted by one so position ``t`` scores the
 token at ``t+1``):

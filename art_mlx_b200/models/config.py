@@ -74,8 +74,11 @@ class ModelConfig:
 
     @classmethod
     def from_hf_dict(cls, d: dict[str, Any], name: str = "custom") -> "ModelConfig":
-        mt = d.get("model_type", "qwen3")
-        family = {"qwen2": "qwen2", "qwen3": "qwen3", "qwen3_moe": "qwen3_moe", "qwen3_next": "qwen3_next"}.get(mt, "qwen3")
+        if "model_type" not in d:
+            raise ValueError("config.json has no model_type: the architecture cannot be identified")
+        # the family is the checkpoint's own model_type: an architecture the
+        # registry does not know is refused there, never trained as another one
+        family = str(d["model_type"])
         heads = d["num_attention_heads"]
         return cls(
             name=name,

@@ -58,6 +58,7 @@ torch::Tensor gemm_tc(torch::Tensor a, torch::Tensor b, c10::optional<torch::Ten
                       c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> bias,
                       c10::optional<torch::Tensor> out, bool accumulate);
 int64_t tc_error_code();
+torch::Tensor tc_error_word();
 torch::Tensor gemm_tc_ag(std::vector<int64_t> a_ptrs, int64_t rows, int64_t K, int64_t lda, torch::Tensor b,
                          c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2,
                          c10::optional<torch::Tensor> bias);
@@ -118,6 +119,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("lse"), py::arg("kend"), py::arg("units"), py::arg("scale"), py::arg("q_off") = 0);
   m.def("gemm_tc", &art::gemm_tc);
   m.def("tc_error_code", &art::tc_error_code);
+  m.def("tc_error_word", &art::tc_error_word);
   m.def("gemm_tc_ag", &art::gemm_tc_ag);
   m.def("gemm_tc_rs", &art::gemm_tc_rs);
   m.def("slot_sum", &art::slot_sum);

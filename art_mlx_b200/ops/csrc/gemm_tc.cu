@@ -306,6 +306,14 @@ static torch::Tensor& error_word(int dev) {
 
 int* tc_error_ptr(int dev) { return error_word(dev).data_ptr<int>(); }
 
+// The device error word itself (int32 [1] on the current device), so a
+// caller can fold it into a step's status read without a separate sync.
+torch::Tensor tc_error_word() {
+  int dev = 0;
+  ART_CUDA_CHECK(cudaGetDevice(&dev));
+  return error_word(dev);
+}
+
 // Returns and clears the device error word of the tensor-core kernels
 // (0 = ok; 1..4 = which pipeline wait timed out).
 int64_t tc_error_code() {

@@ -217,11 +217,30 @@ class StepMetrics:
     kl: torch.Tensor
     grad_norm: torch.Tensor
     n_train: int
-    n_tokens: int
+    n_tokens: int | torch.Tensor
+    # status words of the step's bounded device waits (0 = every wait
+    # completed); read with the metrics in the same device->host copy
+    health: torch.Tensor | None = None
+    health_names: tuple[str, ...] = ()
 
     def to_host(self) -> dict[str, float]:
-        vals = torch.stack([self.loss, self.entropy, self.probs_corr, self.kl, self.grad_norm.reshape(())])
-        loss, ent, pc, kl, gn = vals.float().cpu().tolist()
+        """Metrics as host floats (one device->host copy).  Raises
+        :class:`DeviceWaitTimeout` when a bounded device wait of the step gave
+        up: the step's gradients or parameters are then partial, so no
+        checkpoint may be written from it."""
+        parts = [self.loss, self.entropy, self.probs_corr, self.kl, self.grad_norm.reshape(())]
+        tok = self.n_tokens
+        parts.append(tok.reshape(()) if torch.is_tensor(tok) else self.loss.new_tensor(float(tok)))
+        nh = 0
+        if self.health is not None:
+            nh = int(self.health.numel())
+            parts.extend(self.health.float().unbind(0))
+        vals = torch.stack([p.float().reshape(()) for p in parts]).cpu().tolist()
+        loss, ent, pc, kl, gn, ntok = vals[:6]
+        bad = [f"{name}={int(v)}" for name, v in zip(self.health_names, vals[6 : 6 + nh]) if v != 0]
+        if bad:
+            raise DeviceWaitTimeout("a bounded device wait gave up during the step (" + ", ".join(bad) +
+                                    "); its gradients or parameters are incomplete")
         return {
             "loss/train": loss,
             "loss/entropy": ent,
@@ -229,8 +248,13 @@ class StepMetrics:
             "loss/kl_policy_ref": kl,
             "loss/grad_norm": gn,
             "data/step_trainer_tokens": float(self.n_train),
-            "data/step_packed_tokens": float(self.n_tokens),
+            "data/step_packed_tokens": float(ntok),
         }
+
+
+class DeviceWaitTimeout(RuntimeError):
+    """A kernel's bounded wait (peer barrier, tensor-core pipeline barrier)
+    ran out and recorded a status instead of hanging."""
 
 
 def _probs_corr_device(old: torch.Tensor, new: torch.Tensor) -> torch.Tensor:
@@ -369,11 +393,51 @@ class GRPOTrainer:
             st.reload()
             self._offload = None
 
-    def check_health(self) -> None:
+    def health_words(self) -> tuple[list[str], list[torch.Tensor]]:
+        """The device status words of every bounded wait this trainer's
+        kernels use: the peer barriers of the data-, context-, tensor- and
+        expert-parallel exchanges and the error word of the tensor-core
+        kernels (attention, GEMMs).  Non-zero = a wait gave up."""
+        names: list[str] = []
+        words: list[torch.Tensor] = []
+
+        def add(name: str, t: Any) -> None:
+            if torch.is_tensor(t):
+                names.append(name)
+                words.append(t)
+
         if self.grad_sync is not None:
-            self.grad_sync.check()
+            add("dp_barrier", self.grad_sync.status)
         if self.cp is not None:
-            self.cp.check()
+            add("cp_barrier", getattr(self.cp, "status", None))
+        if self.tp is not None:
+            add("tp_barrier", getattr(self.tp, "status", None))
+        if self.ep is not None:
+            add("ep_barrier", getattr(self.ep.transport, "status", None))
+        if self.etp is not None:
+            add("etp_barrier", getattr(self.etp, "status", None))
+        if self.device.type == "cuda":
+            from ..ops import native
+
+            add("tensor_core_wait", native.lib().tc_error_word())
+        return names, words
+
+    def _health(self) -> tuple[torch.Tensor | None, tuple[str, ...]]:
+        names, words = self.health_words()
+        if not words:
+            return None, ()
+        return torch.stack([w.reshape(-1)[0].to(torch.int32) for w in words]), tuple(names)
+
+    def check_health(self) -> None:
+        """Raise :class:`DeviceWaitTimeout` if any bounded wait gave up (one
+        device->host read)."""
+        health, names = self._health()
+        if health is None:
+            return
+        vals = health.cpu().tolist()
+        bad = [f"{n}={v}" for n, v in zip(names, vals) if v != 0]
+        if bad:
+            raise DeviceWaitTimeout("a bounded device wait gave up (" + ", ".join(bad) + ")")
 
     def set_reference_adapter(self, state: Mapping[str, torch.Tensor] | None) -> None:
         """Use a saved adapter (PEFT state dict) as the KL reference; ``None``
@@ -524,11 +588,13 @@ class GRPOTrainer:
         nmb = max(len(micro_batches), 1)
         acc["probs_corr"] /= nmb
         acc["kl"] /= nmb
+        packed_tokens: int | torch.Tensor = n_tokens
         if self.world > 1:
             # tensor-parallel ranks hold identical copies of the loss statistics
+            # (and of the packed tokens of their row)
             rep = float(self.tp_size)
             stats = torch.stack([acc["loss"] / rep, acc["entropy"] / rep, acc["probs_corr"] / self.world,
-                                 acc["kl"] / self.world])
+                                 acc["kl"] / self.world, acc["loss"].new_tensor(n_tokens / rep)])
             if self.grad_sync is not None:
                 self.grad_sync.reduce_and_step(self.optim, learning_rate, stats)
             else:
@@ -536,12 +602,16 @@ class GRPOTrainer:
                     dist.all_reduce(self.store.grad, group=self.group)
                 dist.all_reduce(stats, group=self.group)
                 self.optim.step(learning_rate)
-            acc["loss"], acc["entropy"], acc["probs_corr"], acc["kl"] = stats.unbind(0)
+            acc["loss"], acc["entropy"], acc["probs_corr"], acc["kl"], packed_tokens = stats.unbind(0)
         else:
             self.optim.step(learning_rate)
+        health, names = self._health()
+        # step_trainer_tokens and step_packed_tokens both count the whole step
+        # (every rank's rows)
         return StepMetrics(
             loss=acc["loss"], entropy=acc["entropy"], probs_corr=acc["probs_corr"], kl=acc["kl"],
-            grad_norm=self.optim.grad_norm, n_train=int(total), n_tokens=n_tokens,
+            grad_norm=self.optim.grad_norm, n_train=int(total), n_tokens=packed_tokens,
+            health=health, health_names=names,
         )
 
     def train_steps(
@@ -587,9 +657,25 @@ class GRPOTrainer:
             loss = -lp.sum() / total
             loss.backward()
             acc += loss.detach()
-        if self.world > 1:
+        if self.grad_sync is not None:
+            # the fused data-parallel step: every rank updates its own shard
+            # of the master weights and moments (a full local step would start
+            # from the other shards' stale copies)
+            stats = acc.reshape(1)
+            self.grad_sync.reduce_and_step(self.optim, learning_rate, stats)
+            acc = stats[0]
+        elif self.world > 1:
             dist.all_reduce(self.store.grad, group=self.group)
             dist.all_reduce(acc, group=self.group)
-        self.optim.step(learning_rate)
-        vals = torch.stack([acc, self.optim.grad_norm.reshape(())]).cpu().tolist()
+            self.optim.step(learning_rate)
+        else:
+            self.optim.step(learning_rate)
+        health, names = self._health()
+        parts = [acc.reshape(()), self.optim.grad_norm.reshape(())]
+        if health is not None:
+            parts.extend(health.float().unbind(0))
+        vals = torch.stack([p.float() for p in parts]).cpu().tolist()
+        bad = [f"{n}={int(v)}" for n, v in zip(names, vals[2:]) if v != 0]
+        if bad:
+            raise DeviceWaitTimeout("a bounded device wait gave up during the SFT step (" + ", ".join(bad) + ")")
         return {"loss/train": vals[0], "loss/grad_norm": vals[1], "data/step_trainer_tokens": float(total)}

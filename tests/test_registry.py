@@ -16,3 +16,20 @@ def test_registry_resolves_presets_and_hf_ids():
     with pytest.raises(ValueError, match="not supported"):
         get_model_support(cfg)
     assert get_model_support(cfg, allow_unvalidated_arch=True).key == "llama"
+
+
+def test_unknown_hf_model_type_is_refused(tmp_path):
+    import json
+
+    d = tmp_path / "ckpt"
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps({
+        "model_type": "some_new_arch", "vocab_size": 64, "hidden_size": 32, "num_hidden_layers": 1,
+        "num_attention_heads": 2, "intermediate_size": 64}))
+    cfg = get_config(str(d))
+    assert cfg.family == "some_new_arch"  # never silently mapped to another family
+    with pytest.raises(ValueError, match="not supported"):
+        get_model_support(str(d))
+    (d / "config.json").write_text(json.dumps({"vocab_size": 64}))
+    with pytest.raises(ValueError, match="model_type"):
+        get_config(str(d))
