@@ -33,6 +33,9 @@ class ModelConfig:
     qk_norm: bool = False  # Qwen3: RMSNorm over head_dim on q and k
     tie_word_embeddings: bool = False
     sliding_window: int | None = None
+    # RoPE frequency scaling of the checkpoint (sorted (key, value) pairs of
+    # its rope_scaling / rope_parameters; empty = plain RoPE)
+    rope_scaling: tuple = ()
     # MoE
     num_experts: int = 0
     num_experts_per_tok: int = 0
@@ -80,6 +83,15 @@ class ModelConfig:
         # registry does not know is refused there, never trained as another one
         family = str(d["model_type"])
         heads = d["num_attention_heads"]
+        # transformers 5 nests the RoPE base and scaling in rope_parameters;
+        # hub checkpoints keep rope_theta / rope_scaling at the top level
+        rp = dict(d.get("rope_parameters") or {})
+        rs = dict(d.get("rope_scaling") or {})
+        theta = d.get("rope_theta", rp.get("rope_theta", 1e6))
+        scaling = {k: v for k, v in {**rp, **rs}.items() if k != "rope_theta"}
+        if (scaling.get("rope_type") or scaling.get("type") or "default") == "default":
+            scaling = {}
+        num_experts = d.get("num_experts", d.get("num_local_experts", 0)) or 0
         return cls(
             name=name,
             family=family,  # type: ignore[arg-type]
@@ -91,11 +103,12 @@ class ModelConfig:
             head_dim=d.get("head_dim") or d["hidden_size"] // heads,
             intermediate_size=d.get("intermediate_size", 0),
             rms_norm_eps=d.get("rms_norm_eps", 1e-6),
-            rope_theta=d.get("rope_theta", 1e6),
+            rope_theta=float(theta),
+            rope_scaling=tuple(sorted((k, v) for k, v in scaling.items() if not isinstance(v, (list, dict)))),
             attention_bias=family == "qwen2" or d.get("attention_bias", False),
             qk_norm=family in ("qwen3", "qwen3_moe", "qwen3_next"),
             tie_word_embeddings=d.get("tie_word_embeddings", False),
-            num_experts=d.get("num_experts", 0),
+            num_experts=num_experts,
             num_experts_per_tok=d.get("num_experts_per_tok", 0),
             moe_intermediate_size=d.get("moe_intermediate_size", 0),
             norm_topk_prob=d.get("norm_topk_prob", True),

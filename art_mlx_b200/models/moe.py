@@ -138,6 +138,10 @@ class ExpertParams:
         self.A_gu, self.B_gu, self.A_d, self.B_d = A_gu, B_gu, A_d, B_d
         self.g_A_gu, self.g_B_gu, self.g_A_d, self.g_B_d = g_A_gu, g_B_gu, g_A_d, g_B_d
         self.scale = scale
+        # every expert's A of gate/up and B of down (origin-side rank rows of
+        # the fused expert-parallel exchange; None without expert parallelism)
+        self.A_all_gu = None
+        self.B_all_d = None
 
     def for_compute(self) -> "ExpertParams":
         """Contiguous copies of the factors the products read (slices under
@@ -147,8 +151,10 @@ class ExpertParams:
         if all(t is None or t.is_contiguous() for t in facs):
             return self
         c = lambda t: None if t is None else t.contiguous()  # noqa: E731
-        return ExpertParams(self.gu_w_t, self.down_w_t, c(self.A_gu), c(self.B_gu), c(self.A_d), c(self.B_d),
-                            self.g_A_gu, self.g_B_gu, self.g_A_d, self.g_B_d, self.scale)
+        out = ExpertParams(self.gu_w_t, self.down_w_t, c(self.A_gu), c(self.B_gu), c(self.A_d), c(self.B_d),
+                           self.g_A_gu, self.g_B_gu, self.g_A_d, self.g_B_d, self.scale)
+        out.A_all_gu, out.B_all_d = self.A_all_gu, self.B_all_d
+        return out
 
 
 def _tc_grouped(x: torch.Tensor, p: ExpertParams) -> bool:
@@ -167,6 +173,37 @@ def _offs(counts: list[int]) -> list[int]:
     return out
 
 
+def _lr_rows(x: torch.Tensor, W: torch.Tensor, counts: list[int], transposed: bool = False,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-expert rank-side product ``x_e @ W_e^T`` with ``W`` [E, R, K]
+    (``transposed``: ``x_e @ W_e`` with ``W`` [E, K, R]) on the low-rank
+    kernels (no library grouped GEMM)."""
+    from ..ops import lowrank
+
+    if transposed:
+        E, K, R = W.shape
+        st = (W.stride(0), W.stride(2), W.stride(1))
+    else:
+        E, R, K = W.shape
+        st = (W.stride(0), W.stride(1), W.stride(2))
+    return lowrank.rows(x, W, st, R, K, counts=counts, out=out)
+
+
+def _lr_wgrad(P: torch.Tensor, Q: torch.Tensor, G: torch.Tensor, counts: list[int], alpha: float,
+              transposed: bool = False) -> None:
+    """Per-expert ``G_e += alpha P_e^T Q_e`` with ``G`` [E, R, C] fp32
+    (``transposed``: ``G`` [E, C, R] receives ``alpha Q_e^T P_e``)."""
+    from ..ops import lowrank
+
+    if transposed:
+        E, C, R = G.shape
+        st = (G.stride(0), G.stride(2), G.stride(1))
+    else:
+        E, R, C = G.shape
+        st = (G.stride(0), G.stride(1), G.stride(2))
+    lowrank.wgrad(P, Q, G, st, R, C, alpha, counts=counts)
+
+
 def _experts_forward_tc(xs, counts, p: ExpertParams, lora: bool):
     """Gate/up and down as grouped tcgen05 GEMMs with the LoRA products as a
     K-extension of each (x A^T is the small library grouped GEMM)."""
@@ -180,7 +217,7 @@ def _experts_forward_tc(xs, counts, p: ExpertParams, lora: bool):
     a2 = b2 = u_gu = u_d = None
     if lora and p.A_gu is not None:
         r = p.B_gu.shape[-1]
-        u_gu = grouped_mm(xs, p.A_gu.transpose(1, 2), counts)  # [N, 2r]
+        u_gu = _lr_rows(xs, p.A_gu, counts)  # [N, 2r]
         bd = xs.new_zeros(E, F2, 2 * r)  # per expert: block-diagonal s*[B_gate, B_up]
         bd[:, :Fh, :r] = s * p.B_gu[:, 0]
         bd[:, Fh:, r:] = s * p.B_gu[:, 1]
@@ -189,7 +226,7 @@ def _experts_forward_tc(xs, counts, p: ExpertParams, lora: bool):
     act = C.swiglu_fwd(gu)  # fused silu(gate) * up over the [gate | up] halves
     a2 = b2 = None
     if lora and p.A_d is not None:
-        u_d = grouped_mm(act, p.A_d.transpose(1, 2), counts).contiguous()  # [N, r]
+        u_d = _lr_rows(act, p.A_d, counts)  # [N, r]
         a2, b2 = u_d, (s * p.B_d).reshape(E * H, -1).contiguous()
     out = C.gemm_tc_grouped(act, p.down_w_t.view(E * Fh, H), offs, H, a2, b2, True)
     return out, (xs, gu, act, u_gu, u_d, counts, lora)
@@ -233,9 +270,9 @@ def experts_backward(dout: torch.Tensor, saved, p: ExpertParams) -> torch.Tensor
     if tc:
         a2 = b2 = None
         if lora and p.A_d is not None:
-            dyB = grouped_mm(dout, p.B_d, counts).contiguous()  # [N, r]
-            grouped_wgrad(dout, u_d, counts, p.g_B_d, s)
-            grouped_wgrad(dyB, act, counts, p.g_A_d, s)
+            dyB = _lr_rows(dout, p.B_d, counts, transposed=True)  # [N, r] = dout_e B_d[e]
+            _lr_wgrad(u_d, dout, p.g_B_d, counts, s, transposed=True)  # dB_d[e] += s dout_e^T u_d
+            _lr_wgrad(dyB, act, p.g_A_d, counts, s)  # dA_d[e] += s dyB^T act
             a2, b2 = dyB, (s * p.A_d.transpose(1, 2)).reshape(E * (F2 // 2), -1).contiguous()
         dact = C.gemm_tc_grouped(dout, p.down_w_t.view(E * (F2 // 2), H), offs, F2 // 2, a2, b2, False)
     else:
@@ -257,12 +294,12 @@ def experts_backward(dout: torch.Tensor, saved, p: ExpertParams) -> torch.Tensor
         a2 = b2 = None
         if lora and p.A_gu is not None:
             r = p.B_gu.shape[-1]
-            dyB = torch.cat(
-                [grouped_mm(dgu[:, :Fh].contiguous(), p.B_gu[:, 0], counts),
-                 grouped_mm(dgu[:, Fh:].contiguous(), p.B_gu[:, 1], counts)], dim=1).contiguous()
-            grouped_wgrad(dgu[:, :Fh], u_gu[:, :r], counts, p.g_B_gu[:, 0], s)
-            grouped_wgrad(dgu[:, Fh:], u_gu[:, r:], counts, p.g_B_gu[:, 1], s)
-            grouped_wgrad(dyB, xs, counts, p.g_A_gu, s)
+            dyB = dgu.new_empty(dgu.shape[0], 2 * r)
+            _lr_rows(dgu[:, :Fh], p.B_gu[:, 0], counts, transposed=True, out=dyB[:, :r])
+            _lr_rows(dgu[:, Fh:], p.B_gu[:, 1], counts, transposed=True, out=dyB[:, r:])
+            _lr_wgrad(u_gu[:, :r], dgu[:, :Fh], p.g_B_gu[:, 0], counts, s, transposed=True)
+            _lr_wgrad(u_gu[:, r:], dgu[:, Fh:], p.g_B_gu[:, 1], counts, s, transposed=True)
+            _lr_wgrad(dyB, xs, p.g_A_gu, counts, s)
             a2, b2 = dyB, (s * p.A_gu.transpose(1, 2)).reshape(E * H, -1).contiguous()
         return C.gemm_tc_grouped(dgu, p.gu_w_t.view(E * H, F2), offs, H, a2, b2, False)
     dxs = grouped_mm(dgu, p.gu_w_t.transpose(1, 2), counts)
@@ -394,6 +431,7 @@ class MoEBlock:
             self.gu_w_t, self.down_w_t, pick(A_gu), pick_bgu(B_gu), pick_ad(A_d), pick(B_d),
             pick(g_A_gu), pick_bgu(g_B_gu), pick_ad(g_A_d), pick(g_B_d), spec.scale,
         )
+        self.params.A_all_gu, self.params.B_all_d = A_gu, B_d
 
     def num_parameters(self) -> int:
         n = self.router_w.numel() + self.gu_w_t.numel() + self.down_w_t.numel()
@@ -428,7 +466,16 @@ class MoEBlock:
         T, H = hx.shape
         params = self.params.for_compute()
         if self.ep is not None and self.ep.world > 1:
-            out = _EPExperts.apply(hx, wx, ix, self.ep, params, enabled, anchor)
+            fused = getattr(self.ep, "fused", None)
+            counts = ctx.get("ep_counts")
+            if fused is not None and counts is not None and self.etp is None:
+                # routes replayed and every rank's counts known on the host:
+                # the exchanges fused into the expert GEMMs
+                from ..parallel.ep_fused import FusedEPExperts
+
+                out = FusedEPExperts.apply(hx, wx, ix, fused, params, enabled, counts[self.index], anchor)
+            else:
+                out = _EPExperts.apply(hx, wx, ix, self.ep, params, enabled, anchor)
         else:
             flat = ix.reshape(-1)
             order = torch.argsort(flat, stable=True)

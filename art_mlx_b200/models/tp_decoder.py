@@ -100,7 +100,7 @@ class TPDecoderLM:
         self.v0 = r0 * self.V_l
         self.lm_head = lm[self.v0 : self.v0 + self.V_l].contiguous()
         self.final_norm = torch.ones(H, device=dev, dtype=dt)
-        self.inv_freq = fused.rope_inv_freq(D, cfg.rope_theta, dev)
+        self.inv_freq = fused.rope_inv_freq(D, cfg.rope_theta, dev, dict(cfg.rope_scaling))
         r, sc = lora.r, lora.scale
         q_lo, q_hi = r0 * self.nq_l * D, (r0 + 1) * self.nq_l * D
         kv_lo, kv_hi = r0 * self.nkv_l * D, (r0 + 1) * self.nkv_l * D

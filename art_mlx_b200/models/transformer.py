@@ -170,7 +170,7 @@ class DecoderLM:
         self.embed = _randn((V, H), gen, dev, dt)
         self.final_norm = torch.ones(H, device=dev, dtype=dt)
         self.lm_head = self.embed if cfg.tie_word_embeddings else _randn((V, H), gen, dev, dt)
-        self.inv_freq = fused.rope_inv_freq(cfg.head_dim, cfg.rope_theta, dev)
+        self.inv_freq = fused.rope_inv_freq(cfg.head_dim, cfg.rope_theta, dev, dict(cfg.rope_scaling))
         self.layers: list[Layer] = []
         for i in range(cfg.num_hidden_layers):
             self.layers.append(self._build_layer(i, gen))

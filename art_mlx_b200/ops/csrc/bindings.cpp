@@ -2,6 +2,24 @@
 #include <torch/extension.h>
 
 namespace art {
+void ep_gemm(torch::Tensor x, torch::Tensor w, std::vector<int64_t> offs, int64_t N, bool w_transposed,
+             c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> src,
+             c10::optional<torch::Tensor> src_ext, c10::optional<torch::Tensor> push_tok,
+             c10::optional<torch::Tensor> push_scale, c10::optional<torch::Tensor> push_rank,
+             c10::optional<torch::Tensor> push_row, c10::optional<torch::Tensor> push_expert,
+             c10::optional<torch::Tensor> push_meta, std::vector<int64_t> recv_x_ptrs,
+             std::vector<int64_t> recv_ext_ptrs, std::vector<int64_t> recv_meta_ptrs, std::vector<int64_t> arrive_ptrs,
+             c10::optional<torch::Tensor> arrive_local, c10::optional<torch::Tensor> arrive_target,
+             c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> row_dst, std::vector<int64_t> slot_ptrs,
+             std::vector<int64_t> slot_count_ptrs);
+torch::Tensor ep_wait_combine(torch::Tensor slots, c10::optional<torch::Tensor> w, int64_t k, torch::Tensor counter,
+                              int64_t target);
+torch::Tensor lowrank_rows(torch::Tensor x, c10::optional<torch::Tensor> src, c10::optional<torch::Tensor> scale,
+                           std::vector<int64_t> seg_off, std::vector<int64_t> seg_group, torch::Tensor w,
+                           int64_t R, int64_t w_gs, int64_t w_rs, int64_t w_ks, int64_t K,
+                           c10::optional<torch::Tensor> out);
+void lowrank_wgrad(torch::Tensor p, torch::Tensor q, std::vector<int64_t> seg_off, std::vector<int64_t> seg_group,
+                   torch::Tensor g, int64_t R, int64_t C, int64_t g_gs, int64_t g_rs, int64_t g_cs, double alpha);
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> res,
                                        torch::Tensor w, double eps, bool legacy);
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor xs, torch::Tensor w, torch::Tensor rstd,
@@ -144,4 +162,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("b2") = py::none(), py::arg("bias") = py::none(), py::arg("out") = py::none(),
         py::arg("accumulate") = false, py::arg("diag") = py::none(), py::arg("b_transposed") = false);
   m.def("gdn_conv_bwd", &art::gdn_conv_bwd);
+  m.def("ep_gemm", &art::ep_gemm);
+  m.def("ep_wait_combine", &art::ep_wait_combine);
+  m.def("lowrank_rows", &art::lowrank_rows, py::arg("x"), py::arg("src"), py::arg("scale"), py::arg("seg_off"),
+        py::arg("seg_group"), py::arg("w"), py::arg("R"), py::arg("w_gs"), py::arg("w_rs"), py::arg("w_ks"),
+        py::arg("K"), py::arg("out") = py::none());
+  m.def("lowrank_wgrad", &art::lowrank_wgrad, py::arg("p"), py::arg("q"), py::arg("seg_off"), py::arg("seg_group"),
+        py::arg("g"), py::arg("R"), py::arg("C"), py::arg("g_gs"), py::arg("g_rs"), py::arg("g_cs"),
+        py::arg("alpha"));
 }

@@ -27,7 +27,7 @@ from typing import Any, Sequence
 
 import torch
 
-from . import native
+from . import lowrank, native
 
 
 def _cuda(t: torch.Tensor) -> bool:
@@ -149,10 +149,27 @@ class AttnMeta:
         )
 
 
-def rope_inv_freq(head_dim: int, theta: float, device: torch.device) -> torch.Tensor:
-    return 1.0 / (
-        theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64, device="cpu") / head_dim)
-    ).to(device=device, dtype=torch.float32)
+def rope_inv_freq(head_dim: int, theta: float, device: torch.device, scaling: dict | None = None) -> torch.Tensor:
+    """RoPE inverse frequencies ``theta^(-2i/d)``, with the checkpoint's
+    frequency scaling: ``linear`` (positions divided by ``factor``) or
+    ``llama3`` (long wavelengths divided by ``factor``, short ones kept, a
+    linear blend in between, as published with Llama 3.1).  Other scaling
+    types are refused rather than silently ignored."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64, device="cpu") / head_dim))
+    kind = (scaling or {}).get("rope_type") or (scaling or {}).get("type") or "default"
+    if kind == "linear":
+        inv = inv / float(scaling["factor"])
+    elif kind == "llama3":
+        factor = float(scaling["factor"])
+        lo, hi = float(scaling["low_freq_factor"]), float(scaling["high_freq_factor"])
+        ctx = float(scaling["original_max_position_embeddings"])
+        wavelen = 2 * math.pi / inv
+        smooth = ((ctx / wavelen - lo) / (hi - lo)).clamp(0.0, 1.0)
+        blended = (1 - smooth) * inv / factor + smooth * inv
+        inv = torch.where(wavelen < ctx / hi, inv, torch.where(wavelen > ctx / lo, inv / factor, blended))
+    elif kind != "default":
+        raise NotImplementedError(f"RoPE scaling {kind!r} is not supported")
+    return inv.to(device=device, dtype=torch.float32)
 
 
 # ---------------------------------------------------------------------------
@@ -362,6 +379,14 @@ class LoRABinding:
             self._fused_version = version
         return self._bd_s, self._at_s
 
+    def block_diag_t(self, version: int) -> torch.Tensor:
+        """``block_diag(version)^T`` as a contiguous ``[n*r, out]`` matrix (the
+        W operand of the rank-side input gradient ``dy B``; cached)."""
+        if getattr(self, "_bdt_version", -1) != version or getattr(self, "_bdt", None) is None:
+            self._bdt = self.block_diag(version).t().contiguous()
+            self._bdt_version = version
+        return self._bdt
+
     def block_diag(self, version: int) -> torch.Tensor:
         """Dense ``[out, n*r]`` B with the slice blocks on its diagonal (cached
         until the parameters change)."""
@@ -376,6 +401,15 @@ class LoRABinding:
             self._bd = bd
             self._bd_version = version
         return self._bd
+
+
+def _lowrank_ok(t: torch.Tensor, R: int, wgrad: bool = False) -> bool:
+    """Whether a rank-side product with ``R`` low-rank columns runs on the
+    low-rank kernels (CUDA bf16, 16-byte rows)."""
+    return (LOWRANK and t.is_cuda and t.dtype == torch.bfloat16 and t.dim() == 2
+            and R in (lowrank.WGRAD_WIDTHS if wgrad else lowrank.ROWS_WIDTHS)
+            and R in lowrank.WGRAD_WIDTHS and t.stride(1) == 1 and t.stride(0) % 8 == 0
+            and t.data_ptr() % 16 == 0 and t.shape[1] % 8 == 0)
 
 
 def _accum_mm(slot: torch.Tensor, a: torch.Tensor, b: torch.Tensor, alpha: float) -> None:
@@ -402,14 +436,18 @@ def grad_anchor(device: torch.device) -> torch.Tensor:
 
 PAIR_GEMM = os.environ.get("ART_B200_PAIR_GEMM", "1") != "0"
 PAIR_MIN_ROWS = 1024
-PAIR_MAX_CONTRACTION = 8192
+PAIR_MAX_CONTRACTION = int(os.environ.get("ART_B200_PAIR_MAX_K", str(1 << 30)))
+# the dense LoRA rank-side products on ops/csrc/lowrank.cu (1) or cuBLAS (0);
+# the MoE experts' grouped rank-side products always use the low-rank kernels
+LOWRANK = os.environ.get("ART_B200_LOWRANK", "0") != "0"
 
 
 def _pair_ok(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None, contraction: int) -> bool:
     """Calls the CTA-pair tcgen05 GEMM takes: bf16, 16-byte rows, out and in
-    features multiples of 128, enough rows to fill the GPU (decode-sized
-    calls stay on cuBLAS) and a contraction of at most 8192 (on longer ones
-    cuBLAS's base GEMM is faster than the fused LoRA pass saves)."""
+    features multiples of 128 and enough rows to fill the GPU (decode-sized
+    calls stay on cuBLAS).  Every contraction length runs on it: under the
+    1 kW power cap the step time ties cuBLAS on the long ones (down
+    projection, gate/up input gradient; ``ART_B200_PAIR_MAX_K`` caps it)."""
     return (PAIR_GEMM and _cuda(x) and x.dim() == 2 and x.dtype == torch.bfloat16 and W.dtype == torch.bfloat16
             and x.shape[0] >= PAIR_MIN_ROWS and W.shape[0] % 128 == 0 and W.shape[1] % 128 == 0
             and contraction <= PAIR_MAX_CONTRACTION
@@ -423,7 +461,11 @@ class _LoRALinear(torch.autograd.Function):
         on = enabled and lora is not None
         pair = _pair_ok(x, W, bias, W.shape[1])
         if on:
-            u = x @ lora.A.t()  # [T, n*r]
+            R, K = lora.A.shape
+            if _lowrank_ok(x, R):
+                u = lowrank.rows(x, lora.A, (0, lora.A.stride(0), 1), R, K)  # [T, n*r]
+            else:
+                u = x @ lora.A.t()  # [T, n*r]
         if pair:
             # base GEMM + LoRA as one more k-block of the same accumulator
             bd_s = lora.fused_factors(version)[0] if on else None
@@ -445,16 +487,33 @@ class _LoRALinear(torch.autograd.Function):
         dy = dy.contiguous()
         dyB = None
         if lora is not None:
-            bd = lora.block_diag(ctx.version)
-            dyB = dy @ bd  # [T, n*r]
             s = lora.scale
-            # dA = s * dyB^T x
-            _accum_mm(lora.gA, dyB.t(), x, s)
-            # dB_k = s * dy[:, slice_k]^T u[:, k-block]
-            for k, (gB, (a, b)) in enumerate(zip(lora.gB_blocks, lora.slices)):
-                if gB is None:
-                    continue
-                _accum_mm(gB, dy[:, a:b].t(), u[:, k * lora.r : (k + 1) * lora.r], s)
+            R = lora.A.shape[0]
+            if _lowrank_ok(dy, R) and _lowrank_ok(x, R):
+                # the rank-side products on the low-rank kernels (ops/csrc/lowrank.cu)
+                bdt = lora.block_diag_t(ctx.version)
+                dyB = lowrank.rows(dy, bdt, (0, bdt.stride(0), 1), R, bdt.shape[1])  # [T, n*r]
+                lowrank.wgrad(dyB, x, lora.gA, (0, lora.gA.stride(0), 1), R, x.shape[1], s)  # dA = s dyB^T x
+                for k, (gB, (a, b)) in enumerate(zip(lora.gB_blocks, lora.slices)):
+                    if gB is None:
+                        continue
+                    uk = u[:, k * lora.r : (k + 1) * lora.r]
+                    dyk = dy[:, a:b]
+                    if _lowrank_ok(uk, lora.r, wgrad=True) and dyk.data_ptr() % 16 == 0 and (b - a) % 8 == 0:
+                        # dB_k^T (r x out_k) = s u_k^T dy_k, stored into dB_k [out_k, r]
+                        lowrank.wgrad(uk, dyk, gB, (0, gB.stride(1), gB.stride(0)), lora.r, b - a, s)
+                    else:
+                        _accum_mm(gB, dyk.t(), uk, s)
+            else:
+                bd = lora.block_diag(ctx.version)
+                dyB = dy @ bd  # [T, n*r]
+                # dA = s * dyB^T x
+                _accum_mm(lora.gA, dyB.t(), x, s)
+                # dB_k = s * dy[:, slice_k]^T u[:, k-block]
+                for k, (gB, (a, b)) in enumerate(zip(lora.gB_blocks, lora.slices)):
+                    if gB is None:
+                        continue
+                    _accum_mm(gB, dy[:, a:b].t(), u[:, k * lora.r : (k + 1) * lora.r], s)
         if not ctx.needs_input_grad[0]:
             # the input needs no gradient (e.g. the first layer over the frozen
             # embedding): the LoRA gradients above are all this pass owes

@@ -25,7 +25,7 @@ from typing import Callable
 import torch
 
 LINK_BPS = 770e9  # measured peer-copy bandwidth per direction per GPU
-GEMM_PEAK = 1.615e15  # measured cuBLAS bf16 burst peak
+GEMM_PEAK = 1.6486e15  # measured cuBLAS bf16 burst peak (8192^3, best of 10)
 
 
 def _timed(fn: Callable[[], object], reps: int = 5, inner: int = 5) -> float:

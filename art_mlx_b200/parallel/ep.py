@@ -29,6 +29,7 @@ path used by the CPU tests).
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -68,6 +69,13 @@ class EPContext:
         if transport is None:
             transport = "p2p" if device.type == "cuda" and self.world > 1 else "a2a"
         self.transport = P2PTransport(self, capacity_rows) if transport == "p2p" else AllToAllTransport(self)
+        # the exchange fused into the expert GEMMs (parallel/ep_fused.py), used
+        # when every rank's route counts are known on the host (routing replay)
+        self.fused = None
+        if transport == "p2p" and os.environ.get("ART_B200_EP_FUSED", "1") != "0" and self.world <= 8:
+            from .ep_fused import FusedEP
+
+            self.fused = FusedEP(group, num_experts, hidden, device, capacity_rows, capacity_rows // 2)
 
     @property
     def first_expert(self) -> int:

@@ -63,6 +63,9 @@ class MicroBatch:
     group_ids: torch.Tensor | None = None  # [L] host copies (tree-structured layers)
     parent_ids: torch.Tensor | None = None
     cp_plan: Any = None  # context-parallel plan (parallel/cp.py) when the row is split across ranks
+    # per MoE layer, [EP world, experts] slots every EP rank routes to each
+    # expert in this micro step (host; from every rank's replayed routes)
+    ep_counts: Any = None
 
     @property
     def L(self) -> int:
@@ -414,6 +417,8 @@ class GRPOTrainer:
             add("tp_barrier", getattr(self.tp, "status", None))
         if self.ep is not None:
             add("ep_barrier", getattr(self.ep.transport, "status", None))
+            if getattr(self.ep, "fused", None) is not None:
+                add("ep_fused_barrier", self.ep.fused.status)
         if self.etp is not None:
             add("etp_barrier", getattr(self.etp, "status", None))
         if self.device.type == "cuda":
@@ -492,6 +497,8 @@ class GRPOTrainer:
             ctx["replay_routes"] = mb.routes
             if mb.route_counts is not None:
                 ctx["replay_counts"] = mb.route_counts
+            if mb.ep_counts is not None:
+                ctx["ep_counts"] = mb.ep_counts
         ref = None
         kl_coef = float(cfg.get("kl_penalty_coef", 0.0) or 0.0)
         if kl_coef > 0:
@@ -578,6 +585,7 @@ class GRPOTrainer:
             micro_batches = self.stage(packed)
         if mutation.active("dp_local_token_normalization"):
             total = float(sum(int(mb.sel.numel()) for mb in micro_batches))
+        self._attach_ep_counts(micro_batches)
         acc = {k: torch.zeros((), device=self.device) for k in ("loss", "entropy", "probs_corr", "kl")}
         n_tokens = 0
         for mb in micro_batches:
@@ -613,6 +621,30 @@ class GRPOTrainer:
             grad_norm=self.optim.grad_norm, n_train=int(total), n_tokens=packed_tokens,
             health=health, health_names=names,
         )
+
+    def _attach_ep_counts(self, micro_batches: list[MicroBatch]) -> None:
+        """With replayed routes, give every micro batch the per-layer slot
+        counts of every expert-parallel rank (one host all-gather per step;
+        the fused exchange then plans each MoE layer without a device sync)."""
+        ep = self.ep
+        if ep is None or getattr(ep, "fused", None) is None or self.etp is not None:
+            return
+        if not micro_batches or any(mb.route_counts is None for mb in micro_batches):
+            return
+        if all(mb.ep_counts is not None for mb in micro_batches):
+            return
+        E = self.model.cfg.num_experts
+        mine = []
+        for mb in micro_batches:
+            per_layer = np.zeros((len(mb.route_counts), E), dtype=np.int64)
+            for j, c in enumerate(mb.route_counts):
+                per_layer[j, : len(c)] = c
+            mine.append(per_layer)
+        gathered: list = [None] * ep.world
+        dist.all_gather_object(gathered, mine, group=ep.group)
+        for m, mb in enumerate(micro_batches):
+            mb.ep_counts = [np.stack([gathered[q][m][j] for q in range(ep.world)])
+                            for j in range(len(mb.route_counts))]
 
     def train_steps(
         self,

@@ -39,18 +39,52 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--model", default="qwen2.5-7b")
-    p.add_argument("--groups", type=int, default=8)
-    p.add_argument("--rollouts", type=int, default=16)
-    p.add_argument("--prompt-len", type=int, default=1024)
-    p.add_argument("--completion-len", type=int, default=512)
-    p.add_argument("--lora-rank", type=int, default=16)
+    p.add_argument("--config", choices=sorted(CONFIGS), default="dense7b",
+                   help="benchmark configuration (the BASELINE configs); flags below override its fields")
+    p.add_argument("--model", default=None)
+    p.add_argument("--groups", type=int, default=None)
+    p.add_argument("--rollouts", type=int, default=None)
+    p.add_argument("--prompt-len", type=int, default=None)
+    p.add_argument("--completion-len", type=int, default=None)
+    p.add_argument("--lora-rank", type=int, default=None)
+    p.add_argument("--kl", type=float, default=None, help="KL penalty coefficient against the frozen base")
     p.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the headline)")
-    p.add_argument("--tp", type=int, default=1, help="tensor-parallel size (dense models)")
-    p.add_argument("--cp", type=int, default=1, help="context-parallel size")
+    p.add_argument("--tp", type=int, default=None, help="tensor-parallel size (dense models)")
+    p.add_argument("--cp", type=int, default=None, help="context-parallel size")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=2)
-    return p.parse_args()
+    a = p.parse_args()
+    c = CONFIGS[a.config]
+    for key in ("model", "groups", "rollouts", "prompt_len", "completion_len", "lora_rank", "kl"):
+        if getattr(a, key) is None:
+            setattr(a, key, c[key])
+    n = max(a.gpus, 1)
+    if a.tp is None:
+        a.tp = n if c["par"] == "tp" else 1
+    if a.cp is None:
+        if c["par"] == "cp":
+            a.cp = n
+        elif c["par"] == "ep":
+            # one packed row per group: the rows are spread over data-parallel
+            # groups and each row over the context-parallel ranks of its group
+            a.cp = max(1, n // min(n, a.groups))
+        else:
+            a.cp = 1
+    return a
+
+
+# The GPU benchmark configurations (model shape, data per step, adapter, how
+# the GPUs split the work).  "dense7b" is the headline.
+CONFIGS = {
+    "dense7b": dict(model="qwen2.5-7b", groups=8, rollouts=16, prompt_len=1024, completion_len=512,
+                    lora_rank=16, kl=0.0, par="dp"),
+    "moe30b": dict(model="qwen3-30b-a3b", groups=4, rollouts=8, prompt_len=2048, completion_len=1024,
+                   lora_rank=8, kl=0.0, par="ep"),
+    "hybrid": dict(model="qwen3-next-hybrid", groups=1, rollouts=8, prompt_len=8192, completion_len=7168,
+                   lora_rank=16, kl=0.0, par="cp"),
+    "dense32b": dict(model="qwen3-32b", groups=16, rollouts=8, prompt_len=4096, completion_len=1024,
+                     lora_rank=32, kl=0.01, par="tp"),
+}
 
 
 BASELINE_VALUE = None  # BASELINE.md publishes no GPU number for this metric
@@ -199,7 +233,7 @@ def main() -> None:
     trainer = GRPOTrainer(cfg, lora, device, seed=0, group=dist.group.WORLD if world > 1 else None,
                           tp_size=args.tp, cp_size=args.cp, max_tokens_per_rank=max(16384, seq_len))
     lr = 1e-5
-    loss_cfg: dict = {}
+    loss_cfg: dict = {"kl_penalty_coef": args.kl} if args.kl else {}
     staged = trainer.stage(packed)
     if cfg.is_moe:
         # routing replay: the top-k experts of every token and layer are
@@ -299,8 +333,9 @@ def main() -> None:
                 "trained_tokens_per_step": int(train_tokens),
                 "packed_tokens_per_step": packed_tokens,
                 "packed_tokens_per_s": round(packed_tokens / (ms / 1000.0), 1),
-                "l2": "256 MiB buffer written before every step; weights (15 GB) exceed L2",
-                "loss": "cispo (default)",
+                "l2": "256 MiB buffer written before every step; the per-GPU weights exceed L2",
+                "loss": "cispo (default)" + (f", KL {args.kl} against the frozen base" if args.kl else ""),
+                "bench_config": args.config,
                 "library_kernels_per_step": lib_kernels,
                 "final_metrics": metrics,
             },

@@ -79,7 +79,24 @@ def _shape(backend: str, cfg: ModelConfig) -> tuple[int, int, int, int]:
     return cfg.vocab_size, 96, 48, 512
 
 
-def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1, cp_size=1, etp_size=1):
+def _replay_routes(mbs, cfg):
+    """Deterministic replayed routes (a function of token id and layer, so
+    every topology sees the same routes for the same tokens), with their
+    per-layer host counts."""
+    from art_mlx_b200.runtime.trainer import _route_counts
+
+    E, k, L = cfg.num_experts, cfg.num_experts_per_tok, cfg.num_hidden_layers
+    for mb in mbs:
+        tok = mb.tokens.to(torch.int64)
+        layer = torch.arange(L, device=tok.device).view(1, L, 1)
+        j = torch.arange(k, device=tok.device).view(1, 1, k)
+        base = (tok.view(-1, 1, 1) * 31 + layer * 17) % E
+        mb.routes = ((base + j) % E).to(torch.int32)
+        mb.route_counts = _route_counts(mb.routes.cpu())
+    return mbs
+
+
+def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1, cp_size=1, etp_size=1, replay=False):
     if backend == "nccl":
         torch.cuda.set_device(rank)
         device = torch.device("cuda", rank)
@@ -97,31 +114,35 @@ def _worker(rank, world, init_file, out_path, backend, cfg_name, tp_size=1, cp_s
         assert (tr.grad_sync is not None) == (backend == "nccl")
         assert (tr.ep is not None) == (cfg.is_moe and world // etp_size > 1)
         assert (tr.etp is not None) == (etp_size > 1)
+        mbs = _replay_routes(tr.stage(packed), cfg) if replay else None
         for _ in range(2):
-            m = tr.train_step(packed, 1e-3, {})
+            m = tr.train_step(packed, 1e-3, {}, micro_batches=mbs)
         host = m.to_host()
         tr.check_health()
         tr.prepare_checkpoint()
+        fused = getattr(tr.ep, "fused", None) if tr.ep is not None else None
         if rank == 0:
-            torch.save({"master": tr.store.master.cpu(), "metrics": host}, out_path)
+            torch.save({"master": tr.store.master.cpu(), "metrics": host,
+                        "fused_exchanges": 0 if fused is None else fused.slot_total}, out_path)
     finally:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def _single(device, cfg, backend):
+def _single(device, cfg, backend, replay=False):
     packed = _packed(*_shape(backend, cfg))
     tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), device, seed=0)
+    mbs = _replay_routes(tr.stage(packed), cfg) if replay else None
     for _ in range(2):
-        m = tr.train_step(packed, 1e-3, {})
+        m = tr.train_step(packed, 1e-3, {}, micro_batches=mbs)
     return tr.store.master.cpu(), m.to_host(), packed
 
 
-def _run(world, backend, cfg_name, tp_size=1, cp_size=1, etp_size=1):
+def _run(world, backend, cfg_name, tp_size=1, cp_size=1, etp_size=1, replay=False):
     d = tempfile.mkdtemp()
     init = os.path.join(d, "init")
     out = os.path.join(d, "out.pt")
-    mp.start_processes(_worker, args=(world, init, out, backend, cfg_name, tp_size, cp_size, etp_size),
+    mp.start_processes(_worker, args=(world, init, out, backend, cfg_name, tp_size, cp_size, etp_size, replay),
                        nprocs=world, start_method="spawn")
     return torch.load(out)
 
@@ -184,6 +205,28 @@ def test_etp_moe_two_gpus_matches_single_gpu():
     err = (res["master"] - master).norm() / master.norm()
     # bf16 partial expert outputs are summed over the two slices in another order than on one GPU
     assert err < 1e-2, err
+
+
+def test_ep_moe_replay_gloo_matches_single_process():
+    """Expert parallelism with replayed routes (all-to-all transport on CPU)."""
+    res = _run(2, "gloo", "moe-tiny", replay=True)
+    master, metrics, _ = _single(torch.device("cpu"), MOE_CPU, "gloo", replay=True)
+    err = (res["master"] - master).norm() / master.norm()
+    assert err < 1e-5, err
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_moe_fused_two_gpus_matches_single_gpu():
+    """Replayed routes: the exchanges fused into the expert GEMMs (P2P stores
+    from the dispatch warps and the scatter epilogue) vs one GPU."""
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    res = _run(2, "nccl", "moe-small", replay=True)
+    assert res["fused_exchanges"] > 0, "the fused exchange did not run"
+    master, metrics, _ = _single(torch.device("cuda", 0), MOE_GPU, "nccl", replay=True)
+    err = (res["master"] - master).norm() / master.norm()
+    assert err < 1e-2, err
+    assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-2 * max(1.0, abs(metrics["loss/train"]))
 
 
 @pytest.mark.gpu

@@ -1,0 +1,67 @@
+"""Parity of :class:`DecoderLM` with Hugging Face transformers.
+
+For each supported family a tiny random model is built with transformers,
+saved with ``save_pretrained`` (safetensors + config.json), loaded through
+this package's own path (``get_config(dir)`` + ``maybe_load_base_weights``)
+and run on the same tokens: the logits must agree in fp32.  This is the
+oracle for the architectures (reference counterpart: the HF-parity suites of
+``tests/integration/megatron/model_support/``) and checks the checkpoint
+loader against real HF checkpoints.
+"""
+
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+from art_mlx_b200.models.config import LoRASpec, get_config  # noqa: E402
+from art_mlx_b200.models.transformer import DecoderLM  # noqa: E402
+from art_mlx_b200.models.weights import maybe_load_base_weights  # noqa: E402
+from art_mlx_b200.ops import fused  # noqa: E402
+
+
+def _tiny(kind: str):
+    common = dict(vocab_size=512, hidden_size=64, num_hidden_layers=2, num_attention_heads=4,
+                  num_key_value_heads=2, max_position_embeddings=512, rms_norm_eps=1e-6, rope_theta=10000.0,
+                  tie_word_embeddings=False)
+    if kind == "qwen2":
+        return transformers.Qwen2Config(intermediate_size=96, **common)
+    if kind == "qwen3":
+        return transformers.Qwen3Config(intermediate_size=96, head_dim=16, **common)
+    if kind == "qwen3_moe":
+        return transformers.Qwen3MoeConfig(intermediate_size=96, head_dim=16, moe_intermediate_size=32,
+                                           num_experts=4, num_experts_per_tok=2, norm_topk_prob=True,
+                                           decoder_sparse_step=1, mlp_only_layers=[], **common)
+    if kind == "llama":
+        return transformers.LlamaConfig(intermediate_size=96, head_dim=16, **common)
+    raise KeyError(kind)
+
+
+def _logits_ours(path: str, tokens: torch.Tensor) -> torch.Tensor:
+    cfg = get_config(path)
+    m = DecoderLM(cfg, LoRASpec(r=4, alpha=8), "cpu", seed=5)
+    assert maybe_load_base_weights(m, path)
+    m.lora_enabled = False
+    T = tokens.numel()
+    meta = fused.AttnMeta.build(torch.arange(T), torch.full((T,), T, dtype=torch.int32), torch.device("cpu"))
+    with torch.no_grad():
+        h = m.forward(tokens, meta, {})
+    return h.float() @ m.lm_head.float().t()
+
+
+@pytest.mark.parametrize("kind", ["qwen2", "qwen3", "qwen3_moe", "llama"])
+def test_logits_match_transformers(kind, tmp_path):
+    torch.manual_seed(0)
+    hf_cfg = _tiny(kind)
+    model = transformers.AutoModelForCausalLM.from_config(hf_cfg).float().eval()
+    with torch.no_grad():  # non-trivial norm weights (HF initialises them to 1)
+        for name, p in model.named_parameters():
+            if "norm" in name:
+                p.add_(0.1 * torch.randn_like(p))
+    model.save_pretrained(tmp_path)
+    tokens = torch.randint(0, hf_cfg.vocab_size, (37,))
+    with torch.no_grad():
+        ref = model(tokens.unsqueeze(0)).logits[0].float()
+    ours = _logits_ours(str(tmp_path), tokens)
+    err = (ours - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-4, f"{kind}: max relative logit error {err}"
