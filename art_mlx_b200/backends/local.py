@@ -223,7 +223,11 @@ class LocalBackend:
         if eng is None:
             from ..runtime.generate import GenerationEngine
 
-            eng = GenerationEngine(self._get_trainer(model).model)
+            # the resolved engine arguments (dev.get_model_config) size the engine
+            ea = dev.get_model_config(model.base_model, self._model_dir(model),
+                                      getattr(model, "_internal_config", None) or {})["engine_args"]
+            eng = GenerationEngine(self._get_trainer(model).model, max_len=int(ea.get("max_model_len", 8192)),
+                                   max_batch=int(ea.get("max_num_seqs", 256)))
             self._engines[model.name] = eng
         return eng
 
@@ -487,6 +491,65 @@ class LocalBackend:
             save_adapter(get_step_checkpoint_dir(d, step), tr.store, model.base_model, tr.model.lora_spec,
                          tr.optim.state_dict())
         _barrier()
+
+    # ------------------------------------------------------------------ S3
+    async def _experimental_push_to_s3(self, model: Any, *, s3_bucket: str | None = None, prefix: str | None = None,
+                                       verbose: bool = False, delete: bool = False) -> None:
+        """Upload the model directory (checkpoints, logs, trajectories) to S3
+        (reference ``local/backend.py:1520``; layout in ``utils/s3.py``)."""
+        from ..utils.s3 import push_model_to_s3
+
+        self._flush()
+        await push_model_to_s3(model.name, model.project, s3_bucket, prefix, verbose, delete, self._path)
+
+    async def _experimental_pull_from_s3(self, model: Any, *, s3_bucket: str | None = None, prefix: str | None = None,
+                                         verbose: bool = False, delete: bool = False,
+                                         only_step: int | str | None = None, exclude: list | None = None) -> None:
+        """Download the model directory, or one step (``only_step``: a step or
+        ``"latest"``), from S3 into this backend's storage."""
+        from ..utils.s3 import get_latest_checkpoint_step_from_s3, pull_model_from_s3
+
+        step = None
+        if only_step == "latest":
+            step = await get_latest_checkpoint_step_from_s3(model.name, model.project, s3_bucket, prefix)
+            if step is None:
+                return
+        elif only_step is not None:
+            step = int(only_step)
+        await pull_model_from_s3(model.name, model.project, step, s3_bucket, prefix, verbose, delete, self._path,
+                                 exclude)
+
+    async def _experimental_pull_model_checkpoint(self, model: Any, *, step: int | str | None = None,
+                                                  local_path: str | None = None, s3_bucket: str | None = None,
+                                                  prefix: str | None = None, verbose: bool = False) -> str:
+        """Path of a local copy of a checkpoint: the local one when present
+        (for ``"latest"`` the newer of local and S3, local on a tie), else
+        pulled from S3; copied to ``local_path`` when given."""
+        from ..utils.output_dirs import list_checkpoint_steps
+        from ..utils.s3 import get_latest_checkpoint_step_from_s3, pull_model_from_s3
+
+        d = self._model_dir(model)
+        local_steps = list_checkpoint_steps(d) if os.path.isdir(d) else []
+        if step in (None, "latest"):
+            s3_step = (await get_latest_checkpoint_step_from_s3(model.name, model.project, s3_bucket, prefix)
+                       if s3_bucket else None)
+            cands = [x for x in (max(local_steps) if local_steps else None, s3_step) if x is not None]
+            if not cands:
+                raise FileNotFoundError(f"no checkpoint of {model.name} locally or in S3")
+            step = max(cands)
+        step = int(step)
+        ck = get_step_checkpoint_dir(d, step)
+        if not os.path.isdir(ck):
+            if not s3_bucket:
+                raise FileNotFoundError(ck)
+            ck = await pull_model_from_s3(model.name, model.project, step, s3_bucket, prefix, verbose, False,
+                                          self._path)
+        if local_path is not None:
+            if os.path.exists(local_path):
+                shutil.rmtree(local_path)
+            shutil.copytree(ck, local_path)
+            return local_path
+        return ck
 
     # ------------------------------------------------------------------
     async def _experimental_fork_checkpoint(self, model: Any, from_model: str, from_project: str | None = None,

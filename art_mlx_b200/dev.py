@@ -63,6 +63,7 @@ class InitArgs(TypedDict, total=False):
     max_seq_length: int
     dtype: str
     seed: int
+    model_name: str
 
 
 class TrainerArgs(TypedDict, total=False):
@@ -76,14 +77,21 @@ class TrainerArgs(TypedDict, total=False):
 
 
 class EngineArgs(TypedDict, total=False):
-    """Rollout-engine arguments forwarded to the inference server."""
+    """Rollout-engine arguments.  The native engine reads ``max_model_len``
+    (KV-cache length per sequence), ``max_num_seqs`` (sequences decoded per
+    batch) and ``max_lora_rank``; ``enable_sleep_mode`` is False in
+    dedicated mode (the engine owns its GPUs).  The other keys are kept for
+    configs shared with a vLLM server."""
 
     gpu_memory_utilization: float
     max_model_len: int
+    max_num_seqs: int
     enable_lora: bool
     max_lora_rank: int
     tensor_parallel_size: int
     enable_sleep_mode: bool
+    lora_target_modules: list[str]
+    generation_config: str
 
 
 class OpenAIServerConfig(TypedDict, total=False):
@@ -156,3 +164,81 @@ def validate_dedicated_config(config: InternalModelConfig) -> None:
         raise ValueError("trainer_gpu_ids and inference_gpu_ids must not overlap")
     if config.get("rollout_weights_mode", "lora") not in ("lora", "merged"):
         raise ValueError("rollout_weights_mode must be 'lora' or 'merged'")
+
+
+class BackendModelConfig(TypedDict, total=False):
+    """Fully resolved model configuration of a backend (defaults merged with
+    the user's ``_internal_config``)."""
+
+    init_args: InitArgs
+    engine_args: EngineArgs
+    lora_config: LoRAConfig
+    trainer_args: TrainerArgs
+    rollout_weights_mode: Literal["lora", "merged"]
+    trainer_gpu_ids: list[int]
+    inference_gpu_ids: list[int]
+    allow_unvalidated_arch: bool
+
+
+def is_dedicated_mode(config: InternalModelConfig) -> bool:
+    """Separate trainer and inference GPUs (both id lists given)."""
+    return bool(config.get("trainer_gpu_ids")) and bool(config.get("inference_gpu_ids"))
+
+
+def get_model_config(base_model: str, output_dir: str, config: InternalModelConfig | None,
+                     lora_config: LoRAConfig | None = None) -> BackendModelConfig:
+    """Defaults merged with ``config`` (reference ``dev/get_model_config.py:22-113``):
+
+    * ``init_args``: ``max_seq_length`` = the architecture's context length,
+      the model to load = the latest checkpoint under ``output_dir`` if any;
+    * ``engine_args``: ``max_model_len`` = ``max_seq_length``, 256 sequences
+      per decode batch, sleep mode only when sharing GPUs with the trainer,
+      LoRA targets of the family;
+    * ``lora_config``: the family's default target modules (model-support
+      registry), r 8, alpha 16;
+    * ``trainer_args``: AdamW lr 5e-6, betas (0.9, 0.99), weight decay 0.1,
+      grad clip 0.1, constant schedule.
+    User values override every default key by key.
+    """
+    import os
+
+    from .models.config import get_config
+    from .models.registry import get_model_support
+    from .utils.output_dirs import get_step_checkpoint_dir, list_checkpoint_steps
+
+    config = dict(config or {})
+    validate_dedicated_config(config)  # type: ignore[arg-type]
+    dedicated = is_dedicated_mode(config)  # type: ignore[arg-type]
+    try:
+        mcfg = get_config(config.get("model_preset") or base_model)
+        max_len = int(min(mcfg.max_position_embeddings, 32768))
+        targets = list(get_model_support(mcfg, allow_unvalidated_arch=True).default_target_modules)
+    except KeyError:
+        max_len, targets = 8192, list(DEFAULT_LORA_TARGETS)
+    init = InitArgs(max_seq_length=max_len)
+    init.update(config.get("init_args") or {})
+    model_name = base_model
+    steps = list_checkpoint_steps(output_dir) if output_dir and os.path.isdir(output_dir) else []
+    if steps:
+        model_name = get_step_checkpoint_dir(output_dir, max(steps))
+    engine = EngineArgs(max_model_len=int(init.get("max_seq_length", max_len)), max_num_seqs=256,
+                        enable_sleep_mode=not dedicated, generation_config="vllm")
+    engine.update(config.get("engine_args") or {})
+    if dedicated:
+        engine["enable_sleep_mode"] = False
+    lora = LoRAConfig(r=8, lora_alpha=16, target_modules=targets, lora_dropout=0.0)
+    lora.update(config.get("peft_args") or {})
+    lora.update(lora_config or {})
+    mode = config.get("rollout_weights_mode", "lora")
+    if mode == "lora":
+        engine.setdefault("lora_target_modules", list(lora["target_modules"]))
+        engine.setdefault("max_lora_rank", int(lora["r"]))
+    trainer = default_trainer_args()
+    trainer.update(config.get("trainer_args") or {})
+    out = BackendModelConfig(init_args=init, engine_args=engine, lora_config=lora, trainer_args=trainer,
+                             rollout_weights_mode=mode)
+    out["init_args"]["model_name"] = model_name  # type: ignore[typeddict-unknown-key]
+    for key in ("trainer_gpu_ids", "inference_gpu_ids", "allow_unvalidated_arch"):
+        if key in config:
+            out[key] = config[key]  # type: ignore[literal-required]
+    return out

@@ -42,6 +42,10 @@ for _spec in (
                      supports=frozenset({"dp", "ep", "cp", "generate"})),
     ModelSupportSpec("qwen3_next", ("qwen3_next",), _DENSE + ("in_proj_qkvz", "out_proj"), is_moe=True,
                      linear_attention=True, supports=frozenset({"dp", "ep", "cp"})),
+    # the default dense decoder (reference: model_support/handlers/default_dense.py): Llama-style
+    # checkpoints run through the same layers (no q/k norm, optional q/k/v bias, RoPE scaling)
+    ModelSupportSpec("llama", ("llama",), _DENSE, supports=frozenset({"dp", "tp", "cp", "generate"})),
+    ModelSupportSpec("mistral", ("mistral",), _DENSE, supports=frozenset({"dp", "tp", "cp", "generate"})),
 ):
     register_model_support(_spec)
 

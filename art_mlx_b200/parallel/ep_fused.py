@@ -52,6 +52,15 @@ def _round(n: int, a: int = 256) -> int:
     return (n + a - 1) // a * a
 
 
+def _h2d(a: np.ndarray, device: torch.device) -> torch.Tensor:
+    """Host array -> device through pinned memory: queued like a kernel (a
+    copy from pageable memory would first wait for the stream to drain)."""
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if device.type == "cuda":
+        return t.pin_memory().to(device, non_blocking=True)
+    return t.to(device)
+
+
 @dataclass
 class FusedPlan:
     T: int
@@ -164,8 +173,8 @@ class FusedEP:
         # rank's slots of the same expert, plus the expert's base
         order = torch.argsort(flat, stable=True)
         first = np.cumsum(mine) - mine
-        first_d = torch.from_numpy(first).to(dev, non_blocking=True)
-        base_d = torch.from_numpy(base_mine).to(dev, non_blocking=True)
+        first_d = _h2d(first, dev)
+        base_d = _h2d(base_mine, dev)
         fs = flat[order]
         dest_row = torch.empty_like(flat)
         dest_row[order] = base_d[fs] + torch.arange(flat.numel(), device=dev) - first_d[fs]
@@ -192,14 +201,14 @@ class FusedEP:
             push_order=push_order,
             push_counts=seg_counts, push_groups=seg_groups,
         )
-        plan.arrive_target = torch.from_numpy(tgt.copy()).to(dev, non_blocking=True)
+        plan.arrive_target = _h2d(tgt, dev)
         return plan
 
     def next_arrive_target(self, plan: FusedPlan) -> torch.Tensor:
         """Targets for a second exchange over the same plan (the backward)."""
         self.arrive_total += np.asarray(plan.local_counts, dtype=np.int64)
         tgt = (self.arrive_total & 0xFFFFFFFF).astype(np.uint32).view(np.int32)
-        return torch.from_numpy(tgt.copy()).to(self.device, non_blocking=True)
+        return _h2d(tgt, self.device)
 
     def combine_target(self, plan: FusedPlan) -> int:
         self.slot_total += plan.T * plan.k * ((self.H + N_TILE - 1) // N_TILE)

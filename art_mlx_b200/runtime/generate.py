@@ -57,11 +57,12 @@ class GenerationResult:
 
 
 class GenerationEngine:
-    def __init__(self, model, max_len: int = 8192) -> None:
+    def __init__(self, model, max_len: int = 8192, max_batch: int = 256) -> None:
         cfg = model.cfg
         self.model, self.cfg = model, cfg
         self.device = model.device
-        self.max_len = max_len
+        self.max_len = max_len  # KV-cache length per sequence (engine_args.max_model_len)
+        self.max_batch = max(1, max_batch)  # sequences decoded together (engine_args.max_num_seqs)
         self.adapters: dict[str, torch.Tensor] = {}
         self._cache: tuple[list[torch.Tensor], list[torch.Tensor]] | None = None
 
@@ -188,7 +189,11 @@ class GenerationEngine:
             st.compute.copy_(self.adapters[adapter])
             st.version += 1
         try:
-            return self._generate([list(x) for x in prompts], p)
+            ps = [list(x) for x in prompts]
+            out: list[GenerationResult] = []
+            for a in range(0, len(ps), self.max_batch):
+                out.extend(self._generate(ps[a : a + self.max_batch], p))
+            return out
         finally:
             m.lora_enabled = prev_enabled
             if saved is not None:

@@ -12,10 +12,11 @@ def test_registry_resolves_presets_and_hf_ids():
     assert set(registered_families()) >= {"qwen2", "qwen3", "qwen3_moe", "qwen3_next"}
     with pytest.raises(ValueError, match="does not support tp"):
         check_parallelism(get_model_support("qwen3-30b-a3b"), tp=2)
-    cfg = get_config("tiny-qwen3").scaled(family="llama")
+    assert get_model_support(get_config("tiny-qwen3").scaled(family="llama")).key == "llama"
+    cfg = get_config("tiny-qwen3").scaled(family="gpt_neox")
     with pytest.raises(ValueError, match="not supported"):
         get_model_support(cfg)
-    assert get_model_support(cfg, allow_unvalidated_arch=True).key == "llama"
+    assert get_model_support(cfg, allow_unvalidated_arch=True).key == "gpt_neox"
 
 
 def test_unknown_hf_model_type_is_refused(tmp_path):
