@@ -76,6 +76,7 @@ class PipelineState:
     last_eval_step: int = -1
     discarded_stale_groups: int = 0
     zero_variance_groups: int = 0
+    collapsed: bool = False  # the zero-variance failsafe stopped training
     done: bool = False
     policy_updated: asyncio.Condition = field(default_factory=asyncio.Condition)
 
@@ -164,6 +165,7 @@ class PipelineTrainer(Generic[ScenarioT, ConfigT]):
         self._scenarios = _as_async_iter(scenarios)
         self._scenario_lock = asyncio.Lock()
         self._discarded: list[TrajectoryGroup] = []
+        self._leases: dict[int, Any] = {}  # step -> held adapter lease (scheduled evals)
         self._eval_queue: asyncio.Queue[int] | None = None
         self._output: asyncio.Queue[TrajectoryGroup | None] | None = None
         self._stop = asyncio.Event()
@@ -259,9 +261,9 @@ class PipelineTrainer(Generic[ScenarioT, ConfigT]):
             if self._zero_variance(g):
                 self.state.zero_variance_groups += 1
                 self._discarded.append(g)
-                if len(self._discarded) > self.discard_limit:
-                    raise RuntimeError(
-                        f"{len(self._discarded)} zero-variance groups in a row: rewards carry no signal")
+                if len(self._discarded) >= self.discard_limit:
+                    self._trigger_collapse()
+                    return None
                 continue
             batch.append(g)
         while len(batch) < self.max_batch_size and not self._output.empty():
@@ -274,6 +276,49 @@ class PipelineTrainer(Generic[ScenarioT, ConfigT]):
         if finished:
             await self._output.put(None)  # keep the end marker for the next call
         return batch or None
+
+    def _trigger_collapse(self) -> None:
+        """Collapse failsafe (reference ``pipeline_trainer/trainer.py:879-911``):
+        ``discard_queue_multiplier * min_batch_size`` zero-variance groups
+        without a trainable batch in between mean the policy has collapsed to
+        a degenerate output (or the reward gives no signal); training stops
+        gracefully instead of spinning on useless rollouts."""
+        if self.state.collapsed:
+            return
+        self.state.collapsed = True
+        self.state.done = True
+        self._stop.set()
+        print(
+            "\nMODEL COLLAPSE DETECTED - training stopped: "
+            f"{len(self._discarded)} trajectory groups had zero reward variance "
+            f"(limit {self.discard_limit} = discard_queue_multiplier {self.discard_limit // self.min_batch_size}"
+            f" x min_batch_size {self.min_batch_size}).  Lower the learning rate, check that the reward "
+            "varies within a group and that prompts are diverse, or raise discard_queue_multiplier.\n",
+            flush=True,
+        )
+
+    def _lease_manager(self):
+        get = getattr(self.backend, "adapter_leases", None)
+        return get(self.model) if callable(get) else None
+
+    async def _take_lease(self, step: int) -> None:
+        """Keep checkpoint ``step`` alive (checkpoint cleanup skips leased
+        steps) until :meth:`_release_lease`."""
+        mgr = self._lease_manager()
+        if mgr is None or step in self._leases:
+            return
+        cm = mgr.lease(step)
+        await cm.__aenter__()
+        self._leases[step] = cm
+
+    async def _release_lease(self, step: int) -> None:
+        cm = self._leases.pop(step, None)
+        if cm is not None:
+            await cm.__aexit__(None, None, None)
+
+    async def _release_all_leases(self) -> None:
+        for step in list(self._leases):
+            await self._release_lease(step)
 
     async def _training_stage(self) -> None:
         while not self._stop.is_set():
@@ -312,6 +357,7 @@ class PipelineTrainer(Generic[ScenarioT, ConfigT]):
             self._persist(res.step)
             if self._eval_queue is not None and self._should_eval(res.step):
                 self._evaluating.add(res.step)
+                await self._take_lease(res.step)  # released when its eval finishes
                 await self._eval_queue.put(res.step)
             if res.step % self.retention_interval == 0:
                 await self._prune(res.step)
@@ -333,6 +379,7 @@ class PipelineTrainer(Generic[ScenarioT, ConfigT]):
                 await self._run_eval(step)
             finally:
                 self._evaluating.discard(step)
+                await self._release_lease(step)
 
     async def _run_eval(self, step: int) -> None:
         assert self.eval_fn is not None
@@ -354,6 +401,9 @@ class PipelineTrainer(Generic[ScenarioT, ConfigT]):
         if not os.path.isdir(ck):
             return
         protected = {current, *self._evaluating}
+        mgr = self._lease_manager()
+        if mgr is not None:
+            protected |= mgr.active_steps()
         infos = []
         for name in os.listdir(ck):
             if not name.isdigit() or int(name) in protected:
@@ -428,5 +478,6 @@ class PipelineTrainer(Generic[ScenarioT, ConfigT]):
             for t in tasks:
                 if not t.done():
                     t.cancel()
+            await self._release_all_leases()
             for sig in installed:
                 loop.remove_signal_handler(sig)

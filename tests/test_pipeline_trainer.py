@@ -75,3 +75,45 @@ def test_pipeline_validates_arguments(tmp_path):
         PipelineTrainer(None, None, None, [], None, min_batch_size=0)
     with pytest.raises(ValueError, match="max_batch_size"):
         PipelineTrainer(None, None, None, [], None, min_batch_size=4, max_batch_size=2)
+
+
+def test_collapse_failsafe_stops_training_gracefully(tmp_path):
+    """Every group has constant rewards: after discard_queue_multiplier x
+    min_batch_size of them the trainer stops (no exception, no step)."""
+    async def go():
+        backend = LocalBackend(path=str(tmp_path), device="cpu")
+        model = _model()
+        await model.register(backend)
+        scen = [dict(s, constant=True) for s in _scenarios(40)]
+        pt = PipelineTrainer(model, backend, make_group_rollout_fn(_single, 2), scen, config=None,
+                             num_rollout_workers=2, min_batch_size=2, max_batch_size=2, max_steps=3,
+                             discard_queue_multiplier=3, learning_rate=1e-4, log_interval_seconds=30)
+        await pt.train(handle_signals=False)
+        assert pt.state.collapsed and pt.state.done
+        assert pt.state.zero_variance_groups >= 6
+        assert await model.get_step() == 0 and not pt.train_results
+
+    asyncio.run(go())
+
+
+def test_scheduled_eval_holds_an_adapter_lease(tmp_path):
+    async def go():
+        backend = LocalBackend(path=str(tmp_path), device="cpu")
+        model = _model()
+        await model.register(backend)
+        seen = []
+
+        async def slow_eval(m, step, config):
+            seen.append((step, step in backend.adapter_leases(m).active_steps()))
+            return [Trajectory(messages_and_choices=[{"role": "user", "content": "e"}], reward=1.0)]
+
+        pt = PipelineTrainer(model, backend, make_group_rollout_fn(_single, 4), _scenarios(20), config=None,
+                             eval_fn=slow_eval, num_rollout_workers=2, min_batch_size=2, max_batch_size=2,
+                             max_steps=2, eval_every_n_steps=1, learning_rate=1e-4, log_interval_seconds=30)
+        await pt.train(handle_signals=False)
+        # evals scheduled after a training step run on a leased checkpoint (the
+        # start-of-run eval runs before training, synchronously)
+        assert seen and all(held for step, held in seen if step > 0) and any(step > 0 for step, _ in seen)
+        assert not backend.adapter_leases(model).active_steps()  # and released afterwards
+
+    asyncio.run(go())
