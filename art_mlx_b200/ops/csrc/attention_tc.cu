@@ -75,6 +75,15 @@ struct FaArgs {
   int Tq, Tk, q_off, Hq, Hkv;
   float scale_log2;
   int* err;
+  // sliding window (window > 0): key j is visible to query i only if also
+  // pos[i] - pos[j] < window (token positions, [Tk]); tile_pmax = max position
+  // over each 128-key tile (tiles wholly out of the window are skipped)
+  const int* pos;
+  const int* tile_pmax;
+  int window;
+  // attention sinks (null: none): one logit per q head (natural-log units)
+  // that joins every row's softmax denominator and attends to nothing
+  const float* sinks;
 };
 
 // Visibility of key tile kt (128 keys) for the query block starting at global
@@ -150,11 +159,20 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   int* tlist = reinterpret_cast<int*>(smem + OFF_TL);
   int* tcount = tlist + MAX_KT;
   if (warp == 0) {
+    // sliding window: smallest position among this block's queries
+    int qpmin = 0x7fffffff;
+    if (p.window > 0) {
+      for (int r = lane; r < FB; r += 32)
+        if (g0 + r <= g_last) qpmin = min(qpmin, __ldg(p.pos + g0 + r));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) qpmin = min(qpmin, __shfl_xor_sync(0xffffffffu, qpmin, o));
+    }
     int count = 0;
     for (int base = 0; base <= kt_last; base += 32) {
       const int kt = base + lane;
-      const bool vis = kt <= kt_last && tile_visible(p, kt, g0);
-      const bool full = vis && tile_full(p, kt, g0, g_last);
+      bool vis = kt <= kt_last && tile_visible(p, kt, g0);
+      if (vis && p.window > 0) vis = qpmin - __ldg(p.tile_pmax + kt) < p.window;
+      const bool full = vis && p.window <= 0 && tile_full(p, kt, g0, g_last);
       const unsigned m = __ballot_sync(0xffffffffu, vis);
       const int pos = count + __popc(m & ((1u << lane) - 1u));
       if (vis && pos < MAX_KT) tlist[pos] = kt | (full ? TILE_FULL : 0);
@@ -240,6 +258,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     const int half = (warp - 2) >> 2;  // key columns (S) and output columns (O) [64*half, 64*half+64)
     const int row = quad * 32 + lane;
     const int gi = g0 + row;  // global query position of this thread's row
+    const int pos_i = (p.window > 0 && gi < p.Tk) ? __ldg(p.pos + gi) : 0;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     float* xch = reinterpret_cast<float*>(smem + OFF_X);  // [slot][half][row]; slots 0/1 max, 2 sum
     float m_ref = -INFINITY, l = 0.f;  // l: this half's share of the row sum
@@ -284,10 +303,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             ke.w = k0 + c + 3 < p.Tk ? __ldg(p.kend + k0 + c + 3) : 0;
           }
           const int kv[4] = {ke.x, ke.y, ke.z, ke.w};
+          int pj[4] = {0, 0, 0, 0};
+          if (p.window > 0) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) pj[e] = k0 + c + e < p.Tk ? __ldg(p.pos + k0 + c + e) : 0;
+          }
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int j = k0 + c + e;
-            const bool vis = (j <= gi) && (gi < kv[e]);
+            const bool vis = (j <= gi) && (gi < kv[e]) && (p.window <= 0 || pos_i - pj[e] < p.window);
             const float x = vis ? sv[c + e] * p.scale_log2 : -INFINITY;
             sv[c + e] = x;
             mx = fmaxf(mx, x);
@@ -357,6 +381,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       if (got) {
         tc_fence_after();
         l += xch[(4 + (half ^ 1)) * FB + row];
+        // a sink adds exp(sink) to the denominator (log2 units relative to m_ref)
+        if (p.sinks && m_ref > -INFINITY) l += exp2f(__ldg(p.sinks + h) * kLog2eF - m_ref);
         const float inv = l > 0.f ? 1.f / l : 0.f;
         // the warp's 32 rows x 64 columns (128 bytes a row) go out through a
         // per-warp block of the (now unused) P region, 16-byte chunks XOR-
@@ -389,12 +415,13 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             *reinterpret_cast<uint4*>(p.o + (int64_t)orow * p.ldo + (int64_t)h * FB + half * 64 + u * 8) = o;
         }
         if (qrow < p.Tq && half == 0)
-          p.lse[(int64_t)h * p.Tq + qrow] = l > 0.f ? (m_ref + log2f(l)) / kLog2eF : -INFINITY;
+          p.lse[(int64_t)h * p.Tq + qrow] =
+              l > 0.f ? (m_ref + log2f(l)) / kLog2eF : (p.sinks ? __ldg(p.sinks + h) : -INFINITY);
       }
     } else if (ok && qrow < p.Tq) {  // no visible key
       __nv_bfloat16* dst = p.o + (int64_t)qrow * p.ldo + (int64_t)h * FB + half * 64;
       for (int j = 0; j < 64; j += 8) *reinterpret_cast<uint4*>(dst + j) = make_uint4(0, 0, 0, 0);
-      if (half == 0) p.lse[(int64_t)h * p.Tq + qrow] = -INFINITY;
+      if (half == 0) p.lse[(int64_t)h * p.Tq + qrow] = p.sinks ? __ldg(p.sinks + h) : -INFINITY;
     }
   }
   tc_fence_before();
@@ -408,7 +435,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 // q [Tq, Hq, 128] (rows at global positions q_off + row), k/v [Tk, Hkv, 128];
 // heads packed, rows 16-byte aligned.  Returns {o [Tq, Hq, 128] bf16, lse [Hq, Tq] fp32}.
 std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kend,
-                                       torch::Tensor tile_kmax, torch::Tensor tile_kmin, double scale, int64_t q_off) {
+                                       torch::Tensor tile_kmax, torch::Tensor tile_kmin, double scale, int64_t q_off,
+                                       c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> tile_pmax,
+                                       int64_t window, c10::optional<torch::Tensor> sinks) {
   const int64_t Tq = q.size(0), Hq = q.size(1), D = q.size(2), Tk = k.size(0), Hkv = k.size(1);
   TORCH_CHECK(D == 128, "attention kernel supports head_dim 128");
   TORCH_CHECK(Hq % Hkv == 0, "GQA: q heads must be a multiple of kv heads");
@@ -449,6 +478,24 @@ std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::
   a.Hkv = (int)Hkv;
   a.scale_log2 = (float)(scale * kLog2eF);
   a.err = tc_error_ptr(dev);
+  a.window = window > 0 ? (int)window : 0;
+  a.pos = nullptr;
+  a.tile_pmax = nullptr;
+  if (a.window) {
+    TORCH_CHECK(pos.has_value() && tile_pmax.has_value(), "a sliding window needs positions and tile position maxima");
+    TORCH_CHECK(pos->is_cuda() && pos->scalar_type() == at::kInt && pos->is_contiguous() && pos->numel() == Tk);
+    TORCH_CHECK(tile_pmax->is_cuda() && tile_pmax->scalar_type() == at::kInt && tile_pmax->is_contiguous() &&
+                tile_pmax->numel() >= (Tk + FB - 1) / FB);
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(pos->data_ptr()) % 16) == 0, "positions must be 16-byte aligned");
+    a.pos = pos->data_ptr<int>();
+    a.tile_pmax = tile_pmax->data_ptr<int>();
+  }
+  a.sinks = nullptr;
+  if (sinks.has_value()) {
+    TORCH_CHECK(sinks->is_cuda() && sinks->scalar_type() == at::kFloat && sinks->is_contiguous() &&
+                sinks->numel() == Hq, "sinks: fp32 [Hq]");
+    a.sinks = sinks->data_ptr<float>();
+  }
   static bool attr = false;
   if (!attr) {
     ART_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM));
@@ -513,6 +560,8 @@ struct FbArgs {
   int Tq, Tk, q_off, Hq, Hkv;
   float scale, scale_log2;
   int* err;
+  const int* pos;  // [Tk] token positions (sliding window only)
+  int window;      // > 0: also pos[query] - pos[key] < window
 };
 
 __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
@@ -671,6 +720,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const int j = kb * FB + row;  // this thread's key
     const int kend_j = j < p.Tk ? __ldg(p.kend + j) : 0;
+    const int pos_j = (p.window > 0 && j < p.Tk) ? __ldg(p.pos + j) : 0;
     const int sw = row & 7;
     bool ok = true;
     for (int i = 0; i < iters && ok; ++i) {
@@ -680,11 +730,13 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       const float* lse_h = p.lse + (int64_t)h * p.Tq;
       const float* del_h = p.delta + (int64_t)h * p.Tq;
       float lse_pf[2], del_pf[2];
+      int pos_pf[2] = {0, 0};
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int ql_mine = t * FB + (2 * half + cc) * 32 + lane;
         lse_pf[cc] = ql_mine < p.Tq ? __ldg(lse_h + ql_mine) * kLog2eF : INFINITY;
         del_pf[cc] = ql_mine < p.Tq ? __ldg(del_h + ql_mine) : 0.f;
+        if (p.window > 0) pos_pf[cc] = ql_mine < p.Tq ? __ldg(p.pos + p.q_off + ql_mine) : 0;
       }
       if (!mbar_wait_warp(sdp_full, i & 1, abort_flag, p.err, 26)) { ok = false; break; }
       tc_fence_after();
@@ -697,6 +749,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         tmem_ld32(tmem + lane_base + 128 + c * 32, rd);
         const float lse_mine = lse_pf[cc];
         const float del_mine = del_pf[cc];
+        const int pos_mine = pos_pf[cc];
         tmem_wait_ld();
         uint32_t dd[16];
 #pragma unroll
@@ -708,7 +761,8 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
             const int qg = p.q_off + ql;
             const float l2 = __shfl_sync(0xffffffffu, lse_mine, e + u);
             const float de = __shfl_sync(0xffffffffu, del_mine, e + u);
-            const bool vis = (j <= qg) && (qg < kend_j) && (ql < p.Tq);
+            const int pq = __shfl_sync(0xffffffffu, pos_mine, e + u);
+            const bool vis = (j <= qg) && (qg < kend_j) && (ql < p.Tq) && (p.window <= 0 || pq - pos_j < p.window);
             const float pr = vis ? exp2f(__uint_as_float(rs[e + u]) * p.scale_log2 - l2) : 0.f;
             pv[u] = pr;
             dv2[u] = pr * (__uint_as_float(rd[e + u]) - de);
@@ -809,7 +863,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
 // 128-query tile).  Returns {dq [Tq,Hq,128], dk [Tk,Hkv,128], dv} fp32.
 std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                        torch::Tensor out, torch::Tensor lse, torch::Tensor kend, torch::Tensor units,
-                                       double scale, int64_t q_off) {
+                                       double scale, int64_t q_off, c10::optional<torch::Tensor> pos, int64_t window) {
   const int64_t Tq = q.size(0), Hq = q.size(1), D = q.size(2), Tk = k.size(0), Hkv = k.size(1);
   TORCH_CHECK(D == 128 && Hq % Hkv == 0 && q_off >= 0 && q_off + Tq <= Tk);
   for (auto* t : {&q, &k, &v, &out}) {
@@ -827,8 +881,8 @@ std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torc
   auto dk = torch::zeros({Tk, Hkv, D}, f32);
   auto dv = torch::zeros({Tk, Hkv, D}, f32);
   const int64_t n = units.size(0);
-  if (Tq == 0 || n == 0) return {dq, dk, dv};
-  auto delta = torch::empty({Hq, Tq}, f32);
+  auto delta = torch::zeros({Hq, Tq}, f32);
+  if (Tq == 0 || n == 0) return {dq, dk, dv, delta};
   auto stream = at::cuda::getCurrentCUDAStream();
   attn_bwd_delta_kernel<<<(unsigned)((Tq * Hq + 3) / 4), 128, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
@@ -858,6 +912,13 @@ std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torc
   a.scale = (float)scale;
   a.scale_log2 = (float)(scale * kLog2eF);
   a.err = tc_error_ptr(dev);
+  a.window = window > 0 ? (int)window : 0;
+  a.pos = nullptr;
+  if (a.window) {
+    TORCH_CHECK(pos.has_value() && pos->is_cuda() && pos->scalar_type() == at::kInt && pos->is_contiguous() &&
+                pos->numel() == Tk, "a sliding window needs int32 positions [Tk]");
+    a.pos = pos->data_ptr<int>();
+  }
   static bool attr = false;
   if (!attr) {
     ART_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM));
@@ -865,7 +926,7 @@ std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torc
   }
   attn_bwd_tc_kernel<<<dim3((unsigned)n, (unsigned)Hkv), FB_THREADS, FB_SMEM, stream>>>(mq, mk, mv, mdo, a);
   ART_CUDA_CHECK(cudaGetLastError());
-  return {dq, dk, dv};
+  return {dq, dk, dv, delta};
 }
 
 }  // namespace art

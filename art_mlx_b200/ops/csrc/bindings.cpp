@@ -46,10 +46,12 @@ void adamw_step(torch::Tensor p, torch::Tensor p16, torch::Tensor g, torch::Tens
 std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                     torch::Tensor kend, torch::Tensor tile_kmax, double scale, int64_t q_off);
 std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kend,
-                                       torch::Tensor tile_kmax, torch::Tensor tile_kmin, double scale, int64_t q_off);
+                                       torch::Tensor tile_kmax, torch::Tensor tile_kmin, double scale, int64_t q_off,
+                                       c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> tile_pmax,
+                                       int64_t window, c10::optional<torch::Tensor> sinks);
 std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                        torch::Tensor out, torch::Tensor lse, torch::Tensor kend, torch::Tensor units,
-                                       double scale, int64_t q_off);
+                                       double scale, int64_t q_off, c10::optional<torch::Tensor> pos, int64_t window);
 torch::Tensor gemm_tc_grouped(torch::Tensor x, torch::Tensor w, std::vector<int64_t> offs, int64_t N,
                               c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, bool w_transposed);
 void peer_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes);
@@ -102,6 +104,10 @@ torch::Tensor gemm_pair(torch::Tensor a, torch::Tensor b, c10::optional<torch::T
                         c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> bias,
                         c10::optional<torch::Tensor> out, bool accumulate, c10::optional<torch::Tensor> diag,
                         bool b_transposed);
+std::vector<torch::Tensor> lm_head_fwd(torch::Tensor h, torch::Tensor w, torch::Tensor targets, bool entropy,
+                                       c10::optional<torch::Tensor> logits_out);
+void lm_head_grad_logits(torch::Tensor h, torch::Tensor w, torch::Tensor targets, torch::Tensor lse, torch::Tensor g,
+                         torch::Tensor out);
 std::vector<torch::Tensor> gdn_conv_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor prev,
                                         torch::Tensor succ_ptr, torch::Tensor succ_idx, torch::Tensor succ_tap);
 }  // namespace art
@@ -125,9 +131,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &art::attn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("kend"), py::arg("tile_kmax"),
         py::arg("scale"), py::arg("q_off") = 0);
   m.def("attn_fwd_tc", &art::attn_fwd_tc, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("kend"),
-        py::arg("tile_kmax"), py::arg("tile_kmin"), py::arg("scale"), py::arg("q_off") = 0);
+        py::arg("tile_kmax"), py::arg("tile_kmin"), py::arg("scale"), py::arg("q_off") = 0,
+        py::arg("pos") = py::none(), py::arg("tile_pmax") = py::none(), py::arg("window") = 0,
+        py::arg("sinks") = py::none());
   m.def("attn_bwd_tc", &art::attn_bwd_tc, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
-        py::arg("out"), py::arg("lse"), py::arg("kend"), py::arg("units"), py::arg("scale"), py::arg("q_off") = 0);
+        py::arg("out"), py::arg("lse"), py::arg("kend"), py::arg("units"), py::arg("scale"), py::arg("q_off") = 0,
+        py::arg("pos") = py::none(), py::arg("window") = 0);
   m.def("gemm_tc_grouped", &art::gemm_tc_grouped, py::arg("x"), py::arg("w"), py::arg("offs"), py::arg("N"),
         py::arg("a2") = py::none(), py::arg("b2") = py::none(), py::arg("w_transposed") = false);
   m.def("peer_copy", &art::peer_copy);
@@ -161,6 +170,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pair", &art::gemm_pair, py::arg("a"), py::arg("b"), py::arg("a2") = py::none(),
         py::arg("b2") = py::none(), py::arg("bias") = py::none(), py::arg("out") = py::none(),
         py::arg("accumulate") = false, py::arg("diag") = py::none(), py::arg("b_transposed") = false);
+  m.def("lm_head_fwd", &art::lm_head_fwd, py::arg("h"), py::arg("w"), py::arg("targets"), py::arg("entropy"),
+        py::arg("logits_out") = py::none());
+  m.def("lm_head_grad_logits", &art::lm_head_grad_logits);
   m.def("gdn_conv_bwd", &art::gdn_conv_bwd);
   m.def("ep_gemm", &art::ep_gemm);
   m.def("ep_wait_combine", &art::ep_wait_combine);

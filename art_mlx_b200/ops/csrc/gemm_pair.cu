@@ -56,7 +56,25 @@ struct PairArgs {
   // accumulator, [2] ns from its first wait to its last commit, [3] k-blocks
   // whose operands were not ready at the first probe, [4] k-blocks issued
   unsigned long long* diag;
+  // LM-head epilogues (C = hidden states x vocabulary rows):
+  const int64_t* targets;  // [M] target vocabulary id of each row (<0: none)
+  float4* stats;           // EPI_STATS: [M, num_n] (max, sum exp(x-max), sum exp(x-max) x, 0)
+  float* tgt;              // EPI_STATS: [M] logit of the target (written by the tile holding it)
+  const float* lse;        // EPI_GRAD: [M] log-sum-exp of the row
+  const float* g;          // EPI_GRAD: [M] d loss / d logprob of the row
 };
+
+// Epilogue variants of the pair GEMM.
+//  EPI_STORE  C = acc (+ bias) (+ C), bf16
+//  EPI_STATS  per row and 256-column tile, the online softmax partials of
+//             the fp32 logits and the target logit; with C null nothing else
+//             is stored (LM-head forward: the [M, N] logits never reach
+//             memory), else the bf16 logits are stored as well (kept for a
+//             backward that does not recompute them)
+//  EPI_GRAD   C = g * (onehot(target) - exp(acc - lse)), bf16 (LM-head
+//             backward: the logits tile is recomputed in TMEM and only its
+//             gradient is written, for the input-gradient GEMM that follows)
+enum { EPI_STORE = 0, EPI_STATS = 1, EPI_GRAD = 2 };
 
 __device__ __forceinline__ int2 pair_tile(int t, int num_m, int num_n, int group_m) {
   const int group = group_m * num_n;
@@ -67,6 +85,7 @@ __device__ __forceinline__ int2 pair_tile(int t, int num_m, int num_n, int group
   return make_int2((first_m + r % gm) * PBM, (r / gm) * PBN);
 }
 
+template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
@@ -230,6 +249,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       tc_fence_after();
       const int2 c = pair_tile(t, num_m, num_n, p.group_m);
       const int row = c.x + (int)rank * 128 + q * 32 + lane;
+      // LM-head epilogues: per-row inputs and the running softmax partials
+      int64_t tgt_id = -1;
+      float row_lse = 0.f, row_g = 0.f;
+      float st_m = -INFINITY, st_s = 0.f, st_sx = 0.f;
+      if constexpr (EPI != EPI_STORE) {
+        if (row < p.M) {
+          tgt_id = p.targets[row];
+          if constexpr (EPI == EPI_GRAD) {
+            row_lse = p.lse[row];
+            row_g = p.g[row];
+          }
+        }
+      }
 #pragma unroll 1
       for (int cc = 0; cc < PBN / 32; cc += 2) {
         uint32_t r2[2][32];
@@ -240,11 +272,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         for (int h = 0; h < 2; ++h) {
           const int col0 = c.y + (cc + h) * 32;
           if (row < p.M && col0 < p.N) {
-            __nv_bfloat16* dst = p.C + (int64_t)row * p.ldc + col0;
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r2[h][j]);
-            if (p.bias) {
+            if constexpr (EPI == EPI_STATS) {
+              // online softmax over this 32-column chunk (fp32 logits)
+              float cm = v[0];
+#pragma unroll
+              for (int j = 1; j < 32; ++j) cm = fmaxf(cm, v[j]);
+              const float mn = fmaxf(st_m, cm);
+              const float sc = (st_m == -INFINITY) ? 0.f : __expf(st_m - mn);
+              float s = st_s * sc, sx = st_sx * sc;
+              const int64_t rel = tgt_id - col0;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float e = __expf(v[j] - mn);
+                s += e;
+                sx = fmaf(e, v[j], sx);
+                if (rel == j) p.tgt[row] = v[j];
+              }
+              st_m = mn;
+              st_s = s;
+              st_sx = sx;
+              if (p.C == nullptr) continue;  // statistics only; else the logits are stored too
+            } else if constexpr (EPI == EPI_GRAD) {
+              const int64_t rel = tgt_id - col0;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                v[j] = row_g * ((rel == j ? 1.f : 0.f) - __expf(v[j] - row_lse));
+            }
+            __nv_bfloat16* dst = p.C + (int64_t)row * p.ldc + col0;
+            if (EPI == EPI_STORE && p.bias) {
 #pragma unroll
               for (int j = 0; j < 32; j += 8) {
                 uint4 bv = *reinterpret_cast<const uint4*>(p.bias + col0 + j);
@@ -253,7 +311,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                 for (int e = 0; e < 8; ++e) v[j + e] += bf2f(be[e]);
               }
             }
-            if (p.accumulate_c) {
+            if (EPI == EPI_STORE && p.accumulate_c) {
 #pragma unroll
               for (int j = 0; j < 32; j += 8) {
                 uint4 cv = *reinterpret_cast<const uint4*>(dst + j);
@@ -274,6 +332,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           }
         }
       }
+      if constexpr (EPI == EPI_STATS) {
+        if (row < p.M) p.stats[(int64_t)row * num_n + c.y / PBN] = make_float4(st_m, st_s, st_sx, 0.f);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acce_leader + buf * 8);
@@ -285,6 +346,78 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem, 512);
   }
+}
+
+// Merge of the per-tile softmax partials of the LM-head forward: one warp
+// per row; lse = M + log S, entropy = lse - SX / S, logprob = x_target - lse.
+__device__ __forceinline__ void part_merge(float& m, float& s, float& sx, float m2, float s2, float sx2) {
+  if (m2 == -INFINITY) return;
+  if (m == -INFINITY) {
+    m = m2;
+    s = s2;
+    sx = sx2;
+    return;
+  }
+  const float mn = fmaxf(m, m2);
+  const float a = __expf(m - mn), b = __expf(m2 - mn);
+  s = s * a + s2 * b;
+  sx = sx * a + sx2 * b;
+  m = mn;
+}
+
+__global__ void lm_head_merge_kernel(const float4* __restrict__ stats, int num_n, int M,
+                                     const int64_t* __restrict__ targets, int V, const float* __restrict__ tgt,
+                                     float* __restrict__ lp, float* __restrict__ ent, float* __restrict__ lse) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  float m = -INFINITY, s = 0.f, sx = 0.f;
+  for (int i = lane; i < num_n; i += 32) {
+    const float4 v = stats[(int64_t)row * num_n + i];
+    part_merge(m, s, sx, v.x, v.y, v.z);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float sx2 = __shfl_xor_sync(0xffffffffu, sx, o);
+    part_merge(m, s, sx, m2, s2, sx2);
+  }
+  if (lane == 0) {
+    const float l = m + logf(s);
+    lse[row] = l;
+    if (ent) ent[row] = l - sx / s;
+    const int64_t t = targets[row];
+    lp[row] = ((t >= 0 && t < V) ? tgt[row] : 0.f) - l;
+  }
+}
+
+template <int EPI>
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2, const CUtensorMap& tb2,
+                 PairArgs& p, int64_t K, int dev) {
+  {
+    const int64_t num_m = (p.M + PBM - 1) / PBM;
+    const int64_t band = (int64_t)PBM * K * 2;  // bytes of one 256-row band of A
+    int64_t g = ((int64_t)48 << 20) / (band > 0 ? band : 1);
+    p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(g, num_m));
+  }
+  p.err = tc_error_ptr(dev);
+  static int max_pairs[64] = {0};
+  if (!max_pairs[dev]) {
+    ART_CUDA_CHECK(cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(P_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = P_SMEM;  // cluster shape comes from __cluster_dims__
+    int n = 0;
+    ART_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<EPI>, &cfg));
+    TORCH_CHECK(n > 0, "no CTA pair of the GEMM fits on this device");
+    max_pairs[dev] = n;
+  }
+  const int tiles = ((p.M + PBM - 1) / PBM) * ((p.N + PBN - 1) / PBN);
+  const int pairs = tiles < max_pairs[dev] ? tiles : max_pairs[dev];
+  gemm_pair_kernel<EPI><<<2 * pairs, P_THREADS, P_SMEM, at::cuda::getCurrentCUDAStream()>>>(ta, tb, ta2, tb2, p);
+  ART_CUDA_CHECK(cudaPeekAtLastError());
 }
 
 }  // namespace
@@ -332,31 +465,100 @@ torch::Tensor gemm_pair(torch::Tensor a, torch::Tensor b, c10::optional<torch::T
     TORCH_CHECK(diag->is_cuda() && diag->scalar_type() == torch::kInt64 && diag->numel() >= 5, "diag: int64[5]");
     p.diag = reinterpret_cast<unsigned long long*>(diag->data_ptr<int64_t>());
   }
-  {
-    const int64_t num_m = (M + PBM - 1) / PBM;
-    const int64_t band = (int64_t)PBM * K * 2;  // bytes of one 256-row band of A
-    int64_t g = ((int64_t)48 << 20) / (band > 0 ? band : 1);
-    p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(g, num_m));
-  }
-  const int dev = a.get_device();
-  p.err = tc_error_ptr(dev);
-  static int max_pairs[64] = {0};
-  if (!max_pairs[dev]) {
-    ART_CUDA_CHECK(cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(P_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = P_SMEM;  // cluster shape comes from __cluster_dims__
-    int n = 0;
-    ART_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel, &cfg));
-    TORCH_CHECK(n > 0, "no CTA pair of the GEMM fits on this device");
-    max_pairs[dev] = n;
-  }
-  const int tiles = (int)(((M + PBM - 1) / PBM) * ((N + PBN - 1) / PBN));
-  const int pairs = tiles < max_pairs[dev] ? tiles : max_pairs[dev];
-  gemm_pair_kernel<<<2 * pairs, P_THREADS, P_SMEM, at::cuda::getCurrentCUDAStream()>>>(ta, tb, ta2, tb2, p);
-  ART_CUDA_CHECK(cudaGetLastError());
+  p.targets = nullptr;
+  p.stats = nullptr;
+  p.tgt = nullptr;
+  p.lse = nullptr;
+  p.g = nullptr;
+  launch_pair<EPI_STORE>(ta, tb, ta2, tb2, p, K, a.get_device());
   return c;
+}
+
+static void lm_head_check(const torch::Tensor& h, const torch::Tensor& w, const torch::Tensor& targets) {
+  TORCH_CHECK(h.is_cuda() && w.is_cuda() && targets.is_cuda(), "LM head: CUDA tensors");
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "LM head: bf16 operands");
+  TORCH_CHECK(h.dim() == 2 && w.dim() == 2 && h.size(1) == w.size(1), "LM head: h [M, H], w [V, H]");
+  TORCH_CHECK(h.size(0) >= 128 && w.size(0) >= 128, "LM head: at least 128 rows and 128 vocabulary entries");
+  TORCH_CHECK(w.size(0) % 32 == 0, "LM head: vocabulary size must be a multiple of 32");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.is_contiguous() && targets.numel() == h.size(0));
+}
+
+static PairArgs lm_head_args(const torch::Tensor& h, const torch::Tensor& w) {
+  PairArgs p;
+  p.M = (int)h.size(0);
+  p.N = (int)w.size(0);
+  p.K2 = 0;
+  p.nk1 = (int)((h.size(1) + PBK - 1) / PBK);
+  p.nk2 = 0;
+  p.C = nullptr;
+  p.ldc = 0;
+  p.bias = nullptr;
+  p.accumulate_c = 0;
+  p.b_mn = 0;
+  p.diag = nullptr;
+  p.targets = nullptr;
+  p.stats = nullptr;
+  p.tgt = nullptr;
+  p.lse = nullptr;
+  p.g = nullptr;
+  return p;
+}
+
+// LM-head forward: per row, log softmax(h w^T)[target] (fp32 logits in TMEM),
+// the entropy (if asked) and the log-sum-exp kept for the backward.  With
+// logits_out ([M, V] bf16) the epilogue also stores the logits.
+// Returns {logprob, entropy or undefined, lse}.
+std::vector<torch::Tensor> lm_head_fwd(torch::Tensor h, torch::Tensor w, torch::Tensor targets, bool entropy,
+                                       c10::optional<torch::Tensor> logits_out) {
+  lm_head_check(h, w, targets);
+  const int64_t M = h.size(0), V = w.size(0);
+  const int64_t num_n = (V + PBN - 1) / PBN;
+  auto f32 = h.options().dtype(at::kFloat);
+  auto stats = torch::empty({M, num_n, 4}, f32);
+  auto tgt = torch::zeros({M}, f32);
+  auto lp = torch::empty({M}, f32), lse = torch::empty({M}, f32);
+  auto ent = entropy ? torch::empty({M}, f32) : torch::Tensor();
+  const CUtensorMap ta = make_tmap_bf16(h, 128), tb = make_tmap_bf16(w, 128);
+  PairArgs p = lm_head_args(h, w);
+  p.targets = targets.data_ptr<int64_t>();
+  p.stats = reinterpret_cast<float4*>(stats.data_ptr<float>());
+  p.tgt = tgt.data_ptr<float>();
+  if (logits_out.has_value()) {
+    const auto& out = *logits_out;
+    TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(0) == M && out.size(1) == V && out.stride(1) == 1 &&
+                out.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16) == 0,
+                "logits_out: bf16 [M, V], 16-byte aligned rows");
+    p.C = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+    p.ldc = out.stride(0);
+  }
+  launch_pair<EPI_STATS>(ta, tb, ta, tb, p, h.size(1), h.get_device());
+  lm_head_merge_kernel<<<(unsigned)((M + 7) / 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const float4*>(stats.data_ptr<float>()), (int)num_n, (int)M, targets.data_ptr<int64_t>(),
+      (int)V, tgt.data_ptr<float>(), lp.data_ptr<float>(), entropy ? ent.data_ptr<float>() : nullptr,
+      lse.data_ptr<float>());
+  ART_CUDA_CHECK(cudaPeekAtLastError());
+  return {lp, ent, lse};
+}
+
+// LM-head backward, first half: the logits of h w^T recomputed tile by tile
+// in TMEM and turned into dlogits = g * (onehot(target) - softmax) in the
+// epilogue; written into out [M, V] bf16 (the input gradient dh = dlogits w
+// follows as a pair GEMM on w in its stored layout).
+void lm_head_grad_logits(torch::Tensor h, torch::Tensor w, torch::Tensor targets, torch::Tensor lse, torch::Tensor g,
+                         torch::Tensor out) {
+  lm_head_check(h, w, targets);
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && g.scalar_type() == at::kFloat && lse.is_contiguous() &&
+              g.is_contiguous() && lse.numel() == h.size(0) && g.numel() == h.size(0));
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(0) == h.size(0) && out.size(1) == w.size(0) &&
+              out.stride(1) == 1 && out.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16) == 0);
+  const CUtensorMap ta = make_tmap_bf16(h, 128), tb = make_tmap_bf16(w, 128);
+  PairArgs p = lm_head_args(h, w);
+  p.C = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldc = out.stride(0);
+  p.targets = targets.data_ptr<int64_t>();
+  p.lse = lse.data_ptr<float>();
+  p.g = g.data_ptr<float>();
+  launch_pair<EPI_GRAD>(ta, tb, ta, tb, p, h.size(1), h.get_device());
 }
 
 }  // namespace art

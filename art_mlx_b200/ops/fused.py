@@ -22,9 +22,10 @@ from __future__ import annotations
 
 import math
 import os
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Any, Sequence
 
+import numpy as np
 import torch
 
 from . import lowrank, native
@@ -125,9 +126,36 @@ class AttnMeta:
     T: int
     bwd_units: torch.Tensor | None = None  # int32 [n, 3]
     tile_kmin: torch.Tensor | None = None  # int32 [ceil(T/64)]
+    # sliding window (0: none): the variant of this row for windowed layers
+    window: int = 0
+    tile_pmax: torch.Tensor | None = None  # int32 [ceil(T/128)]: max position per 128-key tile
+    _windowed: dict = field(default_factory=dict, repr=False)
+    _host: tuple | None = field(default=None, repr=False)  # (positions, kend) on the CPU
+
+    def windowed(self, window: int | None) -> "AttnMeta":
+        """The metadata of this row for a layer with a sliding window of
+        ``window`` tokens (``None``/0: this one).  Key ``j`` then reaches the
+        queries ``i`` with ``j <= i < kend_w[j]`` and ``pos[i] - pos[j] <
+        window``; ``kend_w`` (:func:`window_visibility_ends`) tightens the
+        interval so tile skipping and the backward work list see only the
+        window.  Built once per row and window, shared by the layers."""
+        if not window:
+            return self
+        w = self._windowed.get(window)
+        if w is None:
+            if self._host is None:
+                raise ValueError("this AttnMeta was built without host positions; rebuild it with AttnMeta.build")
+            pos, kend = self._host
+            if pos is None:  # built from device positions: fetch them once
+                pos = self.positions.to("cpu", torch.int32)
+                self._host = (pos, kend)
+            kw = window_visibility_ends(pos, kend, window)
+            w = AttnMeta.build(pos, kw, self.kend.device, window=window)
+            self._windowed[window] = w
+        return w
 
     @staticmethod
-    def build(positions: torch.Tensor, kend: torch.Tensor, device: torch.device) -> "AttnMeta":
+    def build(positions: torch.Tensor, kend: torch.Tensor, device: torch.device, window: int = 0) -> "AttnMeta":
         """``kend`` may live on any device; the work list is planned on the CPU."""
         T = int(kend.numel())
         pad = (-T) % 64
@@ -139,14 +167,58 @@ class AttnMeta:
         units = attention_bwd_units_tc(k_cpu)
         pin = device.type == "cuda"
         mv = lambda t: (t.pin_memory() if pin else t).to(device, non_blocking=True)  # noqa: E731
+        if positions.device.type == "cpu":  # host positions: no device round trip for windowed variants
+            p_cpu = positions.detach().to(torch.int32).contiguous()
+            pos_dev = mv(p_cpu)
+        else:
+            p_cpu = None
+            pos_dev = positions.to(device=device, dtype=torch.int32, non_blocking=True)
+        tile_pmax = None
+        if window:
+            if p_cpu is None:
+                p_cpu = positions.detach().to("cpu", torch.int32)
+            pp = torch.nn.functional.pad(p_cpu, (0, (-T) % 128), value=torch.iinfo(torch.int32).min)
+            tile_pmax = mv(pp.view(-1, 128).amax(dim=1).to(torch.int32))
         return AttnMeta(
-            positions=positions.to(device=device, dtype=torch.int32, non_blocking=True),
+            positions=pos_dev,
             kend=mv(k_cpu),
             tile_kmax=mv(tile),
             T=T,
             bwd_units=mv(units),
             tile_kmin=mv(tile_min),
+            window=int(window or 0),
+            tile_pmax=tile_pmax,
+            _host=(p_cpu, k_cpu),
         )
+
+
+def window_visibility_ends(positions: torch.Tensor, kend: torch.Tensor, window: int) -> torch.Tensor:
+    """Visibility ends under a sliding window of ``window`` positions.
+
+    The packed row is cut into runs where ``kend`` is constant and positions
+    rise by one (a prefix-tree segment, merged with an only child).  Queries
+    of key ``j``'s own run are ``j..run_end`` at positions ``pos[j] + (i -
+    j)``; every later query of its subtree sits at a position of at least
+    ``pos[run_end - 1] + 1``.  So if the run's end is ``window`` or more
+    positions past ``j``, no later query is in the window and the interval
+    shrinks to ``[j, min(run_end, j + window))``; otherwise it stays
+    ``[j, kend[j])``.  The result bounds the visible queries from above; the
+    kernels still check ``pos[i] - pos[j] < window`` per pair (the
+    reference's sliding-window block masks, ``src/art/megatron/
+    prefix_tree_state.py:67,94-102``)."""
+    k = kend.detach().to("cpu", torch.int64).numpy()
+    p = positions.detach().to("cpu", torch.int64).numpy()
+    T = k.shape[0]
+    if T == 0:
+        return kend.to("cpu", torch.int32)
+    brk = np.ones(T, dtype=bool)
+    brk[1:] = (k[1:] != k[:-1]) | (p[1:] != p[:-1] + 1)
+    starts = np.flatnonzero(brk)
+    ends = np.append(starts[1:], T)
+    e = ends[np.cumsum(brk) - 1]
+    j = np.arange(T)
+    kw = np.where((k > e) & (e - j < window), k, np.minimum(e, j + window))
+    return torch.from_numpy(kw.astype(np.int32))
 
 
 def rope_inv_freq(head_dim: int, theta: float, device: torch.device, scaling: dict | None = None) -> torch.Tensor:
@@ -227,9 +299,13 @@ def _rope_ref(x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor) -> tor
 
 
 def attention_ref(
-    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kend: torch.Tensor, scale: float
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kend: torch.Tensor, scale: float,
+    positions: torch.Tensor | None = None, window: int = 0, sinks: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
-    """Dense-mask prefix-tree attention in fp32 math (oracle). q [T,Hq,D]."""
+    """Dense-mask prefix-tree attention in fp32 math (oracle). q [T,Hq,D].
+
+    ``window`` > 0 also requires ``pos[i] - pos[j] < window``; ``sinks``
+    ([Hq], natural log) adds ``exp(sink)`` to every row's denominator."""
     T, Hq, D = q.shape
     G = Hq // k.shape[1]
     kx = _acc(k).repeat_interleave(G, dim=1)
@@ -238,23 +314,33 @@ def attention_ref(
     i = torch.arange(T, device=q.device).view(T, 1)
     j = torch.arange(T, device=q.device).view(1, T)
     mask = (j <= i) & (i < kend.to(q.device).long().view(1, T))
+    if window:
+        pos = positions.to(q.device).long()
+        mask &= (pos.view(T, 1) - pos.view(1, T)) < window
     s = s.masked_fill(~mask.unsqueeze(0), float("-inf"))
-    lse = torch.logsumexp(s, dim=-1)  # [Hq, T]
-    p = torch.softmax(s, dim=-1)
+    if sinks is not None:
+        sk = _acc(sinks).view(Hq, 1, 1).expand(Hq, T, 1)
+        lse = torch.logsumexp(torch.cat([s, sk], -1), dim=-1)  # [Hq, T]
+        p = torch.exp(s - lse.unsqueeze(-1))
+    else:
+        lse = torch.logsumexp(s, dim=-1)  # [Hq, T]
+        p = torch.softmax(s, dim=-1).nan_to_num(0.0)
     o = torch.einsum("hij,jhd->ihd", p, vx)
     return o.to(q.dtype), lse
 
 
 class _RopeAttention(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale):
+    def forward(ctx, qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale, sinks):
         C = native.lib()
         T = qkv.shape[0]
         qk, rstd = C.rope_fwd(qkv, meta.positions, inv_freq, nq, nkv, D, qn_w, kn_w, eps)
         q = qk[:, : nq * D].view(T, nq, D)
         k = qk[:, nq * D :].view(T, nkv, D)
         v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
-        o, lse = C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, scale)
+        win = meta.window
+        o, lse = C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, scale, 0,
+                               meta.positions if win else None, meta.tile_pmax if win else None, win, sinks)
         ctx.save_for_backward(qkv, qk, o, lse, inv_freq, qn_w if qn_w is not None else qkv.new_empty(0),
                               kn_w if kn_w is not None else qkv.new_empty(0),
                               rstd if rstd is not None and rstd.numel() else qkv.new_empty(0, dtype=torch.float32))
@@ -275,14 +361,16 @@ class _RopeAttention(torch.autograd.Function):
         v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
         dqkv = torch.empty_like(qkv)
         dqk = torch.empty_like(qk)
-        dq_acc, dk_acc, dv_acc = C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, meta.bwd_units, scale)
+        win = meta.window
+        dq_acc, dk_acc, dv_acc, _ = C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, meta.bwd_units, scale, 0,
+                                                 meta.positions if win else None, win)
         dqk[:, : nq * D].copy_(dq_acc.view(T, nq * D))
         dqk[:, nq * D :].copy_(dk_acc.view(T, nkv * D))
         dqkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].copy_(dv_acc.view(T, nkv * D))
         C.rope_bwd(dqk, qkv, meta.positions, inv_freq, nq, nkv, D,
                    qn_w if has_norm else None, kn_w if has_norm else None,
                    rstd if has_norm else None, dqkv)
-        return dqkv, None, None, None, None, None, None, None, None, None
+        return dqkv, None, None, None, None, None, None, None, None, None, None
 
 
 def rope_attention(
@@ -295,11 +383,18 @@ def rope_attention(
     qn_w: torch.Tensor | None,
     kn_w: torch.Tensor | None,
     eps: float,
+    sinks: torch.Tensor | None = None,
+    scale: float | None = None,
 ) -> torch.Tensor:
-    """Raw QKV projection ``[T, (nq+2nkv)*D]`` -> attention output ``[T, nq*D]``."""
-    scale = 1.0 / math.sqrt(D)
+    """Raw QKV projection ``[T, (nq+2nkv)*D]`` -> attention output ``[T, nq*D]``.
+
+    ``meta`` carries the row's mask (``meta.windowed(w)`` for a sliding-window
+    layer); ``sinks`` are frozen per-head sink logits (fp32 [nq])."""
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
     if _cuda(qkv):
-        return _RopeAttention.apply(qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale)
+        if sinks is not None:
+            sinks = sinks.float().contiguous()
+        return _RopeAttention.apply(qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale, sinks)
     T = qkv.shape[0]
     q = qkv[:, : nq * D].view(T, nq, D)
     k = qkv[:, nq * D : (nq + nkv) * D].view(T, nkv, D)
@@ -310,7 +405,7 @@ def rope_attention(
     pos = meta.positions
     q = _rope_ref(q, pos, inv_freq)
     k = _rope_ref(k, pos, inv_freq)
-    o, _ = attention_ref(q, k, v, meta.kend, scale)
+    o, _ = attention_ref(q, k, v, meta.kend, scale, pos, meta.window, sinks)
     return o.reshape(T, nq * D)
 
 
@@ -549,39 +644,120 @@ def lora_linear(
 
 
 class _LMHeadLogprobs(torch.autograd.Function):
+    """``log softmax(h W^T)[target]`` without the logits in memory.
+
+    Forward: the CTA-pair tcgen05 GEMM keeps each 256x256 logits tile in TMEM
+    (fp32) and its epilogue folds it into per-row online-softmax partials and
+    the target logit (``lm_head_fwd``); a merge kernel gives lse, logprob and
+    entropy.  Two backward modes, chosen by size (``LMHEAD_KEEP_BYTES``):
+    * kept logits: the forward epilogue also stores the bf16 logits; the
+      backward turns them into ``dlogits`` in place (one elementwise pass)
+      and runs ``dh = dlogits W`` -- no second logits GEMM;
+    * recompute: nothing of size [T, V] survives the forward; per row chunk
+      the same GEMM recomputes the tiles and writes ``dlogits = g (onehot -
+      softmax)`` (bf16) from its epilogue, then ``dh = dlogits W``.
+    ``dh = dlogits W`` runs on the pair GEMM with ``W`` in its stored layout.
+    (``dh`` cannot stay in TMEM across the vocabulary: one 128-row block of it
+    is 128 x hidden fp32, several times the 512 TMEM columns.)
+    Reference: the chunked logprob / entropy of
+    ``src/art/trainer_rank/__init__.py:2162-2290``."""
+
+    @staticmethod
+    def forward(ctx, h, W, targets, chunk, want_entropy):
+        C = native.lib()
+        h = h.contiguous()
+        T, V = h.shape[0], W.shape[0]
+        # keep the bf16 logits for the backward when they fit the budget
+        # (saves the recomputing GEMM); else recompute them tile by tile
+        logits = None
+        if ctx.needs_input_grad[0] and T * V * 2 <= LMHEAD_KEEP_BYTES:
+            logits = torch.empty(T, V, device=h.device, dtype=h.dtype)
+        lp, ent, lse = C.lm_head_fwd(h, W, targets, want_entropy, logits)
+        ctx.save_for_backward(h, W, targets, lse)
+        ctx.logits = logits
+        ctx.chunk = chunk
+        if want_entropy:
+            ctx.mark_non_differentiable(ent)
+            return lp, ent
+        return lp, None
+
+    @staticmethod
+    def backward(ctx, glp, gent):
+        C = native.lib()
+        h, W, targets, lse = ctx.saved_tensors
+        T, V = h.shape[0], W.shape[0]
+        glp = glp.float().contiguous()
+        pair_dgrad = W.shape[1] % 128 == 0
+        if ctx.logits is not None:  # kept logits: gradient in place, then dh = dlogits W
+            logits, ctx.logits = ctx.logits, None
+            C.logits_grad_(logits, targets, lse, glp)
+            return (C.gemm_pair(logits, W, b_transposed=True) if pair_dgrad else logits @ W), None, None, None, None
+        dh = torch.empty_like(h)
+        chunk = max(128, min(ctx.chunk, T))
+        dl = torch.empty(chunk, V, device=h.device, dtype=h.dtype)
+        for s in range(0, T, chunk):
+            e = min(T, s + chunk)
+            if e - s < 128:  # a short tail: recompute over the last 128 rows, keep the new ones
+                s0 = e - 128
+                d = dl[:128]
+                C.lm_head_grad_logits(h[s0:e], W, targets[s0:e], lse[s0:e], glp[s0:e], d)
+                part = C.gemm_pair(d, W, b_transposed=True) if pair_dgrad else d @ W
+                dh[s:e] = part[s - s0 :]
+                continue
+            d = dl[: e - s]
+            C.lm_head_grad_logits(h[s:e], W, targets[s:e], lse[s:e], glp[s:e], d)
+            if pair_dgrad:
+                C.gemm_pair(d, W, out=dh[s:e], b_transposed=True)
+            else:
+                torch.mm(d, W, out=dh[s:e])
+        return dh, None, None, None, None
+
+
+# bf16 logits kept from the LM-head forward to its backward up to this many
+# bytes per call (8192 tokens x 152k vocabulary = 2.5 GB); larger calls
+# recompute the logits tiles in the backward instead
+LMHEAD_KEEP_BYTES = int(float(os.environ.get("ART_B200_LMHEAD_KEEP_GB", "8")) * (1 << 30))
+
+
+# the library baseline of the LM head (cuBLAS logits GEMM kept for the
+# backward, separate statistics and gradient kernels): the unfused
+# comparison point of the benchmark, not the default
+LMHEAD_LIBRARY = os.environ.get("ART_B200_LMHEAD_LIBRARY", "0") != "0"
+
+
+class _LMHeadLogprobsLibrary(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, W, targets, chunk, want_entropy):
         C = native.lib()
         T = h.shape[0]
         lp = torch.empty(T, device=h.device, dtype=torch.float32)
         ent = torch.empty(T, device=h.device, dtype=torch.float32) if want_entropy else None
-        saved_logits = []
-        lses = []
+        saved, lses = [], []
         for s in range(0, T, chunk):
             e = min(T, s + chunk)
-            logits = h[s:e] @ W.t()  # [c, V] bf16, fp32 accumulate
+            logits = h[s:e] @ W.t()
             lse, tgt, en = C.logits_stats(logits, targets[s:e], want_entropy)
             lp[s:e] = tgt - lse
             if want_entropy:
                 ent[s:e] = en
-            saved_logits.append(logits)
+            saved.append(logits)
             lses.append(lse)
-        ctx.saved_logits = saved_logits
+        ctx.saved_logits = saved
         ctx.save_for_backward(W, targets, torch.cat(lses) if lses else lp.new_empty(0))
         ctx.chunk = chunk
-        ctx.mark_non_differentiable(*( [ent] if ent is not None else [] ))
+        if want_entropy:
+            ctx.mark_non_differentiable(ent)
         return lp, ent
 
     @staticmethod
     def backward(ctx, glp, gent):
         C = native.lib()
         W, targets, lse = ctx.saved_tensors
-        chunk = ctx.chunk
         T = targets.shape[0]
         dh = torch.empty(T, W.shape[1], device=W.device, dtype=W.dtype)
         glp = glp.float().contiguous()
-        for idx, s in enumerate(range(0, T, chunk)):
-            e = min(T, s + chunk)
+        for idx, s in enumerate(range(0, T, ctx.chunk)):
+            e = min(T, s + ctx.chunk)
             logits = ctx.saved_logits[idx]
             C.logits_grad_(logits, targets[s:e], lse[s:e], glp[s:e])
             torch.mm(logits, W, out=dh[s:e])
@@ -589,12 +765,28 @@ class _LMHeadLogprobs(torch.autograd.Function):
         return dh, None, None, None, None
 
 
+def _lm_head_native_ok(h: torch.Tensor, W: torch.Tensor) -> bool:
+    return (_cuda(h) and h.dtype == torch.bfloat16 and W.dtype == torch.bfloat16 and W.is_contiguous()
+            and W.shape[0] % 32 == 0 and W.shape[0] >= 128 and h.shape[1] % 8 == 0)
+
+
 def lm_head_logprobs(
     h: torch.Tensor, W: torch.Tensor, targets: torch.Tensor, chunk: int = 4096, entropy: bool = True
 ) -> tuple[torch.Tensor, torch.Tensor | None]:
     """Per-row ``log softmax(h W^T)[target]`` (fp32) and entropy (no grad)."""
     if _cuda(h):
-        return _LMHeadLogprobs.apply(h, W, targets, chunk, entropy)
+        if LMHEAD_LIBRARY:
+            return _LMHeadLogprobsLibrary.apply(h, W, targets.contiguous(), chunk, entropy)
+        if not _lm_head_native_ok(h, W):
+            raise ValueError(f"LM head on the GPU needs bf16 operands and a vocabulary that is a multiple of 32 "
+                             f"(got {h.dtype}/{W.dtype}, V={W.shape[0]})")
+        T = h.shape[0]
+        if T < 128:  # the tile loads want 128 rows: pad with zero rows that have no target
+            hp = torch.cat([h, h.new_zeros(128 - T, h.shape[1])])
+            tp = torch.cat([targets, targets.new_full((128 - T,), -1)])
+            lp, ent = _LMHeadLogprobs.apply(hp, W, tp, chunk, entropy)
+            return lp[:T], (ent[:T] if ent is not None else None)
+        return _LMHeadLogprobs.apply(h, W, targets.contiguous(), chunk, entropy)
     logits = _acc(h @ W.t())
     lse = torch.logsumexp(logits, dim=-1)
     lp = logits.gather(-1, targets.clamp_min(0).unsqueeze(-1)).squeeze(-1) - lse

@@ -283,7 +283,7 @@ class _CPRopeAttention(torch.autograd.Function):
         T = qkv.shape[0]
         do = do.contiguous().view(T, nq, D)
         q = qk[:, : nq * D].view(T, nq, D)
-        dq, dk_full, dv_full = C.attn_bwd_tc(do, q, k_full, v_full, o, lse, plan.meta.kend, plan.meta.bwd_units,
+        dq, dk_full, dv_full, _ = C.attn_bwd_tc(do, q, k_full, v_full, o, lse, plan.meta.kend, plan.meta.bwd_units,
                                              scale, plan.a)
         dk = cp.reduce_scatter(dk_full)
         dv = cp.reduce_scatter(dv_full)

@@ -8,9 +8,11 @@ rank's heads over all tokens; the LM head is vocab-parallel.
 
 Communication-fused kernels (``ops/csrc/gemm_tc.cu``, transport ``"p2p"``):
 
-* AG -> GEMM: each rank publishes its token shard in a peer-mapped arena; the
-  tcgen05 GEMM's producer warp TMA-loads A tiles directly from the owning
-  rank's shard (plain TMA loads of peer memory; no multicast anywhere);
+* AG -> GEMM: each rank publishes its token shard in a peer-mapped arena;
+  every peer shard crosses NVLink once, pulled by the copy engine into a local
+  buffer on a side stream, while the tcgen05 GEMM runs on the shards that
+  have already arrived (own shard first).  No kernel reads peer memory
+  through TMA on this path, and nothing uses multicast;
 * GEMM -> RS: the GEMM epilogue stores each row block of the partial product
   into the owning rank's staging slot over NVLink; the owner sums its slots.
 

@@ -134,8 +134,9 @@ def stage_row(
         routes = dev(host_routes)
         route_counts = _route_counts(host_routes)
     orig = packed.get("original_logprobs")
-    meta = AttnMeta.build(dev(pos), kend, device)
-    moved[0] += sum(t.numel() * t.element_size() for t in (meta.kend, meta.tile_kmax, meta.tile_kmin, meta.bwd_units))
+    meta = AttnMeta.build(pos, kend, device)
+    moved[0] += sum(t.numel() * t.element_size()
+                    for t in (meta.positions, meta.kend, meta.tile_kmax, meta.tile_kmin, meta.bwd_units))
     return MicroBatch(
         tokens=dev(tokens),
         meta=meta,

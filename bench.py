@@ -53,6 +53,11 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--cp", type=int, default=None, help="context-parallel size")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=2)
+    p.add_argument("--unfused", action="store_true",
+                   help="the unfused baseline of this framework: cuBLAS projections and LM head, NCCL all-reduce "
+                        "of the LoRA gradients and a replicated AdamW (the comparison point of the fused kernels)")
+    p.add_argument("--kernel-table", default=None,
+                   help="write the device time per kernel of one profiled (untimed) step to this file, per rank")
     a = p.parse_args()
     c = CONFIGS[a.config]
     for key in ("model", "groups", "rollouts", "prompt_len", "completion_len", "lora_rank", "kl"):
@@ -85,6 +90,30 @@ CONFIGS = {
     "dense32b": dict(model="qwen3-32b", groups=16, rollouts=8, prompt_len=4096, completion_len=1024,
                      lora_rank=32, kl=0.01, par="tp"),
 }
+
+
+def write_kernel_table(path: str, events, rank: int) -> None:
+    """Device time per kernel name of one profiled step (torch.profiler CUDA
+    activity: every launch, no replay), with the span from the first kernel's
+    start to the last one's end, so idle device time shows as the gap."""
+    tot: dict[str, list] = {}
+    t0, t1 = float("inf"), 0.0
+    for e in events:
+        d = e.device_time_total if hasattr(e, "device_time_total") else e.cuda_time_total
+        r = tot.setdefault(e.name, [0.0, 0])
+        r[0] += d
+        r[1] += 1
+        if e.time_range is not None:
+            t0 = min(t0, e.time_range.start)
+            t1 = max(t1, e.time_range.end)
+    busy = sum(v[0] for v in tot.values())
+    span = (t1 - t0) if t1 > t0 else float("nan")
+    root, ext = os.path.splitext(path)
+    with open(f"{root}.rank{rank}{ext or '.txt'}", "w") as f:
+        f.write(f"# busy {busy / 1e3:.1f} ms of a {span / 1e3:.1f} ms span ({len(events)} launches)\n")
+        f.write("share_pct\tms\tlaunches\tkernel\n")
+        for name, (d, n) in sorted(tot.items(), key=lambda kv: -kv[1][0]):
+            f.write(f"{100 * d / busy:.2f}\t{d / 1e3:.2f}\t{n}\t{name[:160]}\n")
 
 
 BASELINE_VALUE = None  # BASELINE.md publishes no GPU number for this metric
@@ -190,6 +219,10 @@ def main() -> None:
         reference_arm(args)
         return
 
+    if args.unfused:  # read at import time by the op wrappers
+        os.environ["ART_B200_PAIR_GEMM"] = "0"
+        os.environ["ART_B200_LMHEAD_LIBRARY"] = "1"
+        os.environ["ART_B200_EP_FUSED"] = "0"
     import torch
     import torch.distributed as dist
 
@@ -231,7 +264,8 @@ def main() -> None:
     packed_tokens = int((packed["group_ids"] >= 0).sum())
 
     trainer = GRPOTrainer(cfg, lora, device, seed=0, group=dist.group.WORLD if world > 1 else None,
-                          tp_size=args.tp, cp_size=args.cp, max_tokens_per_rank=max(16384, seq_len))
+                          tp_size=args.tp, cp_size=args.cp, max_tokens_per_rank=max(16384, seq_len),
+                          fused_dp=not args.unfused)
     lr = 1e-5
     loss_cfg: dict = {"kl_penalty_coef": args.kl} if args.kl else {}
     staged = trainer.stage(packed)
@@ -294,10 +328,16 @@ def main() -> None:
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
             step()
             torch.cuda.synchronize()
-        names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+        events = [e for e in prof.events() if e.device_type.name == "CUDA"]
+        names = [e.name for e in events]
         ours = [n for n in names if "art::" in n]
         launches = len(ours) * args.steps
         lib_kernels = len(names) - len(ours)
+        if args.kernel_table:
+            try:
+                write_kernel_table(args.kernel_table, events, rank)
+            except Exception as exc:  # the table is a diagnostic: never fail the bench line
+                print(f"kernel table not written: {exc!r}", file=sys.stderr)
     except Exception:
         lib_kernels = None
 
@@ -341,7 +381,7 @@ def main() -> None:
             },
             "clocks": clocks,
             "gpu_launches": launches,
-            "impl": "ours",
+            "impl": "ours-unfused" if args.unfused else "ours",
         }
         if e2e is not None:
             out["e2e"] = e2e

@@ -120,11 +120,50 @@ def test_attention_tc_bwd_matches_reference(cuda, shape):
     o, lse = C.attn_fwd(q, k, v, meta.kend, meta.tile_kmax, scale)
     do = torch.randn_like(o)
     units = fused.attention_bwd_units_tc(kend).to(cuda)
-    dq, dk, dv = C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, units, scale)
+    dq, dk, dv, _ = C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, units, scale)
     torch.cuda.synchronize()
     assert C.tc_error_code() == 0
     qr, kr, vr = (t.float().requires_grad_() for t in (q, k, v))
     orf, _ = fused.attention_ref(qr, kr, vr, kend.to(cuda), scale)
+    orf.backward(do.float())
+    assert rel_err(dv, vr.grad) < 2e-2
+    assert rel_err(dk, kr.grad) < 2e-2
+    assert rel_err(dq, qr.grad) < 2e-2
+
+
+def _tree(n_completions, prompt, comp):
+    p = torch.randint(0, 1000, (prompt,))
+    seqs = [torch.cat([p, torch.randint(0, 1000, (comp + 7 * i,))]) for i in range(n_completions)]
+    pack = prefix_tree_pack(seqs, max_depth=4096, shareable_lengths=[prompt - 1] * n_completions)
+    return visibility_ends(pack.group_ids, pack.parent_ids)[0], pack.position_ids[0].to(torch.int32)
+
+
+@pytest.mark.parametrize("window,sink", [(128, False), (200, True), (0, True), (1000, True)])
+def test_attention_tc_window_and_sinks(cuda, window, sink):
+    """Sliding window (positions of the packed prefix tree) and attention
+    sinks, forward and backward, against the fp32 dense-mask reference."""
+    torch.manual_seed(11 + window)
+    kend, pos = _tree(4, 300, 170)
+    T, D, Hq, Hkv = kend.numel(), 128, 4, 2
+    q = torch.randn(T, Hq, D, device=cuda, dtype=torch.bfloat16)
+    k = torch.randn(T, Hkv, D, device=cuda, dtype=torch.bfloat16)
+    v = torch.randn(T, Hkv, D, device=cuda, dtype=torch.bfloat16)
+    sinks = (torch.randn(Hq, device=cuda) * 2).float() if sink else None
+    meta = fused.AttnMeta.build(pos, kend, cuda).windowed(window)
+    scale = 1 / math.sqrt(D)
+    C = native.lib()
+    w = meta.window
+    o, lse = C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, scale, 0,
+                           meta.positions if w else None, meta.tile_pmax if w else None, w, sinks)
+    do = torch.randn_like(o)
+    dq, dk, dv, _ = C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, meta.bwd_units, scale, 0,
+                                  meta.positions if w else None, w)
+    torch.cuda.synchronize()
+    assert C.tc_error_code() == 0
+    qr, kr, vr = (t.float().requires_grad_() for t in (q, k, v))
+    orf, lser = fused.attention_ref(qr, kr, vr, kend.to(cuda), scale, pos.to(cuda), window, sinks)
+    assert rel_err(o, orf) < 1e-2
+    assert torch.allclose(lse, lser, atol=2e-2, rtol=1e-3)
     orf.backward(do.float())
     assert rel_err(dv, vr.grad) < 2e-2
     assert rel_err(dk, kr.grad) < 2e-2
