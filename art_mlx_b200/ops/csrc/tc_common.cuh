@@ -63,6 +63,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait that sleeps between probes: for warps that wait long (a GEMM
+// epilogue waiting for the next accumulator) and share their SM sub-partition
+// with the warps that issue the MMAs or the TMA loads, so their polling does
+// not take issue slots from those.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(256);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 15) == 0) {
+      if (*abort_flag) return false;
+      if (gtimer() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        if (err) atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
 // Bounded wait by a whole warp, with a warp-uniform result: warps that go on
 // to warp-collective instructions (tcgen05.ld/st, shuffles) must not split
 // on the error path.

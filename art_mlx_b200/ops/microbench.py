@@ -157,6 +157,55 @@ def gemm_one() -> None:
     _emit(case="gemm_one", tc_error=int(C.tc_error_code()))
 
 
+def gemm_diag() -> None:
+    """Where the pair GEMM's time goes on the gate_up shape: full kernel vs
+    the mainloop alone (epilogue skipped), and the MMA thread's counters."""
+    from . import native
+
+    C = native.lib()
+    dev = torch.device("cuda")
+    a = torch.randn(9280, 3584, device=dev, dtype=torch.bfloat16)
+    b = torch.randn(37888, 3584, device=dev, dtype=torch.bfloat16) * 0.02
+    fl = 2 * 9280 * 3584 * 37888
+    diag = torch.zeros(5, dtype=torch.int64, device=dev)
+    t_full = _timed(lambda: C.gemm_pair(a, b))
+    t_main = _timed(lambda: C.gemm_pair_mainloop(a, b, diag))
+    diag.zero_()
+    C.gemm_pair_mainloop(a, b, diag)
+    torch.cuda.synchronize()
+    d_main = [int(x) for x in diag.tolist()]
+    diag.zero_()
+    C.gemm_pair(a, b, None, None, None, None, False, diag)
+    torch.cuda.synchronize()
+    d_full = [int(x) for x in diag.tolist()]
+
+    def frac(d):
+        tot = max(d[2], 1)
+        return dict(wait_operands=round(d[0] / tot, 4), wait_accumulator=round(d[1] / tot, 4),
+                    blocks_not_ready=round(d[3] / max(d[4], 1), 4))
+
+    _emit(case="gemm_diag_gate_up", full_ms=round(t_full, 4), mainloop_ms=round(t_main, 4),
+          full_tflops=round(fl / t_full / 1e9, 1), mainloop_tflops=round(fl / t_main / 1e9, 1),
+          full=frac(d_full), mainloop=frac(d_main), tc_error=int(C.tc_error_code()))
+
+
+def gemm_pair_vs_cublas_one() -> None:
+    """Two CTA-pair GEMM calls, then two cuBLAS calls, on the gate_up shape
+    (a small, self-ending target for a profiler capture of both kernels)."""
+    from . import native
+
+    C = native.lib()
+    dev = torch.device("cuda")
+    a = torch.randn(9280, 3584, device=dev, dtype=torch.bfloat16)
+    b = torch.randn(37888, 3584, device=dev, dtype=torch.bfloat16) * 0.02
+    for _ in range(2):
+        C.gemm_pair(a, b)
+    for _ in range(2):
+        torch.matmul(a, b.t())
+    torch.cuda.synchronize()
+    _emit(case="gemm_pair_vs_cublas_one", tc_error=int(C.tc_error_code()))
+
+
 def bench_norm() -> None:
     """Residual add + RMSNorm forward and backward on one packed row of the
     benchmark (9231 tokens x 3584): warp-per-row kernels vs the block-per-row
@@ -394,6 +443,10 @@ def main(argv: list[str]) -> None:
         bench_gemm()
     elif which == "gemm_one":
         gemm_one()
+    elif which == "gemm_diag":
+        gemm_diag()
+    elif which == "gemm_pair_vs_cublas_one":
+        gemm_pair_vs_cublas_one()
     elif which == "gdn":
         bench_gdn()
     elif which == "norm":
@@ -401,7 +454,7 @@ def main(argv: list[str]) -> None:
     elif which == "comm":
         bench_comm()
     else:
-        raise SystemExit(f"unknown case {which!r}: attn | gemm | gemm_one | gdn | norm | comm")
+        raise SystemExit(f"unknown case {which!r}: attn | gemm | gemm_one | gemm_diag | gemm_pair_vs_cublas_one | gdn | norm | comm")
 
 
 if __name__ == "__main__":
