@@ -190,6 +190,7 @@ class LocalBackend:
         self, model: Any, config: dev.OpenAIServerConfig | None = None
     ) -> tuple[str, str]:
         self._flush()
+        _barrier()  # every rank's optimizer shard of the last step is on disk
         tr = self._get_trainer(model)
         d = self._model_dir(model)
         step = get_step_from_dir(d)
@@ -276,6 +277,7 @@ class LocalBackend:
         results: list[TokenizedResult],
         packed_sequence_length: int | None,
         advantage_balance: float,
+        model: Any = None,
     ) -> dict[str, Any]:
         if packed_sequence_length is None:
             from ..preprocessing.prefix_tree import _plan_segments
@@ -291,9 +293,14 @@ class LocalBackend:
                                       [max(0, min(r.prompt_length, len(r.token_ids))) for r in rs])
                 longest = max(longest, sum(s.end - s.start for s in segs))
             packed_sequence_length = max(128, (longest + 127) // 128 * 128)
+        # with several data-parallel ranks each fills only the rows it trains
+        rows_needed = None
+        tr = self._get_trainer(model) if model is not None else None
+        if tr is not None and tr.world > 1:
+            rows_needed = tr.rows_needed
         return packed_tensors_from_tokenized_results(
             results, packed_sequence_length, advantage_balance=advantage_balance,
-            rng=random.Random(self._seed + 7),
+            rng=random.Random(self._seed + 7), rows_needed=rows_needed,
         )
 
     async def train(
@@ -379,9 +386,11 @@ class LocalBackend:
             # nothing trainable: advance the step with an unchanged adapter
             new_step = step + 1
             ck = get_step_checkpoint_dir(d, new_step)
+            if save_checkpoint:
+                self._flush()  # the copy includes the previous optimizer state (every rank's shard)
+                _barrier()
             if save_checkpoint and _rank() == 0:
                 prev = get_step_checkpoint_dir(d, step)
-                self._flush()  # the copy includes the previous optimizer state
                 if os.path.exists(ck):
                     shutil.rmtree(ck)
                 if os.path.exists(prev):
@@ -393,7 +402,7 @@ class LocalBackend:
             base_metrics.update({"data/step_num_groups_trainable": 0.0, "data/step_trainer_tokens": 0.0})
             return LocalTrainResult(step=new_step, metrics=base_metrics, checkpoint_path=ck if save_checkpoint else None)
 
-        packed = self._pack(results, packed_sequence_length, advantage_balance)
+        packed = self._pack(results, packed_sequence_length, advantage_balance, model)
         t_prepared = time.monotonic()
         if plot_tensors and _rank() == 0:
             packed_tensors_to_dir(packed, os.path.join(d, "tensors"))
@@ -454,11 +463,17 @@ class LocalBackend:
                 metrics["time/step_compute_s"] = time.monotonic() - t1
         self.last_d2h_bytes = 5 * 4
         t2 = time.monotonic()
+        shard = tr.optimizer_shard() if out_dir is not None else None
         if out_dir is not None:
-            tr.prepare_checkpoint()
+            # sharded optimizer: only the master weights are gathered (the
+            # adapter rank 0 publishes); every rank writes its own moments
+            tr.prepare_checkpoint(moments=shard is None)
             if _rank() == 0:
-                self._writer.submit(out_dir, tr.store, model.base_model, tr.model.lora_spec)
-        _barrier()
+                self._writer.submit(out_dir, tr.store, model.base_model, tr.model.lora_spec,
+                                    with_optimizer=shard is None)
+        _barrier()  # the adapter directory is published
+        if shard is not None:
+            self._writer.submit_optimizer_shard(out_dir, tr.store, *shard)
         metrics["time/step_checkpoint_s"] = time.monotonic() - t2
         return metrics
 
@@ -487,6 +502,7 @@ class LocalBackend:
             yield m
         self._flush()
         step = get_step_from_dir(d) + 1
+        tr.prepare_checkpoint()  # collective: every shard's master and moments on every rank
         if _rank() == 0:
             save_adapter(get_step_checkpoint_dir(d, step), tr.store, model.base_model, tr.model.lora_spec,
                          tr.optim.state_dict())

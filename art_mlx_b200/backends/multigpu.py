@@ -200,7 +200,8 @@ class MultiGPUBackend(LocalBackend):
         host, port = cfg.get("host", "127.0.0.1"), int(cfg.get("port", 8000))
         return f"http://{host}:{port}/v1", cfg.get("server_args", {}).get("api_key", "default")
 
-    def _pack(self, results, packed_sequence_length, advantage_balance):
+    def _pack(self, results, packed_sequence_length, advantage_balance, model=None):
+        # the client packs every row: the worker ranks read the rows they train from disk
         return super()._pack(results, packed_sequence_length or self._packed_len, advantage_balance)
 
     async def _train_packed(self, model, packed, lr, dev_config, kl_ref_adapter_path, logprob_chunk, out_dir,

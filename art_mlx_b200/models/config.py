@@ -18,7 +18,7 @@ from typing import Any, Literal
 @dataclass(frozen=True)
 class ModelConfig:
     name: str
-    family: Literal["qwen2", "qwen3", "qwen3_moe", "qwen3_next"]
+    family: str  # the checkpoint's model_type: qwen2, qwen3, qwen3_moe, qwen3_next, llama, mistral, gpt_oss
     vocab_size: int
     hidden_size: int
     num_hidden_layers: int
@@ -51,15 +51,35 @@ class ModelConfig:
     linear_conv_kernel_dim: int = 4
     linear_chunk_size: int = 64
     attn_output_gate: bool = False
+    # per-layer kinds of transformers-5 configs ("full_attention",
+    # "sliding_attention", "linear_attention"); empty = from the fields above
+    layer_types: tuple = ()
+    # GPT-OSS: learned per-head attention sinks, bias on o_proj, router and
+    # expert biases, clamped GLU experts ((up + 1) * g * sigmoid(alpha g))
+    attn_sinks: bool = False
+    o_bias: bool = False
+    router_bias: bool = False
+    expert_bias: bool = False
+    expert_act: str = "swiglu"  # or "clamped_glu"
+    glu_alpha: float = 1.702
+    glu_limit: float = 7.0
 
     @property
     def is_moe(self) -> bool:
         return self.num_experts > 0
 
     def layer_kind(self, i: int) -> Literal["attention", "linear_attention"]:
+        if self.layer_types:
+            return "linear_attention" if self.layer_types[i] == "linear_attention" else "attention"
         if self.full_attention_interval and (i + 1) % self.full_attention_interval != 0:
             return "linear_attention"
         return "attention"
+
+    def layer_window(self, i: int) -> int:
+        """Sliding-window size of layer ``i`` (0: full attention)."""
+        if self.layer_types and self.layer_types[i] == "sliding_attention" and self.sliding_window:
+            return int(self.sliding_window)
+        return 0
 
     @property
     def q_size(self) -> int:
@@ -92,6 +112,8 @@ class ModelConfig:
         if (scaling.get("rope_type") or scaling.get("type") or "default") == "default":
             scaling = {}
         num_experts = d.get("num_experts", d.get("num_local_experts", 0)) or 0
+        gpt_oss = family == "gpt_oss"
+        layer_types = tuple(d.get("layer_types") or ())
         return cls(
             name=name,
             family=family,  # type: ignore[arg-type]
@@ -110,7 +132,7 @@ class ModelConfig:
             tie_word_embeddings=d.get("tie_word_embeddings", False),
             num_experts=num_experts,
             num_experts_per_tok=d.get("num_experts_per_tok", 0),
-            moe_intermediate_size=d.get("moe_intermediate_size", 0),
+            moe_intermediate_size=d.get("moe_intermediate_size", 0) or (d.get("intermediate_size", 0) if gpt_oss else 0),
             norm_topk_prob=d.get("norm_topk_prob", True),
             shared_expert_intermediate_size=d.get("shared_expert_intermediate_size", 0),
             full_attention_interval=d.get("full_attention_interval", 0),
@@ -119,6 +141,15 @@ class ModelConfig:
             linear_key_head_dim=d.get("linear_key_head_dim", 0),
             linear_value_head_dim=d.get("linear_value_head_dim", 0),
             linear_conv_kernel_dim=d.get("linear_conv_kernel_dim", 4),
+            sliding_window=d.get("sliding_window") if any(t == "sliding_attention" for t in layer_types) else None,
+            layer_types=layer_types,
+            attn_sinks=gpt_oss,
+            o_bias=gpt_oss and bool(d.get("attention_bias", True)),
+            router_bias=gpt_oss,
+            expert_bias=gpt_oss,
+            expert_act="clamped_glu" if gpt_oss else "swiglu",
+            glu_alpha=float(d.get("swiglu_alpha", 1.702)) if gpt_oss else 1.702,
+            glu_limit=float(d.get("swiglu_limit", 7.0)) if gpt_oss else 7.0,
         )
 
 

@@ -142,6 +142,12 @@ class ExpertParams:
         # the fused expert-parallel exchange; None without expert parallelism)
         self.A_all_gu = None
         self.B_all_d = None
+        # GPT-OSS experts: frozen biases ([E_l, 2F] of [gate | up], [E_l, H])
+        # and the clamped GLU instead of SwiGLU
+        self.gu_b = None
+        self.down_b = None
+        self.act = "swiglu"
+        self.alpha, self.limit = 1.702, 7.0
 
     def for_compute(self) -> "ExpertParams":
         """Contiguous copies of the factors the products read (slices under
@@ -154,7 +160,62 @@ class ExpertParams:
         out = ExpertParams(self.gu_w_t, self.down_w_t, c(self.A_gu), c(self.B_gu), c(self.A_d), c(self.B_d),
                            self.g_A_gu, self.g_B_gu, self.g_A_d, self.g_B_d, self.scale)
         out.A_all_gu, out.B_all_d = self.A_all_gu, self.B_all_d
+        out.gu_b, out.down_b, out.act, out.alpha, out.limit = self.gu_b, self.down_b, self.act, self.alpha, self.limit
         return out
+
+    @property
+    def plain(self) -> bool:
+        """SwiGLU experts without biases (what the expert-parallel paths run)."""
+        return self.act == "swiglu" and self.gu_b is None and self.down_b is None
+
+
+def _row_bias(b: torch.Tensor | None, counts: list[int], like: torch.Tensor) -> torch.Tensor | None:
+    """Per-row bias of expert-sorted rows: ``b[e]`` for the rows of expert e."""
+    if b is None:
+        return None
+    idx = torch.repeat_interleave(torch.arange(len(counts), device=like.device),
+                                  torch.tensor(counts, device=like.device))
+    return b[idx].to(like.dtype)
+
+
+def _act_fwd(gu: torch.Tensor, p: "ExpertParams") -> torch.Tensor:
+    """Expert activation over the [gate | up] halves of ``gu``."""
+    Fh = gu.shape[1] // 2
+    if gu.device.type == "cuda" and gu.dtype == torch.bfloat16:
+        from ..ops import native
+
+        C = native.lib()
+        if p.act == "clamped_glu":
+            return C.glu_clamp_fwd(gu.contiguous(), p.alpha, p.limit)
+        return C.swiglu_fwd(gu.contiguous())
+    g, up = gu[:, :Fh].float(), gu[:, Fh:].float()
+    if p.act == "clamped_glu":
+        g = g.clamp(max=p.limit)
+        up = up.clamp(-p.limit, p.limit)
+        return ((up + 1) * g * torch.sigmoid(g * p.alpha)).to(gu.dtype)
+    return (g * torch.sigmoid(g)).to(gu.dtype) * gu[:, Fh:]
+
+
+def _act_bwd(dact: torch.Tensor, gu: torch.Tensor, p: "ExpertParams") -> torch.Tensor:
+    Fh = gu.shape[1] // 2
+    if gu.device.type == "cuda" and gu.dtype == torch.bfloat16:
+        from ..ops import native
+
+        C = native.lib()
+        if p.act == "clamped_glu":
+            return C.glu_clamp_bwd(dact.contiguous(), gu.contiguous(), p.alpha, p.limit)
+        return C.swiglu_bwd(dact.contiguous(), gu)
+    g, up = gu[:, :Fh].float(), gu[:, Fh:].float()
+    da = dact.float()
+    if p.act == "clamped_glu":
+        gc = g.clamp(max=p.limit)
+        uc = up.clamp(-p.limit, p.limit)
+        sg = torch.sigmoid(gc * p.alpha)
+        du = torch.where((up >= -p.limit) & (up <= p.limit), da * gc * sg, torch.zeros_like(da))
+        dg = torch.where(g <= p.limit, da * (uc + 1) * (sg + p.alpha * gc * sg * (1 - sg)), torch.zeros_like(da))
+        return torch.cat([dg, du], dim=1).to(gu.dtype)
+    sg = torch.sigmoid(g)
+    return torch.cat([da * up * sg * (1 + g * (1 - sg)), da * g * sg], dim=1).to(gu.dtype)
 
 
 def _tc_grouped(x: torch.Tensor, p: ExpertParams) -> bool:
@@ -223,12 +284,16 @@ def _experts_forward_tc(xs, counts, p: ExpertParams, lora: bool):
         bd[:, Fh:, r:] = s * p.B_gu[:, 1]
         a2, b2 = u_gu.contiguous(), bd.view(E * F2, 2 * r)
     gu = C.gemm_tc_grouped(xs.contiguous(), p.gu_w_t.view(E * H, F2), offs, F2, a2, b2, True)
-    act = C.swiglu_fwd(gu)  # fused silu(gate) * up over the [gate | up] halves
+    if p.gu_b is not None:
+        gu.add_(_row_bias(p.gu_b, counts, gu))
+    act = _act_fwd(gu, p)  # fused activation over the [gate | up] halves
     a2 = b2 = None
     if lora and p.A_d is not None:
         u_d = _lr_rows(act, p.A_d, counts)  # [N, r]
         a2, b2 = u_d, (s * p.B_d).reshape(E * H, -1).contiguous()
     out = C.gemm_tc_grouped(act, p.down_w_t.view(E * Fh, H), offs, H, a2, b2, True)
+    if p.down_b is not None:
+        out.add_(_row_bias(p.down_b, counts, out))
     return out, (xs, gu, act, u_gu, u_d, counts, lora)
 
 
@@ -246,13 +311,15 @@ def experts_forward(xs: torch.Tensor, counts: list[int], p: ExpertParams, lora: 
         lo = grouped_mm(u_gu[:, :r].contiguous(), p.B_gu[:, 0].transpose(1, 2), counts)
         hi = grouped_mm(u_gu[:, r:].contiguous(), p.B_gu[:, 1].transpose(1, 2), counts)
         gu = gu + s * torch.cat([lo, hi], dim=1)
-    Fh = gu.shape[1] // 2
-    g, up = gu[:, :Fh], gu[:, Fh:]
-    act = (g.float() * torch.sigmoid(g.float())).to(gu.dtype) * up
+    if p.gu_b is not None:
+        gu = gu + _row_bias(p.gu_b, counts, gu)
+    act = _act_fwd(gu, p)
     out = grouped_mm(act, p.down_w_t, counts)
     if lora and p.A_d is not None:
         u_d = grouped_mm(act, p.A_d.transpose(1, 2), counts)  # [N, r]
         out = out + s * grouped_mm(u_d, p.B_d.transpose(1, 2), counts)
+    if p.down_b is not None:
+        out = out + _row_bias(p.down_b, counts, out)
     return out, (xs, gu, act, u_gu, u_d, counts, lora)
 
 
@@ -283,13 +350,7 @@ def experts_backward(dout: torch.Tensor, saved, p: ExpertParams) -> torch.Tensor
         grouped_wgrad(dyB, act, counts, p.g_A_d, s)
         dact = dact + s * grouped_mm(dyB, p.A_d, counts)
     Fh = gu.shape[1] // 2
-    if tc:
-        dgu = C.swiglu_bwd(dact.contiguous(), gu)  # fused SwiGLU backward into [dgate | dup]
-    else:
-        g, up = gu[:, :Fh].float(), gu[:, Fh:].float()
-        sg = torch.sigmoid(g)
-        da = dact.float()
-        dgu = torch.cat([da * up * sg * (1 + g * (1 - sg)), da * g * sg], dim=1).to(gu.dtype)
+    dgu = _act_bwd(dact, gu, p)  # [dgate | dup] (fused kernel on the GPU)
     if tc:
         a2 = b2 = None
         if lora and p.A_gu is not None:
@@ -388,6 +449,7 @@ class MoEBlock:
         self.cfg, self.index, self.ep, self.etp = cfg, i, ep, etp
         E, H, F = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size
         self.router_w = _randn((E, H), gen, dev, dt)
+        self.router_b = _randn((E,), gen, dev, dt) if cfg.router_bias else None
         e0 = ep.first_expert if ep is not None else 0
         El = ep.E_local if ep is not None else E
         f0, Fl = etp.slice(F) if etp is not None else (0, F)
@@ -432,6 +494,10 @@ class MoEBlock:
             pick(g_A_gu), pick_bgu(g_B_gu), pick_ad(g_A_d), pick(g_B_d), spec.scale,
         )
         self.params.A_all_gu, self.params.B_all_d = A_gu, B_d
+        if cfg.expert_bias:
+            self.params.gu_b = _randn((El, 2 * Fl), gen, dev, dt)
+            self.params.down_b = _randn((El, H), gen, dev, dt)
+        self.params.act, self.params.alpha, self.params.limit = cfg.expert_act, cfg.glu_alpha, cfg.glu_limit
 
     def num_parameters(self) -> int:
         n = self.router_w.numel() + self.gu_w_t.numel() + self.down_w_t.numel()
@@ -442,6 +508,8 @@ class MoEBlock:
     def route(self, h: torch.Tensor, ctx: dict[str, Any]) -> tuple[torch.Tensor, torch.Tensor]:
         cfg = self.cfg
         logits = (h @ self.router_w.t()).float()
+        if self.router_b is not None:
+            logits = logits + self.router_b.float()
         probs = torch.softmax(logits, dim=-1)
         replay = ctx.get("replay_routes")  # [T, L, k] int
         if replay is not None:
@@ -466,6 +534,8 @@ class MoEBlock:
         T, H = hx.shape
         params = self.params.for_compute()
         if self.ep is not None and self.ep.world > 1:
+            if not params.plain:
+                raise NotImplementedError("expert parallelism runs SwiGLU experts without biases (not GPT-OSS)")
             fused = getattr(self.ep, "fused", None)
             counts = ctx.get("ep_counts")
             if fused is not None and counts is not None and self.etp is None:
@@ -500,9 +570,23 @@ class MoEBlock:
         return out
 
     def load_hf(self, sd: dict[str, torch.Tensor], prefix: str, g: Callable[[str], torch.Tensor]) -> None:
-        self.router_w.copy_(g(prefix + "gate.weight"))
         e0 = self.ep.first_expert if self.ep is not None else 0
         fs = slice(self.f0, self.f0 + self.F_local)
+        if prefix + "router.weight" in sd:  # GPT-OSS: stacked experts, gate/up interleaved by column
+            El = self.gu_w_t.shape[0]
+            es = slice(e0, e0 + El)
+            self.router_w.copy_(g(prefix + "router.weight"))
+            if self.router_b is not None:
+                self.router_b.copy_(g(prefix + "router.bias"))
+            gu = g(prefix + "experts.gate_up_proj")[es]  # [E, H, 2F]
+            self.gu_w_t.copy_(torch.cat([gu[..., 0::2][..., fs], gu[..., 1::2][..., fs]], dim=2))
+            self.down_w_t.copy_(g(prefix + "experts.down_proj")[es][:, fs])
+            if self.params.gu_b is not None:
+                b = g(prefix + "experts.gate_up_proj_bias")[es]
+                self.params.gu_b.copy_(torch.cat([b[:, 0::2][:, fs], b[:, 1::2][:, fs]], dim=1))
+                self.params.down_b.copy_(g(prefix + "experts.down_proj_bias")[es])
+            return
+        self.router_w.copy_(g(prefix + "gate.weight"))
         for le in range(self.gu_w_t.shape[0]):
             p = f"{prefix}experts.{e0 + le}."
             self.gu_w_t[le].copy_(torch.cat([g(p + "gate_proj.weight")[fs], g(p + "up_proj.weight")[fs]]).t())

@@ -46,6 +46,11 @@ for _spec in (
     # checkpoints run through the same layers (no q/k norm, optional q/k/v bias, RoPE scaling)
     ModelSupportSpec("llama", ("llama",), _DENSE, supports=frozenset({"dp", "tp", "cp", "generate"})),
     ModelSupportSpec("mistral", ("mistral",), _DENSE, supports=frozenset({"dp", "tp", "cp", "generate"})),
+    # GPT-OSS (reference model_support/registry.py GPT_OSS_MOE_SPEC): attention
+    # sinks, sliding-window layers, biased projections and clamped-GLU experts
+    # on the data-parallel path (the expert-parallel exchange runs plain SwiGLU
+    # experts; the decode kernel has no sinks or windows)
+    ModelSupportSpec("gpt_oss", ("gpt_oss",), _DENSE, is_moe=True, supports=frozenset({"dp"})),
 ):
     register_model_support(_spec)
 

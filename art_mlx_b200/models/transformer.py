@@ -52,6 +52,9 @@ class Layer:
     o_w: torch.Tensor | None = None
     qkv_lora: LoRABinding | None = None
     o_lora: LoRABinding | None = None
+    o_b: torch.Tensor | None = None  # GPT-OSS: bias of o_proj
+    sinks: torch.Tensor | None = None  # GPT-OSS: fp32 [heads] attention-sink logits
+    window: int = 0  # sliding-window size (0: full attention)
     mlp: DenseMLP | None = None
     moe: MoEBlock | None = None
     gdn: Any = None
@@ -171,6 +174,8 @@ class DecoderLM:
         self.final_norm = torch.ones(H, device=dev, dtype=dt)
         self.lm_head = self.embed if cfg.tie_word_embeddings else _randn((V, H), gen, dev, dt)
         self.inv_freq = fused.rope_inv_freq(cfg.head_dim, cfg.rope_theta, dev, dict(cfg.rope_scaling))
+        # a RoPE that scales cos / sin (YaRN) scales q and k: the scores carry its square
+        self.attn_scale = fused.rope_attention_factor(dict(cfg.rope_scaling)) ** 2 / math.sqrt(cfg.head_dim)
         self.layers: list[Layer] = []
         for i in range(cfg.num_hidden_layers):
             self.layers.append(self._build_layer(i, gen))
@@ -196,6 +201,11 @@ class DecoderLM:
                 layer.q_norm = torch.ones(cfg.head_dim, device=dev, dtype=dt)
                 layer.k_norm = torch.ones(cfg.head_dim, device=dev, dtype=dt)
             layer.o_w = _randn((H, cfg.q_size), gen, dev, dt)
+            if cfg.o_bias:
+                layer.o_b = _randn((H,), gen, dev, dt)
+            if cfg.attn_sinks:
+                layer.sinks = torch.zeros(cfg.num_attention_heads, device=dev, dtype=torch.float32)
+            layer.window = cfg.layer_window(i)
             layer.qkv_lora = make_binding(
                 st, i, "self_attn", [("q_proj", qo), ("k_proj", cfg.kv_size), ("v_proj", cfg.kv_size)], spec
             )
@@ -231,17 +241,20 @@ class DecoderLM:
             gate = qg[..., D:].reshape(T, cfg.q_size)
             qkv = torch.cat([qg[..., :D].reshape(T, cfg.q_size), qkv[:, 2 * cfg.q_size :]], dim=1)
         if ctx is not None and ctx.get("cp_plan") is not None:
+            if layer.window or layer.sinks is not None:
+                raise NotImplementedError("context parallelism with sliding windows or attention sinks")
             from ..parallel.cp import cp_rope_attention
 
             o = cp_rope_attention(qkv, ctx["cp_plan"], ctx["cp"], self.inv_freq, nq, nkv, D,
                                   layer.q_norm, layer.k_norm, cfg.rms_norm_eps)
         else:
             o = fused.rope_attention(
-                qkv, meta, self.inv_freq, nq, nkv, D, layer.q_norm, layer.k_norm, cfg.rms_norm_eps
+                qkv, meta.windowed(layer.window), self.inv_freq, nq, nkv, D, layer.q_norm, layer.k_norm,
+                cfg.rms_norm_eps, sinks=layer.sinks, scale=self.attn_scale,
             )
         if gate is not None:
             o = o * torch.sigmoid(gate)
-        return fused.lora_linear(o, layer.o_w, None, layer.o_lora, v, en)
+        return fused.lora_linear(o, layer.o_w, layer.o_b, layer.o_lora, v, en)
 
     def mlp(self, layer: Layer, h: torch.Tensor, ctx: dict[str, Any]) -> torch.Tensor:
         if layer.moe is not None:
@@ -344,6 +357,10 @@ class DecoderLM:
                     layer.q_norm.copy_(g(a + "q_norm.weight"))
                     layer.k_norm.copy_(g(a + "k_norm.weight"))
                 layer.o_w.copy_(g(a + "o_proj.weight"))
+                if layer.o_b is not None:
+                    layer.o_b.copy_(g(a + "o_proj.bias"))
+                if layer.sinks is not None:
+                    layer.sinks.copy_(sd[a + "sinks"].to(device=self.device, dtype=torch.float32))
             if layer.mlp is not None:
                 m = p + "mlp."
                 layer.mlp.gu_w.copy_(torch.cat([g(m + "gate_proj.weight"), g(m + "up_proj.weight")]))

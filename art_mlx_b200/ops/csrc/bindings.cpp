@@ -106,6 +106,8 @@ torch::Tensor gemm_pair(torch::Tensor a, torch::Tensor b, c10::optional<torch::T
                         bool b_transposed);
 std::vector<torch::Tensor> lm_head_fwd(torch::Tensor h, torch::Tensor w, torch::Tensor targets, bool entropy,
                                        c10::optional<torch::Tensor> logits_out);
+torch::Tensor glu_clamp_fwd(torch::Tensor gu, double alpha, double limit);
+torch::Tensor glu_clamp_bwd(torch::Tensor da, torch::Tensor gu, double alpha, double limit);
 void gemm_pair_mainloop(torch::Tensor a, torch::Tensor b, torch::Tensor diag);
 void lm_head_grad_logits(torch::Tensor h, torch::Tensor w, torch::Tensor targets, torch::Tensor lse, torch::Tensor g,
                          torch::Tensor out);
@@ -175,6 +177,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("logits_out") = py::none());
   m.def("lm_head_grad_logits", &art::lm_head_grad_logits);
   m.def("gemm_pair_mainloop", &art::gemm_pair_mainloop);
+  m.def("glu_clamp_fwd", &art::glu_clamp_fwd);
+  m.def("glu_clamp_bwd", &art::glu_clamp_bwd);
   m.def("gdn_conv_bwd", &art::gdn_conv_bwd);
   m.def("ep_gemm", &art::ep_gemm);
   m.def("ep_wait_combine", &art::ep_wait_combine);

@@ -45,9 +45,11 @@ constexpr int XA_TILE = XBM * XBK * 2;
 constexpr int XB_TILE = XBN * XBK * 2;
 constexpr int XSTAGE_BYTES = XA_TILE + XB_TILE;
 constexpr int XTHREADS = 256;  // warps 0 TMA, 1 MMA, 2..5 epilogue, 6..7 dispatch
-constexpr int XSMEM = XSTAGES * XSTAGE_BYTES + 1024 + 512;
+constexpr int X_STG_WARP = 32 * 128;  // epilogue staging per warp: 32 rows x 64 bf16
+constexpr int XSMEM = XSTAGES * XSTAGE_BYTES + 1024 + 512 + 4 * X_STG_WARP;
 constexpr int XMAX_RANKS = 8;
 constexpr int PUSH_BATCH = 8;
+constexpr int kPushSeg = 8;  // 16-byte loads in flight per lane while pushing a row
 constexpr uint64_t kEpWaitNs = 3ull * 1000 * 1000 * 1000;
 constexpr int kExtLd = 64;  // row stride (elements) of the receive buffer of rank-side rows
 
@@ -257,23 +259,42 @@ __global__ void __launch_bounds__(XTHREADS, 1)
           dst_row = p.C + (int64_t)row * p.ldc;
         }
       }
+      // 64 columns per pass through the warp's staging block (16-byte units
+      // XOR-swizzled by row), then 4 rows x 128 contiguous bytes per store
+      // instruction: whole lines into the (local or peer) destination rows
+      uint8_t* stg = smem + XSTAGES * XSTAGE_BYTES + 512 + (warp - 2) * X_STG_WARP;
 #pragma unroll 1
-      for (int c = 0; c < XBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * XBN + c * 32, r);
+      for (int c = 0; c < XBN / 32; c += 2) {
+        uint32_t r[2][32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * XBN + c * 32, r[0]);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * XBN + (c + 1) * 32, r[1]);
         tmem_wait_ld();
-        const int col0 = n0 + c * 32;
-        if (valid && col0 < p.N) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
             uint4 o;
-            o.x = pack_bf16x2(__uint_as_float(r[j + 0]), __uint_as_float(r[j + 1]));
-            o.y = pack_bf16x2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-            o.z = pack_bf16x2(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5]));
-            o.w = pack_bf16x2(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7]));
-            *reinterpret_cast<uint4*>(dst_row + col0 + j) = o;
+            o.x = pack_bf16x2(__uint_as_float(r[h][j + 0]), __uint_as_float(r[h][j + 1]));
+            o.y = pack_bf16x2(__uint_as_float(r[h][j + 2]), __uint_as_float(r[h][j + 3]));
+            o.z = pack_bf16x2(__uint_as_float(r[h][j + 4]), __uint_as_float(r[h][j + 5]));
+            o.w = pack_bf16x2(__uint_as_float(r[h][j + 6]), __uint_as_float(r[h][j + 7]));
+            const int u = h * 4 + j / 8;
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((u ^ (lane & 7)) << 4)) = o;
+          }
+        __syncwarp();
+        const int cbase = n0 + c * 32;
+        const uint64_t my_dst = reinterpret_cast<uint64_t>(dst_row);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int rr = 4 * k + (lane >> 3), u = lane & 7;
+          const uint64_t dr = __shfl_sync(0xffffffffu, my_dst, rr);
+          const int gcol = cbase + u * 8;
+          if (dr != 0 && gcol < p.N) {
+            const uint4 o = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((u ^ (rr & 7)) << 4));
+            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dr) + gcol) = o;
           }
         }
+        __syncwarp();
       }
       if (p.row_dst) {
         // publish the delivered rows: each thread's stores, then one release
@@ -312,14 +333,28 @@ __global__ void __launch_bounds__(XTHREADS, 1)
         const __nv_bfloat16* s = p.src + __ldg(p.push_tok + i) * p.ld_src;
         __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.recv_x[rk]) + row * p.H;
         const float sc = p.push_scale ? __ldg(p.push_scale + i) : 1.f;
-        for (int c = lane * 8; c < p.H; c += 256) {
-          uint4 v = *reinterpret_cast<const uint4*>(s + c);
-          if (p.push_scale) {
-            __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&v);
+        // a segment of up to 2048 elements per pass: all of a lane's loads
+        // are issued before its stores, so a warp waits one memory latency
+        // per segment instead of one per 512-byte chunk
+        for (int c0 = 0; c0 < p.H; c0 += kPushSeg * 256) {
+          uint4 v[kPushSeg];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) e[k] = f2bf(bf2f(e[k]) * sc);
+          for (int u = 0; u < kPushSeg; ++u) {
+            const int c = c0 + u * 256 + lane * 8;
+            if (c < p.H) v[u] = __ldg(reinterpret_cast<const uint4*>(s + c));
           }
-          *reinterpret_cast<uint4*>(d + c) = v;
+#pragma unroll
+          for (int u = 0; u < kPushSeg; ++u) {
+            const int c = c0 + u * 256 + lane * 8;
+            if (c < p.H) {
+              if (p.push_scale) {
+                __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&v[u]);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) e[k] = f2bf(bf2f(e[k]) * sc);
+              }
+              *reinterpret_cast<uint4*>(d + c) = v[u];
+            }
+          }
         }
         if (p.src_ext) {
           const __nv_bfloat16* se = p.src_ext + (int64_t)i * p.ext_cols;

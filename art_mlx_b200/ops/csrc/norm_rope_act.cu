@@ -613,4 +613,91 @@ torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu) {
   return dgu;
 }
 
+// Clamped GLU of the GPT-OSS experts over a [gate | up] row:
+//   g' = min(g, limit), u' = clamp(u, -limit, limit)
+//   a  = (u' + 1) * g' * sigmoid(alpha * g')
+// Backward: d up = da * g' sigmoid(alpha g') where |u| <= limit (else 0);
+//           d gate = da * (u' + 1) * (s + alpha g' s (1 - s)) where g <= limit.
+__global__ void glu_clamp_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ a, int64_t T,
+                                     int F, float alpha, float limit) {
+  const int64_t nvec = T * (F / 8);
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = v / (F / 8);
+    const int c = (v % (F / 8)) * 8;
+    uint4 gv = *reinterpret_cast<const uint4*>(gu + t * 2 * F + c);
+    uint4 uv = *reinterpret_cast<const uint4*>(gu + t * 2 * F + F + c);
+    const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv);
+    const __nv_bfloat16* ue = reinterpret_cast<const __nv_bfloat16*>(&uv);
+    uint4 ov;
+    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float g = fminf(bf2f(ge[k]), limit);
+      const float u = fminf(fmaxf(bf2f(ue[k]), -limit), limit);
+      const float sg = 1.f / (1.f + __expf(-alpha * g));
+      oe[k] = f2bf((u + 1.f) * g * sg);
+    }
+    *reinterpret_cast<uint4*>(a + t * F + c) = ov;
+  }
+}
+
+__global__ void glu_clamp_bwd_kernel(const __nv_bfloat16* __restrict__ da, const __nv_bfloat16* __restrict__ gu,
+                                     __nv_bfloat16* __restrict__ dgu, int64_t T, int F, float alpha, float limit) {
+  const int64_t nvec = T * (F / 8);
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = v / (F / 8);
+    const int c = (v % (F / 8)) * 8;
+    uint4 dv = *reinterpret_cast<const uint4*>(da + t * F + c);
+    uint4 gv = *reinterpret_cast<const uint4*>(gu + t * 2 * F + c);
+    uint4 uv = *reinterpret_cast<const uint4*>(gu + t * 2 * F + F + c);
+    const __nv_bfloat16* de = reinterpret_cast<const __nv_bfloat16*>(&dv);
+    const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv);
+    const __nv_bfloat16* ue = reinterpret_cast<const __nv_bfloat16*>(&uv);
+    uint4 dg, du;
+    __nv_bfloat16* dge = reinterpret_cast<__nv_bfloat16*>(&dg);
+    __nv_bfloat16* due = reinterpret_cast<__nv_bfloat16*>(&du);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float graw = bf2f(ge[k]), uraw = bf2f(ue[k]), d = bf2f(de[k]);
+      const float g = fminf(graw, limit);
+      const float u = fminf(fmaxf(uraw, -limit), limit);
+      const float sg = 1.f / (1.f + __expf(-alpha * g));
+      const float glu = g * sg;
+      due[k] = f2bf((uraw >= -limit && uraw <= limit) ? d * glu : 0.f);
+      dge[k] = f2bf(graw <= limit ? d * (u + 1.f) * (sg + alpha * g * sg * (1.f - sg)) : 0.f);
+    }
+    *reinterpret_cast<uint4*>(dgu + t * 2 * F + c) = dg;
+    *reinterpret_cast<uint4*>(dgu + t * 2 * F + F + c) = du;
+  }
+}
+
+torch::Tensor glu_clamp_fwd(torch::Tensor gu, double alpha, double limit) {
+  TORCH_CHECK(gu.is_cuda() && gu.scalar_type() == at::kBFloat16 && gu.is_contiguous() && gu.size(-1) % 16 == 0);
+  const int F = gu.size(-1) / 2;
+  const int64_t T = gu.numel() / (2 * F);
+  auto sizes = gu.sizes().vec();
+  sizes.back() = F;
+  auto a = torch::empty(sizes, gu.options());
+  if (T > 0)
+    glu_clamp_fwd_kernel<<<ew_blocks(T * F / 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), reinterpret_cast<__nv_bfloat16*>(a.data_ptr()), T, F,
+        (float)alpha, (float)limit);
+  ART_CUDA_CHECK(cudaGetLastError());
+  return a;
+}
+
+torch::Tensor glu_clamp_bwd(torch::Tensor da, torch::Tensor gu, double alpha, double limit) {
+  TORCH_CHECK(da.is_contiguous() && gu.is_contiguous() && gu.scalar_type() == at::kBFloat16);
+  const int F = gu.size(-1) / 2;
+  const int64_t T = gu.numel() / (2 * F);
+  TORCH_CHECK(da.numel() == T * F, "da must be [T, F]");
+  auto dgu = torch::empty_like(gu);
+  if (T > 0)
+    glu_clamp_bwd_kernel<<<ew_blocks(T * F / 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(da.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), T, F, (float)alpha, (float)limit);
+  ART_CUDA_CHECK(cudaGetLastError());
+  return dgu;
+}
+
 }  // namespace art

@@ -239,9 +239,56 @@ def rope_inv_freq(head_dim: int, theta: float, device: torch.device, scaling: di
         smooth = ((ctx / wavelen - lo) / (hi - lo)).clamp(0.0, 1.0)
         blended = (1 - smooth) * inv / factor + smooth * inv
         inv = torch.where(wavelen < ctx / hi, inv, torch.where(wavelen > ctx / lo, inv / factor, blended))
+    elif kind == "yarn":
+        inv = _yarn_inv_freq(inv, head_dim, theta, scaling)
     elif kind != "default":
         raise NotImplementedError(f"RoPE scaling {kind!r} is not supported")
     return inv.to(device=device, dtype=torch.float32)
+
+
+def _yarn_mscale(scale: float, m: float = 1.0) -> float:
+    return 0.1 * m * math.log(scale) + 1.0 if scale > 1 else 1.0
+
+
+def _yarn_inv_freq(inv: torch.Tensor, head_dim: int, theta: float, sc: dict) -> torch.Tensor:
+    """YaRN (Peng et al., 2023, "YaRN: Efficient Context Window Extension of
+    Large Language Models"): frequencies that complete fewer than
+    ``beta_slow`` turns over the original context are interpolated (divided
+    by ``factor``), those with more than ``beta_fast`` turns kept, with a
+    linear ramp in between over the dimension index."""
+    factor = float(sc["factor"])
+    ctx = float(sc.get("original_max_position_embeddings") or 4096)
+    b_fast, b_slow = float(sc.get("beta_fast", 32.0)), float(sc.get("beta_slow", 1.0))
+
+    def dim_of(turns: float) -> float:  # dimension index whose wavelength gives `turns` over ctx
+        return head_dim * math.log(ctx / (turns * 2 * math.pi)) / (2 * math.log(theta))
+
+    lo, hi = dim_of(b_fast), dim_of(b_slow)
+    if sc.get("truncate", True):
+        lo, hi = math.floor(lo), math.ceil(hi)
+    lo, hi = max(lo, 0), min(hi, head_dim - 1)
+    if lo == hi:
+        hi += 0.001
+    ramp = ((torch.arange(head_dim // 2, dtype=torch.float64) - lo) / (hi - lo)).clamp(0.0, 1.0)
+    keep = 1.0 - ramp  # 1: extrapolate (keep), 0: interpolate
+    return inv / factor * (1 - keep) + inv * keep
+
+
+def rope_attention_factor(scaling: dict | None) -> float:
+    """Factor by which the checkpoint's RoPE scales cos / sin (YaRN's
+    ``0.1 ln(factor) + 1``, or the configured ``attention_factor``); q and k
+    both carry it, so attention scores carry its square."""
+    sc = scaling or {}
+    kind = sc.get("rope_type") or sc.get("type") or "default"
+    if kind != "yarn":
+        return 1.0
+    if sc.get("attention_factor") is not None:
+        return float(sc["attention_factor"])
+    factor = float(sc["factor"])
+    m, m_all = sc.get("mscale"), sc.get("mscale_all_dim")
+    if m and m_all:
+        return _yarn_mscale(factor, float(m)) / _yarn_mscale(factor, float(m_all))
+    return _yarn_mscale(factor)
 
 
 # ---------------------------------------------------------------------------
@@ -329,6 +376,20 @@ def attention_ref(
     return o.to(q.dtype), lse
 
 
+ATTN_HEAD_DIM = 128  # head size of the tcgen05 attention kernels
+
+
+def _pad_head(x: torch.Tensor) -> torch.Tensor:
+    """Heads narrower than the kernels' 128 columns, zero-padded (zero
+    columns change no score and give zero output columns)."""
+    D = x.shape[-1]
+    if D == ATTN_HEAD_DIM:
+        return x
+    if D > ATTN_HEAD_DIM:
+        raise NotImplementedError(f"attention head_dim {D} > {ATTN_HEAD_DIM} on the GPU")
+    return torch.nn.functional.pad(x, (0, ATTN_HEAD_DIM - D)).contiguous()
+
+
 class _RopeAttention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale, sinks):
@@ -339,6 +400,7 @@ class _RopeAttention(torch.autograd.Function):
         k = qk[:, nq * D :].view(T, nkv, D)
         v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
         win = meta.window
+        q, k, v = _pad_head(q), _pad_head(k), _pad_head(v)
         o, lse = C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, scale, 0,
                                meta.positions if win else None, meta.tile_pmax if win else None, win, sinks)
         ctx.save_for_backward(qkv, qk, o, lse, inv_freq, qn_w if qn_w is not None else qkv.new_empty(0),
@@ -346,7 +408,7 @@ class _RopeAttention(torch.autograd.Function):
                               rstd if rstd is not None and rstd.numel() else qkv.new_empty(0, dtype=torch.float32))
         ctx.meta = meta
         ctx.dims = (nq, nkv, D, scale, qn_w is not None)
-        return o.view(T, nq * D)
+        return o[..., :D].reshape(T, nq * D)
 
     @staticmethod
     def backward(ctx, do):
@@ -355,18 +417,18 @@ class _RopeAttention(torch.autograd.Function):
         nq, nkv, D, scale, has_norm = ctx.dims
         meta = ctx.meta
         T = qkv.shape[0]
-        do = do.contiguous().view(T, nq, D)
-        q = qk[:, : nq * D].view(T, nq, D)
-        k = qk[:, nq * D :].view(T, nkv, D)
-        v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
+        do = _pad_head(do.contiguous().view(T, nq, D))
+        q = _pad_head(qk[:, : nq * D].view(T, nq, D))
+        k = _pad_head(qk[:, nq * D :].view(T, nkv, D))
+        v = _pad_head(qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D)))
         dqkv = torch.empty_like(qkv)
         dqk = torch.empty_like(qk)
         win = meta.window
         dq_acc, dk_acc, dv_acc, _ = C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, meta.bwd_units, scale, 0,
                                                  meta.positions if win else None, win)
-        dqk[:, : nq * D].copy_(dq_acc.view(T, nq * D))
-        dqk[:, nq * D :].copy_(dk_acc.view(T, nkv * D))
-        dqkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].copy_(dv_acc.view(T, nkv * D))
+        dqk[:, : nq * D].copy_(dq_acc[..., :D].reshape(T, nq * D))
+        dqk[:, nq * D :].copy_(dk_acc[..., :D].reshape(T, nkv * D))
+        dqkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].copy_(dv_acc[..., :D].reshape(T, nkv * D))
         C.rope_bwd(dqk, qkv, meta.positions, inv_freq, nq, nkv, D,
                    qn_w if has_norm else None, kn_w if has_norm else None,
                    rstd if has_norm else None, dqkv)

@@ -145,12 +145,15 @@ class FusedDataParallel:
             dist.all_reduce(stats, group=self.group)
         return optim.grad_norm
 
-    def gather_full_state(self, store) -> None:
-        """All-gather the master weights and moments of every shard (before a
-        checkpoint is written; cold path over NCCL)."""
+    def gather_full_state(self, store, moments: bool = True) -> None:
+        """All-gather the master weights (and, with ``moments``, the AdamW
+        moments) of every shard, before a checkpoint is written (cold path
+        over NCCL).  Without ``moments`` each rank keeps only its own moment
+        shard current and writes it itself (sharded optimizer state)."""
         per = self.shards[0][1]
         off, n = self.shards[self.rank]
-        for buf in (store.master, store.exp_avg, store.exp_avg_sq):
+        bufs = (store.master, store.exp_avg, store.exp_avg_sq) if moments else (store.master,)
+        for buf in bufs:
             mine = torch.zeros(per, dtype=buf.dtype, device=buf.device)
             mine[:n].copy_(buf[off : off + n])
             out = torch.empty(per * self.world, dtype=buf.dtype, device=buf.device)

@@ -22,7 +22,7 @@ import math
 import os
 import random
 from dataclasses import dataclass
-from typing import Any, NamedTuple, TypedDict
+from typing import Callable, Any, NamedTuple, TypedDict
 
 import numpy as np
 import torch
@@ -59,6 +59,8 @@ class PackedTensors(TypedDict):
     pixel_values: list[torch.Tensor | None]
     image_grid_thw: list[torch.Tensor | None]
     moe_routing_replay: PackedMoeRoutingReplay | None
+    # set when only some rows were filled: the step's scored-token count
+    trainable_tokens: NotRequired[int]
 
 
 class DiskPackedTensors(TypedDict):
@@ -217,6 +219,35 @@ def _same_routes(a: Any, b: Any) -> bool:
     return x.shape == y.shape and bool((np.sort(x, axis=-1) == np.sort(y, axis=-1)).all())
 
 
+def _step_normalisation(rows: list[list[_Item]], advantage_balance: float) -> tuple[float, float, int]:
+    """(weight scale, advantage scale, scored tokens) of a step from its
+    sequences: weights are divided by their mean over masked tokens, then
+    advantages by the mean of |advantage| x weight; scored tokens exclude a
+    masked token at a row's first position (it has no predecessor)."""
+    n = w = a = 0.0
+    items = []
+    first_masked = 0
+    for row in rows:
+        for k, it in enumerate(row):
+            c = float(sum(it.assistant_mask))
+            if k == 0 and it.assistant_mask and it.assistant_mask[0]:
+                first_masked += 1
+            items.append((c, it.weight, it.advantage))
+            n += c
+            w += c * it.weight
+    if n == 0:
+        return 1.0, 1.0, 0
+    mean_w = w / n
+    for c, wt, adv in items:
+        if advantage_balance > 0.0 and adv <= 0:
+            adv *= 1 - advantage_balance
+        elif advantage_balance < 0.0 and adv >= 0:
+            adv *= 1 + advantage_balance
+        a += c * abs(adv) * (wt / mean_w)
+    mean_a = a / n
+    return 1.0 / mean_w, (1.0 / mean_a if mean_a > 0 else 1.0), int(n) - first_masked
+
+
 def _padded(rows: list, seq_len: int, value: Any, dtype: torch.dtype) -> torch.Tensor:
     out = torch.full((len(rows), seq_len), value, dtype=dtype)
     for r, vals in enumerate(rows):
@@ -235,7 +266,16 @@ def packed_tensors_from_tokenized_results(
     pack_results: bool = True,
     include_moe_routing: bool = False,
     rng: random.Random | None = None,
+    rows_needed: Callable[[int], set[int]] | None = None,
 ) -> PackedTensors:
+    """Pack tokenized results into prefix-tree rows (reference
+    ``src/art/preprocessing/pack.py``).
+
+    ``rows_needed(n_rows)`` (optional) names the rows the caller will read
+    (a data-parallel rank's own rows): the others keep their place but are
+    left empty, and the weight / advantage normalisation and the step's
+    trainable-token count (``trainable_tokens``) come from the per-sequence
+    sums instead of the filled rows, so every rank sees the same values."""
     rows: list[list[_Item]] = [[]]
     # upper bound of the current row's packed length: an added sequence grows
     # the prefix tree by at most its own length, so the exact (re-planned)
@@ -262,21 +302,31 @@ def packed_tensors_from_tokenized_results(
         rows[-1].append(it)
         bound = grown
     (rng or random).shuffle(rows)
-    packed = [_pack_row(row, seq_len, pack_results) for row in rows]
+    keep = rows_needed(len(rows)) if rows_needed is not None else None
+    packed = [_pack_row(row if keep is None or r in keep else [], seq_len, pack_results)
+              for r, row in enumerate(rows)]
 
     mask = _padded([p["assistant_mask"] for p in packed], seq_len, 0, torch.bool)
     weights = _padded([p["weights"] for p in packed], seq_len, 0.0, torch.float32)
     weights = torch.where(mask, weights, torch.zeros_like(weights))
-    if mask.any():
-        weights[mask] /= weights[mask].mean()
     adv = _padded([p["advantages"] for p in packed], seq_len, 0.0, torch.float32)
     adv = torch.where(mask, adv, torch.zeros_like(adv))
     if advantage_balance > 0.0:
         adv = torch.where(adv > 0, adv, adv * (1 - advantage_balance))
     elif advantage_balance < 0.0:
         adv = torch.where(adv < 0, adv, adv * (1 + advantage_balance))
-    if mask.any():
-        adv[mask] /= (adv[mask].abs() * weights[mask]).mean()
+    trainable = None
+    if keep is None:
+        if mask.any():
+            weights[mask] /= weights[mask].mean()
+            adv[mask] /= (adv[mask].abs() * weights[mask]).mean()
+    else:
+        # the whole step's normalisation from per-sequence sums: every masked
+        # token of a sequence carries its weight and advantage, and no masked
+        # token is shared between sequences
+        w_scale, a_scale, trainable = _step_normalisation(rows, advantage_balance)
+        weights *= w_scale
+        adv *= a_scale
 
     out: PackedTensors = {
         "tokens": _padded([p["tokens"] for p in packed], seq_len, pad_token_id, torch.long),
@@ -291,6 +341,8 @@ def packed_tensors_from_tokenized_results(
         "image_grid_thw": [None] * len(packed),
         "moe_routing_replay": None,
     }
+    if trainable is not None:
+        out["trainable_tokens"] = trainable
     if include_moe_routing:
         replay = tensorize_routes([p["routes"] for p in packed], seq_len)
         replay.shared_route_tokens = sum(p["route_stats"][0] for p in packed)

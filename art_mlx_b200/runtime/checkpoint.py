@@ -7,7 +7,10 @@ Format (what the rollout server loads, reference
 ``checkpoints/{step:04d}/adapter_model.safetensors`` — PEFT keys
 ``base_model.model.model.layers.{i}.self_attn.q_proj.lora_A.weight`` ...
 ``checkpoints/{step:04d}/adapter_config.json`` — PEFT ``LoraConfig``.
-``checkpoints/{step:04d}/optimizer.pt`` — AdamW moments and step (resume).
+``checkpoints/{step:04d}/optimizer.pt`` — AdamW moments and step (resume);
+with the sharded data-parallel optimizer instead one
+``optimizer-shard-{rank:02d}-of-{world:02d}.pt`` per rank (its slice of the
+flat moments, with the slice's offset), assembled again on load.
 
 A checkpoint is written into a staging directory and renamed into place, so
 readers never observe a partial checkpoint (reference
@@ -99,9 +102,37 @@ def save_adapter(
 
 
 def _write_optimizer(path: str, optimizer_state: dict) -> None:
-    tmp = os.path.join(path, f".optimizer-{uuid.uuid4().hex[:8]}.tmp")
-    torch.save(optimizer_state, tmp)
-    os.replace(tmp, os.path.join(path, "optimizer.pt"))
+    _write_file(path, "optimizer.pt", optimizer_state)
+
+
+def _write_file(path: str, name: str, obj: dict) -> None:
+    tmp = os.path.join(path, f".{name}-{uuid.uuid4().hex[:8]}.tmp")
+    torch.save(obj, tmp)
+    os.replace(tmp, os.path.join(path, name))
+
+
+def load_optimizer_state(path: str) -> dict | None:
+    """The checkpoint's AdamW state: ``optimizer.pt``, or the per-rank shard
+    files assembled into full flat moments (``None`` if absent or if a shard
+    of the set is missing)."""
+    full = os.path.join(path, "optimizer.pt")
+    if os.path.exists(full):
+        return torch.load(full, map_location="cpu")
+    names = sorted(n for n in os.listdir(path) if n.startswith("optimizer-shard-") and n.endswith(".pt"))
+    if not names:
+        return None
+    shards = [torch.load(os.path.join(path, n), map_location="cpu") for n in names]
+    world = int(shards[0]["world"])
+    if len(shards) != world or sorted(int(x["rank"]) for x in shards) != list(range(world)):
+        return None  # an incomplete set (a writer did not finish): no moments
+    total = int(shards[0]["total"])
+    ea = torch.zeros(total, dtype=torch.float32)
+    eq = torch.zeros(total, dtype=torch.float32)
+    for x in shards:
+        o, n = int(x["offset"]), int(x["numel"])
+        ea[o : o + n] = x["exp_avg"]
+        eq[o : o + n] = x["exp_avg_sq"]
+    return {"exp_avg": ea, "exp_avg_sq": eq, "step": int(shards[0]["step"])}
 
 
 class _PinnedSlot:
@@ -202,6 +233,23 @@ class AsyncCheckpointWriter:
             self._pending.append(fut)
         return path
 
+    def submit_optimizer_shard(self, path: str, store: LoRAStore, offset: int, numel: int, rank: int,
+                               world: int) -> None:
+        """Write this rank's slice of the AdamW moments into the published
+        checkpoint ``path`` (one device-to-host copy of the slice, the file
+        written on the background thread)."""
+        cuda = store.master.device.type == "cuda"
+        mk = lambda: torch.empty(numel, dtype=torch.float32, pin_memory=cuda)  # noqa: E731
+        ea, eq = mk(), mk()
+        ea.copy_(store.exp_avg[offset : offset + numel], non_blocking=cuda)
+        eq.copy_(store.exp_avg_sq[offset : offset + numel], non_blocking=cuda)
+        if cuda:
+            torch.cuda.current_stream(store.master.device).synchronize()
+        shard = {"offset": offset, "numel": numel, "total": store.numel, "exp_avg": ea, "exp_avg_sq": eq,
+                 "step": store.step, "rank": rank, "world": world}
+        name = f"optimizer-shard-{rank:02d}-of-{world:02d}.pt"
+        self._pending.append(self._pool.submit(_write_file, path, name, shard))
+
     def wait(self) -> None:
         pending, self._pending = self._pending, []
         for f in pending:
@@ -216,8 +264,7 @@ def load_adapter(path: str, store: LoRAStore, strict: bool = True) -> dict | Non
     """Load adapter weights (and return the optimizer state if present)."""
     sd = load_file(os.path.join(path, "adapter_model.safetensors"))
     store.load_state_dict(sd, strict=strict)
-    opt = os.path.join(path, "optimizer.pt")
-    return torch.load(opt, map_location="cpu") if os.path.exists(opt) else None
+    return load_optimizer_state(path)
 
 
 def load_adapter_config(path: str) -> dict[str, Any]:

@@ -374,12 +374,23 @@ class GRPOTrainer:
         self.logprob_chunk = logprob_chunk
         self.ref_flat: torch.Tensor | None = None  # KL reference adapter (compute dtype)
 
-    def prepare_checkpoint(self) -> None:
-        """Collective: make the full master weights / moments current on every
-        rank (with the fused data-parallel optimizer each rank updates only its
-        shard).  Every rank must call it before rank 0 writes a checkpoint."""
+    def prepare_checkpoint(self, moments: bool = True) -> None:
+        """Collective: make the full master weights (and, with ``moments``,
+        the AdamW moments) current on every rank (with the fused data-parallel
+        optimizer each rank updates only its shard).  Every rank must call it
+        before rank 0 writes a checkpoint.  With ``moments=False`` the moments
+        stay sharded: each rank then writes its own shard
+        (:meth:`optimizer_shard`)."""
         if self.grad_sync is not None:
-            self.grad_sync.gather_full_state(self.store)
+            self.grad_sync.gather_full_state(self.store, moments)
+
+    def optimizer_shard(self) -> tuple[int, int, int, int] | None:
+        """``(offset, numel, rank, world)`` of the optimizer-state shard this
+        rank owns under the fused data-parallel optimizer (else ``None``)."""
+        if self.grad_sync is None:
+            return None
+        off, n = self.grad_sync.shards[self.grad_sync.rank]
+        return off, n, self.grad_sync.rank, self.grad_sync.world
 
     def offload(self) -> int:
         """Move the model, LoRA store and optimizer state to pinned host
@@ -535,6 +546,17 @@ class GRPOTrainer:
             "kl": kl.detach() if torch.is_tensor(kl) else lp.new_tensor(float(kl)),
         }
 
+    def rows_needed(self, n_rows: int) -> set[int]:
+        """Rows of a step of ``n_rows`` packed rows that this rank stages
+        (:meth:`stage`): a packer may materialize only these."""
+        shard = self.tp_size * self.cp_size
+        dp_world = self.world // shard
+        dp_rank = self.rank // shard
+        rows = set(range(n_rows)[dp_rank::dp_world])
+        if (self.ep is not None or self.etp is not None) and n_rows:
+            rows.add(dp_rank % n_rows)  # the zero-weight copy of a short rank
+        return rows
+
     def stage(self, packed: Mapping[str, Any]) -> list[MicroBatch]:
         """Stage this rank's rows of ``packed`` on the device.
 
@@ -581,7 +603,9 @@ class GRPOTrainer:
         """
         cfg = dict(cfg or {})
         mask = packed["assistant_mask"]
-        total = float(mask[:, 1:].sum().item())  # trainable (scored) tokens of the whole step
+        # trainable (scored) tokens of the whole step (a packer that filled
+        # only this rank's rows states the step's count itself)
+        total = float(packed["trainable_tokens"]) if "trainable_tokens" in packed else float(mask[:, 1:].sum().item())
         if micro_batches is None:
             micro_batches = self.stage(packed)
         if mutation.active("dp_local_token_normalization"):

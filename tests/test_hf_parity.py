@@ -34,6 +34,16 @@ def _tiny(kind: str):
                                            decoder_sparse_step=1, mlp_only_layers=[], **common)
     if kind == "llama":
         return transformers.LlamaConfig(intermediate_size=96, head_dim=16, **common)
+    if kind == "gpt_oss":
+        # sinks, a sliding window on alternate layers (shorter than the
+        # sequence), biases everywhere, clamped GLU experts, YaRN RoPE
+        c = dict(common, num_hidden_layers=4, rope_theta=150000.0)
+        return transformers.GptOssConfig(
+            intermediate_size=48, head_dim=16, num_local_experts=4, num_experts_per_tok=2, sliding_window=8,
+            layer_types=["sliding_attention", "full_attention"] * 2,
+            rope_parameters={"rope_type": "yarn", "factor": 4.0, "beta_fast": 32.0, "beta_slow": 1.0,
+                             "truncate": False, "original_max_position_embeddings": 64, "rope_theta": 150000.0},
+            **{k: v for k, v in c.items() if k != "rope_theta"})
     raise KeyError(kind)
 
 
@@ -49,15 +59,17 @@ def _logits_ours(path: str, tokens: torch.Tensor) -> torch.Tensor:
     return h.float() @ m.lm_head.float().t()
 
 
-@pytest.mark.parametrize("kind", ["qwen2", "qwen3", "qwen3_moe", "llama"])
+@pytest.mark.parametrize("kind", ["qwen2", "qwen3", "qwen3_moe", "llama", "gpt_oss"])
 def test_logits_match_transformers(kind, tmp_path):
     torch.manual_seed(0)
     hf_cfg = _tiny(kind)
     model = transformers.AutoModelForCausalLM.from_config(hf_cfg).float().eval()
-    with torch.no_grad():  # non-trivial norm weights (HF initialises them to 1)
+    with torch.no_grad():  # non-trivial norm weights, biases and sinks (HF initialises them to 1 / 0)
         for name, p in model.named_parameters():
-            if "norm" in name:
+            if "norm" in name or "bias" in name or "sinks" in name:
                 p.add_(0.1 * torch.randn_like(p))
+            if kind == "gpt_oss" and "experts" in name and "bias" not in name:
+                p.normal_(0, 0.5)  # large enough that the GLU clamp (limit 7) is active somewhere
     model.save_pretrained(tmp_path)
     tokens = torch.randint(0, hf_cfg.vocab_size, (37,))
     with torch.no_grad():
