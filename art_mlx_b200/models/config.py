@@ -63,6 +63,12 @@ class ModelConfig:
     expert_act: str = "swiglu"  # or "clamped_glu"
     glu_alpha: float = 1.702
     glu_limit: float = 7.0
+    # Qwen3-Next / Qwen3.5: RoPE on the first rotary_dim dims of a head only
+    # (0: all), RMSNorm weights stored as offsets from one, gated DeltaNet
+    # projections stored split (in_proj_qkv / z / b / a) instead of grouped
+    rotary_dim: int = 0
+    norm_zero_centered: bool = False
+    gdn_split_proj: bool = False
 
     @property
     def is_moe(self) -> bool:
@@ -102,6 +108,9 @@ class ModelConfig:
         # the family is the checkpoint's own model_type: an architecture the
         # registry does not know is refused there, never trained as another one
         family = str(d["model_type"])
+        if isinstance(d.get("text_config"), dict):  # multimodal wrappers: the language model's config
+            d = {**d["text_config"], "model_type": d["text_config"].get("model_type", family)}
+            family = str(d["model_type"])
         heads = d["num_attention_heads"]
         # transformers 5 nests the RoPE base and scaling in rope_parameters;
         # hub checkpoints keep rope_theta / rope_scaling at the top level
@@ -111,9 +120,13 @@ class ModelConfig:
         scaling = {k: v for k, v in {**rp, **rs}.items() if k != "rope_theta"}
         if (scaling.get("rope_type") or scaling.get("type") or "default") == "default":
             scaling = {}
+        family = {"qwen3_5_text": "qwen3_5", "qwen3_5_moe_text": "qwen3_5_moe"}.get(family, family)
         num_experts = d.get("num_experts", d.get("num_local_experts", 0)) or 0
         gpt_oss = family == "gpt_oss"
+        hybrid = family in ("qwen3_next", "qwen3_5", "qwen3_5_moe")
         layer_types = tuple(d.get("layer_types") or ())
+        prf = float(d.get("partial_rotary_factor", rp.get("partial_rotary_factor", 1.0)) or 1.0)
+        head_dim = d.get("head_dim") or d["hidden_size"] // heads
         return cls(
             name=name,
             family=family,  # type: ignore[arg-type]
@@ -122,13 +135,13 @@ class ModelConfig:
             num_hidden_layers=d["num_hidden_layers"],
             num_attention_heads=heads,
             num_key_value_heads=d.get("num_key_value_heads", heads),
-            head_dim=d.get("head_dim") or d["hidden_size"] // heads,
+            head_dim=head_dim,
             intermediate_size=d.get("intermediate_size", 0),
             rms_norm_eps=d.get("rms_norm_eps", 1e-6),
             rope_theta=float(theta),
             rope_scaling=tuple(sorted((k, v) for k, v in scaling.items() if not isinstance(v, (list, dict)))),
             attention_bias=family == "qwen2" or d.get("attention_bias", False),
-            qk_norm=family in ("qwen3", "qwen3_moe", "qwen3_next"),
+            qk_norm=family in ("qwen3", "qwen3_moe") or hybrid,
             tie_word_embeddings=d.get("tie_word_embeddings", False),
             num_experts=num_experts,
             num_experts_per_tok=d.get("num_experts_per_tok", 0),
@@ -150,6 +163,10 @@ class ModelConfig:
             expert_act="clamped_glu" if gpt_oss else "swiglu",
             glu_alpha=float(d.get("swiglu_alpha", 1.702)) if gpt_oss else 1.702,
             glu_limit=float(d.get("swiglu_limit", 7.0)) if gpt_oss else 7.0,
+            attn_output_gate=hybrid and bool(d.get("attn_output_gate", True)),
+            rotary_dim=int(head_dim * prf) if prf < 1.0 else 0,
+            norm_zero_centered=hybrid,
+            gdn_split_proj=family in ("qwen3_5", "qwen3_5_moe"),
         )
 
 

@@ -52,7 +52,14 @@ def gdn_lora_specs(cfg: ModelConfig, i: int, spec: LoRASpec) -> list[tuple[str, 
     vd = cfg.linear_num_value_heads * cfg.linear_value_head_dim
     t = set(spec.target_modules)
     out: list[tuple[str, tuple[int, ...], str]] = []
-    if t & {"q_proj", "k_proj", "v_proj", "in_proj_qkvz"}:
+    if cfg.gdn_split_proj:  # Qwen3.5: in_proj_qkv and in_proj_z are separate modules (adapter keys too)
+        sel = [(p, o) for p, o in (("in_proj_qkv", 2 * kd + vd), ("in_proj_z", vd))
+               if p in t or t & {"q_proj", "k_proj", "v_proj"}]
+        for p, _ in sel:
+            out.append((peft_key(i, "linear_attn", p, "A"), (r, H), "A"))
+        for p, o in sel:
+            out.append((peft_key(i, "linear_attn", p, "B"), (o, r), "B"))
+    elif t & {"q_proj", "k_proj", "v_proj", "in_proj_qkvz"}:
         out.append((peft_key(i, "linear_attn", "in_proj_qkvz", "A"), (r, H), "A"))
         out.append((peft_key(i, "linear_attn", "in_proj_qkvz", "B"), (2 * kd + 2 * vd, r), "B"))
     if t & {"o_proj", "out_proj"}:
@@ -269,11 +276,37 @@ class GatedDeltaNet:
         self.A_log = torch.log(torch.arange(1, self.nv + 1, device=dev, dtype=torch.float32))
         self.norm_w = torch.ones(self.dv, device=dev, dtype=dt)
         self.out_w = _randn((H, vd), gen, dev, dt)
-        self.qkvz_lora = make_binding(store, i, "linear_attn", [("in_proj_qkvz", 2 * kd + 2 * vd)], spec)
+        projs = ([("in_proj_qkv", 2 * kd + vd), ("in_proj_z", vd)] if cfg.gdn_split_proj
+                 else [("in_proj_qkvz", 2 * kd + 2 * vd)])
+        self.qkvz_lora = make_binding(store, i, "linear_attn", projs, spec)
         self.out_lora = make_binding(store, i, "linear_attn", [("out_proj", H)], spec)
 
     def num_parameters(self) -> int:
         return sum(t.numel() for t in (self.qkvz_w, self.ba_w, self.conv_w, self.out_w, self.norm_w))
+
+    def load_hf(self, sd: dict[str, torch.Tensor], prefix: str, g) -> None:
+        """Hugging Face weights into the [q | k | v | z] and [b | a] layouts:
+        Qwen3.5 stores the projections split (``in_proj_qkv``, ``in_proj_z``,
+        ``in_proj_b``, ``in_proj_a``), Qwen3-Next grouped per key head
+        (``in_proj_qkvz`` rows ``[q | k | v_group | z_group]`` per key head,
+        ``in_proj_ba`` rows ``[b_group | a_group]``)."""
+        nk, nv, dk, dv, H = self.nk, self.nv, self.dk, self.dv, self.cfg.hidden_size
+        rep = nv // nk
+        if prefix + "in_proj_qkv.weight" in sd:
+            self.qkvz_w.copy_(torch.cat([g(prefix + "in_proj_qkv.weight"), g(prefix + "in_proj_z.weight")]))
+            self.ba_w.copy_(torch.cat([g(prefix + "in_proj_b.weight"), g(prefix + "in_proj_a.weight")]))
+        else:
+            w = g(prefix + "in_proj_qkvz.weight").view(nk, 2 * dk + 2 * rep * dv, H)
+            q, k = w[:, :dk], w[:, dk : 2 * dk]
+            v, z = w[:, 2 * dk : 2 * dk + rep * dv], w[:, 2 * dk + rep * dv :]
+            self.qkvz_w.copy_(torch.cat([t.reshape(-1, H) for t in (q, k, v, z)]))
+            ba = g(prefix + "in_proj_ba.weight").view(nk, 2 * rep, H)
+            self.ba_w.copy_(torch.cat([ba[:, :rep].reshape(nv, H), ba[:, rep:].reshape(nv, H)]))
+        self.conv_w.copy_(g(prefix + "conv1d.weight").reshape(self.conv_w.shape))
+        self.dt_bias.copy_(sd[prefix + "dt_bias"].to(self.dt_bias.device, torch.float32))
+        self.A_log.copy_(sd[prefix + "A_log"].to(self.A_log.device, torch.float32))
+        self.norm_w.copy_(g(prefix + "norm.weight"))
+        self.out_w.copy_(g(prefix + "out_proj.weight"))
 
     def mix(self, h: torch.Tensor, version: int, enabled: bool):
         """Projections + conv inputs: returns (qkv_pre_conv, z, g, beta)."""
@@ -299,8 +332,10 @@ class GatedDeltaNet:
         q = x[:, :kd].view(T, self.nk, self.dk)
         k = x[:, kd : 2 * kd].view(T, self.nk, self.dk)
         v = x[:, 2 * kd :].view(T, self.nv, self.dv)
-        q = torch.nn.functional.normalize(q, dim=-1) / math.sqrt(self.dk)
-        k = torch.nn.functional.normalize(k, dim=-1)
+        # L2 normalisation with the eps inside the root (x / sqrt(|x|^2 + 1e-6)),
+        # as the published gated-DeltaNet kernels and Qwen3-Next do
+        q = q * torch.rsqrt(q.float().pow(2).sum(-1, keepdim=True) + 1e-6).to(q.dtype) / math.sqrt(self.dk)
+        k = k * torch.rsqrt(k.float().pow(2).sum(-1, keepdim=True) + 1e-6).to(k.dtype)
         return q, k, v
 
     def expand_heads(self, q, k):

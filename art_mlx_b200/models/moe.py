@@ -587,6 +587,11 @@ class MoEBlock:
                 self.params.down_b.copy_(g(prefix + "experts.down_proj_bias")[es])
             return
         self.router_w.copy_(g(prefix + "gate.weight"))
+        if self.shared is not None and prefix + "shared_expert.gate_proj.weight" in sd:
+            gu_w, down_w, gate_w = self.shared
+            gu_w.copy_(torch.cat([g(prefix + "shared_expert.gate_proj.weight"), g(prefix + "shared_expert.up_proj.weight")]))
+            down_w.copy_(g(prefix + "shared_expert.down_proj.weight"))
+            gate_w.copy_(g(prefix + "shared_expert_gate.weight"))
         for le in range(self.gu_w_t.shape[0]):
             p = f"{prefix}experts.{e0 + le}."
             self.gu_w_t[le].copy_(torch.cat([g(p + "gate_proj.weight")[fs], g(p + "up_proj.weight")[fs]]).t())

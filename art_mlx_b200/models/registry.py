@@ -42,6 +42,14 @@ for _spec in (
                      supports=frozenset({"dp", "ep", "cp", "generate"})),
     ModelSupportSpec("qwen3_next", ("qwen3_next",), _DENSE + ("in_proj_qkvz", "out_proj"), is_moe=True,
                      linear_attention=True, supports=frozenset({"dp", "ep", "cp"})),
+    # Qwen3.5 (reference model_support/handlers/qwen3_5.py): the Qwen3-Next
+    # hybrid with split gated-DeltaNet projections; dense and MoE variants
+    ModelSupportSpec("qwen3_5", ("qwen3_5", "qwen3_5_text"),
+                     _DENSE + ("in_proj_qkv", "in_proj_z", "out_proj"), linear_attention=True,
+                     supports=frozenset({"dp", "cp"})),
+    ModelSupportSpec("qwen3_5_moe", ("qwen3_5_moe", "qwen3_5_moe_text"),
+                     _DENSE + ("in_proj_qkv", "in_proj_z", "out_proj"), is_moe=True, linear_attention=True,
+                     supports=frozenset({"dp", "ep", "cp"})),
     # the default dense decoder (reference: model_support/handlers/default_dense.py): Llama-style
     # checkpoints run through the same layers (no q/k norm, optional q/k/v bias, RoPE scaling)
     ModelSupportSpec("llama", ("llama",), _DENSE, supports=frozenset({"dp", "tp", "cp", "generate"})),

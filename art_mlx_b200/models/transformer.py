@@ -173,7 +173,13 @@ class DecoderLM:
         self.embed = _randn((V, H), gen, dev, dt)
         self.final_norm = torch.ones(H, device=dev, dtype=dt)
         self.lm_head = self.embed if cfg.tie_word_embeddings else _randn((V, H), gen, dev, dt)
-        self.inv_freq = fused.rope_inv_freq(cfg.head_dim, cfg.rope_theta, dev, dict(cfg.rope_scaling))
+        self.rope_perm = None
+        if cfg.rotary_dim and cfg.rotary_dim < cfg.head_dim:  # partial rotary (Qwen3-Next / Qwen3.5)
+            self.inv_freq, perm = fused.partial_rotary(cfg.head_dim, cfg.rotary_dim, cfg.rope_theta, dev,
+                                                       dict(cfg.rope_scaling))
+            self.rope_perm = perm.to(torch.int16)
+        else:
+            self.inv_freq = fused.rope_inv_freq(cfg.head_dim, cfg.rope_theta, dev, dict(cfg.rope_scaling))
         # a RoPE that scales cos / sin (YaRN) scales q and k: the scores carry its square
         self.attn_scale = fused.rope_attention_factor(dict(cfg.rope_scaling)) ** 2 / math.sqrt(cfg.head_dim)
         self.layers: list[Layer] = []
@@ -246,11 +252,11 @@ class DecoderLM:
             from ..parallel.cp import cp_rope_attention
 
             o = cp_rope_attention(qkv, ctx["cp_plan"], ctx["cp"], self.inv_freq, nq, nkv, D,
-                                  layer.q_norm, layer.k_norm, cfg.rms_norm_eps)
+                                  layer.q_norm, layer.k_norm, cfg.rms_norm_eps, self.rope_perm, self.attn_scale)
         else:
             o = fused.rope_attention(
                 qkv, meta.windowed(layer.window), self.inv_freq, nq, nkv, D, layer.q_norm, layer.k_norm,
-                cfg.rms_norm_eps, sinks=layer.sinks, scale=self.attn_scale,
+                cfg.rms_norm_eps, sinks=layer.sinks, scale=self.attn_scale, perm=self.rope_perm,
             )
         if gate is not None:
             o = o * torch.sigmoid(gate)
@@ -339,23 +345,30 @@ class DecoderLM:
         """Copy Hugging Face weights (``model.layers.{i}.self_attn.q_proj.weight``
         etc.) into the fused layout."""
         cfg = self.cfg
+        if "model.embed_tokens.weight" not in sd and "model.language_model.embed_tokens.weight" in sd:
+            # multimodal checkpoints (Qwen3.5): the language model under model.language_model.
+            pre = "model.language_model."
+            sd = {("model." + k[len(pre):]) if k.startswith(pre) else k: v for k, v in sd.items()}
         g = lambda k: sd[k].to(device=self.device, dtype=self.dtype)  # noqa: E731
+        # Qwen3-Next / Qwen3.5 store RMSNorm weights as offsets from one
+        nz = (lambda k: sd[k].to(device=self.device, dtype=torch.float32).add(1.0).to(self.dtype)) \
+            if cfg.norm_zero_centered else g
         self.embed.copy_(g("model.embed_tokens.weight"))
-        self.final_norm.copy_(g("model.norm.weight"))
+        self.final_norm.copy_(nz("model.norm.weight"))
         if not cfg.tie_word_embeddings and "lm_head.weight" in sd:
             self.lm_head.copy_(g("lm_head.weight"))
         for i, layer in enumerate(self.layers):
             p = f"model.layers.{i}."
-            layer.in_norm.copy_(g(p + "input_layernorm.weight"))
-            layer.post_norm.copy_(g(p + "post_attention_layernorm.weight"))
+            layer.in_norm.copy_(nz(p + "input_layernorm.weight"))
+            layer.post_norm.copy_(nz(p + "post_attention_layernorm.weight"))
             if layer.kind == "attention":
                 a = p + "self_attn."
                 layer.qkv_w.copy_(torch.cat([g(a + "q_proj.weight"), g(a + "k_proj.weight"), g(a + "v_proj.weight")]))
                 if layer.qkv_b is not None:
                     layer.qkv_b.copy_(torch.cat([g(a + "q_proj.bias"), g(a + "k_proj.bias"), g(a + "v_proj.bias")]))
                 if layer.q_norm is not None:
-                    layer.q_norm.copy_(g(a + "q_norm.weight"))
-                    layer.k_norm.copy_(g(a + "k_norm.weight"))
+                    layer.q_norm.copy_(nz(a + "q_norm.weight"))
+                    layer.k_norm.copy_(nz(a + "k_norm.weight"))
                 layer.o_w.copy_(g(a + "o_proj.weight"))
                 if layer.o_b is not None:
                     layer.o_b.copy_(g(a + "o_proj.bias"))
@@ -367,3 +380,5 @@ class DecoderLM:
                 layer.mlp.down_w.copy_(g(m + "down_proj.weight"))
             if layer.moe is not None:
                 layer.moe.load_hf(sd, p + "mlp.", g)
+            if layer.gdn is not None:
+                layer.gdn.load_hf(sd, p + "linear_attn.", g)

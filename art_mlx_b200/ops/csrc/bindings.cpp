@@ -27,11 +27,12 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor xs, torch::Tensor w, t
 std::vector<torch::Tensor> rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
                                     int64_t nq, int64_t nkv, int64_t D,
                                     c10::optional<torch::Tensor> qn_w,
-                                    c10::optional<torch::Tensor> kn_w, double eps);
+                                    c10::optional<torch::Tensor> kn_w, double eps,
+                                    c10::optional<torch::Tensor> perm);
 void rope_bwd(torch::Tensor dqk, torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
               int64_t nq, int64_t nkv, int64_t D, c10::optional<torch::Tensor> qn_w,
               c10::optional<torch::Tensor> kn_w, c10::optional<torch::Tensor> rstd,
-              torch::Tensor dqkv);
+              torch::Tensor dqkv, c10::optional<torch::Tensor> perm);
 torch::Tensor swiglu_fwd(torch::Tensor gu);
 torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu);
 std::vector<torch::Tensor> logits_stats(torch::Tensor logits, torch::Tensor targets, bool entropy);
@@ -122,8 +123,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("legacy") = false);
   m.def("rmsnorm_bwd", &art::rmsnorm_bwd, py::arg("dy"), py::arg("xs"), py::arg("w"), py::arg("rstd"),
         py::arg("dres"), py::arg("legacy") = false);
-  m.def("rope_fwd", &art::rope_fwd);
-  m.def("rope_bwd", &art::rope_bwd);
+  m.def("rope_fwd", &art::rope_fwd, py::arg("qkv"), py::arg("pos"), py::arg("inv_freq"), py::arg("nq"),
+        py::arg("nkv"), py::arg("D"), py::arg("qn_w"), py::arg("kn_w"), py::arg("eps"), py::arg("perm") = py::none());
+  m.def("rope_bwd", &art::rope_bwd, py::arg("dqk"), py::arg("qkv"), py::arg("pos"), py::arg("inv_freq"),
+        py::arg("nq"), py::arg("nkv"), py::arg("D"), py::arg("qn_w"), py::arg("kn_w"), py::arg("rstd"),
+        py::arg("dqkv"), py::arg("perm") = py::none());
   m.def("swiglu_fwd", &art::swiglu_fwd);
   m.def("swiglu_bwd", &art::swiglu_bwd);
   m.def("logits_stats", &art::logits_stats);

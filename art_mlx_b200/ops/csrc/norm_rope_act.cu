@@ -343,8 +343,12 @@ __global__ void rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t l
                                 const __nv_bfloat16* __restrict__ qn_w,
                                 const __nv_bfloat16* __restrict__ kn_w,
                                 __nv_bfloat16* __restrict__ out, float* __restrict__ rstd_out,
-                                int64_t T, int nq, int nkv, float eps) {
+                                int64_t T, int nq, int nkv, float eps, const short* __restrict__ perm) {
   constexpr int PER = D / 32;  // elements per lane; lane owns pairs (i, i + D/2)
+  // perm (optional): column of the head that internal element i is read from
+  // (partial rotary: the rotated dims and their partners moved to the pair
+  // layout, the rest paired with zero frequencies); out keeps internal order
+#define ART_P(i) (perm ? (int)__ldg(perm + (i)) : (i))
   const int nh = nq + nkv;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x / 32);
   const int lane = threadIdx.x & 31;
@@ -358,8 +362,8 @@ __global__ void rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t l
   float a[PER / 2], b[PER / 2];
 #pragma unroll
   for (int k = 0; k < PER / 2; ++k) {
-    a[k] = bf2f(src[lane * (PER / 2) + k]);
-    b[k] = bf2f(src[D / 2 + lane * (PER / 2) + k]);
+    a[k] = bf2f(src[ART_P(lane * (PER / 2) + k)]);
+    b[k] = bf2f(src[ART_P(D / 2 + lane * (PER / 2) + k)]);
   }
   float r = 1.f;
   if (nw) {
@@ -371,8 +375,8 @@ __global__ void rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t l
 #pragma unroll
     for (int k = 0; k < PER / 2; ++k) {
       const int i = lane * (PER / 2) + k;
-      a[k] = bf2f(f2bf(a[k] * r)) * bf2f(nw[i]);
-      b[k] = bf2f(f2bf(b[k] * r)) * bf2f(nw[i + D / 2]);
+      a[k] = bf2f(f2bf(a[k] * r)) * bf2f(nw[ART_P(i)]);
+      b[k] = bf2f(f2bf(b[k] * r)) * bf2f(nw[ART_P(i + D / 2)]);
       a[k] = bf2f(f2bf(a[k]));
       b[k] = bf2f(f2bf(b[k]));
     }
@@ -399,7 +403,7 @@ __global__ void rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqk,
                                 const __nv_bfloat16* __restrict__ qn_w,
                                 const __nv_bfloat16* __restrict__ kn_w,
                                 const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dqkv,
-                                int64_t T, int nq, int nkv) {
+                                int64_t T, int nq, int nkv, const short* __restrict__ perm) {
   constexpr int PER = D / 32;
   const int nh = nq + nkv;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x / 32);
@@ -431,28 +435,29 @@ __global__ void rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqk,
 #pragma unroll
     for (int k = 0; k < PER / 2; ++k) {
       const int i = lane * (PER / 2) + k;
-      xa[k] = bf2f(src[i]) * r;
-      xb[k] = bf2f(src[i + D / 2]) * r;
-      ga[k] *= bf2f(nw[i]);
-      gb[k] *= bf2f(nw[i + D / 2]);
+      xa[k] = bf2f(src[ART_P(i)]) * r;
+      xb[k] = bf2f(src[ART_P(i + D / 2)]) * r;
+      ga[k] *= bf2f(nw[ART_P(i)]);
+      gb[k] *= bf2f(nw[ART_P(i + D / 2)]);
       dot += ga[k] * xa[k] + gb[k] * xb[k];
     }
     const float mean = warp_sum(dot) / D;
 #pragma unroll
     for (int k = 0; k < PER / 2; ++k) {
       const int i = lane * (PER / 2) + k;
-      dst[i] = f2bf(r * (ga[k] - xa[k] * mean));
-      dst[i + D / 2] = f2bf(r * (gb[k] - xb[k] * mean));
+      dst[ART_P(i)] = f2bf(r * (ga[k] - xa[k] * mean));
+      dst[ART_P(i + D / 2)] = f2bf(r * (gb[k] - xb[k] * mean));
     }
   } else {
 #pragma unroll
     for (int k = 0; k < PER / 2; ++k) {
       const int i = lane * (PER / 2) + k;
-      dst[i] = f2bf(ga[k]);
-      dst[i + D / 2] = f2bf(gb[k]);
+      dst[ART_P(i)] = f2bf(ga[k]);
+      dst[ART_P(i + D / 2)] = f2bf(gb[k]);
     }
   }
 }
+#undef ART_P
 
 #define ART_DISPATCH_HEAD_DIM(D, ...)                       \
   [&] {                                                     \
@@ -472,8 +477,13 @@ __global__ void rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqk,
 std::vector<torch::Tensor> rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
                                     int64_t nq, int64_t nkv, int64_t D,
                                     c10::optional<torch::Tensor> qn_w,
-                                    c10::optional<torch::Tensor> kn_w, double eps) {
+                                    c10::optional<torch::Tensor> kn_w, double eps,
+                                    c10::optional<torch::Tensor> perm) {
   TORCH_CHECK(qkv.stride(-1) == 1 && pos.scalar_type() == at::kInt && pos.is_contiguous());
+  if (perm.has_value())
+    TORCH_CHECK(perm->is_cuda() && perm->scalar_type() == at::kShort && perm->numel() == D && perm->is_contiguous(),
+                "perm: int16 [head_dim]");
+  const short* pp = perm.has_value() ? perm->data_ptr<short>() : nullptr;
   const int64_t T = qkv.size(0);
   const int64_t ld = qkv.stride(0);
   const int nh = nq + nkv;
@@ -491,7 +501,7 @@ std::vector<torch::Tensor> rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch:
           norm ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,
           norm ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr,
           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), norm ? rstd.data_ptr<float>() : nullptr,
-          T, (int)nq, (int)nkv, (float)eps);
+          T, (int)nq, (int)nkv, (float)eps, pp);
     });
   ART_CUDA_CHECK(cudaGetLastError());
   return {out, rstd};
@@ -500,8 +510,12 @@ std::vector<torch::Tensor> rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch:
 void rope_bwd(torch::Tensor dqk, torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
               int64_t nq, int64_t nkv, int64_t D, c10::optional<torch::Tensor> qn_w,
               c10::optional<torch::Tensor> kn_w, c10::optional<torch::Tensor> rstd,
-              torch::Tensor dqkv) {
+              torch::Tensor dqkv, c10::optional<torch::Tensor> perm) {
   TORCH_CHECK(dqk.is_contiguous() && dqkv.stride(-1) == 1 && dqkv.stride(0) == qkv.stride(0));
+  if (perm.has_value())
+    TORCH_CHECK(perm->is_cuda() && perm->scalar_type() == at::kShort && perm->numel() == D && perm->is_contiguous(),
+                "perm: int16 [head_dim]");
+  const short* pp = perm.has_value() ? perm->data_ptr<short>() : nullptr;
   const int64_t T = dqk.size(0);
   const int nh = nq + nkv;
   const int64_t warps = T * nh;
@@ -517,7 +531,7 @@ void rope_bwd(torch::Tensor dqk, torch::Tensor qkv, torch::Tensor pos, torch::Te
           norm ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,
           norm ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr,
           norm ? rstd->data_ptr<float>() : nullptr,
-          reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), T, (int)nq, (int)nkv);
+          reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), T, (int)nq, (int)nkv, pp);
     });
   ART_CUDA_CHECK(cudaGetLastError());
 }

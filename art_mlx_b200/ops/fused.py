@@ -274,6 +274,31 @@ def _yarn_inv_freq(inv: torch.Tensor, head_dim: int, theta: float, sc: dict) -> 
     return inv / factor * (1 - keep) + inv * keep
 
 
+def partial_rotary(head_dim: int, rotary_dim: int, theta: float, device: torch.device,
+                   scaling: dict | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """RoPE on the first ``rotary_dim`` dims of each head only (rotate-half
+    within them; Qwen3-Next / Qwen3.5).  Returns the frequencies of the
+    kernels' pair layout (pair ``i`` = dims ``(i, i + head_dim/2)`` of an
+    internal order) and ``perm``: internal dim -> head column.  The rotated
+    dims and their partners take the first pairs; the untouched dims fill the
+    rest with zero frequency.  Attention reads q and k in the internal order
+    (dot products do not change when both are permuted alike); weights,
+    LoRA factors and v stay in the checkpoint's order."""
+    D, rd = head_dim, rotary_dim
+    assert rd % 2 == 0 and 0 < rd <= D
+    inv = torch.zeros(D // 2, dtype=torch.float32)
+    inv[: rd // 2] = rope_inv_freq(rd, theta, torch.device("cpu"), scaling)
+    perm = torch.empty(D, dtype=torch.int64)
+    half, rest = rd // 2, (D - rd) // 2
+    for i in range(D // 2):
+        if i < half:
+            perm[i], perm[i + D // 2] = i, i + half
+        else:
+            j = i - half
+            perm[i], perm[i + D // 2] = rd + j, rd + rest + j
+    return inv.to(device), perm.to(device)
+
+
 def rope_attention_factor(scaling: dict | None) -> float:
     """Factor by which the checkpoint's RoPE scales cos / sin (YaRN's
     ``0.1 ln(factor) + 1``, or the configured ``attention_factor``); q and k
@@ -392,10 +417,10 @@ def _pad_head(x: torch.Tensor) -> torch.Tensor:
 
 class _RopeAttention(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale, sinks):
+    def forward(ctx, qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale, sinks, perm):
         C = native.lib()
         T = qkv.shape[0]
-        qk, rstd = C.rope_fwd(qkv, meta.positions, inv_freq, nq, nkv, D, qn_w, kn_w, eps)
+        qk, rstd = C.rope_fwd(qkv, meta.positions, inv_freq, nq, nkv, D, qn_w, kn_w, eps, perm)
         q = qk[:, : nq * D].view(T, nq, D)
         k = qk[:, nq * D :].view(T, nkv, D)
         v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D))
@@ -407,6 +432,7 @@ class _RopeAttention(torch.autograd.Function):
                               kn_w if kn_w is not None else qkv.new_empty(0),
                               rstd if rstd is not None and rstd.numel() else qkv.new_empty(0, dtype=torch.float32))
         ctx.meta = meta
+        ctx.perm = perm
         ctx.dims = (nq, nkv, D, scale, qn_w is not None)
         return o[..., :D].reshape(T, nq * D)
 
@@ -431,8 +457,8 @@ class _RopeAttention(torch.autograd.Function):
         dqkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].copy_(dv_acc[..., :D].reshape(T, nkv * D))
         C.rope_bwd(dqk, qkv, meta.positions, inv_freq, nq, nkv, D,
                    qn_w if has_norm else None, kn_w if has_norm else None,
-                   rstd if has_norm else None, dqkv)
-        return dqkv, None, None, None, None, None, None, None, None, None, None
+                   rstd if has_norm else None, dqkv, ctx.perm)
+        return dqkv, None, None, None, None, None, None, None, None, None, None, None
 
 
 def rope_attention(
@@ -447,6 +473,7 @@ def rope_attention(
     eps: float,
     sinks: torch.Tensor | None = None,
     scale: float | None = None,
+    perm: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Raw QKV projection ``[T, (nq+2nkv)*D]`` -> attention output ``[T, nq*D]``.
 
@@ -456,7 +483,9 @@ def rope_attention(
     if _cuda(qkv):
         if sinks is not None:
             sinks = sinks.float().contiguous()
-        return _RopeAttention.apply(qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale, sinks)
+        if perm is not None:
+            perm = perm.to(device=qkv.device, dtype=torch.int16).contiguous()
+        return _RopeAttention.apply(qkv, meta, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale, sinks, perm)
     T = qkv.shape[0]
     q = qkv[:, : nq * D].view(T, nq, D)
     k = qkv[:, nq * D : (nq + nkv) * D].view(T, nkv, D)
@@ -465,6 +494,8 @@ def rope_attention(
         q = _rmsnorm_ref(q, qn_w, eps)
         k = _rmsnorm_ref(k, kn_w, eps)
     pos = meta.positions
+    if perm is not None:  # partial rotary: the kernels' internal dim order
+        q, k = q[..., perm.long()], k[..., perm.long()]
     q = _rope_ref(q, pos, inv_freq)
     k = _rope_ref(k, pos, inv_freq)
     o, _ = attention_ref(q, k, v, meta.kend, scale, pos, meta.window, sinks)

@@ -256,11 +256,11 @@ class CPPlan:
 
 class _CPRopeAttention(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv, plan, cp, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale):
+    def forward(ctx, qkv, plan, cp, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale, perm):
         C = native.lib()
         meta = plan.meta
         T = qkv.shape[0]
-        qk, rstd = C.rope_fwd(qkv, meta.positions, inv_freq, nq, nkv, D, qn_w, kn_w, eps)
+        qk, rstd = C.rope_fwd(qkv, meta.positions, inv_freq, nq, nkv, D, qn_w, kn_w, eps, perm)
         q = qk[:, : nq * D].view(T, nq, D)
         k_loc = qk[:, nq * D :].reshape(T, nkv, D)
         v_loc = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].reshape(T, nkv, D)
@@ -272,6 +272,7 @@ class _CPRopeAttention(torch.autograd.Function):
                               kn_w if kn_w is not None else qkv.new_empty(0),
                               rstd if rstd is not None and rstd.numel() else qkv.new_empty(0, dtype=torch.float32))
         ctx.plan, ctx.cp, ctx.dims = plan, cp, (nq, nkv, D, scale, qn_w is not None)
+        ctx.perm = perm
         return o.view(T, nq * D)
 
     @staticmethod
@@ -293,14 +294,19 @@ class _CPRopeAttention(torch.autograd.Function):
         dqk[:, nq * D :].copy_(dk.view(T, nkv * D))
         dqkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].copy_(dv.view(T, nkv * D))
         C.rope_bwd(dqk, qkv, plan.meta.positions, inv_freq, nq, nkv, D,
-                   qn_w if has_norm else None, kn_w if has_norm else None, rstd if has_norm else None, dqkv)
-        return dqkv, None, None, None, None, None, None, None, None, None, None
+                   qn_w if has_norm else None, kn_w if has_norm else None, rstd if has_norm else None, dqkv,
+                   ctx.perm)
+        return dqkv, None, None, None, None, None, None, None, None, None, None, None
 
 
-def cp_rope_attention(qkv, plan: CPPlan, cp: CPContext, inv_freq, nq, nkv, D, qn_w, kn_w, eps):
-    scale = 1.0 / math.sqrt(D)
+def cp_rope_attention(qkv, plan: CPPlan, cp: CPContext, inv_freq, nq, nkv, D, qn_w, kn_w, eps,
+                      perm=None, scale=None):
+    """``perm``: partial-rotary dim order (see ``ops.fused.partial_rotary``)."""
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
     if qkv.device.type == "cuda":
-        return _CPRopeAttention.apply(qkv, plan, cp, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale)
+        if perm is not None:
+            perm = perm.to(device=qkv.device, dtype=torch.int16).contiguous()
+        return _CPRopeAttention.apply(qkv, plan, cp, inv_freq, nq, nkv, D, qn_w, kn_w, eps, scale, perm)
     # CPU: the same exchange around the dense-mask oracle
     T = qkv.shape[0]
     q = qkv[:, : nq * D].view(T, nq, D)
@@ -310,6 +316,8 @@ def cp_rope_attention(qkv, plan: CPPlan, cp: CPContext, inv_freq, nq, nkv, D, qn
         q = fused._rmsnorm_ref(q, qn_w, eps)
         k = fused._rmsnorm_ref(k, kn_w, eps)
     pos = plan.meta.positions
+    if perm is not None:
+        q, k = q[..., perm.long()], k[..., perm.long()]
     q = fused._rope_ref(q, pos, inv_freq)
     k = fused._rope_ref(k, pos, inv_freq)
     k_full = gather(k.contiguous(), cp)

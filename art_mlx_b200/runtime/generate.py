@@ -107,15 +107,18 @@ class GenerationEngine:
         nq, nkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         T = qkv.shape[0]
         v = qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].view(T, nkv, D)
+        perm = getattr(m, "rope_perm", None)  # partial rotary: q / k in the kernels' dim order
         if qkv.is_cuda:
             qk, _ = native.lib().rope_fwd(qkv, positions, m.inv_freq, nq, nkv, D, layer.q_norm, layer.k_norm,
-                                          cfg.rms_norm_eps)
+                                          cfg.rms_norm_eps, None if perm is None else perm.to(qkv.device))
             return qk[:, : nq * D].view(T, nq, D), qk[:, nq * D :].view(T, nkv, D), v
         q = qkv[:, : nq * D].view(T, nq, D)
         k = qkv[:, nq * D : (nq + nkv) * D].view(T, nkv, D)
         if layer.q_norm is not None:
             q = fused._rmsnorm_ref(q, layer.q_norm, cfg.rms_norm_eps)
             k = fused._rmsnorm_ref(k, layer.k_norm, cfg.rms_norm_eps)
+        if perm is not None:
+            q, k = q[..., perm.long()], k[..., perm.long()]
         return fused._rope_ref(q, positions, m.inv_freq), fused._rope_ref(k, positions, m.inv_freq), v
 
     def _layers(self, tokens: torch.Tensor, positions: torch.Tensor, attend, linear=None) -> torch.Tensor:

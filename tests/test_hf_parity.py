@@ -44,6 +44,22 @@ def _tiny(kind: str):
             rope_parameters={"rope_type": "yarn", "factor": 4.0, "beta_fast": 32.0, "beta_slow": 1.0,
                              "truncate": False, "original_max_position_embeddings": 64, "rope_theta": 150000.0},
             **{k: v for k, v in c.items() if k != "rope_theta"})
+    hybrid = dict(common, num_hidden_layers=4, linear_num_key_heads=2, linear_num_value_heads=4,
+                  linear_key_head_dim=16, linear_value_head_dim=16,
+                  layer_types=["linear_attention", "linear_attention", "linear_attention", "full_attention"])
+    if kind == "qwen3_next":  # gated DeltaNet + gated attention with partial RoPE + MoE with a shared expert
+        return transformers.Qwen3NextConfig(intermediate_size=96, head_dim=16, moe_intermediate_size=32,
+                                            num_experts=4, num_experts_per_tok=2,
+                                            shared_expert_intermediate_size=32, **hybrid)
+    if kind == "qwen3_5":
+        from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
+
+        return Qwen3_5TextConfig(intermediate_size=96, head_dim=16, **hybrid)
+    if kind == "qwen3_5_moe":
+        from transformers.models.qwen3_5_moe.configuration_qwen3_5_moe import Qwen3_5MoeTextConfig
+
+        return Qwen3_5MoeTextConfig(head_dim=16, moe_intermediate_size=32, num_experts=4, num_experts_per_tok=2,
+                                    shared_expert_intermediate_size=32, **hybrid)
     raise KeyError(kind)
 
 
@@ -59,7 +75,8 @@ def _logits_ours(path: str, tokens: torch.Tensor) -> torch.Tensor:
     return h.float() @ m.lm_head.float().t()
 
 
-@pytest.mark.parametrize("kind", ["qwen2", "qwen3", "qwen3_moe", "llama", "gpt_oss"])
+@pytest.mark.parametrize("kind", ["qwen2", "qwen3", "qwen3_moe", "llama", "gpt_oss", "qwen3_next", "qwen3_5",
+                                  "qwen3_5_moe"])
 def test_logits_match_transformers(kind, tmp_path):
     torch.manual_seed(0)
     hf_cfg = _tiny(kind)
