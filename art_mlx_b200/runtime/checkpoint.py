@@ -52,6 +52,15 @@ def adapter_config(base_model: str, spec: LoRASpec, **extra: Any) -> dict[str, A
     return cfg
 
 
+def _config_for(base_model: str, spec: LoRASpec, names) -> dict[str, Any]:
+    """``adapter_config.json`` of an adapter with tensors ``names`` (MoE
+    adapters list ``experts`` among the targets, as vLLM expects)."""
+    from ..models.adapter_formats import moe_adapter_config
+
+    cfg = adapter_config(base_model, spec)
+    return moe_adapter_config(cfg) if any(".mlp.experts." in n for n in names) else cfg
+
+
 def snapshot_adapter(store: LoRAStore, optimizer_state: dict | None = None,
                      dtype: torch.dtype = torch.float32) -> tuple[dict[str, torch.Tensor], dict | None]:
     """Host copies of the adapter (and optimizer state) that later training
@@ -76,7 +85,7 @@ def write_adapter(path: str, sd: dict[str, torch.Tensor], base_model: str, spec:
     try:
         save_file(sd, os.path.join(stage, "adapter_model.safetensors"), metadata={"format": "pt"})
         with open(os.path.join(stage, "adapter_config.json"), "w") as f:
-            json.dump(adapter_config(base_model, spec), f, indent=2)
+            json.dump(_config_for(base_model, spec, sd), f, indent=2)
         if optimizer_state is not None:
             torch.save(optimizer_state, os.path.join(stage, "optimizer.pt"))
         if os.path.exists(path):
@@ -219,7 +228,7 @@ class AsyncCheckpointWriter:
             write_safetensors_from_flat(os.path.join(stage, "adapter_model.safetensors"), slot.master,
                                         store.entries)
             with open(os.path.join(stage, "adapter_config.json"), "w") as f:
-                json.dump(adapter_config(base_model, spec), f, indent=2)
+                json.dump(_config_for(base_model, spec, store.entries), f, indent=2)
             if os.path.exists(path):
                 shutil.rmtree(path)
             os.replace(stage, path)
@@ -263,6 +272,10 @@ class AsyncCheckpointWriter:
 def load_adapter(path: str, store: LoRAStore, strict: bool = True) -> dict | None:
     """Load adapter weights (and return the optimizer state if present)."""
     sd = load_file(os.path.join(path, "adapter_model.safetensors"))
+    from ..models.adapter_formats import expand_fused_moe_lora, has_fused_moe_lora
+
+    if has_fused_moe_lora(sd):  # fused expert blocks (PEFT target_parameters): per-expert keys
+        sd = expand_fused_moe_lora(sd, int(load_adapter_config(path)["r"]))
     store.load_state_dict(sd, strict=strict)
     return load_optimizer_state(path)
 
