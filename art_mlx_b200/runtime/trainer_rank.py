@@ -46,6 +46,18 @@ class ForwardInput:
     parent_ids: Sequence[int] | None = None
     positions: Sequence[int] | None = None
     entropy: bool = False
+    # extra outputs at the scored positions (reference ForwardInput.top_k /
+    # logits / hidden_states): the k most likely next tokens with their
+    # log-probabilities, the full logits, the final-normed hidden states
+    top_k: int | None = None
+    logits: bool = False
+    hidden_states: bool = False
+
+
+@dataclass(frozen=True)
+class TopK:
+    logprobs: torch.Tensor  # [n_scored, k] fp32, descending
+    tokens: torch.Tensor  # [n_scored, k] int64
 
 
 @dataclass
@@ -53,6 +65,56 @@ class ForwardOutput:
     logprobs: torch.Tensor  # [n_scored], attached to autograd
     entropy: torch.Tensor | None = None
     targets: torch.Tensor = field(default_factory=lambda: torch.empty(0, dtype=torch.long))
+    top_k: TopK | None = None
+    logits: torch.Tensor | None = None  # [n_scored, V], attached to autograd
+    hidden_states: torch.Tensor | None = None  # [n_scored, hidden], attached to autograd
+
+
+def top_k_logprobs(h: torch.Tensor, W: torch.Tensor, k: int, chunk: int = 2048) -> TopK:
+    """Top-``k`` next tokens and their log-probabilities from hidden states
+    ``h`` [n, H] and the LM head ``W`` [V, H], ``chunk`` rows of logits at a
+    time (no [n, V] tensor), in fp32 after the GEMM."""
+    n = h.shape[0]
+    lp = torch.empty(n, k, device=h.device, dtype=torch.float32)
+    tok = torch.empty(n, k, device=h.device, dtype=torch.long)
+    with torch.no_grad():
+        for s in range(0, n, chunk):
+            logits = (h[s : s + chunk] @ W.t()).float()
+            v, i = logits.topk(k, dim=-1)
+            lp[s : s + chunk] = v - torch.logsumexp(logits, dim=-1, keepdim=True)
+            tok[s : s + chunk] = i
+    return TopK(logprobs=lp, tokens=tok)
+
+
+def activation_bytes_per_token(cfg, dtype_bytes: int = 2) -> int:
+    """Activations the backward keeps per token and layer of this trainer's
+    decoder (inputs of every projection, attention output and statistics,
+    the gate/up product), summed over layers: the planner's estimate."""
+    H = cfg.hidden_size
+    F = cfg.moe_intermediate_size * cfg.num_experts_per_tok if cfg.is_moe else cfg.intermediate_size
+    per_layer = (4 * H + (cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * cfg.head_dim
+                 + cfg.num_attention_heads * cfg.head_dim + 3 * F) * dtype_bytes + 8 * cfg.num_attention_heads
+    return per_layer * cfg.num_hidden_layers
+
+
+def plan_micro_batches(token_counts: Sequence[int], budget_bytes: int, bytes_per_token: int) -> list[list[int]]:
+    """Group inputs (in order) into micro batches whose summed activation
+    estimate stays under ``budget_bytes``; an input larger than the budget
+    gets a micro batch of its own (reference ``trainer_rank`` memory-checked
+    micro batching, ``__init__.py:895-977``)."""
+    groups: list[list[int]] = []
+    cur: list[int] = []
+    used = 0
+    for i, n in enumerate(token_counts):
+        need = int(n) * bytes_per_token
+        if cur and used + need > budget_bytes:
+            groups.append(cur)
+            cur, used = [], 0
+        cur.append(i)
+        used += need
+    if cur:
+        groups.append(cur)
+    return groups
 
 
 class TrainerRank:
@@ -61,6 +123,8 @@ class TrainerRank:
         self.slots: dict[str, torch.Tensor] = {}
         self._active: str | None = None
         self._stack: list[str | None] = []
+        self.checkpoints: dict[str, dict] = {}  # trainable slots with their optimizer state
+        self._live_checkpoint: str | None = None
 
     # ------------------------------------------------------------------ slots
     def load_lora_slot(self, name: str, path: str) -> None:
@@ -156,12 +220,87 @@ class TrainerRank:
             ctx = {"group_ids": None if inp.group_ids is None else torch.tensor(list(inp.group_ids)),
                    "parent_ids": None if inp.parent_ids is None else torch.tensor(list(inp.parent_ids))}
             grad = self._active is None and torch.is_grad_enabled()
+            W = self.tr.model.lm_head
             with self._adapter(), torch.set_grad_enabled(grad):
                 h = self.tr.model.forward(toks.to(dev), meta, ctx)
-                lp, ent = fused.lm_head_logprobs(h.index_select(0, sel.to(dev)), self.tr.model.lm_head, targets,
-                                                 self.tr.logprob_chunk, inp.entropy)
-            outs.append(ForwardOutput(logprobs=lp, entropy=ent, targets=targets))
+                hs = h.index_select(0, sel.to(dev))
+                lp, ent = fused.lm_head_logprobs(hs, W, targets, self.tr.logprob_chunk, inp.entropy)
+                logits = hs @ W.t() if inp.logits else None
+            topk = top_k_logprobs(hs.detach(), W, inp.top_k) if inp.top_k else None
+            outs.append(ForwardOutput(logprobs=lp, entropy=ent, targets=targets, top_k=topk, logits=logits,
+                                      hidden_states=hs if inp.hidden_states else None))
         return outs
+
+    def forward_micro_batches(self, inputs: Sequence[ForwardInput], memory_budget_bytes: int | None = None):
+        """Yield ``(indices, outputs)`` per micro batch, sized so the kept
+        activations of one micro batch stay under ``memory_budget_bytes``
+        (default: half of the device's free memory); the caller runs its
+        loss and ``backward()`` per micro batch before the next forward."""
+        counts = [len(inp.tokens) for inp in inputs]
+        if memory_budget_bytes is None:
+            if self.tr.device.type == "cuda":
+                free, _ = torch.cuda.mem_get_info(self.tr.device)
+                memory_budget_bytes = free // 2
+            else:
+                memory_budget_bytes = 1 << 34
+        bpt = activation_bytes_per_token(self.tr.model.cfg, torch.empty(0, dtype=self.tr.model.dtype).element_size())
+        for group in plan_micro_batches(counts, memory_budget_bytes, bpt):
+            yield group, self.forward([inputs[i] for i in group])
+
+    # ------------------------------------------------------------------ checkpoint slots
+    def save_checkpoint_slot(self, name: str) -> None:
+        """Keep the live adapter and its optimizer state as a named slot
+        (reference checkpoint slots: several adapters trained in turn, each
+        with its own AdamW moments)."""
+        tr = self.tr
+        tr.prepare_checkpoint()
+        st = tr.store
+        self.checkpoints[name] = {"master": st.master.clone(), "exp_avg": st.exp_avg.clone(),
+                                  "exp_avg_sq": st.exp_avg_sq.clone(), "step": st.step}
+
+    def set_checkpoint(self, name: str) -> None:
+        """Make slot ``name`` the live, trainable adapter (the live one is
+        kept under the slot name it was last loaded from, if any)."""
+        if name not in self.checkpoints:
+            raise KeyError(f"no checkpoint slot named {name!r}")
+        if self._live_checkpoint is not None and self._live_checkpoint != name:
+            self.save_checkpoint_slot(self._live_checkpoint)
+        st, c = self.tr.store, self.checkpoints[name]
+        st.master.copy_(c["master"])
+        st.exp_avg.copy_(c["exp_avg"])
+        st.exp_avg_sq.copy_(c["exp_avg_sq"])
+        st.step = int(c["step"])
+        st.sync_compute()
+        st.grad.zero_()
+        self._live_checkpoint = name
+
+    def load_checkpoint_slot(self, name: str, path: str) -> None:
+        """A PEFT checkpoint directory (adapter + optimizer state, if present)
+        as checkpoint slot ``name``."""
+        from .checkpoint import load_adapter
+
+        st = self.tr.store
+        saved = {k: getattr(st, k).clone() for k in ("master", "exp_avg", "exp_avg_sq")}
+        step = st.step
+        try:
+            st.exp_avg.zero_()
+            st.exp_avg_sq.zero_()
+            st.step = 0
+            opt = load_adapter(path, st, strict=False)
+            if opt is not None:
+                self.tr.optim.load_state_dict(opt)
+            self.checkpoints[name] = {"master": st.master.clone(), "exp_avg": st.exp_avg.clone(),
+                                      "exp_avg_sq": st.exp_avg_sq.clone(), "step": st.step}
+        finally:
+            for k, v in saved.items():
+                getattr(st, k).copy_(v)
+            st.step = step
+
+    def checkpoint_slot_optimizer_state(self, name: str) -> dict | None:
+        c = self.checkpoints.get(name)
+        if c is None:
+            return None
+        return {"exp_avg": c["exp_avg"], "exp_avg_sq": c["exp_avg_sq"], "step": c["step"]}
 
     def zero_grad(self) -> None:
         self.tr.store.grad.zero_()

@@ -45,3 +45,42 @@ def test_custom_objective_and_slots(tmp_path):
     with rank.push_lora("base"):
         base = rank.forward(inputs[:1])[0].logprobs
     assert not torch.allclose(base, live, atol=1e-4)
+
+
+def test_extra_outputs_checkpoint_slots_and_planner(tmp_path):
+    from art_mlx_b200.runtime.trainer_rank import plan_micro_batches
+
+    torch.manual_seed(1)
+    tr = GRPOTrainer(get_config("tiny-qwen3"), LoRASpec(r=8, alpha=16), "cpu", seed=0)
+    rank = TrainerRank(tr)
+    seq = torch.randint(0, 1024, (30,)).tolist()
+    out = rank.forward([ForwardInput(tokens=seq, top_k=5, logits=True, hidden_states=True)])[0]
+    # top-k: sorted, consistent with the full logits and with the target logprob
+    logp = torch.log_softmax(out.logits.detach().float(), -1)
+    ref_v, ref_i = logp.topk(5, dim=-1)
+    assert torch.allclose(out.top_k.logprobs, ref_v, atol=1e-4) and torch.equal(out.top_k.tokens, ref_i)
+    assert torch.allclose(logp.gather(1, out.targets[:, None])[:, 0], out.logprobs.detach(), atol=1e-4)
+    assert out.hidden_states.shape == (29, tr.model.cfg.hidden_size) and out.hidden_states.requires_grad
+    # two checkpoint slots trained in turn keep separate adapters and moments
+    rank.save_checkpoint_slot("a")
+    rank.save_checkpoint_slot("b")
+    for name in ("a", "b", "a"):
+        rank.set_checkpoint(name)
+        rank.zero_grad()
+        lp = rank.forward([ForwardInput(tokens=seq)])[0].logprobs
+        (-(lp.mean() if name == "a" else -lp.mean())).backward()
+        rank.optim_step(1e-2)
+    rank.save_checkpoint_slot("a")
+    sa, sb = rank.checkpoint_slot_optimizer_state("a"), rank.checkpoint_slot_optimizer_state("b")
+    assert sa["step"] == 2 and sb["step"] == 1
+    assert not torch.allclose(rank.checkpoints["a"]["master"], rank.checkpoints["b"]["master"])
+    # a slot written to disk comes back with its optimizer state
+    rank.set_checkpoint("b")
+    rank.save_lora_slot(None, str(tmp_path / "b"))
+    rank.load_checkpoint_slot("b2", str(tmp_path / "b"))
+    assert torch.allclose(rank.checkpoints["b2"]["master"], rank.checkpoints["b"]["master"])
+    assert rank.checkpoint_slot_optimizer_state("b2")["step"] == 1
+    # planner: budget respected, order kept, oversize inputs alone
+    assert plan_micro_batches([10, 10, 10, 50, 5], 25 * 4, 4) == [[0, 1], [2], [3], [4]]
+    groups = list(rank.forward_micro_batches([ForwardInput(tokens=seq), ForwardInput(tokens=seq[:20])]))
+    assert sum(len(g) for g, _ in groups) == 2
