@@ -282,6 +282,14 @@ class DecoderLM:
         x = self.embed[tokens.clamp_min(0)]
         resid = None
         out = x
+        trace = ctx.get("trace")  # utils.trace.ForwardTraceCapture: per-layer outputs by token UID
+        uids = None
+        if trace is not None or ctx.get("token_uids") is not None:
+            uids = ctx.get("token_uids")
+            if uids is None:  # the row's global token indices (a CP rank holds a contiguous slice)
+                plan = ctx.get("cp_plan")
+                start = plan.a if plan is not None else 0
+                uids = torch.arange(start, start + tokens.shape[0])
         for layer in self.layers:
             h, resid = fused.add_rmsnorm(out, resid, layer.in_norm, eps)
             if layer.kind == "attention":
@@ -294,7 +302,12 @@ class DecoderLM:
                 a = layer.gdn(h, meta, self.store.version, self.lora_enabled, ctx)
             h, resid = fused.add_rmsnorm(a, resid, layer.post_norm, eps)
             out = self.mlp(layer, h, ctx)
+            if trace is not None:
+                trace.record(layer.index, "mixer", a, uids)
+                trace.record(layer.index, "mlp", out, uids)
         h, _ = fused.add_rmsnorm(out, resid, self.final_norm, eps)
+        if trace is not None:
+            trace.record(len(self.layers), "hidden", h, uids)
         return h
 
     # ------------------------------------------------------------------
