@@ -103,7 +103,7 @@ class MultiGPUBackend(LocalBackend):
             packed_sequence_length = rc.packed_sequence_length
         self._world = num_gpus or (torch.cuda.device_count() if dev_type == "cuda" else 2)
         topo = TopologyConfig.model_validate(topology) if isinstance(topology, dict) else topology
-        self._topology = topo or TopologyConfig(tp=1, cp=1, ep=self._world)
+        self._topology = topo  # None: the default layout policy, resolved per model
         self._packed_len = packed_sequence_length
         self._dev_type = dev_type
         self._groups: dict[str, _WorkerGroup] = {}
@@ -137,6 +137,13 @@ class MultiGPUBackend(LocalBackend):
         peft = dict(internal.get("peft_args") or {})
         peft.update(getattr(model, "lora_config", None) or {})
         topo = self._topology
+        if topo is None:  # no layout named: the default policy for this model and GPU count
+            from ..models.config import get_config
+            from ..parallel.topology import default_topology
+
+            layout = default_topology(get_config(preset), self._world,
+                                      row_tokens=self._packed_len if getattr(self, "_packed_len", None) else None)
+            topo = TopologyConfig(tp=layout["tp"], cp=layout["cp"], ep=layout["ep"])
         tp = topo.tp if topo.tp > 1 else 1
         cp = topo.cp if (topo.cp > 1 and topo.cp <= self._world and tp == 1) else 1
         etp = topo.etp if (topo.etp > 1 and self._world % topo.etp == 0) else 1

@@ -61,3 +61,47 @@ def strided_subgroup(group: dist.ProcessGroup | None, stride: int) -> dist.Proce
         if me in members:
             mine = g
     return mine
+
+
+def default_topology(cfg, world: int, row_tokens: int | None = None, gpu_bytes: int = 180 << 30,
+                     tokens_per_rank: int = 16384) -> dict[str, int]:
+    """The layout a job gets when the caller names none.
+
+    The reference puts every GPU into context parallelism (or tensor
+    parallelism for families without CP) and expert parallelism over all
+    GPUs for MoE models (``src/art/megatron/provider.py:371-385``).  On
+    180 GB B200s most LoRA jobs fit one GPU per replica, and data
+    parallelism then moves the least data per token, so the policy here is:
+
+    * MoE: expert parallelism over every GPU (the experts are the memory);
+    * the bf16 base weights plus a working margin exceed one GPU: tensor
+      parallelism over the smallest power of two that fits;
+    * packed rows longer than ``tokens_per_rank``: context parallelism over
+      the smallest power of two that brings a row slice under it (rows are
+      not split otherwise), for families whose layers support it;
+    * the remaining factor is data parallelism.
+    Returns ``{"dp", "tp", "cp", "ep", "etp"}``."""
+    from ..models.registry import get_model_support
+
+    spec = get_model_support(cfg, allow_unvalidated_arch=True)
+    H, L, V = cfg.hidden_size, cfg.num_hidden_layers, cfg.vocab_size
+    if cfg.is_moe:
+        F = cfg.moe_intermediate_size
+        mlp = 3 * H * F * cfg.num_experts + 3 * H * cfg.shared_expert_intermediate_size
+    else:
+        mlp = 3 * H * cfg.intermediate_size
+    attn = H * (cfg.q_size * (2 if cfg.attn_output_gate else 1) + 2 * cfg.kv_size) + cfg.q_size * H
+    weight_bytes = 2 * (L * (attn + mlp) + 2 * V * H)
+    tp = cp = 1
+    ep = world if cfg.is_moe else 1
+    if not cfg.is_moe:
+        while tp < world and weight_bytes / tp > 0.6 * gpu_bytes:
+            tp *= 2
+        if tp > 1 and "tp" not in spec.supports:
+            raise ValueError(f"{spec.key}: the base weights do not fit one GPU and the family has no tensor parallelism")
+    if row_tokens is not None and "cp" in spec.supports and tp == 1:
+        while cp < world and row_tokens / cp > tokens_per_rank:
+            cp *= 2
+    if world % (tp * cp):
+        raise ValueError(f"tp={tp} x cp={cp} does not divide {world} GPUs")
+    return {"dp": world // (tp * cp), "tp": tp, "cp": cp, "ep": ep, "etp": 1}

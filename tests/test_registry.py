@@ -34,3 +34,16 @@ def test_unknown_hf_model_type_is_refused(tmp_path):
     (d / "config.json").write_text(json.dumps({"vocab_size": 64}))
     with pytest.raises(ValueError, match="model_type"):
         get_config(str(d))
+
+
+def test_default_topology_policy():
+    from art_mlx_b200.models.config import get_config
+    from art_mlx_b200.parallel.topology import default_topology
+
+    # dense 7B fits one GPU: data parallel; a long row turns on context parallelism
+    assert default_topology(get_config("qwen2.5-7b"), 8) == {"dp": 8, "tp": 1, "cp": 1, "ep": 1, "etp": 1}
+    assert default_topology(get_config("qwen2.5-7b"), 8, row_tokens=65536)["cp"] == 4
+    # MoE: experts over every GPU
+    assert default_topology(get_config("qwen3-30b-a3b"), 8)["ep"] == 8
+    # a model whose bf16 weights exceed the budget of one GPU: tensor parallel
+    assert default_topology(get_config("qwen3-32b"), 8, gpu_bytes=40 << 30)["tp"] == 4
