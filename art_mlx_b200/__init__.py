@@ -40,6 +40,10 @@ def __getattr__(name: str):
         from .backends.local import LocalBackend
 
         return LocalBackend
+    if name == "ServerlessBackend":
+        from .backends.serverless import ServerlessBackend
+
+        return ServerlessBackend
     if name in ("MultiGPUBackend", "MegatronBackend"):
         from .backends.multigpu import MultiGPUBackend
 
@@ -71,6 +75,7 @@ __all__ = [
     "Model",
     "MegatronBackend",
     "MultiGPUBackend",
+    "ServerlessBackend",
     "PipelineTrainer",
     "RuntimeConfig",
     "ServerlessTrainResult",
