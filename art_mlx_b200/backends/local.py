@@ -63,7 +63,9 @@ class LocalBackend:
         trainer: GRPOTrainer | None = None,
         device: str | torch.device | None = None,
         seed: int = 0,
-        inference: Literal["none", "native"] = "none",
+        inference: Literal["none", "native", "vllm"] = "none",
+        vllm_gpus: str | None = None,
+        vllm_engine_args: dict | None = None,
     ) -> None:
         self._path = path or os.path.join(os.getcwd(), ".art")
         os.makedirs(self._path, exist_ok=True)
@@ -73,6 +75,12 @@ class LocalBackend:
         self._device = torch.device(device) if device is not None else self._default_device()
         self._seed = seed
         self._inference = inference
+        # inference="vllm": a vLLM OpenAI server (runtime/vllm_runtime.py) on the GPUs
+        # named by vllm_gpus (dedicated mode); each published step is hot-loaded
+        # as the adapter "{model}@{step}"
+        self._vllm_gpus = vllm_gpus
+        self._vllm_engine_args = dict(vllm_engine_args or {})
+        self._vllm: dict[str, Any] = {}
         self._servers: dict[str, Any] = {}
         self._engines: dict[str, Any] = {}
         # step checkpoints are written in the background (the write of step n
@@ -105,6 +113,9 @@ class LocalBackend:
         for server in self._servers.values():
             server.stop()
         self._servers.clear()
+        for rt in self._vllm.values():
+            rt.close()
+        self._vllm.clear()
 
     # ------------------------------------------------------------------
     def _model_dir(self, model: Any) -> str:
@@ -214,7 +225,27 @@ class LocalBackend:
                                    host=host, port=port, api_key=api_key)
             server.start()
             self._servers[model.name] = server
+        if self._inference == "vllm":
+            if _rank() == 0 and model.name not in self._vllm:
+                from ..runtime.vllm_runtime import ManagedVllmRuntime, VllmRuntimeConfig
+
+                rt = ManagedVllmRuntime(
+                    VllmRuntimeConfig(base_model=model.base_model, served_model_name=model.name, host=host,
+                                      port=port, gpus=self._vllm_gpus, api_key=api_key,
+                                      max_lora_rank=max(8, self._lora_spec(model).r),
+                                      engine_args=self._vllm_engine_args),
+                    log_path=os.path.join(self._model_dir(model), "logs", "vllm.log"))
+                await rt.start()
+                self._vllm[model.name] = rt
+                await rt.load_lora(f"{model.name}@{step}", ck)
+            _barrier()
         return f"http://{host}:{port}/v1", api_key
+
+    async def _publish_to_vllm(self, model: Any, step: int, path: str) -> None:
+        """Hot-load a published checkpoint into the model's vLLM server."""
+        rt = self._vllm.get(model.name)
+        if rt is not None:
+            await rt.load_lora(f"{model.name}@{step}", path)
 
     # ------------------------------------------------------------------ generation
     def _engine(self, model: Any):
@@ -418,6 +449,8 @@ class LocalBackend:
         builder = self._metrics.setdefault(model.name, MetricsBuilder())
         metrics = builder.update(metrics)
         metrics = aggregate_rl_training_metrics([metrics], groups)
+        if save_checkpoint and _rank() == 0:
+            await self._publish_to_vllm(model, new_step, ck)
         return LocalTrainResult(step=new_step, metrics=metrics, checkpoint_path=ck if save_checkpoint else None)
 
     async def _train_packed(

@@ -109,6 +109,8 @@ std::vector<torch::Tensor> lm_head_fwd(torch::Tensor h, torch::Tensor w, torch::
                                        c10::optional<torch::Tensor> logits_out);
 torch::Tensor glu_clamp_fwd(torch::Tensor gu, double alpha, double limit);
 torch::Tensor glu_clamp_bwd(torch::Tensor da, torch::Tensor gu, double alpha, double limit);
+void gemm_pair_rs(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2,
+                  std::vector<int64_t> c_ptrs, int64_t rows, int64_t ldc, int64_t slot);
 void gemm_pair_mainloop(torch::Tensor a, torch::Tensor b, torch::Tensor diag);
 void lm_head_grad_logits(torch::Tensor h, torch::Tensor w, torch::Tensor targets, torch::Tensor lse, torch::Tensor g,
                          torch::Tensor out);
@@ -181,6 +183,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("logits_out") = py::none());
   m.def("lm_head_grad_logits", &art::lm_head_grad_logits);
   m.def("gemm_pair_mainloop", &art::gemm_pair_mainloop);
+  m.def("gemm_pair_rs", &art::gemm_pair_rs);
   m.def("glu_clamp_fwd", &art::glu_clamp_fwd);
   m.def("glu_clamp_bwd", &art::glu_clamp_bwd);
   m.def("gdn_conv_bwd", &art::gdn_conv_bwd);

@@ -29,6 +29,8 @@
 // stays in L2 while B streams through once per group (B is read once in
 // all when A fits).
 // Every wait is bounded (tc_common.cuh); TMEM is always freed.
+#include <cmath>
+#include <cstdlib>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <cudaTypedefs.h>
@@ -40,12 +42,25 @@ using namespace tc;
 
 namespace {
 
-constexpr int PBM = 256, PBN = 256, PBK = 64, PSTAGES = 6;
+constexpr int PBM = 256, PBN = 256, PBK = 64;  // PBN: N of one MMA
 constexpr int P_HALF = 128 * PBK * 2;  // 16 KB: 128 rows x 64 bf16
-constexpr int P_STAGE = 2 * P_HALF;    // A half + B half, per CTA
 constexpr int P_THREADS = 192;
 constexpr int P_STG_WARP = 32 * 128;   // epilogue staging per warp: 32 rows x 64 bf16 (128 B a row)
-constexpr int P_SMEM = PSTAGES * P_STAGE + 1024 /*align*/ + 256 /*barriers*/ + 4 * P_STG_WARP;
+
+// Tile shapes of the pair kernel.  TN = 256: one N=256 MMA per k-step, two
+// accumulator buffers (the epilogue of tile t overlaps the mainloop of t+1).
+// TN = 512: two N=256 MMAs per k-step reuse each staged A tile, so a k-block
+// stages 48 KB per CTA for twice the MMAs (shared memory carries the TMA
+// writes and the MMA operand reads at once; the wide tile lowers the former
+// by a quarter per FLOP), at the price of one accumulator buffer.
+template <int TN>
+struct PTile {
+  static constexpr int NB = TN / 256;                 // N=256 MMAs per k-step
+  static constexpr int NBUF = TN == 256 ? 2 : 1;      // accumulator buffers in the 512 TMEM columns
+  static constexpr int STAGES = TN == 256 ? 6 : 4;
+  static constexpr int STAGE = P_HALF * (1 + NB);     // A half + this CTA's B halves
+  static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/ + 4 * P_STG_WARP;
+};
 
 struct PairArgs {
   int M, N, K2;
@@ -68,6 +83,12 @@ struct PairArgs {
   float* tgt;              // EPI_STATS: [M] logit of the target (written by the tile holding it)
   const float* lse;        // EPI_GRAD: [M] log-sum-exp of the row
   const float* g;          // EPI_GRAD: [M] d loss / d logprob of the row
+  // reduce-scatter epilogue (scatter_rows > 0): output rows [r*scatter_rows,
+  // (r+1)*scatter_rows) go to rank r's staging buffer peer[r] (a peer-mapped
+  // address) at row offset slot*scatter_rows, with row stride ldc
+  int scatter_rows;
+  int scatter_slot;
+  long long peer[8];
 };
 
 // Epilogue variants of the pair GEMM.
@@ -84,20 +105,23 @@ struct PairArgs {
 //             mainloop alone: operand delivery and MMA issue)
 enum { EPI_STORE = 0, EPI_STATS = 1, EPI_GRAD = 2, EPI_NONE = 3 };
 
+template <int TN>
 __device__ __forceinline__ int2 pair_tile(int t, int num_m, int num_n, int group_m) {
   const int group = group_m * num_n;
   const int g = t / group;
   const int first_m = g * group_m;
   const int gm = min(num_m - first_m, group_m);
   const int r = t - g * group;
-  return make_int2((first_m + r % gm) * PBM, (r / gm) * PBN);
+  return make_int2((first_m + r % gm) * PBM, (r / gm) * TN);
 }
 
-template <int EPI>
+template <int EPI, int TN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                      const PairArgs p) {
+  using T = PTile<TN>;
+  constexpr int PSTAGES = T::STAGES, P_STAGE = T::STAGE, NB = T::NB, NBUF = T::NBUF;
   extern __shared__ uint8_t smem_raw[];
   // same offset in both CTAs: the MMA descriptors and mapa rely on it
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -113,7 +137,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int num_m = (p.M + PBM - 1) / PBM;
-  const int num_n = (p.N + PBN - 1) / PBN;
+  const int num_n = (p.N + TN - 1) / TN;
   const int num_tiles = num_m * num_n;
   const int nk = p.nk1 + p.nk2;
 
@@ -147,8 +171,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       const uint32_t full_leader = mapa_shared(smem_addr(full), 0);
       int it = 0;
       for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
-        const int2 c = pair_tile(t, num_m, num_n, p.group_m);
-        const int am = c.x + (int)rank * 128, bn = c.y + (int)rank * 128;
+        const int2 c = pair_tile<TN>(t, num_m, num_n, p.group_m);
+        const int am = c.x + (int)rank * 128;
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % PSTAGES;
@@ -158,21 +182,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             break;
           }
           uint8_t* a = smem + s * P_STAGE;
-          uint8_t* b = a + P_HALF;
           const uint32_t fb = full_leader + s * 8;
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * P_STAGE);  // both CTAs' bytes
-          if (kb < p.nk1) {
-            tma_load_2d_pair(a, &tmA, fb, kb * PBK, am);
-            if (p.b_mn) {  // two 64-column boxes of the [K, N] matrix: 64 K rows each
-              tma_load_2d_pair(b, &tmB, fb, bn, kb * PBK);
-              tma_load_2d_pair(b + P_HALF / 2, &tmB, fb, bn + 64, kb * PBK);
+          if (kb < p.nk1) tma_load_2d_pair(a, &tmA, fb, kb * PBK, am);
+          else tma_load_2d_pair(a, &tmA2, fb, (kb - p.nk1) * PBK, am);
+#pragma unroll
+          for (int h = 0; h < NB; ++h) {  // this CTA's 128 columns of each N=256 half
+            uint8_t* b = a + P_HALF * (1 + h);
+            const int bn = c.y + h * 256 + (int)rank * 128;
+            if (kb < p.nk1) {
+              if (p.b_mn) {  // two 64-column boxes of the [K, N] matrix: 64 K rows each
+                tma_load_2d_pair(b, &tmB, fb, bn, kb * PBK);
+                tma_load_2d_pair(b + P_HALF / 2, &tmB, fb, bn + 64, kb * PBK);
+              } else {
+                tma_load_2d_pair(b, &tmB, fb, kb * PBK, bn);
+              }
             } else {
-              tma_load_2d_pair(b, &tmB, fb, kb * PBK, bn);
+              tma_load_2d_pair(b, &tmB2, fb, (kb - p.nk1) * PBK, bn);
             }
-          } else {
-            const int k2 = (kb - p.nk1) * PBK;
-            tma_load_2d_pair(a, &tmA2, fb, k2, am);
-            tma_load_2d_pair(b, &tmB2, fb, k2, bn);
           }
         }
         if (!ok) break;
@@ -186,13 +213,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       const uint64_t t_start = p.diag ? gtimer() : 0;
       int it = 0, tl = 0;
       for (int t = pair; t < num_tiles && !*abort_flag; t += npairs, ++tl) {
-        const int buf = tl & 1;
-        const uint32_t use = (uint32_t)(tl >> 1);
+        const int buf = NBUF == 2 ? (tl & 1) : 0;
+        const uint32_t use = (uint32_t)(NBUF == 2 ? (tl >> 1) : tl);
         const uint64_t ta = p.diag ? gtimer() : 0;
         if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, p.err, 22)) break;
         if (p.diag) d_acc += gtimer() - ta;
         tc_fence_after();
-        const uint32_t d = tmem + buf * PBN;
+        const uint32_t d = tmem + buf * TN;  // half h accumulates at d + 256 h
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % PSTAGES;
@@ -215,22 +242,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           // operands arrive through the async proxy (TMA) and the barrier
           // orders them for the MMA: no thread-sync fence per k-block
           const uint32_t a_addr = smem_addr(smem + s * P_STAGE);
-          const uint64_t da = desc_k_sw128(a_addr), db = desc_k_sw128(a_addr + P_HALF);
+          const uint64_t da = desc_k_sw128(a_addr);
           if (kb < p.nk1 && p.b_mn) {
             // MN-major B: 16 K rows of 128 B per step (+2048 B), 64-column chunks 8 KB apart
-            const uint64_t dbm = desc_mn_sw128(a_addr + P_HALF, P_HALF / 2);
 #pragma unroll
             for (int kk = 0; kk < PBK / 16; ++kk)
-              mma_bf16_pair(d, da + 2 * kk, dbm + 128 * kk, idesc | (1u << 16), (kb > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+              for (int h = 0; h < NB; ++h)
+                mma_bf16_pair(d + 256 * h, da + 2 * kk,
+                              desc_mn_sw128(a_addr + P_HALF * (1 + h), P_HALF / 2) + 128 * kk,
+                              idesc | (1u << 16), (kb > 0 || kk > 0) ? 1u : 0u);
           } else if (kb < p.nk1) {
 #pragma unroll
             for (int kk = 0; kk < PBK / 16; ++kk)  // +32 bytes per K=16 step (descriptor units of 16 B)
-              mma_bf16_pair(d, da + 2 * kk, db + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+              for (int h = 0; h < NB; ++h)
+                mma_bf16_pair(d + 256 * h, da + 2 * kk, desc_k_sw128(a_addr + P_HALF * (1 + h)) + 2 * kk, idesc,
+                              (kb > 0 || kk > 0) ? 1u : 0u);
           } else {
             const int rem = p.K2 - (kb - p.nk1) * PBK;
             const int ksteps = min(PBK / 16, (rem + 15) / 16);
             for (int kk = 0; kk < ksteps; ++kk)
-              mma_bf16_pair(d, da + 2 * kk, db + 2 * kk, idesc, 1u);
+#pragma unroll
+              for (int h = 0; h < NB; ++h)
+                mma_bf16_pair(d + 256 * h, da + 2 * kk, desc_k_sw128(a_addr + P_HALF * (1 + h)) + 2 * kk, idesc, 1u);
           }
           mma_commit_pair_both(&empty[s], 0x3);
         }
@@ -252,8 +287,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     uint8_t* stg = smem + PSTAGES * P_STAGE + 256 + (warp - 2) * P_STG_WARP;
     int tl = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++tl) {
-      const int buf = tl & 1;
-      const uint32_t use = (uint32_t)(tl >> 1);
+      const int buf = NBUF == 2 ? (tl & 1) : 0;
+      const uint32_t use = (uint32_t)(NBUF == 2 ? (tl >> 1) : tl);
       if (!__all_sync(0xffffffffu, mbar_wait_sleep(&acc_full[buf], use & 1, abort_flag, p.err, 24))) break;
       tc_fence_after();
       if constexpr (EPI == EPI_NONE) {
@@ -262,7 +297,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         if (lane == 0) mbar_arrive_cluster(acce_leader + buf * 8);
         continue;
       }
-      const int2 c = pair_tile(t, num_m, num_n, p.group_m);
+      const int2 c = pair_tile<TN>(t, num_m, num_n, p.group_m);
       const int row = c.x + (int)rank * 128 + q * 32 + lane;
       // LM-head epilogues: per-row inputs and the running softmax partials
       int64_t tgt_id = -1;
@@ -278,10 +313,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         }
       }
 #pragma unroll 1
-      for (int cc = 0; cc < PBN / 32; cc += 2) {
+      for (int cc = 0; cc < TN / 32; cc += 2) {
         uint32_t r2[2][32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * PBN + cc * 32, r2[0]);
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * PBN + (cc + 1) * 32, r2[1]);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * TN + cc * 32, r2[0]);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * TN + (cc + 1) * 32, r2[1]);
         tmem_wait_ld();
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -350,7 +385,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           const int gcol = cbase + u * 8;
           if (grow < p.M && gcol < p.N) {
             uint4 o = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((u ^ (rr & 7)) << 4));
-            __nv_bfloat16* dst = p.C + (int64_t)grow * p.ldc + gcol;
+            __nv_bfloat16* dst;
+            if (p.scatter_rows) {  // the owning rank's staging slot (P2P stores over NVLink)
+              const int owner = grow / p.scatter_rows;
+              dst = reinterpret_cast<__nv_bfloat16*>(p.peer[owner]) +
+                    ((int64_t)p.scatter_slot * p.scatter_rows + (grow - owner * p.scatter_rows)) * p.ldc + gcol;
+            } else {
+              dst = p.C + (int64_t)grow * p.ldc + gcol;
+            }
             if (EPI == EPI_STORE && p.accumulate_c) {  // out += product (a second bf16 rounding)
               const uint4 cv = *reinterpret_cast<const uint4*>(dst);
               const __nv_bfloat16* ce = reinterpret_cast<const __nv_bfloat16*>(&cv);
@@ -366,7 +408,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         __syncwarp();
       }
       if constexpr (EPI == EPI_STATS) {
-        if (row < p.M) p.stats[(int64_t)row * num_n + c.y / PBN] = make_float4(st_m, st_s, st_sx, 0.f);
+        if (row < p.M) p.stats[(int64_t)row * num_n + c.y / TN] = make_float4(st_m, st_s, st_sx, 0.f);
       }
       tc_fence_before();
       __syncwarp();
@@ -425,9 +467,47 @@ __global__ void lm_head_merge_kernel(const float4* __restrict__ stats, int num_n
   }
 }
 
-template <int EPI>
-void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2, const CUtensorMap& tb2,
-                 PairArgs& p, int64_t K, int dev) {
+template <int EPI, int TN>
+int pair_capacity(int dev) {
+  static int max_pairs[64] = {0};
+  if (!max_pairs[dev]) {
+    ART_CUDA_CHECK(cudaFuncSetAttribute(gemm_pair_kernel<EPI, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        PTile<TN>::SMEM));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(P_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = PTile<TN>::SMEM;  // cluster shape comes from __cluster_dims__
+    int n = 0;
+    ART_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<EPI, TN>, &cfg));
+    TORCH_CHECK(n > 0, "no CTA pair of the GEMM fits on this device");
+    max_pairs[dev] = n;
+  }
+  return max_pairs[dev];
+}
+
+// Tile width of a call: the 512-wide tile (less staging traffic per FLOP,
+// one accumulator buffer) where its tile count fills the resident pairs about
+// as evenly as the 256-wide one; ART_B200_PAIR_WIDE=0 / 1 forces 256 / 512.
+constexpr int kPairWideDefault = -1;  // -1: chosen per call (ART_B200_PAIR_WIDE=0 / 1 force 256 / 512)
+
+inline int pair_tile_n(int64_t M, int64_t N, int pairs) {
+  const char* e = std::getenv("ART_B200_PAIR_WIDE");  // read per call: tests and benchmarks switch it
+  const int force = e ? std::atoi(e) : kPairWideDefault;
+  if (force == 0 || N < 512) return 256;
+  if (force == 1) return 512;
+  const double num_m = (double)((M + PBM - 1) / PBM);
+  auto fill = [&](int64_t tn) {
+    const double tiles = num_m * (double)((N + tn - 1) / tn);
+    const double waves = tiles / pairs;
+    return waves / std::ceil(waves);
+  };
+  // the wide tile's mainloop runs ~10 % faster when it is not limited by tile quantisation
+  return fill(512) * 1.10 > fill(256) ? 512 : 256;
+}
+
+template <int EPI, int TN>
+void launch_pair_tn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2, const CUtensorMap& tb2,
+                    PairArgs& p, int64_t K, int dev) {
   {
     const int64_t num_m = (p.M + PBM - 1) / PBM;
     const int64_t band = (int64_t)PBM * K * 2;  // bytes of one 256-row band of A
@@ -435,22 +515,23 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap
     p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(g, num_m));
   }
   p.err = tc_error_ptr(dev);
-  static int max_pairs[64] = {0};
-  if (!max_pairs[dev]) {
-    ART_CUDA_CHECK(cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(P_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = P_SMEM;  // cluster shape comes from __cluster_dims__
-    int n = 0;
-    ART_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<EPI>, &cfg));
-    TORCH_CHECK(n > 0, "no CTA pair of the GEMM fits on this device");
-    max_pairs[dev] = n;
-  }
-  const int tiles = ((p.M + PBM - 1) / PBM) * ((p.N + PBN - 1) / PBN);
-  const int pairs = tiles < max_pairs[dev] ? tiles : max_pairs[dev];
-  gemm_pair_kernel<EPI><<<2 * pairs, P_THREADS, P_SMEM, at::cuda::getCurrentCUDAStream()>>>(ta, tb, ta2, tb2, p);
+  const int cap = pair_capacity<EPI, TN>(dev);
+  const int tiles = ((p.M + PBM - 1) / PBM) * ((p.N + TN - 1) / TN);
+  const int pairs = tiles < cap ? tiles : cap;
+  gemm_pair_kernel<EPI, TN><<<2 * pairs, P_THREADS, PTile<TN>::SMEM, at::cuda::getCurrentCUDAStream()>>>(
+      ta, tb, ta2, tb2, p);
   ART_CUDA_CHECK(cudaPeekAtLastError());
+}
+
+// Launch with the tile width chosen for the call (returned: the LM-head
+// statistics are laid out per tile of that width).
+template <int EPI>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2, const CUtensorMap& tb2,
+                PairArgs& p, int64_t K, int dev, int tn = 0) {
+  if (!tn) tn = pair_tile_n(p.M, p.N, pair_capacity<EPI, 256>(dev));
+  if (tn == 512) launch_pair_tn<EPI, 512>(ta, tb, ta2, tb2, p, K, dev);
+  else launch_pair_tn<EPI, 256>(ta, tb, ta2, tb2, p, K, dev);
+  return tn;
 }
 
 }  // namespace
@@ -503,8 +584,48 @@ torch::Tensor gemm_pair(torch::Tensor a, torch::Tensor b, c10::optional<torch::T
   p.tgt = nullptr;
   p.lse = nullptr;
   p.g = nullptr;
+  p.scatter_rows = 0;
+  p.scatter_slot = 0;
+  for (int i = 0; i < 8; ++i) p.peer[i] = 0;
   launch_pair<EPI_STORE>(ta, tb, ta2, tb2, p, K, a.get_device());
   return c;
+}
+
+// RS(a @ b^T (+ a2 @ b2^T)): the product's row block r goes straight into
+// rank r's staging slot `slot` (peer pointers c_ptrs, row stride ldc); the
+// owner sums its slots afterwards.  Same contract as gemm_tc_rs, on CTA pairs.
+void gemm_pair_rs(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2,
+                  std::vector<int64_t> c_ptrs, int64_t rows, int64_t ldc, int64_t slot) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.size(1) == b.size(1));
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+  const int ndst = (int)c_ptrs.size();
+  TORCH_CHECK(ndst >= 1 && ndst <= 8 && rows * ndst == M && N % 32 == 0 && ldc % 8 == 0);
+  if (a2.has_value()) TORCH_CHECK(b2.has_value() && a2->size(0) == M && b2->size(0) == N && a2->size(1) == b2->size(1));
+  const CUtensorMap ta = make_tmap_bf16(a, 128), tb = make_tmap_bf16(b, 128);
+  const CUtensorMap ta2 = a2.has_value() ? make_tmap_bf16(*a2, 128) : ta;
+  const CUtensorMap tb2 = a2.has_value() ? make_tmap_bf16(*b2, 128) : tb;
+  PairArgs p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K2 = a2.has_value() ? (int)a2->size(1) : 0;
+  p.nk1 = (int)((K + PBK - 1) / PBK);
+  p.nk2 = a2.has_value() ? (p.K2 + PBK - 1) / PBK : 0;
+  p.C = nullptr;
+  p.ldc = ldc;
+  p.bias = nullptr;
+  p.accumulate_c = 0;
+  p.b_mn = 0;
+  p.diag = nullptr;
+  p.targets = nullptr;
+  p.stats = nullptr;
+  p.tgt = nullptr;
+  p.lse = nullptr;
+  p.g = nullptr;
+  p.scatter_rows = (int)rows;
+  p.scatter_slot = (int)slot;
+  for (int i = 0; i < 8; ++i) p.peer[i] = i < ndst ? c_ptrs[i] : 0;
+  if (M == 0) return;
+  launch_pair<EPI_STORE>(ta, tb, ta2, tb2, p, K, a.get_device());
 }
 
 // The mainloop alone (EPI_NONE) with the MMA-thread counters of PairArgs::diag:
@@ -530,6 +651,9 @@ void gemm_pair_mainloop(torch::Tensor a, torch::Tensor b, torch::Tensor diag) {
   p.tgt = nullptr;
   p.lse = nullptr;
   p.g = nullptr;
+  p.scatter_rows = 0;
+  p.scatter_slot = 0;
+  for (int i = 0; i < 8; ++i) p.peer[i] = 0;
   launch_pair<EPI_NONE>(ta, tb, ta, tb, p, a.size(1), a.get_device());
 }
 
@@ -560,6 +684,9 @@ static PairArgs lm_head_args(const torch::Tensor& h, const torch::Tensor& w) {
   p.tgt = nullptr;
   p.lse = nullptr;
   p.g = nullptr;
+  p.scatter_rows = 0;
+  p.scatter_slot = 0;
+  for (int i = 0; i < 8; ++i) p.peer[i] = 0;
   return p;
 }
 
@@ -571,7 +698,8 @@ std::vector<torch::Tensor> lm_head_fwd(torch::Tensor h, torch::Tensor w, torch::
                                        c10::optional<torch::Tensor> logits_out) {
   lm_head_check(h, w, targets);
   const int64_t M = h.size(0), V = w.size(0);
-  const int64_t num_n = (V + PBN - 1) / PBN;
+  const int tn = pair_tile_n(M, V, pair_capacity<EPI_STATS, 256>(h.get_device()));
+  const int64_t num_n = (V + tn - 1) / tn;
   auto f32 = h.options().dtype(at::kFloat);
   auto stats = torch::empty({M, num_n, 4}, f32);
   auto tgt = torch::zeros({M}, f32);
@@ -590,7 +718,7 @@ std::vector<torch::Tensor> lm_head_fwd(torch::Tensor h, torch::Tensor w, torch::
     p.C = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
     p.ldc = out.stride(0);
   }
-  launch_pair<EPI_STATS>(ta, tb, ta, tb, p, h.size(1), h.get_device());
+  launch_pair<EPI_STATS>(ta, tb, ta, tb, p, h.size(1), h.get_device(), tn);
   lm_head_merge_kernel<<<(unsigned)((M + 7) / 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const float4*>(stats.data_ptr<float>()), (int)num_n, (int)M, targets.data_ptr<int64_t>(),
       (int)V, tgt.data_ptr<float>(), lp.data_ptr<float>(), entropy ? ent.data_ptr<float>() : nullptr,

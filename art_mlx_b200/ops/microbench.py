@@ -114,10 +114,15 @@ def bench_gemm() -> None:
         b = torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02
         fl = 2 * rows * K * N
         t_ours = _timed(lambda: C.gemm_tc(a, b, None, None, None, None, False))
+        os.environ["ART_B200_PAIR_WIDE"] = "1"
+        t_wide = _timed(lambda: C.gemm_pair(a, b, None, None, None, None, False))
+        os.environ["ART_B200_PAIR_WIDE"] = "0"
         t_pair = _timed(lambda: C.gemm_pair(a, b, None, None, None, None, False))
+        os.environ.pop("ART_B200_PAIR_WIDE")
         t_cublas = _timed(lambda: torch.matmul(a, b.t()))
         row = dict(case=f"gemm_{name}", M=rows, K=K, N=N, ours_1cta_ms=round(t_ours, 4),
-                   ours_pair_ms=round(t_pair, 4), cublas_ms=round(t_cublas, 4),
+                   ours_pair_ms=round(t_pair, 4), ours_wide_ms=round(t_wide, 4), cublas_ms=round(t_cublas, 4),
+                   ours_wide_tflops=round(fl / t_wide / 1e9, 1),
                    ours_1cta_tflops=round(fl / t_ours / 1e9, 1), ours_pair_tflops=round(fl / t_pair / 1e9, 1),
                    cublas_tflops=round(fl / t_cublas / 1e9, 1))
         if r:

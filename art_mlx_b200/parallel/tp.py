@@ -14,7 +14,8 @@ Communication-fused kernels (``ops/csrc/gemm_tc.cu``, transport ``"p2p"``):
   have already arrived (own shard first).  No kernel reads peer memory
   through TMA on this path, and nothing uses multicast;
 * GEMM -> RS: the GEMM epilogue stores each row block of the partial product
-  into the owning rank's staging slot over NVLink; the owner sums its slots.
+  into the owning rank's staging slot over NVLink (whole 128-byte lines from
+  the CTA-pair kernel's staged epilogue); the owner sums its slots.
 
 The NCCL transport (``"nccl"``) is the baseline: ``all_gather_into_tensor``
 and ``reduce_scatter_tensor`` around cuBLAS GEMMs (also the gloo CPU path).
@@ -154,7 +155,10 @@ class TPContext:
             if q != self.rank:
                 main.wait_event(events[q])
             r = slice(q * rows, (q + 1) * rows)
-            C.gemm_tc(src, W, None if a2 is None else a2[r], b2, bias, out[r], False)
+            if _pair(rows, W):
+                C.gemm_pair(src.contiguous(), W, None if a2 is None else a2[r].contiguous(), b2, bias, out[r])
+            else:
+                C.gemm_tc(src, W, None if a2 is None else a2[r], b2, bias, out[r], False)
         gathered.record_stream(side)
         return out
 
@@ -185,10 +189,22 @@ class TPContext:
         self._rs_turn ^= 1
         off = self.off_rs + turn * self.stage_bytes
         ptrs = [b + off for b in self.arena.bases]
-        native.lib().gemm_tc_rs(x.contiguous(), W, a2, b2, ptrs, rows, N, self.rank)
+        if _pair(T, W):
+            native.lib().gemm_pair_rs(x.contiguous(), W, a2, b2, ptrs, rows, N, self.rank)
+        else:
+            native.lib().gemm_tc_rs(x.contiguous(), W, a2, b2, ptrs, rows, N, self.rank)
         self.barrier()  # every rank's partial rows have landed in the owners' slots
         staging = self.arena.view(off, T * N, x.dtype).view(T, N)
         return native.lib().slot_sum(staging, self.world, rows, None)
+
+
+def _pair(rows: int, W: torch.Tensor) -> bool:
+    """The CTA-pair tcgen05 GEMM for a TP product (else the 1-CTA kernel):
+    bf16, at least a full tile of rows, 128-multiple widths."""
+    from ..ops import fused
+
+    return (fused.PAIR_GEMM and W.dtype == torch.bfloat16 and rows >= 256 and W.shape[0] % 128 == 0
+            and W.shape[1] % 128 == 0 and W.is_contiguous())
 
 
 # ---------------------------------------------------------------------------

@@ -248,8 +248,17 @@ class AsyncCheckpointWriter:
         checkpoint ``path`` (one device-to-host copy of the slice, the file
         written on the background thread)."""
         cuda = store.master.device.type == "cuda"
-        mk = lambda: torch.empty(numel, dtype=torch.float32, pin_memory=cuda)  # noqa: E731
-        ea, eq = mk(), mk()
+        # two pinned slots reused across steps (a pinned allocation per call
+        # costs more than the copy)
+        key = (numel, cuda)
+        if getattr(self, "_shard_key", None) != key:
+            self.wait()
+            mk = lambda: torch.empty(numel, dtype=torch.float32, pin_memory=cuda)  # noqa: E731
+            self._shard_slots = [(mk(), mk(), None), (mk(), mk(), None)]
+            self._shard_key, self._shard_turn = key, 0
+        ea, eq, pending = self._shard_slots[self._shard_turn]
+        if pending is not None:
+            pending.result()
         ea.copy_(store.exp_avg[offset : offset + numel], non_blocking=cuda)
         eq.copy_(store.exp_avg_sq[offset : offset + numel], non_blocking=cuda)
         if cuda:
@@ -257,7 +266,10 @@ class AsyncCheckpointWriter:
         shard = {"offset": offset, "numel": numel, "total": store.numel, "exp_avg": ea, "exp_avg_sq": eq,
                  "step": store.step, "rank": rank, "world": world}
         name = f"optimizer-shard-{rank:02d}-of-{world:02d}.pt"
-        self._pending.append(self._pool.submit(_write_file, path, name, shard))
+        fut = self._pool.submit(_write_file, path, name, shard)
+        self._shard_slots[self._shard_turn] = (ea, eq, fut)
+        self._shard_turn ^= 1
+        self._pending.append(fut)
 
     def wait(self) -> None:
         pending, self._pending = self._pending, []

@@ -85,6 +85,37 @@ def _valid_length(group_ids: torch.Tensor) -> int:
     return int(nz[-1].item()) + 1 if nz.numel() else 0
 
 
+_PAD_VALUES = {"tokens": -100, "group_ids": -1, "parent_ids": -1, "input_pos": 0, "assistant_mask": False,
+               "logprobs": float("nan"), "advantages": 0.0, "weights": 0.0, "original_logprobs": float("nan")}
+
+
+def pad_packed_length(packed: Mapping[str, Any], multiple: int) -> dict[str, Any]:
+    """A copy of ``packed`` whose row length is padded up to a multiple of
+    ``multiple`` with padding tokens (group -1: never attended, never
+    trained); replayed routes are padded with expert 0 and no coverage."""
+    S = int(packed["tokens"].shape[1])
+    extra = (-S) % multiple
+    if not extra:
+        return dict(packed)
+    out = dict(packed)
+    for k, v in _PAD_VALUES.items():
+        t = packed.get(k)
+        if isinstance(t, torch.Tensor) and t.dim() == 2 and t.shape[1] == S:
+            out[k] = torch.nn.functional.pad(t, (0, extra), value=v) if t.dtype != torch.bool else torch.cat(
+                [t, t.new_zeros(t.shape[0], extra)], dim=1)
+    rr = packed.get("moe_routing_replay")
+    if rr is not None:
+        import dataclasses
+
+        ei = rr.expert_indices
+        pad_e = ei.new_zeros((ei.shape[0], extra) + tuple(ei.shape[2:]))
+        tm = rr.token_mask
+        out["moe_routing_replay"] = dataclasses.replace(
+            rr, expert_indices=torch.cat([ei, pad_e], dim=1),
+            token_mask=torch.cat([tm, tm.new_zeros((tm.shape[0], extra) + tuple(tm.shape[2:]))], dim=1))
+    return out
+
+
 def stage_row(
     packed: Mapping[str, Any],
     row: int,
@@ -575,6 +606,9 @@ class GRPOTrainer:
             # the ETP all-gather wants equal token counts on every member: rows
             # keep their full packed length
             pad_to = max(int(packed["tokens"].shape[1]), 1)
+        if shard > 1 and int(packed["tokens"].shape[1]) % pad_to:
+            # rows split over ranks need a length the split divides evenly
+            packed = pad_packed_length(packed, pad_to)
         cfgm = self.model.cfg
         linear = any(cfgm.layer_kind(i) != "attention" for i in range(cfgm.num_hidden_layers))
 

@@ -224,3 +224,20 @@ def test_row_assignment_matches_planning_every_candidate_row():
         _random.Random(trial).shuffle(rows)
         ref = P._padded([P._pack_row(row, seq_len, True)["tokens"] for row in rows], seq_len, -100, torch.long)
         assert torch.equal(got["tokens"], ref), trial
+
+
+def test_pad_packed_length_keeps_rows_inert():
+    import random as _r
+
+    from art_mlx_b200.preprocessing.pack import packed_tensors_from_tokenized_results
+    from art_mlx_b200.preprocessing.synthetic import synthetic_groups
+    from art_mlx_b200.preprocessing.tokenize import tokenize_trajectory_groups
+    from art_mlx_b200.runtime.trainer import pad_packed_length
+
+    groups = synthetic_groups(num_groups=2, rollouts_per_group=3, prompt_len=30, completion_len=9, vocab_size=99, seed=1)
+    res = list(tokenize_trajectory_groups(None, groups, False, True, rng=_r.Random(0)))
+    p = packed_tensors_from_tokenized_results(res, 100, rng=_r.Random(0))
+    q = pad_packed_length(p, 128)
+    assert q["tokens"].shape[1] == 128 and torch.equal(q["tokens"][:, :100], p["tokens"])
+    assert bool((q["group_ids"][:, 100:] == -1).all()) and not bool(q["assistant_mask"][:, 100:].any())
+    assert float(q["assistant_mask"].sum()) == float(p["assistant_mask"].sum())

@@ -99,8 +99,11 @@ def test_gemm_tc_grouped_matches_fp32(cuda, E, K, N, K2, wt):
         (2048, 2048, 800, 16, False, False),
     ],
 )
-def test_gemm_pair_matches_fp32(cuda, M, K, N, K2, bias, acc):
-    """The CTA-pair (cta_group::2) tcgen05 GEMM against an fp32 reference."""
+@pytest.mark.parametrize("wide", ["0", "1"])
+def test_gemm_pair_matches_fp32(cuda, M, K, N, K2, bias, acc, wide, monkeypatch):
+    """The CTA-pair (cta_group::2) tcgen05 GEMM against an fp32 reference,
+    with 256- and 512-wide tiles (ART_B200_PAIR_WIDE forces the width)."""
+    monkeypatch.setenv("ART_B200_PAIR_WIDE", wide)
     C = native.lib()
     torch.manual_seed(M + K + N + 1)
     a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
@@ -123,8 +126,10 @@ def test_gemm_pair_matches_fp32(cuda, M, K, N, K2, bias, acc):
 
 
 @pytest.mark.parametrize("M,K,N,K2", [(300, 512, 256, 0), (1000, 3584, 3584, 48), (2048, 4608, 3584, 16)])
-def test_gemm_pair_transposed_b_matches_fp32(cuda, M, K, N, K2):
+@pytest.mark.parametrize("wide", ["0", "1"])
+def test_gemm_pair_transposed_b_matches_fp32(cuda, M, K, N, K2, wide, monkeypatch):
     """Input-gradient form: out = a @ bt (+ a2 @ b2^T) with bt = [K, N] row-major."""
+    monkeypatch.setenv("ART_B200_PAIR_WIDE", wide)
     C = native.lib()
     torch.manual_seed(M + K + N + 2)
     a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
@@ -138,3 +143,27 @@ def test_gemm_pair_transposed_b_matches_fp32(cuda, M, K, N, K2):
     torch.cuda.synchronize()
     assert C.tc_error_code() == 0
     assert rel_err(got, ref) < 1e-2
+
+
+@pytest.mark.parametrize("wide", ["0", "1"])
+def test_gemm_pair_reduce_scatter_epilogue(cuda, wide, monkeypatch):
+    """The pair GEMM's reduce-scatter epilogue: row block r of the product
+    lands in destination r's slot (here local buffers stand in for the
+    peers' staging arenas)."""
+    monkeypatch.setenv("ART_B200_PAIR_WIDE", wide)
+    C = native.lib()
+    torch.manual_seed(9)
+    world, rows, K, N, K2 = 3, 320, 1024, 1536, 16
+    a = torch.randn(world * rows, K, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=cuda, dtype=torch.bfloat16) * 0.05
+    a2 = torch.randn(world * rows, K2, device=cuda, dtype=torch.bfloat16)
+    b2 = torch.randn(N, K2, device=cuda, dtype=torch.bfloat16) * 0.05
+    slot = 1
+    stages = [torch.zeros(2 * rows, N, device=cuda, dtype=torch.bfloat16) for _ in range(world)]
+    C.gemm_pair_rs(a, b, a2, b2, [t.data_ptr() for t in stages], rows, N, slot)
+    torch.cuda.synchronize()
+    assert C.tc_error_code() == 0
+    ref = a.float() @ b.float().t() + a2.float() @ b2.float().t()
+    for r in range(world):
+        assert rel_err(stages[r][slot * rows :], ref[r * rows : (r + 1) * rows]) < 1e-2
+        assert not bool(stages[r][:rows].any())  # the other slot is untouched

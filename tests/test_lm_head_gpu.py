@@ -28,11 +28,14 @@ def _ref(h, W, tgt):
     return hf, lp, ent
 
 
+@pytest.mark.parametrize("wide", ["0", "1"])
 @pytest.mark.parametrize("keep", [True, False])
 @pytest.mark.parametrize("T,H,V", [(300, 256, 4096), (77, 128, 2080), (1000, 512, 32000 + 32), (4100, 3584, 152064)])
-def test_lm_head_fwd_bwd_matches_fp32(cuda, T, H, V, keep, monkeypatch):
-    """Both backward modes: logits kept from the forward, or recomputed."""
+def test_lm_head_fwd_bwd_matches_fp32(cuda, T, H, V, keep, wide, monkeypatch):
+    """Both backward modes (logits kept from the forward, or recomputed) and
+    both tile widths of the pair GEMM."""
     monkeypatch.setattr(fused, "LMHEAD_KEEP_BYTES", 1 << 40 if keep else 0)
+    monkeypatch.setenv("ART_B200_PAIR_WIDE", wide)
     torch.manual_seed(T + V)
     h = (torch.randn(T, H, device=cuda) * 0.5).to(torch.bfloat16).requires_grad_()
     W = (torch.randn(V, H, device=cuda) / H**0.5 * 2).to(torch.bfloat16)
