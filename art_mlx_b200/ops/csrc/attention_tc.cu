@@ -14,23 +14,28 @@
 //               tensor cores instead of sitting on the per-tile critical path
 //   warp 1      TMEM allocation (512 columns) and the MMA issuer:
 //                 S[b] = Q K^T         (M=128, N=128, K=128; both K-major,
-//                                       b = tile & 1)
+//                                       b = tile mod 3)
 //                 O   += P V           (P read from TMEM, where the softmax
 //                                       stored it over S[b]; V MN-major
 //                                       straight from its TMA tile)
-//               S of tile n+1 is issued before P V of tile n, so the tensor
-//               cores compute the next scores while the softmax runs; the
-//               commit after P V releases S[b] and the V slot
+//               issued as S(0), S(1), then S(n+2), P V(n) per tile: with
+//               three S buffers the scores of the next two tiles are computed
+//               while the softmax runs, and S(n+2) overwrites the buffer of
+//               tile n-1 right after issuing its P V (tcgen05.mma operations
+//               of one thread execute in order); the commit after P V
+//               releases the V slot
 //   warps 2..9  softmax, two warps per TMEM lane quadrant (one query row per
 //               thread, each warp 64 of the 128 key columns and 64 of the
-//               output columns): read the S half-row (tcgen05.ld), mask,
+//               output columns): read the S half-row (tcgen05.ld), mask
+//               (kend of partially visible tiles staged per warp in shared
+//               memory, loaded while the warp waits for S),
 //               running max (exchanged with the partner warp through a
 //               bounded mbarrier handshake) with lazy rescaling of O (only
 //               when the max grows by more than 2^8, the only time the
 //               softmax waits for the previous P V), exp2, row sum, P as
 //               bf16 pairs into the first 32 columns of the warp's S columns
 //               (tcgen05.st); finally O / l to global memory and the LSE.
-// TMEM columns: S[0] 0..127, S[1] 128..255, O 256..383.
+// TMEM columns: S[0] 0..127, S[1] 128..255, S[2] 256..383, O 384..511.
 // All mbarrier waits are bounded (tc_common.cuh): on timeout the kernel
 // records an error code, every role leaves its loop and TMEM is freed.
 #include <torch/extension.h>
@@ -56,7 +61,9 @@ constexpr int OFF_BAR = OFF_P + TILE_BYTES;
 constexpr int MAX_KT = 1024;                 // key tiles per row the tile list holds (131072 keys)
 constexpr int OFF_TL = OFF_BAR + 256;        // visible key-tile list (+ count)
 constexpr int OFF_X = OFF_TL + MAX_KT * 4 + 16;  // exchange [3][2 half][128]: row max (2 parities), row sum
-constexpr int FA_SMEM = OFF_X + 3 * 2 * FB * 4 + 1024;  // + alignment slack
+constexpr int OFF_KE = OFF_X + 3 * 2 * FB * 4;    // per softmax warp: kend of its 64 keys of the current tile
+constexpr int FA_SMEM = OFF_KE + 8 * 64 * 4 + 1024;  // + alignment slack
+constexpr int FA_NS = 3;                          // S / P buffers in tensor memory (O after them)
 constexpr int TILE_FULL = 1 << 30;           // list flag: every (query, key) pair of the tile is visible
 // 2 control warps + 8 softmax warps: two warps per TMEM lane quadrant, each
 // owning 64 of a row's 128 key columns (and 64 of its 128 output columns)
@@ -64,6 +71,22 @@ constexpr int FA_THREADS = 320;
 constexpr int FA_SOFT = 256;
 constexpr float kLog2eF = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kExp2PolyEvery = 8;           // softmax: one exponent pair in 8 on the FMA pipe
+
+// 2^x on the FMA pipe (x <= 2^22): x = r + f with r = round(x) (the 1.5 * 2^23
+// shifter leaves r in the low mantissa bits), 2^f for f in [-1/2, 1/2] from a
+// cubic with constant term 1 whose other coefficients were fitted for minimum
+// maximum relative error on that interval (Lawson's iteratively reweighted
+// least squares, 20001 points; relative error <= 1.02e-4, far below the
+// bf16 rounding of P), and 2^r added to the exponent field.  Arguments below
+// -127 are clamped there, which reconstructs exactly +0.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -127.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float q = fmaf(fmaf(fmaf(0.05500869f, f, 0.24221063f), f, 0.69328290f), f, 1.f);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
 
 struct FaArgs {
   const int* kend;
@@ -84,7 +107,10 @@ struct FaArgs {
   // attention sinks (null: none): one logit per q head (natural-log units)
   // that joins every row's softmax denominator and attends to nothing
   const float* sinks;
+  // phase clocks per CTA (null: off), kFaDiag int64 slots each: see attn_fwd_tc
+  long long* diag;
 };
+constexpr int kFaDiag = 96;
 
 // Visibility of key tile kt (128 keys) for the query block starting at global
 // position g0: some key of the tile has kend > g0.
@@ -106,6 +132,9 @@ __device__ __forceinline__ bool tile_full(const FaArgs& p, int kt, int g0, int g
 
 }  // namespace
 
+// DIAG: the phase-clock build (FaArgs::diag), kept out of the production
+// instance so that its code does not take instruction-cache space there
+template <bool DIAG>
 __global__ void __launch_bounds__(FA_THREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const FaArgs p) {
@@ -117,13 +146,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   uint64_t* k_empty = bars + 3;   // [2]
   uint64_t* v_full = bars + 5;    // [2]
   uint64_t* v_empty = bars + 7;   // [2]
-  uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* s_empty = bars + 11;  // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* pv_done = bars + 14;  // [2]: P V of tile m completes phase m>>1 of pv_done[m&1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* s_full = bars + 9;    // [FA_NS]: S of tile m completes phase (m/3)&1 of s_full[m%3]
+  // [FA_NS]: P of tile m (all softmax threads) completes phase (m/3)&1 of
+  // p_full[m%3]; one barrier per S buffer, as the softmax may finish tile
+  // m+1 before the MMA thread has waited for tile m
+  uint64_t* p_full = bars + 15;
+  uint64_t* pv_done = bars + 18;  // [FA_NS]: P V of tile m completes phase (m/3)&1 of pv_done[m%3]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint64_t* xbar = bars + 18;  // [4]: the two softmax warps of a lane quadrant exchange row max / sum
+  uint64_t* xbar = bars + 23;  // [4]: the two softmax warps of a lane quadrant exchange row max / sum
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * FB;  // local query row of the block
@@ -132,19 +163,23 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   const int g0 = p.q_off + q0;  // global position of the first query
   const int g_last = min(g0 + FB - 1, p.q_off + p.Tq - 1);
   const int kt_last = min(g_last / FB, (p.Tk - 1) / FB);
+  long long* dg = DIAG ? p.diag + (int64_t)(blockIdx.y * gridDim.x + blockIdx.x) * kFaDiag : nullptr;
+  auto tick = [&]() -> long long { return DIAG ? (long long)clock64() : 0ll; };
 
   if (threadIdx.x == 0) {
+    if (dg) dg[0] = clock64();
     mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 1);  // committed after the P V that read P from this buffer
-      mbar_init(&pv_done[s], 1);
     }
-    mbar_init(p_full, FA_SOFT);
+    for (int s = 0; s < FA_NS; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&pv_done[s], 1);
+      mbar_init(&p_full[s], FA_SOFT);
+    }
     for (int qd = 0; qd < 4; ++qd) mbar_init(&xbar[qd], 64);
     *abort_flag = 0;
     fence_barrier_init();
@@ -185,28 +220,53 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_o = tmem + 256;
+  const uint32_t tmem_o = tmem + FA_NS * FB;
   const int ntl = *tcount;
+  if (dg && threadIdx.x == 64) {
+    dg[1] = clock64();
+    dg[36] = ntl;
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      for (int n = 0; n < ntl; ++n) {
-        const int kt = tlist[n] & (TILE_FULL - 1);
-        const int s = n & 1;
-        const uint32_t ph = ((n >> 1) & 1) ^ 1;
-        if (!mbar_wait(&k_empty[s], ph, abort_flag, p.err, 11)) break;
+      long long wke = 0, wve = 0;
+      // K runs one tile ahead of V: K(0), K(1), V(0), K(2), V(1), ...  The
+      // S of tile n+2 is issued once P V of tile n-1 completes, and its K
+      // load must not queue behind the V load that waits for that P V
+      auto load_k = [&](int n) -> bool {
+        const int s = n & 1, kt = tlist[n] & (TILE_FULL - 1);
+        const long long c0 = tick();
+        if (!mbar_wait(&k_empty[s], ((n >> 1) & 1) ^ 1, abort_flag, p.err, 11)) return false;
+        wke += tick() - c0;
         uint8_t* kb = smem + OFF_K + s * TILE_BYTES;
         mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
         tma_load_2d(kb, &tmK, &k_full[s], hk * FB, kt * FB);
         tma_load_2d(kb + CHUNK_BYTES, &tmK, &k_full[s], hk * FB + 64, kt * FB);
-        if (!mbar_wait(&v_empty[s], ph, abort_flag, p.err, 19)) break;
+        return true;
+      };
+      auto load_v = [&](int n) -> bool {
+        const int s = n & 1, kt = tlist[n] & (TILE_FULL - 1);
+        const long long c0 = tick();
+        if (!mbar_wait(&v_empty[s], ((n >> 1) & 1) ^ 1, abort_flag, p.err, 19)) return false;
+        wve += tick() - c0;
         uint8_t* vb = smem + OFF_V + s * TILE_BYTES;
         mbar_arrive_expect_tx(&v_full[s], TILE_BYTES);
         tma_load_2d(vb, &tmV, &v_full[s], hk * FB, kt * FB);
         tma_load_2d(vb + CHUNK_BYTES, &tmV, &v_full[s], hk * FB + 64, kt * FB);
+        return true;
+      };
+      bool ok = ntl == 0 || load_k(0);
+      if (ok && ntl > 1) ok = load_k(1);
+      for (int n = 0; ok && n < ntl; ++n) {
+        ok = load_v(n);
+        if (ok && n + 2 < ntl) ok = load_k(n + 2);
+      }
+      if (dg) {
+        dg[44] = wke;
+        dg[45] = wve;
       }
     }
   } else if (warp == 1) {
@@ -215,41 +275,78 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       constexpr uint32_t idS = idesc_bf16(FB, FB);
       constexpr uint32_t idO = idesc_bf16_bmn(FB, FB);
       const uint32_t qa = smem_addr(smem + OFF_Q);
+      long long c0 = tick();
       bool ok = mbar_wait(q_full, 0, abort_flag, p.err, 12);
+      long long wq = tick() - c0, wk = 0, ws = 0, wp = 0, wv = 0, is = 0, ipv = 0;
       tc_fence_after();
-      auto issue_pv = [&](int n) -> bool {  // O += P_n V_n, P_n read from TMEM (S buffer n&1)
-        const int s = n & 1;
-        if (!mbar_wait(p_full, n & 1, abort_flag, p.err, 13)) return false;
+      auto issue_pv = [&](int n) -> bool {  // O += P_n V_n, P_n read from TMEM (S buffer n%3)
+        const int s = n & 1, b = n % FA_NS;
+        long long c1 = tick();
+        if (!mbar_wait(&p_full[b], (n / FA_NS) & 1, abort_flag, p.err, 13)) return false;
+        wp += tick() - c1;
+        c1 = tick();
         if (!mbar_wait(&v_full[s], (n >> 1) & 1, abort_flag, p.err, 10)) return false;
+        wv += tick() - c1;
         tc_fence_after();
         const uint32_t va = smem_addr(smem + OFF_V + s * TILE_BYTES);
-        const uint32_t pt = tmem + s * FB;  // each half's P in the first 32 columns of its S columns
+        const uint32_t pt = tmem + b * FB;  // each half's P in the first 32 columns of its S columns
+        c1 = tick();
 #pragma unroll
         for (int kk = 0; kk < FB / 16; ++kk)
           mma_bf16_ts(tmem_o, pt + (kk >> 2) * 64 + (kk & 3) * 8, desc_mn_sw128(va + kk * 2048, CHUNK_BYTES), idO,
                       (n > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&v_empty[s]);
-        mma_commit(&s_empty[s]);
-        mma_commit(&pv_done[s]);
+        mma_commit(&pv_done[b]);
+        if (dg) {
+          const long long c2 = clock64();
+          ipv += c2 - c1;
+          if (n < 16) dg[64 + n] = c2;
+        }
         return true;
       };
-      int n = 0;
-      if (ok) {
-        for (; n < ntl; ++n) {
-          const int s = n & 1, b = n & 1;
-          if (!mbar_wait(&k_full[s], (n >> 1) & 1, abort_flag, p.err, 14)) { ok = false; break; }
-          if (!mbar_wait(&s_empty[b], ((n >> 1) & 1) ^ 1, abort_flag, p.err, 15)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t ka = smem_addr(smem + OFF_K + s * TILE_BYTES);
+      // S(0), S(1), then per tile n: S(n+2) (into the buffer of tile n-1,
+      // whose P V was issued just before) and P V(n) (after the softmax of
+      // tile n), so the scores run two tiles ahead of the softmax
+      auto issue_s = [&](int n) -> bool {
+        const int s = n & 1, b = n % FA_NS;
+        long long c1 = tick();
+        if (!mbar_wait(&k_full[s], (n >> 1) & 1, abort_flag, p.err, 14)) return false;
+        wk += tick() - c1;
+        // no wait for the buffer: its last reader, P V of tile n-3, was
+        // issued before by this thread, and tcgen05.mma operations issued by
+        // one thread execute in issue order
+        if (dg && n == 0) dg[42] = clock64();
+        tc_fence_after();
+        const uint32_t ka = smem_addr(smem + OFF_K + s * TILE_BYTES);
+        c1 = tick();
 #pragma unroll
-          for (int kk = 0; kk < FB / 16; ++kk)
-            mma_bf16(tmem + b * FB, desc_k_sw128(qa + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32),
-                     desc_k_sw128(ka + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32), idS, kk > 0 ? 1u : 0u);
-          mma_commit(&s_full[b]);
-          mma_commit(&k_empty[s]);
-          if (n > 0 && !issue_pv(n - 1)) { ok = false; break; }
+        for (int kk = 0; kk < FB / 16; ++kk)
+          mma_bf16(tmem + b * FB, desc_k_sw128(qa + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32),
+                   desc_k_sw128(ka + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32), idS, kk > 0 ? 1u : 0u);
+        mma_commit(&s_full[b]);
+        mma_commit(&k_empty[s]);
+        if (dg) {
+          const long long c2 = clock64();
+          is += c2 - c1;
+          if (n < 16) dg[48 + n] = c2;
         }
-        if (ok && n > 0) issue_pv(n - 1);
+        return true;
+      };
+      if (ok && ntl > 0) ok = issue_s(0);
+      if (ok && ntl > 1) ok = issue_s(1);
+      for (int n = 0; ok && n < ntl; ++n) {
+        if (n + 2 < ntl) ok = issue_s(n + 2);
+        if (ok) ok = issue_pv(n);
+      }
+      if (dg) {
+        dg[37] = wk;
+        dg[38] = ws;
+        dg[39] = wp;
+        dg[40] = wv;
+        dg[41] = wq;
+        dg[43] = clock64();
+        dg[80] = is;
+        dg[81] = ipv;
       }
     }
   } else {
@@ -262,13 +359,30 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     float* xch = reinterpret_cast<float*>(smem + OFF_X);  // [slot][half][row]; slots 0/1 max, 2 sum
     float m_ref = -INFINITY, l = 0.f;  // l: this half's share of the row sum
+    int* ke_w = reinterpret_cast<int*>(smem + OFF_KE) + (warp - 2) * 64;
     int n = 0;
     bool ok = true;
     for (; n < ntl; ++n) {
       const int kt = tlist[n] & (TILE_FULL - 1);
       const bool full_tile = (tlist[n] & TILE_FULL) != 0;
-      const int b = n & 1;
-      if (!mbar_wait_warp(&s_full[b], (n >> 1) & 1, abort_flag, p.err, 16)) { ok = false; break; }
+      const int b = n % FA_NS, par = n & 1;
+      const int k0 = kt * FB + half * 64;
+      // a partially visible tile needs kend of the warp's 64 keys: each lane
+      // loads two before the wait for S (the load latency runs under it) and
+      // the warp shares them through its shared-memory slot afterwards
+      int2 kev = make_int2(0, 0);
+      if (!full_tile) {
+        const int j = k0 + 2 * lane;
+        if (j + 1 < p.Tk) kev = __ldg(reinterpret_cast<const int2*>(p.kend + j));
+        else if (j < p.Tk) kev.x = __ldg(p.kend + j);
+      }
+      if (!mbar_wait_warp(&s_full[b], (n / FA_NS) & 1, abort_flag, p.err, 16)) { ok = false; break; }
+      if (dg && threadIdx.x == 64 && n < 16) dg[2 + 2 * n] = clock64();
+      if (!full_tile) {
+        __syncwarp();  // the previous partial tile's reads are done
+        reinterpret_cast<int2*>(ke_w)[lane] = kev;
+        __syncwarp();
+      }
       tc_fence_after();
       float sv[64];
       {
@@ -281,27 +395,17 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(r[c][e]);
       }
-      // mask + scale, running max (fully visible tiles skip the mask)
-      const int k0 = kt * FB + half * 64;
-      float mx = -INFINITY;
+      // mask and running max on the raw scores (the scale is positive, so it
+      // is applied once to the max and folded into the exponent's FMA below);
+      // four independent max chains instead of one 64-long dependency chain
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (full_tile) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          sv[c] *= p.scale_log2;
-          mx = fmaxf(mx, sv[c]);
-        }
+        for (int c = 0; c < 64; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
       } else {
 #pragma unroll
         for (int c = 0; c < 64; c += 4) {
-          int4 ke = make_int4(0, 0, 0, 0);
-          if (k0 + c + 3 < p.Tk) {
-            ke = __ldg(reinterpret_cast<const int4*>(p.kend + k0 + c));
-          } else {
-            ke.x = k0 + c + 0 < p.Tk ? __ldg(p.kend + k0 + c + 0) : 0;
-            ke.y = k0 + c + 1 < p.Tk ? __ldg(p.kend + k0 + c + 1) : 0;
-            ke.z = k0 + c + 2 < p.Tk ? __ldg(p.kend + k0 + c + 2) : 0;
-            ke.w = k0 + c + 3 < p.Tk ? __ldg(p.kend + k0 + c + 3) : 0;
-          }
+          const int4 ke = reinterpret_cast<const int4*>(ke_w)[c / 4];  // keys past Tk hold 0: not visible
           const int kv[4] = {ke.x, ke.y, ke.z, ke.w};
           int pj[4] = {0, 0, 0, 0};
           if (p.window > 0) {
@@ -312,17 +416,18 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           for (int e = 0; e < 4; ++e) {
             const int j = k0 + c + e;
             const bool vis = (j <= gi) && (gi < kv[e]) && (p.window <= 0 || pos_i - pj[e] < p.window);
-            const float x = vis ? sv[c + e] * p.scale_log2 : -INFINITY;
+            const float x = vis ? sv[c + e] : -INFINITY;
             sv[c + e] = x;
-            mx = fmaxf(mx, x);
+            mx4[e] = fmaxf(mx4[e], x);
           }
         }
       }
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
       // row max over both halves (bounded mbarrier exchange between the two warps)
-      xch[(b * 2 + half) * FB + row] = mx;
+      xch[(par * 2 + half) * FB + row] = mx;
       mbar_arrive(&xbar[quad]);
       if (!mbar_wait_warp(&xbar[quad], n & 1, abort_flag, p.err, 19)) { ok = false; break; }
-      mx = fmaxf(mx, xch[(b * 2 + (half ^ 1)) * FB + row]);
+      mx = fmaxf(mx, xch[(par * 2 + (half ^ 1)) * FB + row]);
       // lazy rescale: a row moves its reference max only when the tile max
       // exceeds it by more than 2^8 (both halves decide alike: same max).
       // tcgen05.ld/st are warp-collective, so the warp rescales its O columns
@@ -330,11 +435,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       // does it wait for P V of the previous tile (O is being accumulated);
       // otherwise the softmax runs ahead of the P V MMAs.  The wait stays
       // within one phase: s_full of this tile already implies P V of tile
-      // n-2 completed (both were committed by the MMA thread in order).
+      // n-3 completed (both were committed by the MMA thread in order), and
+      // tile n-4 was the previous user of the barrier.
       const bool move = mx > m_ref + kRescaleThreshold || (m_ref == -INFINITY && mx > -INFINITY);
       const bool scale_o = move && n > 0 && m_ref > -INFINITY;
       if (__any_sync(0xffffffffu, scale_o)) {
-        if (!mbar_wait_warp(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort_flag, p.err, 17)) { ok = false; break; }
+        if (!mbar_wait_warp(&pv_done[(n - 1) % FA_NS], ((n - 1) / FA_NS) & 1, abort_flag, p.err, 17)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const float alpha = scale_o ? exp2f(m_ref - mx) : 1.f;
 #pragma unroll 1
@@ -353,28 +462,42 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       // P = exp2(s - m_ref) as bf16 into tensor memory: this half's 64 keys
       // as 32 columns of bf16 pairs over the first half of its own S columns
       // (the P V MMA reads its A operand there)
-      float rs = 0.f;
+      // exponent = s * scale_log2 - m_ref in one FMA; a masked score (-inf)
+      // gives exp2(-inf) = 0, and a row with no visible key yet (m_ref =
+      // -inf) subtracts 0 instead.  One pair in kExp2PolyEvery goes through
+      // the polynomial exp2 on the FMA pipe instead of the MUFU pipe, whose
+      // 16 results per clock per SM would otherwise bound the softmax.
+      const float nm = m_ref == -INFINITY ? 0.f : -m_ref;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const float x0 = sv[2 * c], x1 = sv[2 * c + 1];
-        const float e0 = (x0 == -INFINITY) ? 0.f : exp2f(x0 - m_ref);
-        const float e1 = (x1 == -INFINITY) ? 0.f : exp2f(x1 - m_ref);
-        rs += e0 + e1;
+        const float x0 = fmaf(sv[2 * c], p.scale_log2, nm), x1 = fmaf(sv[2 * c + 1], p.scale_log2, nm);
+        float e0, e1;
+        if (c % kExp2PolyEvery == kExp2PolyEvery - 1) {
+          e0 = exp2_poly(x0);
+          e1 = exp2_poly(x1);
+        } else {
+          e0 = exp2f(x0);
+          e1 = exp2f(x1);
+        }
+        rs4[c & 3] += e0 + e1;
         pk[c] = pack_bf16x2(e0, e1);
       }
       tmem_st32(tmem + lane_base + b * FB + half * 64, pk);
       tmem_wait_st();
-      l += rs;
+      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[b]);
+      if (dg && threadIdx.x == 64 && n < 16) dg[3 + 2 * n] = clock64();
     }
+    if (dg && threadIdx.x == 64) dg[34] = clock64();
     // epilogue: O / l and the LSE (the two halves' sums are exchanged once more)
     const int qrow = q0 + row;
     if (ok && n > 0) {
       xch[(4 + half) * FB + row] = l;  // own slot: the max slots may still be read by the partner
       bool got = false;
-      if (mbar_wait_warp(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort_flag, p.err, 18)) {
+      if (mbar_wait_warp(&pv_done[(n - 1) % FA_NS], ((n - 1) / FA_NS) & 1, abort_flag, p.err, 18)) {
         mbar_arrive(&xbar[quad]);
         got = mbar_wait_warp(&xbar[quad], n & 1, abort_flag, p.err, 20);
       }
@@ -423,9 +546,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       for (int j = 0; j < 64; j += 8) *reinterpret_cast<uint4*>(dst + j) = make_uint4(0, 0, 0, 0);
       if (half == 0) p.lse[(int64_t)h * p.Tq + qrow] = p.sinks ? __ldg(p.sinks + h) : -INFINITY;
     }
+    if (dg && threadIdx.x == 64) dg[35] = clock64();
   }
   tc_fence_before();
   __syncthreads();
+  if (dg && threadIdx.x == 0) dg[46] = clock64();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -437,7 +562,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kend,
                                        torch::Tensor tile_kmax, torch::Tensor tile_kmin, double scale, int64_t q_off,
                                        c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> tile_pmax,
-                                       int64_t window, c10::optional<torch::Tensor> sinks) {
+                                       int64_t window, c10::optional<torch::Tensor> sinks,
+                                       c10::optional<torch::Tensor> diag) {
   const int64_t Tq = q.size(0), Hq = q.size(1), D = q.size(2), Tk = k.size(0), Hkv = k.size(1);
   TORCH_CHECK(D == 128, "attention kernel supports head_dim 128");
   TORCH_CHECK(Hq % Hkv == 0, "GQA: q heads must be a multiple of kv heads");
@@ -496,13 +622,24 @@ std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::
                 sinks->numel() == Hq, "sinks: fp32 [Hq]");
     a.sinks = sinks->data_ptr<float>();
   }
+  a.diag = nullptr;
+  if (diag.has_value()) {
+    TORCH_CHECK(diag->is_cuda() && diag->scalar_type() == at::kLong && diag->is_contiguous() &&
+                diag->numel() >= ((Tq + FB - 1) / FB) * Hq * kFaDiag, "diag: int64 [ctas, ", kFaDiag, "]");
+    a.diag = reinterpret_cast<long long*>(diag->data_ptr<int64_t>());
+  }
   static bool attr = false;
   if (!attr) {
-    ART_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM));
+    const auto smem_attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    ART_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<false>, smem_attr, FA_SMEM));
+    ART_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<true>, smem_attr, FA_SMEM));
     attr = true;
   }
   dim3 grid((unsigned)((Tq + FB - 1) / FB), (unsigned)Hq);
-  attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, at::cuda::getCurrentCUDAStream()>>>(mq, mk, mv, a);
+  if (a.diag)
+    attn_fwd_tc_kernel<true><<<grid, FA_THREADS, FA_SMEM, at::cuda::getCurrentCUDAStream()>>>(mq, mk, mv, a);
+  else
+    attn_fwd_tc_kernel<false><<<grid, FA_THREADS, FA_SMEM, at::cuda::getCurrentCUDAStream()>>>(mq, mk, mv, a);
   ART_CUDA_CHECK(cudaGetLastError());
   return {o, lse};
 }

@@ -49,7 +49,8 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
 std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kend,
                                        torch::Tensor tile_kmax, torch::Tensor tile_kmin, double scale, int64_t q_off,
                                        c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> tile_pmax,
-                                       int64_t window, c10::optional<torch::Tensor> sinks);
+                                       int64_t window, c10::optional<torch::Tensor> sinks,
+                                       c10::optional<torch::Tensor> diag);
 std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                        torch::Tensor out, torch::Tensor lse, torch::Tensor kend, torch::Tensor units,
                                        double scale, int64_t q_off, c10::optional<torch::Tensor> pos, int64_t window);
@@ -142,7 +143,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_tc", &art::attn_fwd_tc, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("kend"),
         py::arg("tile_kmax"), py::arg("tile_kmin"), py::arg("scale"), py::arg("q_off") = 0,
         py::arg("pos") = py::none(), py::arg("tile_pmax") = py::none(), py::arg("window") = 0,
-        py::arg("sinks") = py::none());
+        py::arg("sinks") = py::none(), py::arg("diag") = py::none());
   m.def("attn_bwd_tc", &art::attn_bwd_tc, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
         py::arg("out"), py::arg("lse"), py::arg("kend"), py::arg("units"), py::arg("scale"), py::arg("q_off") = 0,
         py::arg("pos") = py::none(), py::arg("window") = 0);

@@ -99,6 +99,64 @@ def bench_attn(small: bool = False) -> None:
           dv=rel(g2[2], g1[2]), tc_error=int(C.tc_error_code()))
 
 
+def attn_diag(small: bool = False) -> None:
+    """Where a forward attention CTA's cycles go on the benchmark row: the
+    kernel's phase clocks (per CTA, SM cycles), as medians over CTAs."""
+    from . import fused, native
+    from ..preprocessing.prefix_tree import prefix_tree_pack, visibility_ends
+
+    torch.manual_seed(0)
+    n, P, Cl = (4, 512, 256) if small else (16, 1024, 512)
+    p = torch.randint(0, 1000, (P,))
+    seqs = [torch.cat([p, torch.randint(0, 1000, (Cl,))]) for _ in range(n)]
+    pack = prefix_tree_pack(seqs, max_depth=4096, shareable_lengths=[P - 1] * n)
+    kend = visibility_ends(pack.group_ids, pack.parent_ids)[0]
+    T, D, Hq, Hkv = kend.numel(), 128, 28, 4
+    dev = torch.device("cuda")
+    q = torch.randn(T, Hq, D, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(T, Hkv, D, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(T, Hkv, D, device=dev, dtype=torch.bfloat16)
+    meta = fused.AttnMeta.build(torch.arange(T), kend, dev)
+    C = native.lib()
+    sc = 1 / math.sqrt(D)
+    ctas = (T + 127) // 128 * Hq
+    dg = torch.zeros(ctas, 96, dtype=torch.int64, device=dev)
+    t_plain = _timed(lambda: C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, sc))
+    t_diag = _timed(lambda: C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, sc, diag=dg))
+    dg.zero_()
+    C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, sc, diag=dg)
+    torch.cuda.synchronize()
+    d = dg.cpu().double()
+    t0 = d[:, 0:1]
+    ntl = d[:, 36].clamp(min=1)
+    med = lambda x: round(float(x.median()), 1)  # noqa: E731
+    tiles = [n for n in range(16)]
+    soft = torch.stack([d[:, 3 + 2 * n] - d[:, 2 + 2 * n] for n in tiles], 1)
+    gap = torch.stack([d[:, 2 + 2 * (n + 1)] - d[:, 3 + 2 * n] for n in tiles[:-1]], 1)
+    valid = torch.arange(16).view(1, 16) < d[:, 36:37]
+    vgap = torch.arange(15).view(1, 15) < (d[:, 36:37] - 1)
+    _emit(case="attn_fwd_diag", T=T, ctas=ctas, ms_plain=round(t_plain, 4), ms_diag=round(t_diag, 4),
+          tiles_per_cta=med(ntl), cycles_total=med(d[:, 46] - t0), setup=med(d[:, 1] - t0),
+          first_s_issue=med(d[:, 42] - t0), first_s_ready=med(d[:, 2] - t0),
+          loop=med(d[:, 34] - d[:, 2]), loop_per_tile=med((d[:, 34] - d[:, 2]) / ntl),
+          softmax_per_tile=round(float(soft[valid].median()), 1),
+          wait_s_per_tile=round(float(gap[vgap].median()), 1) if vgap.any() else None,
+          epilogue=med(d[:, 35] - d[:, 34]), tail=med(d[:, 46] - d[:, 35]),
+          mma_wait_k=med(d[:, 37] / ntl), mma_wait_s_empty=med(d[:, 38] / ntl), mma_wait_p=med(d[:, 39] / ntl),
+          mma_wait_v=med(d[:, 40] / ntl), mma_wait_q=med(d[:, 41]), prod_wait_k_empty=med(d[:, 44] / ntl),
+          prod_wait_v_empty=med(d[:, 45] / ntl), mma_issue_s=med(d[:, 80] / ntl), mma_issue_pv=med(d[:, 81] / ntl),
+          tc_error=int(C.tc_error_code()))
+    # one CTA's timeline (SM cycles from its start): MMA-thread issue ends and softmax spans per tile
+    i = int(torch.argmax((d[:, 36] >= 10).double() * (d[:, 0] > 0).double()))
+    row = d[i]
+    rel = lambda x: int(x - row[0]) if x > 0 else None  # noqa: E731
+    m = int(min(row[36].item(), 16))
+    _emit(case="attn_fwd_diag_timeline", cta=i, tiles=int(row[36]), setup=rel(row[1]),
+          s_issued=[rel(row[48 + n]) for n in range(m)], pv_issued=[rel(row[64 + n]) for n in range(m)],
+          softmax_start=[rel(row[2 + 2 * n]) for n in range(m)], softmax_end=[rel(row[3 + 2 * n]) for n in range(m)],
+          epilogue_end=rel(row[35]), end=rel(row[46]))
+
+
 # ---------------------------------------------------------------------------
 def bench_gemm() -> None:
     from . import native
@@ -450,6 +508,8 @@ def main(argv: list[str]) -> None:
         gemm_one()
     elif which == "gemm_diag":
         gemm_diag()
+    elif which == "attn_diag":
+        attn_diag(small="--small" in argv)
     elif which == "gemm_pair_vs_cublas_one":
         gemm_pair_vs_cublas_one()
     elif which == "gdn":
@@ -459,7 +519,7 @@ def main(argv: list[str]) -> None:
     elif which == "comm":
         bench_comm()
     else:
-        raise SystemExit(f"unknown case {which!r}: attn | gemm | gemm_one | gemm_diag | gemm_pair_vs_cublas_one | gdn | norm | comm")
+        raise SystemExit(f"unknown case {which!r}: attn | attn_diag | gemm | gemm_one | gemm_diag | gemm_pair_vs_cublas_one | gdn | norm | comm")
 
 
 if __name__ == "__main__":

@@ -247,6 +247,9 @@ class AsyncCheckpointWriter:
         """Write this rank's slice of the AdamW moments into the published
         checkpoint ``path`` (one device-to-host copy of the slice, the file
         written on the background thread)."""
+        if not os.path.isdir(path):
+            raise FileNotFoundError(f"optimizer shard of rank {rank}: checkpoint directory {path} not published "
+                                    "(every rank must share the model directory)")
         cuda = store.master.device.type == "cuda"
         # two pinned slots reused across steps (a pinned allocation per call
         # costs more than the copy)

@@ -263,8 +263,10 @@ def main() -> None:
     train_tokens = float(packed["assistant_mask"][:, 1:].sum())
     packed_tokens = int((packed["group_ids"] >= 0).sum())
 
+    # tokens a rank holds: a context-parallel row is padded to 128 tokens per rank
+    rank_tokens = max(16384, -(-seq_len // (128 * args.cp)) * 128)
     trainer = GRPOTrainer(cfg, lora, device, seed=0, group=dist.group.WORLD if world > 1 else None,
-                          tp_size=args.tp, cp_size=args.cp, max_tokens_per_rank=max(16384, seq_len),
+                          tp_size=args.tp, cp_size=args.cp, max_tokens_per_rank=rank_tokens,
                           fused_dp=not args.unfused)
     lr = 1e-5
     loss_cfg: dict = {"kl_penalty_coef": args.kl} if args.kl else {}
@@ -405,7 +407,12 @@ def run_e2e(args, cfg, lora, groups, trainer, device, world, rank, train_tokens)
     except Exception as exc:  # pragma: no cover
         return {"value": None, "unavailable": f"{type(exc).__name__}: {exc}"}
 
-    tmp = tempfile.mkdtemp(prefix="artb200_bench_")
+    # one model directory for the whole job: rank 0 publishes the adapter
+    # there and every rank adds its optimizer shard
+    tmp = [tempfile.mkdtemp(prefix="artb200_bench_") if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(tmp, src=0)
+    tmp = tmp[0]
     backend = LocalBackend(path=tmp, trainer=trainer)
     model = TrainableModel(
         name="bench", project="bench", base_model=cfg.name,
