@@ -380,15 +380,30 @@ class _LocalExperts(torch.autograd.Function):
     @staticmethod
     def forward(ctx, xs, counts, params, lora, anchor):
         out, saved = experts_forward(xs, counts, params, lora)
-        ctx.saved = saved
+        _save_expert_state(ctx, saved)
         ctx.params = params
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        dxs = experts_backward(dout, ctx.saved, ctx.params)
-        ctx.saved = None
+        dxs = experts_backward(dout, _expert_state(ctx, ctx.saved_tensors), ctx.params)
         return dxs, None, None, None, None
+
+
+def _save_expert_state(ctx, saved, *extra: torch.Tensor | None) -> None:
+    """Keep the expert activations through ``save_for_backward`` (so that
+    activation recompute can drop and regenerate them); the group sizes and
+    the LoRA flag stay on ``ctx``."""
+    xs, gu, act, u_gu, u_d, counts, lora = saved
+    ctx.save_for_backward(xs, gu, act, u_gu, u_d, *extra)
+    ctx.expert_meta = (counts, lora)
+
+
+def _expert_state(ctx, saved_tensors):
+    """The ``experts_backward`` state from ``ctx.saved_tensors`` (read once
+    per backward: under recompute each read regenerates the tensors)."""
+    xs, gu, act, u_gu, u_d = saved_tensors[:5]
+    return (xs, gu, act, u_gu, u_d, *ctx.expert_meta)
 
 
 def native_combine(slots: torch.Tensor, w: torch.Tensor | None, k: int) -> torch.Tensor:
@@ -420,24 +435,24 @@ class _EPExperts(torch.autograd.Function):
         from ..parallel import mutation
 
         y = native_combine(slots, None if mutation.active("ep_skip_combine_weights") else w, plan.k)
-        ctx.plan, ctx.ep, ctx.params, ctx.saved = plan, ep, params, saved
-        ctx.save_for_backward(slots, w)
+        ctx.plan, ctx.ep, ctx.params = plan, ep, params
+        _save_expert_state(ctx, saved, slots, w)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        slots, w = ctx.saved_tensors
+        saved = ctx.saved_tensors
+        slots, w = saved[5:]
         plan, ep, params = ctx.plan, ctx.ep, ctx.params
         tr = ep.transport
         dy = dy.contiguous()
         T, k = plan.T, plan.k
         dw = (slots.view(T, k, -1).float() * dy.view(T, 1, -1).float()).sum(-1)
         d_recv = tr.push(plan, dy, w.reshape(-1).float().contiguous(), 2)
-        dxs = experts_backward(d_recv.clone(), ctx.saved, params)
+        dxs = experts_backward(d_recv.clone(), _expert_state(ctx, saved), params)
         tr.publish(dxs, 3)
         dslots = tr.pull(plan, 3)
         dh = native_combine(dslots, None, k)
-        ctx.saved = None
         return dh, dw.to(w.dtype), None, None, None, None, None
 
 

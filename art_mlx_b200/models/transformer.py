@@ -19,6 +19,7 @@ parameter names onto the fused layout when real weights are available.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -58,6 +59,13 @@ class Layer:
     mlp: DenseMLP | None = None
     moe: MoEBlock | None = None
     gdn: Any = None
+
+
+def recompute_enabled() -> bool:
+    """``ART_B200_RECOMPUTE=full`` (or 1): recompute every layer's
+    activations in the backward (the reference's Megatron provider default,
+    uniform full recompute of one layer at a time)."""
+    return os.environ.get("ART_B200_RECOMPUTE", "").strip().lower() in {"1", "full", "true", "yes", "on"}
 
 
 def _randn(shape, gen, device, dtype, std=0.02) -> torch.Tensor:
@@ -186,6 +194,9 @@ class DecoderLM:
         for i in range(cfg.num_hidden_layers):
             self.layers.append(self._build_layer(i, gen))
         self.lora_enabled = True
+        # full activation recompute per layer (the training forward keeps each
+        # layer's inputs only); off by default
+        self.recompute = recompute_enabled()
 
     # ------------------------------------------------------------------
     def _build_layer(self, i: int, gen: torch.Generator) -> Layer:
@@ -272,6 +283,23 @@ class DecoderLM:
         a = fused.swiglu(gu)
         return fused.lora_linear(a, m.down_w, None, m.down_lora, v, en)
 
+    def _layer(self, layer: Layer, out: torch.Tensor, resid: torch.Tensor | None, meta: AttnMeta,
+               ctx: dict[str, Any]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """One decoder layer on the residual stream: ``(mlp out, residual,
+        mixer out)``."""
+        eps = self.cfg.rms_norm_eps
+        h, resid = fused.add_rmsnorm(out, resid, layer.in_norm, eps)
+        if layer.kind == "attention":
+            a = self.attention(layer, h, meta, ctx)
+        elif ctx.get("cp_plan") is not None:
+            from ..parallel.cp import cp_gdn
+
+            a = cp_gdn(layer.gdn, h, ctx["cp_plan"], ctx["cp"], self.store.version, self.lora_enabled)
+        else:
+            a = layer.gdn(h, meta, self.store.version, self.lora_enabled, ctx)
+        h, resid = fused.add_rmsnorm(a, resid, layer.post_norm, eps)
+        return self.mlp(layer, h, ctx), resid, a
+
     def forward(
         self, tokens: torch.Tensor, meta: AttnMeta, ctx: dict[str, Any] | None = None
     ) -> torch.Tensor:
@@ -290,18 +318,18 @@ class DecoderLM:
                 plan = ctx.get("cp_plan")
                 start = plan.a if plan is not None else 0
                 uids = torch.arange(start, start + tokens.shape[0])
+        # full activation recompute: a layer keeps only its inputs and runs
+        # its forward again in the backward (every rank in the same order, so
+        # the collectives inside a layer stay matched)
+        recompute = self.recompute and torch.is_grad_enabled() and trace is None
         for layer in self.layers:
-            h, resid = fused.add_rmsnorm(out, resid, layer.in_norm, eps)
-            if layer.kind == "attention":
-                a = self.attention(layer, h, meta, ctx)
-            elif ctx.get("cp_plan") is not None:
-                from ..parallel.cp import cp_gdn
+            if recompute and resid is not None:
+                from torch.utils.checkpoint import checkpoint
 
-                a = cp_gdn(layer.gdn, h, ctx["cp_plan"], ctx["cp"], self.store.version, self.lora_enabled)
+                out, resid, a = checkpoint(self._layer, layer, out, resid, meta, ctx, use_reentrant=False,
+                                           preserve_rng_state=False)
             else:
-                a = layer.gdn(h, meta, self.store.version, self.lora_enabled, ctx)
-            h, resid = fused.add_rmsnorm(a, resid, layer.post_norm, eps)
-            out = self.mlp(layer, h, ctx)
+                out, resid, a = self._layer(layer, out, resid, meta, ctx)
             if trace is not None:
                 trace.record(layer.index, "mixer", a, uids)
                 trace.record(layer.index, "mlp", out, uids)

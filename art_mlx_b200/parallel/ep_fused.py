@@ -290,17 +290,15 @@ class FusedEPExperts(torch.autograd.Function):
                               fep.slot_count, target)
         slots = fep.slots[: plan.T * plan.k].clone()
         ctx.fep, ctx.plan, ctx.p, ctx.lora = fep, plan, p, lora
-        ctx.saved = (xs, gu, act, u_gu, u_d, row_dst, slots)
-        ctx.save_for_backward(w)
+        # through save_for_backward, so that activation recompute can drop them
+        ctx.save_for_backward(w, xs, gu, act, u_gu, u_d, row_dst, slots)
         return y
 
     @staticmethod
     def backward(ctx, dy):
         C = native.lib()
-        (w,) = ctx.saved_tensors
+        w, xs, gu, act, u_gu, u_d, row_dst, slots = ctx.saved_tensors
         fep, plan, p, lora = ctx.fep, ctx.plan, ctx.p, ctx.lora
-        xs, gu, act, u_gu, u_d, row_dst, slots = ctx.saved
-        ctx.saved = None
         dy = dy.contiguous()
         T, k = plan.T, plan.k
         s = p.scale

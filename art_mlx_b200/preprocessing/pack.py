@@ -84,23 +84,16 @@ DISK_DTYPES: dict[str, torch.dtype] = {
 
 
 class _Item(NamedTuple):
-    token_ids: tuple[int, ...]
-    input_pos: tuple[int, ...]
-    assistant_mask: tuple[int, ...]
-    logprobs: tuple[float, ...]
+    token_ids: tuple[int, ...]  # a tuple: the planner compares sequences lexicographically
+    input_pos: np.ndarray  # int64
+    assistant_mask: np.ndarray  # int64
+    logprobs: np.ndarray  # float64
     advantage: float
     weight: float
     prompt_id: int
     shareable: int
     routes: tuple[Any, ...] | None
-
-
-def _first_trainable(r: TokenizedResult) -> int:
-    n = min(len(r.assistant_mask), len(r.logprobs))
-    m = np.asarray(r.assistant_mask[:n], dtype=bool)
-    lp = np.asarray(r.logprobs[:n], dtype=np.float64)
-    hit = np.flatnonzero(m | ~np.isnan(lp))
-    return int(hit[0]) if hit.size else len(r.token_ids)
+    tokens: np.ndarray  # int64 copy of token_ids
 
 
 def _ints(v: Any) -> tuple:
@@ -108,17 +101,26 @@ def _ints(v: Any) -> tuple:
 
 
 def _item(r: TokenizedResult, seq_len: int) -> _Item:
-    share = min(int(r.prompt_length), max(_first_trainable(r) - 1, 0))
+    """The packer's view of a result: numpy arrays converted once, so the
+    row packer works on them without per-row list conversions."""
+    toks = np.asarray(r.token_ids, dtype=np.int64)
+    am = np.asarray(r.assistant_mask, dtype=np.int64)
+    lp = np.asarray(r.logprobs, dtype=np.float64)
+    n = min(len(am), len(lp))
+    hit = np.flatnonzero((am[:n] != 0) | ~np.isnan(lp[:n]))
+    first = int(hit[0]) if hit.size else len(toks)
+    share = min(int(r.prompt_length), max(first - 1, 0))
     it = _Item(
         _ints(r.token_ids),
-        _ints(r.input_pos),
-        _ints(r.assistant_mask),
-        _ints(r.logprobs),
+        np.asarray(r.input_pos, dtype=np.int64),
+        am,
+        lp,
         float(r.advantage),
         float(r.weight),
         int(r.prompt_id),
         share,
         tuple(r.moe_routed_experts) if r.moe_routed_experts is not None else None,
+        toks,
     )
     return _truncate(it, seq_len)
 
@@ -133,6 +135,7 @@ def _truncate(it: _Item, seq_len: int) -> _Item:
         logprobs=it.logprobs[:seq_len],
         shareable=min(it.shareable, seq_len),
         routes=it.routes[:seq_len] if it.routes is not None else None,
+        tokens=it.tokens[:seq_len],
     )
 
 
@@ -169,12 +172,9 @@ def _pack_row(row: list[_Item], seq_len: int, share: bool) -> dict[str, list]:
     for k, it in enumerate(row):
         dst = per_seq[k]
         m = len(dst)
-        tk = np.asarray(it.token_ids[:m], dtype=np.int64)
-        if (toks[dst] != tk).any():
+        if (toks[dst] != it.tokens[:m]).any():
             raise RuntimeError("Prefix-tree pack token assignment mismatch")
-        ip = np.asarray(it.input_pos[:m], dtype=np.int64)
-        am = np.asarray(it.assistant_mask[:m], dtype=np.int64)
-        lp = np.asarray(it.logprobs[:m], dtype=np.float64)
+        ip, am, lp = it.input_pos[:m], it.assistant_mask[:m], it.logprobs[:m]
         shared = owned[dst]
         if shared.any():
             if (pos[dst[shared]] != ip[shared]).any():
@@ -229,8 +229,8 @@ def _step_normalisation(rows: list[list[_Item]], advantage_balance: float) -> tu
     first_masked = 0
     for row in rows:
         for k, it in enumerate(row):
-            c = float(sum(it.assistant_mask))
-            if k == 0 and it.assistant_mask and it.assistant_mask[0]:
+            c = float(it.assistant_mask.sum())
+            if k == 0 and len(it.assistant_mask) and it.assistant_mask[0]:
                 first_masked += 1
             items.append((c, it.weight, it.advantage))
             n += c

@@ -329,7 +329,10 @@ class GRPOTrainer:
         cp_size: int = 1,
         etp_size: int = 1,
         allow_unvalidated_arch: bool = False,
+        recompute: bool | None = None,
     ) -> None:
+        """``recompute``: full activation recompute per layer (``None``: the
+        ``ART_B200_RECOMPUTE`` environment switch)."""
         from ..models.registry import check_parallelism, get_model_support
 
         self.support = get_model_support(cfg, allow_unvalidated_arch)
@@ -400,6 +403,11 @@ class GRPOTrainer:
             self.model = TPDecoderLM(cfg, lora, self.device, self.tp, seed=seed, store=store)
         else:
             self.model = DecoderLM(cfg, lora, self.device, seed=seed, store=store, ep=self.ep, etp=self.etp)
+        if recompute is not None:
+            if recompute and not hasattr(self.model, "recompute"):
+                raise ValueError("activation recompute is not available for the tensor-parallel decoder")
+            if hasattr(self.model, "recompute"):
+                self.model.recompute = bool(recompute)
         self.store = self.model.store
         self.optim = FlatAdamW(self.store, adamw)
         self.logprob_chunk = logprob_chunk

@@ -56,6 +56,9 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--unfused", action="store_true",
                    help="the unfused baseline of this framework: cuBLAS projections and LM head, NCCL all-reduce "
                         "of the LoRA gradients and a replicated AdamW (the comparison point of the fused kernels)")
+    p.add_argument("--recompute", default=None, choices=["none", "full"],
+                   help="activation recompute per layer (default: the config's choice; the hybrid config "
+                        "recomputes, as its 65,536-token row does not leave room for every layer's activations)")
     p.add_argument("--kernel-table", default=None,
                    help="write the device time per kernel of one profiled (untimed) step to this file, per rank")
     a = p.parse_args()
@@ -86,7 +89,7 @@ CONFIGS = {
     "moe30b": dict(model="qwen3-30b-a3b", groups=4, rollouts=8, prompt_len=2048, completion_len=1024,
                    lora_rank=8, kl=0.0, par="ep"),
     "hybrid": dict(model="qwen3-next-hybrid", groups=1, rollouts=8, prompt_len=8192, completion_len=7168,
-                   lora_rank=16, kl=0.0, par="cp"),
+                   lora_rank=16, kl=0.0, par="cp", recompute=True),
     "dense32b": dict(model="qwen3-32b", groups=16, rollouts=8, prompt_len=4096, completion_len=1024,
                      lora_rank=32, kl=0.01, par="tp"),
 }
@@ -265,8 +268,10 @@ def main() -> None:
 
     # tokens a rank holds: a context-parallel row is padded to 128 tokens per rank
     rank_tokens = max(16384, -(-seq_len // (128 * args.cp)) * 128)
+    recompute = args.recompute == "full" if args.recompute else bool(CONFIGS[args.config].get("recompute"))
     trainer = GRPOTrainer(cfg, lora, device, seed=0, group=dist.group.WORLD if world > 1 else None,
                           tp_size=args.tp, cp_size=args.cp, max_tokens_per_rank=rank_tokens,
+                          recompute=recompute,
                           fused_dp=not args.unfused)
     lr = 1e-5
     loss_cfg: dict = {"kl_penalty_coef": args.kl} if args.kl else {}
@@ -371,6 +376,7 @@ def main() -> None:
                 "completion_len": args.completion_len,
                 "lora_rank": args.lora_rank,
                 "parallelism": parallelism,
+                "activation_recompute": "full" if recompute else "none",
                 "rows_per_step": n_rows,
                 "trained_tokens_per_step": int(train_tokens),
                 "packed_tokens_per_step": packed_tokens,
