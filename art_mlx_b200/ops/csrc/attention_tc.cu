@@ -672,14 +672,19 @@ std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::
 namespace {
 
 constexpr int QDO_ST = 1;  // Q / dO stages (shared memory goes to the dQ staging below)
-constexpr int DQ_LD = 36;  // row stride (floats) of a warp's 32x32 dQ staging block: conflict-free both ways
 constexpr int B_OFF_K = 0;
 constexpr int B_OFF_V = TILE_BYTES;
 constexpr int B_OFF_Q = 2 * TILE_BYTES;
 constexpr int B_OFF_DO = B_OFF_Q + QDO_ST * TILE_BYTES;
 constexpr int B_OFF_DS = B_OFF_DO + QDO_ST * TILE_BYTES;
-constexpr int B_OFF_DQ = B_OFF_DS + TILE_BYTES;       // 8 warps x [32][DQ_LD] fp32
-constexpr int B_OFF_BAR = B_OFF_DQ + 8 * 32 * DQ_LD * 4;
+// per softmax warp a 32 x 32 fp32 block in the 128-byte-swizzled layout of a
+// TMA box (the source of the dQ / dK / dV reduce-adds); 1024-byte aligned
+constexpr int B_OFF_DQ = B_OFF_DS + TILE_BYTES;
+constexpr int B_STG = 32 * 32 * 4;
+// per softmax warp: log2-scaled LSE, delta and (sliding window) positions of
+// its 64 query columns of the current tile
+constexpr int B_OFF_LD = B_OFF_DQ + 8 * B_STG;
+constexpr int B_OFF_BAR = B_OFF_LD + 8 * 3 * 64 * 4;
 constexpr int FB_SMEM = B_OFF_BAR + 256 + 1024;
 // 2 control warps + 8 softmax warps: two warps per TMEM lane quadrant, each
 // taking 64 of the 128 query columns (the backward needs no row reduction)
@@ -699,12 +704,10 @@ struct FbArgs {
   int* err;
   const int* pos;  // [Tk] token positions (sliding window only)
   int window;      // > 0: also pos[query] - pos[key] < window
+  long long* diag;  // phase clocks per CTA (diag build only), kFbDiag int64 slots each
 };
+constexpr int kFbDiag = 96;
 
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
 
 }  // namespace
 
@@ -724,10 +727,13 @@ __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ dout, co
   if (lane == 0) delta[(int64_t)h * Tq + t] = s;
 }
 
+// DIAG: the phase-clock build (FbArgs::diag), kept out of the production instance
+template <bool DIAG>
 __global__ void __launch_bounds__(FB_THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                       const FbArgs p) {
+                       const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmDK,
+                       const __grid_constant__ CUtensorMap tmDV, const FbArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + B_OFF_BAR);
@@ -749,8 +755,14 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
   const int G = p.Hq / p.Hkv;
   const int ntiles = t_hi - t_lo;
   const int iters = G * ntiles;  // iteration i: head hk*G + i / ntiles, tile t_lo + i % ntiles
+  long long* dg = DIAG ? p.diag + (int64_t)(blockIdx.y * gridDim.x + blockIdx.x) * kFbDiag : nullptr;
+  auto tick = [&]() -> long long { return DIAG ? (long long)clock64() : 0ll; };
 
   if (threadIdx.x == 0) {
+    if (dg) {
+      dg[0] = clock64();
+      dg[2] = iters;
+    }
     mbar_init(kv_full, 1);
     for (int st = 0; st < 2; ++st) {
       mbar_init(&qdo_full[st], 1);
@@ -769,10 +781,12 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (dg && threadIdx.x == 64) dg[1] = clock64();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      long long wqe = 0;
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
@@ -785,7 +799,9 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       for (int i = 0; i < iters; ++i) {  // Q / dO double-buffered: tile i+1 loads while tile i computes
         const int h = hk * G + i / ntiles, t = t_lo + i % ntiles;
         const int st = i % QDO_ST;
+        const long long c0 = tick();
         if (!mbar_wait(&qdo_empty[st], ((i / QDO_ST) & 1) ^ 1, abort_flag, p.err, 21)) break;
+        wqe += tick() - c0;
         uint8_t* qb = smem + B_OFF_Q + st * TILE_BYTES;
         uint8_t* db = smem + B_OFF_DO + st * TILE_BYTES;
         mbar_arrive_expect_tx(&qdo_full[st], 2 * TILE_BYTES);
@@ -794,6 +810,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         tma_load_2d(db, &tmDO, &qdo_full[st], h * FB, t * FB);
         tma_load_2d(db + CHUNK_BYTES, &tmDO, &qdo_full[st], h * FB + 64, t * FB);
       }
+      if (dg) dg[78] = wqe;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -803,32 +820,46 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       constexpr uint32_t idMM = idesc_bf16_bmn(FB, FB) | (1u << 15);  // A and B MN-major
       const uint32_t ka = smem_addr(smem + B_OFF_K), va = smem_addr(smem + B_OFF_V);
       const uint32_t dsa = smem_addr(smem + B_OFF_DS);
+      long long w_q = 0, w_dv = 0, i_dp = 0, w_dq = 0, i_s = 0, w_ds = 0, i_dvdk = 0, i_dq = 0, c0 = 0;
       if (mbar_wait(kv_full, 0, abort_flag, p.err, 22)) {
         for (int i = 0; i < iters; ++i) {
           const int st = i % QDO_ST;
           const uint32_t qa = smem_addr(smem + B_OFF_Q + st * TILE_BYTES);
           const uint32_t doa = smem_addr(smem + B_OFF_DO + st * TILE_BYTES);
+          c0 = tick();
           if (!mbar_wait(&qdo_full[st], (i / QDO_ST) & 1, abort_flag, p.err, 23)) break;
+          w_q += tick() - c0;
           // dP^T = V dO^T first: its columns (128..255) only have to be free of
           // the previous tile's P^T, i.e. its dV MMA done; it then runs while
           // the softmax warps still read the previous dQ out of columns 0..127
+          c0 = tick();
           if (i > 0 && !mbar_wait(dv_done, (i - 1) & 1, abort_flag, p.err, 28)) break;
+          w_dv += tick() - c0;
           tc_fence_after();
+          c0 = tick();
 #pragma unroll
           for (int kk = 0; kk < FB / 16; ++kk) {
             const uint32_t ko = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
             mma_bf16(tmem + 128, desc_k_sw128(va + ko), desc_k_sw128(doa + ko), idKK, kk > 0 ? 1u : 0u);
           }
+          i_dp += tick() - c0;
+          c0 = tick();
           if (!mbar_wait(dq_free, (i & 1) ^ 1, abort_flag, p.err, 24)) break;
+          w_dq += tick() - c0;
           tc_fence_after();
+          c0 = tick();
 #pragma unroll
           for (int kk = 0; kk < FB / 16; ++kk) {
             const uint32_t ko = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
             mma_bf16(tmem + 0, desc_k_sw128(ka + ko), desc_k_sw128(qa + ko), idKK, kk > 0 ? 1u : 0u);
           }
           mma_commit(sdp_full);
+          i_s += tick() - c0;
+          c0 = tick();
           if (!mbar_wait(ds_full, i & 1, abort_flag, p.err, 25)) break;
+          w_ds += tick() - c0;
           tc_fence_after();
+          c0 = tick();
 #pragma unroll
           for (int kk = 0; kk < FB / 16; ++kk) {
             const uint32_t ko = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
@@ -841,12 +872,25 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
           }
           mma_commit(&qdo_empty[st]);
           mma_commit(dv_done);
+          i_dvdk += tick() - c0;
+          c0 = tick();
 #pragma unroll
           for (int kk = 0; kk < FB / 16; ++kk)
             mma_bf16(tmem + 0, desc_mn_sw128(dsa + kk * 2048, CHUNK_BYTES),
                      desc_mn_sw128(ka + kk * 2048, CHUNK_BYTES), idMM, kk > 0 ? 1u : 0u);
           mma_commit(dq_full);
+          i_dq += tick() - c0;
         }
+      }
+      if (dg) {
+        dg[70] = w_q;
+        dg[71] = w_dv;
+        dg[72] = i_dp;
+        dg[73] = w_dq;
+        dg[74] = i_s;
+        dg[75] = w_ds;
+        dg[76] = i_dvdk;
+        dg[77] = i_dq;
       }
     }
   } else {
@@ -859,11 +903,22 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
     const int kend_j = j < p.Tk ? __ldg(p.kend + j) : 0;
     const int pos_j = (p.window > 0 && j < p.Tk) ? __ldg(p.pos + j) : 0;
     const int sw = row & 7;
+    // the warp's 32 keys: a 32-query chunk is fully visible to all of them
+    // when it lies at or after the last key and before the smallest kend
+    int kmin_w = j < p.Tk ? kend_j : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) kmin_w = min(kmin_w, __shfl_xor_sync(0xffffffffu, kmin_w, o));
+    const int jmax_w = kb * FB + quad * 32 + 31;
+    float* lsw = reinterpret_cast<float*>(smem + B_OFF_LD) + (warp - 2) * 3 * 64;  // [lse2 64][delta 64][pos 64]
+    int* psw = reinterpret_cast<int*>(lsw + 128);
+    uint8_t* stg = smem + B_OFF_DQ + (warp - 2) * B_STG;
+    // the warp's own rows of the dS tile: 32 keys x 64 queries = 4 KB, 1024-byte aligned
+    uint8_t* stg2 = smem + B_OFF_DS + half * CHUNK_BYTES + quad * 32 * 128;
     bool ok = true;
     for (int i = 0; i < iters && ok; ++i) {
       const int h = hk * G + i / ntiles, t = t_lo + i % ntiles;
-      // lane e fetches the LSE / delta of query column c*32+e (shared by
-      // shuffles); issued before the MMA wait so the loads overlap it
+      // lane e fetches the LSE / delta of query columns 64*half + e and +32,
+      // issued before the MMA wait so the loads overlap it
       const float* lse_h = p.lse + (int64_t)h * p.Tq;
       const float* del_h = p.delta + (int64_t)h * p.Tq;
       float lse_pf[2], del_pf[2];
@@ -876,6 +931,17 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         if (p.window > 0) pos_pf[cc] = ql_mine < p.Tq ? __ldg(p.pos + p.q_off + ql_mine) : 0;
       }
       if (!mbar_wait_warp(sdp_full, i & 1, abort_flag, p.err, 26)) { ok = false; break; }
+      if (dg && threadIdx.x == 64 && i < 16) dg[4 + 4 * i] = clock64();
+      // shared with the whole warp through its slot (broadcast reads below
+      // instead of three shuffles per element)
+      __syncwarp();
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        lsw[cc * 32 + lane] = lse_pf[cc];
+        lsw[64 + cc * 32 + lane] = del_pf[cc];
+        psw[cc * 32 + lane] = pos_pf[cc];
+      }
+      __syncwarp();
       tc_fence_after();
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
@@ -884,30 +950,41 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         uint32_t pp[16];  // P^T of these 32 queries, bf16 pairs
         tmem_ld32(tmem + lane_base + c * 32, rs);
         tmem_ld32(tmem + lane_base + 128 + c * 32, rd);
-        const float lse_mine = lse_pf[cc];
-        const float del_mine = del_pf[cc];
-        const int pos_mine = pos_pf[cc];
+        const int q0c = t * FB + c * 32;  // local query of the chunk's first column
+        const bool full = p.window <= 0 && jmax_w <= p.q_off + q0c && kmin_w > p.q_off + q0c + 31 &&
+                          q0c + 31 < p.Tq;
         tmem_wait_ld();
+        if (dg && threadIdx.x == 64 && i < 8 && cc == 0) dg[80 + 2 * i] = clock64();
         uint32_t dd[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float pv[2], dv2[2];
+        for (int e = 0; e < 32; e += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(lsw + cc * 32 + e);
+          const float4 d4 = *reinterpret_cast<const float4*>(lsw + 64 + cc * 32 + e);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+          float pv[4], ds[4];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int ql = t * FB + c * 32 + e + u;
-            const int qg = p.q_off + ql;
-            const float l2 = __shfl_sync(0xffffffffu, lse_mine, e + u);
-            const float de = __shfl_sync(0xffffffffu, del_mine, e + u);
-            const int pq = __shfl_sync(0xffffffffu, pos_mine, e + u);
-            const bool vis = (j <= qg) && (qg < kend_j) && (ql < p.Tq) && (p.window <= 0 || pq - pos_j < p.window);
-            const float pr = vis ? exp2f(__uint_as_float(rs[e + u]) * p.scale_log2 - l2) : 0.f;
+          for (int u = 0; u < 4; ++u) {
+            // queries past Tq carry LSE = +inf: their P is 0 on either path
+            float pr = exp2f(fmaf(__uint_as_float(rs[e + u]), p.scale_log2, -lv[u]));
+            if (!full) {
+              const int qg = p.q_off + q0c + e + u;
+              const bool vis = (j <= qg) && (qg < kend_j) && (p.window <= 0 || psw[cc * 32 + e + u] - pos_j < p.window);
+              pr = vis ? pr : 0.f;
+            }
             pv[u] = pr;
-            dv2[u] = pr * (__uint_as_float(rd[e + u]) - de);
+            ds[u] = pr * (__uint_as_float(rd[e + u]) - dv4[u]);
           }
           pp[e >> 1] = pack_bf16x2(pv[0], pv[1]);
-          dd[e >> 1] = pack_bf16x2(dv2[0], dv2[1]);
+          pp[(e >> 1) + 1] = pack_bf16x2(pv[2], pv[3]);
+          dd[e >> 1] = pack_bf16x2(ds[0], ds[1]);
+          dd[(e >> 1) + 1] = pack_bf16x2(ds[2], ds[3]);
         }
-        // 32 queries = 4 units of 16 bytes of this key's row
+        // 32 queries = 4 units of 16 bytes of this key's row (the warp's dS
+        // block doubles as dQ staging: the reduce that read it has finished)
+        if (cc == 0) {
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+        }
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           const int u = c * 4 + w;  // unit along the 128-query row
@@ -919,75 +996,83 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         // warp has already read (chunk cc = 0)
         tmem_st16(tmem + lane_base + 128 + half * 64 + cc * 16, pp);
       }
+      if (dg && threadIdx.x == 64 && i < 8) dg[81 + 2 * i] = clock64();
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
+      if (dg && threadIdx.x == 64 && i < 16) dg[5 + 4 * i] = clock64();
       // dQ tile: lanes are queries now
       if (!mbar_wait_warp(dq_full, i & 1, abort_flag, p.err, 27)) { ok = false; break; }
+      if (dg && threadIdx.x == 64 && i < 16) dg[6 + 4 * i] = clock64();
       tc_fence_after();
-      // Each lane holds one query row of the chunk; the atomic adds go out
-      // transposed through a per-warp staging block so that one warp
-      // instruction covers 4 rows x 128 contiguous bytes (whole L2 sectors)
-      // instead of 32 rows x 16 bytes.
-      float* stg = reinterpret_cast<float*>(smem + B_OFF_DQ) + (warp - 2) * 32 * DQ_LD;
-#pragma unroll 1
-      for (int c = 2 * half; c < 2 * half + 2; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + c * 32, r);
-        tmem_wait_ld();
+      // both 32-column chunks of dQ into registers, then the TMEM columns are
+      // released at once (the next S^T may overwrite them) and the adds go
+      // out as TMA reduce-adds from the warp's swizzled staging block
+      uint32_t r[2][32];
 #pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          *reinterpret_cast<float4*>(stg + lane * DQ_LD + e) =
-              make_float4(__uint_as_float(r[e]) * p.scale, __uint_as_float(r[e + 1]) * p.scale,
-                          __uint_as_float(r[e + 2]) * p.scale, __uint_as_float(r[e + 3]) * p.scale);
-        __syncwarp();
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int rr = 4 * k + (lane >> 3);  // row within the warp's 32
-          const int ql2 = t * FB + quad * 32 + rr;
-          const float4 v = *reinterpret_cast<const float4*>(stg + rr * DQ_LD + (lane & 7) * 4);
-          if (ql2 < p.Tq)
-            red_add_v4(p.dq + ((int64_t)ql2 * p.Hq + h) * FB + c * 32 + (lane & 7) * 4, v.x, v.y, v.z, v.w);
-        }
-        __syncwarp();
-      }
+      for (int cc = 0; cc < 2; ++cc) tmem_ld32(tmem + lane_base + (2 * half + cc) * 32, r[cc]);
+      tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(dq_free);
+      // chunk 0 through the warp's staging block, chunk 1 through its 4 KB
+      // block of the dS tile (free now: dq_full covered the MMAs that read
+      // it; the softmax waits for this reduce's read before writing dS again)
+      if (lane == 0) bulk_wait_read_all();  // the blocks' previous reduces have read them
+      __syncwarp();
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint8_t* blk = cc ? stg2 : stg;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<float4*>(blk + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(r[cc][4 * u]) * p.scale, __uint_as_float(r[cc][4 * u + 1]) * p.scale,
+                          __uint_as_float(r[cc][4 * u + 2]) * p.scale, __uint_as_float(r[cc][4 * u + 3]) * p.scale);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_2d(&tmDQ, stg, h * FB + (2 * half) * 32, t * FB + quad * 32);
+        tma_reduce_add_2d(&tmDQ, stg2, h * FB + (2 * half + 1) * 32, t * FB + quad * 32);
+        bulk_commit_group();
+      }
+      if (dg && threadIdx.x == 64 && i < 16) dg[7 + 4 * i] = clock64();
     }
-    // dK, dV of the block (all MMAs completed: the last dq_full covered them).
-    // Every lane runs the warp-collective TMEM loads; rows past Tk skip the stores.
+    if (dg && threadIdx.x == 64) dg[68] = clock64();
+    // dK, dV of the block (all MMAs completed: the last dq_full covered them),
+    // added with the same TMA reduce-adds; every lane runs the warp-collective
+    // TMEM loads, and rows past Tk are not written by the TMA
     if (ok && iters > 0) {
-      // same transposed atomic adds as dQ: 4 key rows x 128 bytes per instruction
-      float* stg = reinterpret_cast<float*>(smem + B_OFF_DQ) + (warp - 2) * 32 * DQ_LD;
 #pragma unroll 1
       for (int c = 2 * half; c < 2 * half + 2; ++c) {
-#pragma unroll 1
-        for (int which = 0; which < 2; ++which) {  // 0: dK (x scale), 1: dV
-          uint32_t a[32];
-          tmem_ld32(tmem + lane_base + (which ? 256 : 384) + c * 32, a);
-          tmem_wait_ld();
+        uint32_t a[2][32];  // [0] dK (x scale), [1] dV: through the two staging blocks
+        tmem_ld32(tmem + lane_base + 384 + c * 32, a[0]);
+        tmem_ld32(tmem + lane_base + 256 + c * 32, a[1]);
+        tmem_wait_ld();
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          uint8_t* blk = which ? stg2 : stg;
           const float f = which ? 1.f : p.scale;
 #pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            *reinterpret_cast<float4*>(stg + lane * DQ_LD + e) =
-                make_float4(__uint_as_float(a[e]) * f, __uint_as_float(a[e + 1]) * f, __uint_as_float(a[e + 2]) * f,
-                            __uint_as_float(a[e + 3]) * f);
-          __syncwarp();
-          float* base = which ? p.dv : p.dk;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int rr = 4 * k + (lane >> 3);
-            const int jj = kb * FB + quad * 32 + rr;  // key row
-            const float4 v = *reinterpret_cast<const float4*>(stg + rr * DQ_LD + (lane & 7) * 4);
-            if (jj < p.Tk)
-              red_add_v4(base + ((int64_t)jj * p.Hkv + hk) * FB + c * 32 + (lane & 7) * 4, v.x, v.y, v.z, v.w);
-          }
-          __syncwarp();
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(blk + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+                make_float4(__uint_as_float(a[which][4 * u]) * f, __uint_as_float(a[which][4 * u + 1]) * f,
+                            __uint_as_float(a[which][4 * u + 2]) * f, __uint_as_float(a[which][4 * u + 3]) * f);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tmDK, stg, hk * FB + c * 32, kb * FB + quad * 32);
+          tma_reduce_add_2d(&tmDV, stg2, hk * FB + c * 32, kb * FB + quad * 32);
+          bulk_commit_group();
         }
       }
     }
+    if (lane == 0) bulk_wait_all();  // every reduce-add has completed before the CTA exits
   }
+  if (dg && threadIdx.x == 64) dg[69] = clock64();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -1000,7 +1085,8 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
 // 128-query tile).  Returns {dq [Tq,Hq,128], dk [Tk,Hkv,128], dv} fp32.
 std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                        torch::Tensor out, torch::Tensor lse, torch::Tensor kend, torch::Tensor units,
-                                       double scale, int64_t q_off, c10::optional<torch::Tensor> pos, int64_t window) {
+                                       double scale, int64_t q_off, c10::optional<torch::Tensor> pos, int64_t window,
+                                       c10::optional<torch::Tensor> diag) {
   const int64_t Tq = q.size(0), Hq = q.size(1), D = q.size(2), Tk = k.size(0), Hkv = k.size(1);
   TORCH_CHECK(D == 128 && Hq % Hkv == 0 && q_off >= 0 && q_off + Tq <= Tk);
   for (auto* t : {&q, &k, &v, &out}) {
@@ -1031,6 +1117,9 @@ std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torc
   auto v2 = v.as_strided({Tk, Hkv * D}, {v.stride(0), 1});
   const CUtensorMap mq = make_tmap_bf16(q2, FB), mk = make_tmap_bf16(k2, FB), mv = make_tmap_bf16(v2, FB),
                     mdo = make_tmap_bf16(do2, FB);
+  // fp32 gradients as [rows, heads*128]: targets of the TMA reduce-adds
+  const CUtensorMap mdq = make_tmap_f32_32(dq.view({Tq, Hq * D})), mdk = make_tmap_f32_32(dk.view({Tk, Hkv * D})),
+                    mdv = make_tmap_f32_32(dv.view({Tk, Hkv * D}));
   int dev = 0;
   ART_CUDA_CHECK(cudaGetDevice(&dev));
   FbArgs a;
@@ -1056,12 +1145,24 @@ std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torc
                 pos->numel() == Tk, "a sliding window needs int32 positions [Tk]");
     a.pos = pos->data_ptr<int>();
   }
+  a.diag = nullptr;
+  if (diag.has_value()) {
+    TORCH_CHECK(diag->is_cuda() && diag->scalar_type() == at::kLong && diag->is_contiguous() &&
+                diag->numel() >= n * Hkv * kFbDiag, "diag: int64 [units * kv heads, ", kFbDiag, "]");
+    a.diag = reinterpret_cast<long long*>(diag->data_ptr<int64_t>());
+  }
   static bool attr = false;
   if (!attr) {
-    ART_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM));
+    const auto smem_attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    ART_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_tc_kernel<false>, smem_attr, FB_SMEM));
+    ART_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_tc_kernel<true>, smem_attr, FB_SMEM));
     attr = true;
   }
-  attn_bwd_tc_kernel<<<dim3((unsigned)n, (unsigned)Hkv), FB_THREADS, FB_SMEM, stream>>>(mq, mk, mv, mdo, a);
+  const dim3 grid((unsigned)n, (unsigned)Hkv);
+  if (a.diag)
+    attn_bwd_tc_kernel<true><<<grid, FB_THREADS, FB_SMEM, stream>>>(mq, mk, mv, mdo, mdq, mdk, mdv, a);
+  else
+    attn_bwd_tc_kernel<false><<<grid, FB_THREADS, FB_SMEM, stream>>>(mq, mk, mv, mdo, mdq, mdk, mdv, a);
   ART_CUDA_CHECK(cudaGetLastError());
   return {dq, dk, dv, delta};
 }

@@ -53,7 +53,8 @@ std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::
                                        c10::optional<torch::Tensor> diag);
 std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                        torch::Tensor out, torch::Tensor lse, torch::Tensor kend, torch::Tensor units,
-                                       double scale, int64_t q_off, c10::optional<torch::Tensor> pos, int64_t window);
+                                       double scale, int64_t q_off, c10::optional<torch::Tensor> pos, int64_t window,
+                                       c10::optional<torch::Tensor> diag);
 torch::Tensor gemm_tc_grouped(torch::Tensor x, torch::Tensor w, std::vector<int64_t> offs, int64_t N,
                               c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, bool w_transposed);
 void peer_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes);
@@ -146,7 +147,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("sinks") = py::none(), py::arg("diag") = py::none());
   m.def("attn_bwd_tc", &art::attn_bwd_tc, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
         py::arg("out"), py::arg("lse"), py::arg("kend"), py::arg("units"), py::arg("scale"), py::arg("q_off") = 0,
-        py::arg("pos") = py::none(), py::arg("window") = 0);
+        py::arg("pos") = py::none(), py::arg("window") = 0, py::arg("diag") = py::none());
   m.def("gemm_tc_grouped", &art::gemm_tc_grouped, py::arg("x"), py::arg("w"), py::arg("offs"), py::arg("N"),
         py::arg("a2") = py::none(), py::arg("b2") = py::none(), py::arg("w_transposed") = false);
   m.def("peer_copy", &art::peer_copy);

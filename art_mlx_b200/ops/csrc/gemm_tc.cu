@@ -297,6 +297,22 @@ static CUtensorMap make_tmap_2d(const torch::Tensor& t, int box_rows) {
 
 CUtensorMap make_tmap_bf16(const at::Tensor& t, int box_rows) { return make_tmap_2d(t, box_rows); }
 
+CUtensorMap make_tmap_f32_32(const at::Tensor& t) {
+  TORCH_CHECK(t.scalar_type() == at::kFloat && t.dim() == 2 && t.stride(1) == 1, "fp32 row-major 2-D tensor");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((t.stride(0) * 4) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)t.size(1), (cuuint64_t)t.size(0)};
+  cuuint64_t strides[1] = {(cuuint64_t)(t.stride(0) * 4)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, t.data_ptr(), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
 static torch::Tensor& error_word(int dev) {
   static std::vector<torch::Tensor> words(64);
   if (!words[dev].defined())

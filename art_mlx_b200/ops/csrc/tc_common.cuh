@@ -182,6 +182,20 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// global[c1.., c0..] += the shared-memory box at src (TMA reduce-add, bulk
+// group completion; no multicast).  Coordinates must be non-negative; rows or
+// columns past the tensor's end are not written.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory sources of this thread's bulk groups have been read
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// this thread's bulk groups have completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ---- CTA pairs (cluster of 2, cta_group::2) ----
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -276,6 +290,9 @@ __host__ __device__ constexpr uint32_t idesc_bf16_bmn(int M, int N) { return ide
 // includers include <torch/extension.h> first).
 // 2-D bf16 row-major tensor map, 128-byte swizzle, box = 64 columns x box_rows.
 CUtensorMap make_tmap_bf16(const at::Tensor& t, int box_rows);
+// 2-D fp32 row-major tensor map, 128-byte swizzle, box = 32 columns x 32 rows
+// (the staging block of one warp's 32 rows for a TMA reduce-add).
+CUtensorMap make_tmap_f32_32(const at::Tensor& t);
 // Device error word of the tensor-core kernels (read and cleared by tc_error_code).
 int* tc_error_ptr(int dev);
 

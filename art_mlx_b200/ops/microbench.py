@@ -157,6 +157,61 @@ def attn_diag(small: bool = False) -> None:
           epilogue_end=rel(row[35]), end=rel(row[46]))
 
 
+def attn_bwd_diag(small: bool = False) -> None:
+    """Where a backward attention CTA's cycles go on the benchmark row
+    (phase clocks of the diag build, medians over CTAs, SM cycles)."""
+    from . import fused, native
+    from ..preprocessing.prefix_tree import prefix_tree_pack, visibility_ends
+
+    torch.manual_seed(0)
+    n, P, Cl = (4, 512, 256) if small else (16, 1024, 512)
+    p = torch.randint(0, 1000, (P,))
+    seqs = [torch.cat([p, torch.randint(0, 1000, (Cl,))]) for _ in range(n)]
+    pack = prefix_tree_pack(seqs, max_depth=4096, shareable_lengths=[P - 1] * n)
+    kend = visibility_ends(pack.group_ids, pack.parent_ids)[0]
+    T, D, Hq, Hkv = kend.numel(), 128, 28, 4
+    dev = torch.device("cuda")
+    q = torch.randn(T, Hq, D, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(T, Hkv, D, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(T, Hkv, D, device=dev, dtype=torch.bfloat16)
+    meta = fused.AttnMeta.build(torch.arange(T), kend, dev)
+    C = native.lib()
+    sc = 1 / math.sqrt(D)
+    units = fused.attention_bwd_units_tc(kend).to(dev)
+    o, lse = C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, sc)
+    do = torch.randn_like(o)
+    ctas = units.shape[0] * Hkv
+    dg = torch.zeros(ctas, 96, dtype=torch.int64, device=dev)
+    t_plain = _timed(lambda: C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, units, sc))
+    t_diag = _timed(lambda: C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, units, sc, diag=dg))
+    dg.zero_()
+    C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, units, sc, diag=dg)
+    torch.cuda.synchronize()
+    d = dg.cpu().double()
+    it = d[:, 2].clamp(min=1)
+    med = lambda x: round(float(x.median()), 1)  # noqa: E731
+    m = 16
+    valid = torch.arange(m).view(1, m) < d[:, 2:3]
+    soft = torch.stack([d[:, 5 + 4 * i] - d[:, 4 + 4 * i] for i in range(m)], 1)
+    wdq = torch.stack([d[:, 6 + 4 * i] - d[:, 5 + 4 * i] for i in range(m)], 1)
+    rdq = torch.stack([d[:, 7 + 4 * i] - d[:, 6 + 4 * i] for i in range(m)], 1)
+    vn = torch.arange(m - 1).view(1, m - 1) < (d[:, 2:3] - 1)
+    wsd = torch.stack([d[:, 4 + 4 * (i + 1)] - d[:, 7 + 4 * i] for i in range(m - 1)], 1)
+    _emit(case="attn_bwd_diag", T=T, ctas=ctas, ms_plain=round(t_plain, 4), ms_diag=round(t_diag, 4),
+          iters_per_cta=med(it), setup=med(d[:, 1] - d[:, 0]), loop_per_iter=med((d[:, 68] - d[:, 4]) / it),
+          softmax=round(float(soft[valid].median()), 1), wait_dq=round(float(wdq[valid].median()), 1),
+          dq_readout=round(float(rdq[valid].median()), 1),
+          wait_next_s=round(float(wsd[vn].median()), 1) if vn.any() else None,
+          epilogue=med(d[:, 69] - d[:, 68]), mma_wait_qdo=med(d[:, 70] / it), mma_wait_dv_done=med(d[:, 71] / it),
+          mma_issue_dp=med(d[:, 72] / it), mma_wait_dq_free=med(d[:, 73] / it), mma_issue_s=med(d[:, 74] / it),
+          mma_wait_ds=med(d[:, 75] / it), mma_issue_dvdk=med(d[:, 76] / it), mma_issue_dq=med(d[:, 77] / it),
+          prod_wait_qdo_empty=med(d[:, 78] / it),
+          softmax_to_first_ld=med(torch.stack([d[:, 80 + 2 * i] - d[:, 4 + 4 * i] for i in range(8)], 1)[:, 1:].flatten()),
+          softmax_compute=med(torch.stack([d[:, 81 + 2 * i] - d[:, 80 + 2 * i] for i in range(8)], 1)[:, 1:].flatten()),
+          softmax_tail=med(torch.stack([d[:, 5 + 4 * i] - d[:, 81 + 2 * i] for i in range(8)], 1)[:, 1:].flatten()),
+          tc_error=int(C.tc_error_code()))
+
+
 # ---------------------------------------------------------------------------
 def bench_gemm() -> None:
     from . import native
@@ -510,6 +565,8 @@ def main(argv: list[str]) -> None:
         gemm_diag()
     elif which == "attn_diag":
         attn_diag(small="--small" in argv)
+    elif which == "attn_bwd_diag":
+        attn_bwd_diag(small="--small" in argv)
     elif which == "gemm_pair_vs_cublas_one":
         gemm_pair_vs_cublas_one()
     elif which == "gdn":
@@ -519,7 +576,7 @@ def main(argv: list[str]) -> None:
     elif which == "comm":
         bench_comm()
     else:
-        raise SystemExit(f"unknown case {which!r}: attn | attn_diag | gemm | gemm_one | gemm_diag | gemm_pair_vs_cublas_one | gdn | norm | comm")
+        raise SystemExit(f"unknown case {which!r}: attn | attn_diag | attn_bwd_diag | gemm | gemm_one | gemm_diag | gemm_pair_vs_cublas_one | gdn | norm | comm")
 
 
 if __name__ == "__main__":
