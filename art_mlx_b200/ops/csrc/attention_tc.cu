@@ -706,7 +706,7 @@ struct FbArgs {
   int window;      // > 0: also pos[query] - pos[key] < window
   long long* diag;  // phase clocks per CTA (diag build only), kFbDiag int64 slots each
 };
-constexpr int kFbDiag = 96;
+constexpr int kFbDiag = 128;
 
 
 }  // namespace
@@ -956,35 +956,50 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         tmem_wait_ld();
         if (dg && threadIdx.x == 64 && i < 8 && cc == 0) dg[80 + 2 * i] = clock64();
         uint32_t dd[16];
+        // three passes over the 32 columns, each of 32 independent chains (the
+        // exponentials, then dS, then the bf16 packs), so that the latencies
+        // of one column's steps overlap the other columns' instead of queuing
+        const float4* l4p = reinterpret_cast<const float4*>(lsw + cc * 32);
+        const float4* d4p = reinterpret_cast<const float4*>(lsw + 64 + cc * 32);
+        float pv[32];
 #pragma unroll
         for (int e = 0; e < 32; e += 4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(lsw + cc * 32 + e);
-          const float4 d4 = *reinterpret_cast<const float4*>(lsw + 64 + cc * 32 + e);
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-          float pv[4], ds[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            // queries past Tq carry LSE = +inf: their P is 0 on either path
-            float pr = exp2f(fmaf(__uint_as_float(rs[e + u]), p.scale_log2, -lv[u]));
-            if (!full) {
-              const int qg = p.q_off + q0c + e + u;
-              const bool vis = (j <= qg) && (qg < kend_j) && (p.window <= 0 || psw[cc * 32 + e + u] - pos_j < p.window);
-              pr = vis ? pr : 0.f;
-            }
-            pv[u] = pr;
-            ds[u] = pr * (__uint_as_float(rd[e + u]) - dv4[u]);
-          }
-          pp[e >> 1] = pack_bf16x2(pv[0], pv[1]);
-          pp[(e >> 1) + 1] = pack_bf16x2(pv[2], pv[3]);
-          dd[e >> 1] = pack_bf16x2(ds[0], ds[1]);
-          dd[(e >> 1) + 1] = pack_bf16x2(ds[2], ds[3]);
+          const float4 l4 = l4p[e / 4];
+          // queries past Tq carry LSE = +inf: their P is 0 on either path
+          pv[e + 0] = exp2f(fmaf(__uint_as_float(rs[e + 0]), p.scale_log2, -l4.x));
+          pv[e + 1] = exp2f(fmaf(__uint_as_float(rs[e + 1]), p.scale_log2, -l4.y));
+          pv[e + 2] = exp2f(fmaf(__uint_as_float(rs[e + 2]), p.scale_log2, -l4.z));
+          pv[e + 3] = exp2f(fmaf(__uint_as_float(rs[e + 3]), p.scale_log2, -l4.w));
         }
+        if (!full) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int qg = p.q_off + q0c + e;
+            const bool vis = (j <= qg) && (qg < kend_j) && (p.window <= 0 || psw[cc * 32 + e] - pos_j < p.window);
+            pv[e] = vis ? pv[e] : 0.f;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const float4 d4 = d4p[e / 4];
+          rd[e + 0] = __float_as_uint(pv[e + 0] * (__uint_as_float(rd[e + 0]) - d4.x));
+          rd[e + 1] = __float_as_uint(pv[e + 1] * (__uint_as_float(rd[e + 1]) - d4.y));
+          rd[e + 2] = __float_as_uint(pv[e + 2] * (__uint_as_float(rd[e + 2]) - d4.z));
+          rd[e + 3] = __float_as_uint(pv[e + 3] * (__uint_as_float(rd[e + 3]) - d4.w));
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          pp[e] = pack_bf16x2(pv[2 * e], pv[2 * e + 1]);
+          dd[e] = pack_bf16x2(__uint_as_float(rd[2 * e]), __uint_as_float(rd[2 * e + 1]));
+        }
+        if (dg && threadIdx.x == 64 && i < 8 && cc == 0) dg[96 + 4 * i] = clock64();
         // 32 queries = 4 units of 16 bytes of this key's row (the warp's dS
         // block doubles as dQ staging: the reduce that read it has finished)
         if (cc == 0) {
           if (lane == 0) bulk_wait_read_all();
           __syncwarp();
         }
+        if (dg && threadIdx.x == 64 && i < 8 && cc == 0) dg[97 + 4 * i] = clock64();
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           const int u = c * 4 + w;  // unit along the 128-query row
@@ -995,6 +1010,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         // + 16*cc: over dP^T columns of queries 64*half .. +32, which this
         // warp has already read (chunk cc = 0)
         tmem_st16(tmem + lane_base + 128 + half * 64 + cc * 16, pp);
+        if (dg && threadIdx.x == 64 && i < 8 && cc == 0) dg[98 + 4 * i] = clock64();
       }
       if (dg && threadIdx.x == 64 && i < 8) dg[81 + 2 * i] = clock64();
       tmem_wait_st();

@@ -181,7 +181,7 @@ def attn_bwd_diag(small: bool = False) -> None:
     o, lse = C.attn_fwd_tc(q, k, v, meta.kend, meta.tile_kmax, meta.tile_kmin, sc)
     do = torch.randn_like(o)
     ctas = units.shape[0] * Hkv
-    dg = torch.zeros(ctas, 96, dtype=torch.int64, device=dev)
+    dg = torch.zeros(ctas, 128, dtype=torch.int64, device=dev)
     t_plain = _timed(lambda: C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, units, sc))
     t_diag = _timed(lambda: C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, units, sc, diag=dg))
     dg.zero_()
@@ -209,6 +209,10 @@ def attn_bwd_diag(small: bool = False) -> None:
           softmax_to_first_ld=med(torch.stack([d[:, 80 + 2 * i] - d[:, 4 + 4 * i] for i in range(8)], 1)[:, 1:].flatten()),
           softmax_compute=med(torch.stack([d[:, 81 + 2 * i] - d[:, 80 + 2 * i] for i in range(8)], 1)[:, 1:].flatten()),
           softmax_tail=med(torch.stack([d[:, 5 + 4 * i] - d[:, 81 + 2 * i] for i in range(8)], 1)[:, 1:].flatten()),
+          chunk0_math=med(torch.stack([d[:, 96 + 4 * i] - d[:, 80 + 2 * i] for i in range(8)], 1)[:, 1:].flatten()),
+          chunk0_stage_wait=med(torch.stack([d[:, 97 + 4 * i] - d[:, 96 + 4 * i] for i in range(8)], 1)[:, 1:].flatten()),
+          chunk0_stores=med(torch.stack([d[:, 98 + 4 * i] - d[:, 97 + 4 * i] for i in range(8)], 1)[:, 1:].flatten()),
+          chunk1_all=med(torch.stack([d[:, 81 + 2 * i] - d[:, 98 + 4 * i] for i in range(8)], 1)[:, 1:].flatten()),
           tc_error=int(C.tc_error_code()))
 
 
