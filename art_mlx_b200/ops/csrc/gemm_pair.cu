@@ -326,24 +326,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r2[h][j]);
             if constexpr (EPI == EPI_STATS) {
-              // online softmax over this 32-column chunk (fp32 logits)
-              float cm = v[0];
+              // online softmax over this 32-column chunk (fp32 logits); the
+              // max, the exponentials and the sums each run over independent
+              // columns (four chains for the reductions) so latencies overlap
+              float cm4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
-              for (int j = 1; j < 32; ++j) cm = fmaxf(cm, v[j]);
-              const float mn = fmaxf(st_m, cm);
+              for (int j = 4; j < 32; ++j) cm4[j & 3] = fmaxf(cm4[j & 3], v[j]);
+              const float mn = fmaxf(st_m, fmaxf(fmaxf(cm4[0], cm4[1]), fmaxf(cm4[2], cm4[3])));
               const float sc = (st_m == -INFINITY) ? 0.f : __expf(st_m - mn);
-              float s = st_s * sc, sx = st_sx * sc;
-              const int64_t rel = tgt_id - col0;
+              float e[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) e[j] = __expf(v[j] - mn);
+              float s4[4] = {0.f, 0.f, 0.f, 0.f}, sx4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                const float e = __expf(v[j] - mn);
-                s += e;
-                sx = fmaf(e, v[j], sx);
-                if (rel == j) p.tgt[row] = v[j];
+                s4[j & 3] += e[j];
+                sx4[j & 3] = fmaf(e[j], v[j], sx4[j & 3]);
               }
+              const int64_t rel = tgt_id - col0;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (rel == j) p.tgt[row] = v[j];
               st_m = mn;
-              st_s = s;
-              st_sx = sx;
+              st_s = fmaf(st_s, sc, (s4[0] + s4[1]) + (s4[2] + s4[3]));
+              st_sx = fmaf(st_sx, sc, (sx4[0] + sx4[1]) + (sx4[2] + sx4[3]));
               if (p.C == nullptr) continue;  // statistics only; else the logits are stored too
             } else if constexpr (EPI == EPI_GRAD) {
               const int64_t rel = tgt_id - col0;

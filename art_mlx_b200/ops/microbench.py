@@ -264,6 +264,31 @@ def bench_gemm() -> None:
         _emit(**row)
 
 
+def bench_lmhead() -> None:
+    """LM head of the benchmark (8192 rows x 3584 -> 152,064 vocab): the fused
+    statistics epilogue (with and without the kept bf16 logits) against the
+    plain CTA-pair GEMM of the same shape, and the gradient-logits pass."""
+    from . import native
+
+    C = native.lib()
+    dev = torch.device("cuda")
+    T, H, V = 8192, 3584, 152064
+    h = torch.randn(T, H, device=dev, dtype=torch.bfloat16)
+    w = torch.randn(V, H, device=dev, dtype=torch.bfloat16) * 0.02
+    tg = torch.randint(0, V, (T,), device=dev)
+    logits = torch.empty(T, V, device=dev, dtype=torch.bfloat16)
+    fl = 2 * T * H * V
+    t_gemm = _timed(lambda: C.gemm_pair(h, w, None, None, None, None, False))
+    t_stats = _timed(lambda: C.lm_head_fwd(h, w, tg, True, None))
+    t_keep = _timed(lambda: C.lm_head_fwd(h, w, tg, True, logits))
+    _, _, lse = C.lm_head_fwd(h, w, tg, False, None)
+    g = torch.randn(T, device=dev)
+    d = torch.empty(T, V, device=dev, dtype=torch.bfloat16)
+    t_grad = _timed(lambda: C.lm_head_grad_logits(h, w, tg, lse, g, d))
+    _emit(case="lm_head", gemm_ms=round(t_gemm, 4), stats_ms=round(t_stats, 4), stats_keep_ms=round(t_keep, 4),
+          grad_logits_ms=round(t_grad, 4), stats_tflops=round(fl / t_stats / 1e9, 1), tc_error=int(C.tc_error_code()))
+
+
 def gemm_one() -> None:
     """Three CTA-pair GEMM calls on the gate_up shape: a small, self-ending
     target for a one-launch profiler capture."""
@@ -563,6 +588,8 @@ def main(argv: list[str]) -> None:
         bench_attn(small="--small" in argv)
     elif which == "gemm":
         bench_gemm()
+    elif which == "lmhead":
+        bench_lmhead()
     elif which == "gemm_one":
         gemm_one()
     elif which == "gemm_diag":
@@ -580,7 +607,7 @@ def main(argv: list[str]) -> None:
     elif which == "comm":
         bench_comm()
     else:
-        raise SystemExit(f"unknown case {which!r}: attn | attn_diag | attn_bwd_diag | gemm | gemm_one | gemm_diag | gemm_pair_vs_cublas_one | gdn | norm | comm")
+        raise SystemExit(f"unknown case {which!r}: attn | attn_diag | attn_bwd_diag | gemm | lmhead | gemm_one | gemm_diag | gemm_pair_vs_cublas_one | gdn | norm | comm")
 
 
 if __name__ == "__main__":
