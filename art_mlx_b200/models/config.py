@@ -69,6 +69,14 @@ class ModelConfig:
     rotary_dim: int = 0
     norm_zero_centered: bool = False
     gdn_split_proj: bool = False
+    # family-specific settings as sorted (key, value) pairs (Gemma-4: global
+    # head size and kv heads, key = value attention, kv sharing, per-layer
+    # inputs, the MoE block, logit soft-capping, per-kind RoPE)
+    extra: tuple = ()
+
+    @property
+    def ex(self) -> dict[str, Any]:
+        return dict(self.extra)
 
     @property
     def is_moe(self) -> bool:
@@ -120,7 +128,9 @@ class ModelConfig:
         scaling = {k: v for k, v in {**rp, **rs}.items() if k != "rope_theta"}
         if (scaling.get("rope_type") or scaling.get("type") or "default") == "default":
             scaling = {}
-        family = {"qwen3_5_text": "qwen3_5", "qwen3_5_moe_text": "qwen3_5_moe"}.get(family, family)
+        family = {"qwen3_5_text": "qwen3_5", "qwen3_5_moe_text": "qwen3_5_moe", "gemma4_text": "gemma4"}.get(family, family)
+        if family == "gemma4":
+            return _gemma4_config(d, name)
         num_experts = d.get("num_experts", d.get("num_local_experts", 0)) or 0
         gpt_oss = family == "gpt_oss"
         hybrid = family in ("qwen3_next", "qwen3_5", "qwen3_5_moe")
@@ -168,6 +178,53 @@ class ModelConfig:
             norm_zero_centered=hybrid,
             gdn_split_proj=family in ("qwen3_5", "qwen3_5_moe"),
         )
+
+
+def _gemma4_config(d: dict[str, Any], name: str) -> ModelConfig:
+    """Gemma-4 text model: sliding / full attention layers with their own head
+    sizes and RoPE, the family's settings kept in ``extra`` (its experts run
+    beside the dense MLP and are not routed through the MoE machinery of the
+    other families, so ``num_experts`` stays 0)."""
+    heads = d["num_attention_heads"]
+    L = d["num_hidden_layers"]
+    layer_types = tuple(d.get("layer_types") or
+                        ["sliding_attention" if (i + 1) % 6 else "full_attention" for i in range(L)])
+    rp = dict(d.get("rope_parameters") or {})
+    sl = dict(rp.get("sliding_attention") or {"rope_type": "default", "rope_theta": 10_000.0})
+    fu = dict(rp.get("full_attention") or {"rope_type": "proportional", "partial_rotary_factor": 0.25,
+                                           "rope_theta": 1_000_000.0})
+    head_dim = d.get("head_dim") or d["hidden_size"] // heads
+    extra = {
+        "hidden_activation": d.get("hidden_activation", "gelu_pytorch_tanh"),
+        "global_head_dim": int(d.get("global_head_dim") or head_dim),
+        "num_global_key_value_heads": int(d.get("num_global_key_value_heads") or d.get("num_key_value_heads", heads)),
+        "attention_k_eq_v": bool(d.get("attention_k_eq_v", False)),
+        "num_kv_shared_layers": int(d.get("num_kv_shared_layers", 0) or 0),
+        "hidden_size_per_layer_input": int(d.get("hidden_size_per_layer_input", 0) or 0),
+        "vocab_size_per_layer_input": int(d.get("vocab_size_per_layer_input", d["vocab_size"]) or d["vocab_size"]),
+        "use_double_wide_mlp": bool(d.get("use_double_wide_mlp", False)),
+        "enable_moe_block": bool(d.get("enable_moe_block", False)),
+        "moe_num_experts": int(d.get("num_experts", 0) or 0),
+        "moe_top_k": int(d.get("top_k_experts", 0) or 0),
+        "moe_intermediate_size": int(d.get("moe_intermediate_size", 0) or 0),
+        "final_logit_softcapping": float(d["final_logit_softcapping"]) if d.get("final_logit_softcapping") else 0.0,
+        "rope_sliding_theta": float(sl.get("rope_theta", 10_000.0)),
+        "rope_sliding_type": str(sl.get("rope_type", "default")),
+        "rope_full_theta": float(fu.get("rope_theta", 1_000_000.0)),
+        "rope_full_type": str(fu.get("rope_type", "default")),
+        "rope_full_partial": float(fu.get("partial_rotary_factor", 1.0)),
+        "rope_full_factor": float(fu.get("factor", 1.0)),
+        "rope_sliding_factor": float(sl.get("factor", 1.0)),
+    }
+    return ModelConfig(
+        name=name, family="gemma4", vocab_size=d["vocab_size"], hidden_size=d["hidden_size"], num_hidden_layers=L,
+        num_attention_heads=heads, num_key_value_heads=d.get("num_key_value_heads", heads), head_dim=head_dim,
+        intermediate_size=d.get("intermediate_size", 0), rms_norm_eps=d.get("rms_norm_eps", 1e-6),
+        rope_theta=extra["rope_sliding_theta"], max_position_embeddings=d.get("max_position_embeddings", 131072),
+        attention_bias=bool(d.get("attention_bias", False)), qk_norm=True,
+        tie_word_embeddings=bool(d.get("tie_word_embeddings", True)), sliding_window=d.get("sliding_window"),
+        layer_types=layer_types, extra=tuple(sorted(extra.items())),
+    )
 
 
 PRESETS: dict[str, ModelConfig] = {

@@ -59,6 +59,11 @@ for _spec in (
     # on the data-parallel path (the expert-parallel exchange runs plain SwiGLU
     # experts; the decode kernel has no sinks or windows)
     ModelSupportSpec("gpt_oss", ("gpt_oss",), _DENSE, is_moe=True, supports=frozenset({"dp"})),
+    # Gemma-4 dense / MoE (reference model_support/handlers/gemma4.py): sandwich
+    # norms, sliding / full layers with their own head sizes, key = value
+    # attention, kv-shared layers, per-layer inputs, soft-capped logits; its
+    # expert block runs beside the dense MLP on every rank (models/gemma4.py)
+    ModelSupportSpec("gemma4", ("gemma4", "gemma4_text"), _DENSE, supports=frozenset({"dp"})),
 ):
     register_model_support(_spec)
 

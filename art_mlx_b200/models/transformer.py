@@ -80,6 +80,10 @@ def lora_specs_for(cfg: ModelConfig, spec: LoRASpec) -> list[tuple[str, tuple[in
     Factors of one fused projection are stored back to back (all ``A`` then
     all ``B``) so the concatenated ``A`` is a single view.
     """
+    if cfg.family == "gemma4":
+        from .gemma4 import gemma4_lora_specs
+
+        return gemma4_lora_specs(cfg, spec)
     r = spec.r
     H = cfg.hidden_size
     out: list[tuple[str, tuple[int, ...], str]] = []

@@ -58,6 +58,9 @@ class GenerationResult:
 
 class GenerationEngine:
     def __init__(self, model, max_len: int = 8192, max_batch: int = 256) -> None:
+        if getattr(getattr(model, "cfg", None), "family", "") == "gemma4":
+            raise NotImplementedError("the native rollout engine does not run Gemma-4; serve it with vLLM "
+                                      "(LocalBackend(inference='vllm'))")
         cfg = model.cfg
         self.model, self.cfg = model, cfg
         self.device = model.device

@@ -401,11 +401,15 @@ class GRPOTrainer:
             from ..models.tp_decoder import TPDecoderLM
 
             self.model = TPDecoderLM(cfg, lora, self.device, self.tp, seed=seed, store=store)
+        elif cfg.family == "gemma4":
+            from ..models.gemma4 import Gemma4LM
+
+            self.model = Gemma4LM(cfg, lora, self.device, seed=seed, store=store, ep=self.ep, etp=self.etp)
         else:
             self.model = DecoderLM(cfg, lora, self.device, seed=seed, store=store, ep=self.ep, etp=self.etp)
         if recompute is not None:
             if recompute and not hasattr(self.model, "recompute"):
-                raise ValueError("activation recompute is not available for the tensor-parallel decoder")
+                raise ValueError(f"activation recompute is not available for {type(self.model).__name__}")
             if hasattr(self.model, "recompute"):
                 self.model.recompute = bool(recompute)
         self.store = self.model.store
@@ -534,6 +538,9 @@ class GRPOTrainer:
             return self.model.token_logprobs(mb.tokens, mb.meta, mb.sel, mb.targets, ctx, entropy)
         h = self.model.forward(mb.tokens, mb.meta, ctx)
         hs = h.index_select(0, mb.sel)
+        own = getattr(self.model, "token_logprobs_hidden", None)  # families with their own logits (soft-capping)
+        if own is not None:
+            return own(hs, mb.targets, self.logprob_chunk, entropy)
         return fused.lm_head_logprobs(hs, self.model.lm_head, mb.targets, self.logprob_chunk, entropy)
 
     def micro_step(

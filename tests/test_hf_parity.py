@@ -94,3 +94,53 @@ def test_logits_match_transformers(kind, tmp_path):
     ours = _logits_ours(str(tmp_path), tokens)
     err = (ours - ref).abs().max().item() / ref.abs().max().item()
     assert err < 1e-4, f"{kind}: max relative logit error {err}"
+
+
+def _tiny_gemma4():
+    from transformers.models.gemma4.configuration_gemma4 import Gemma4TextConfig
+
+    # every Gemma-4 feature at once: sliding (window shorter than the sequence)
+    # and full layers with different head sizes, key = value attention on the
+    # full layers, the last two layers sharing keys / values, per-layer inputs,
+    # double-wide MLPs on the shared layers, the expert block, soft-capping
+    return Gemma4TextConfig(
+        vocab_size=512, hidden_size=64, intermediate_size=48, num_hidden_layers=6, num_attention_heads=4,
+        num_key_value_heads=2, head_dim=16, global_head_dim=32, num_global_key_value_heads=1, attention_k_eq_v=True,
+        num_kv_shared_layers=2, hidden_size_per_layer_input=8, vocab_size_per_layer_input=512,
+        use_double_wide_mlp=True, enable_moe_block=True, num_experts=4, top_k_experts=2, moe_intermediate_size=24,
+        final_logit_softcapping=30.0, sliding_window=8, layer_types=["sliding_attention", "full_attention"] * 3,
+        max_position_embeddings=512, tie_word_embeddings=True)
+
+
+def test_gemma4_logits_match_transformers(tmp_path):
+    from art_mlx_b200.models.gemma4 import Gemma4LM
+
+    torch.manual_seed(0)
+    hf_cfg = _tiny_gemma4()
+    model = transformers.AutoModelForCausalLM.from_config(hf_cfg).float().eval()
+    with torch.no_grad():  # non-trivial norms, router scales and layer scalars (HF initialises them to 1)
+        for name, p in model.named_parameters():
+            if "norm" in name or "scale" in name:
+                p.add_(0.1 * torch.randn_like(p))
+        for name, b in model.named_buffers():
+            if "layer_scalar" in name:
+                b.add_(0.1 * torch.randn_like(b))
+    model.save_pretrained(tmp_path)
+    tokens = torch.randint(0, hf_cfg.vocab_size, (37,))
+    with torch.no_grad():  # use_cache: the kv-shared layers read their source layer's keys / values
+        ref = model(tokens.unsqueeze(0), use_cache=True).logits[0].float()
+    cfg = get_config(str(tmp_path))
+    assert cfg.family == "gemma4" and not cfg.is_moe
+    m = Gemma4LM(cfg, LoRASpec(r=4, alpha=8), "cpu", seed=5)
+    assert maybe_load_base_weights(m, str(tmp_path))
+    m.lora_enabled = False
+    T = tokens.numel()
+    meta = fused.AttnMeta.build(torch.arange(T), torch.full((T,), T, dtype=torch.int32), torch.device("cpu"))
+    with torch.no_grad():
+        h = m.forward(tokens, meta, {})
+        lp, _ = m.token_logprobs_hidden(h, tokens, entropy=False)
+    z = torch.tanh((h.float() @ m.lm_head.float().t()) / 30.0) * 30.0
+    err = (z - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-4, f"gemma4: max relative logit error {err}"
+    ref_lp = torch.log_softmax(ref, -1).gather(-1, tokens.unsqueeze(-1)).squeeze(-1)
+    assert torch.allclose(lp, ref_lp, atol=1e-4)
