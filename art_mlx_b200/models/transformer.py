@@ -201,6 +201,18 @@ class DecoderLM:
         # full activation recompute per layer (the training forward keeps each
         # layer's inputs only); off by default
         self.recompute = recompute_enabled()
+        self.streamer = None  # runtime.weight_stream.LayerWeightStreamer when streaming
+
+    def enable_weight_streaming(self, slots: int = 2) -> None:
+        """Keep the layers' base weights in pinned host memory and stream
+        them in one layer at a time (``slots`` device buffers); turns on
+        activation recompute, which brings each layer back for its backward."""
+        from ..runtime.weight_stream import LayerWeightStreamer
+
+        if self.ep is not None or self.etp is not None:
+            raise NotImplementedError("weight streaming runs without expert parallelism")
+        self.recompute = True
+        self.streamer = LayerWeightStreamer(self, slots)
 
     # ------------------------------------------------------------------
     def _build_layer(self, i: int, gen: torch.Generator) -> Layer:
@@ -291,6 +303,8 @@ class DecoderLM:
                ctx: dict[str, Any]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """One decoder layer on the residual stream: ``(mlp out, residual,
         mixer out)``."""
+        if self.streamer is not None:  # base weights streamed in from the host
+            self.streamer.ensure(layer.index)
         eps = self.cfg.rms_norm_eps
         h, resid = fused.add_rmsnorm(out, resid, layer.in_norm, eps)
         if layer.kind == "attention":
@@ -327,7 +341,7 @@ class DecoderLM:
         # the collectives inside a layer stay matched)
         recompute = self.recompute and torch.is_grad_enabled() and trace is None
         for layer in self.layers:
-            if recompute and resid is not None:
+            if recompute:
                 from torch.utils.checkpoint import checkpoint
 
                 out, resid, a = checkpoint(self._layer, layer, out, resid, meta, ctx, use_reentrant=False,

@@ -330,9 +330,12 @@ class GRPOTrainer:
         etp_size: int = 1,
         allow_unvalidated_arch: bool = False,
         recompute: bool | None = None,
+        stream_weights: bool = False,
     ) -> None:
         """``recompute``: full activation recompute per layer (``None``: the
-        ``ART_B200_RECOMPUTE`` environment switch)."""
+        ``ART_B200_RECOMPUTE`` environment switch).  ``stream_weights``: the
+        layers' base weights stay in pinned host memory and are streamed to
+        the GPU one layer at a time (implies recompute)."""
         from ..models.registry import check_parallelism, get_model_support
 
         self.support = get_model_support(cfg, allow_unvalidated_arch)
@@ -412,6 +415,10 @@ class GRPOTrainer:
                 raise ValueError(f"activation recompute is not available for {type(self.model).__name__}")
             if hasattr(self.model, "recompute"):
                 self.model.recompute = bool(recompute)
+        if stream_weights:
+            if not hasattr(self.model, "enable_weight_streaming"):
+                raise ValueError(f"weight streaming is not available for {type(self.model).__name__}")
+            self.model.enable_weight_streaming()
         self.store = self.model.store
         self.optim = FlatAdamW(self.store, adamw)
         self.logprob_chunk = logprob_chunk

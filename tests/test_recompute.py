@@ -51,9 +51,8 @@ def test_recompute_runs_layers_again(monkeypatch):
         tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), "cpu", seed=0, recompute=rc)
         tr.train_step(packed, 1e-3, {})
         seen.append(calls["n"])
-    rows = seen[0] // cfg.num_hidden_layers
-    # every layer but the first (whose residual input is the embedding) runs twice
-    assert seen[1] == seen[0] + rows * (cfg.num_hidden_layers - 1)
+    # every layer runs twice
+    assert seen[1] == 2 * seen[0]
 
 
 def test_recompute_env_switch(monkeypatch):
