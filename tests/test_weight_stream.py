@@ -27,15 +27,21 @@ def test_streamed_step_matches_resident_step(name):
     dev = torch.device("cuda", 0)
     packed = _packed(*_shape("nccl", cfg))
     runs = []
-    for stream in (False, True):
+    for stream in (False, False, True):  # two resident runs: the run-to-run spread of the GPU step
         tr = GRPOTrainer(cfg, LoRASpec(r=8, alpha=16), dev, seed=0, recompute=True, stream_weights=stream)
-        for _ in range(2):
-            m = tr.train_step(packed, 1e-3, {}).to_host()
-        runs.append((tr.store.master.float().cpu(), m, tr.model.streamer))
-    (m0, h0, _), (m1, h1, st) = runs
-    err = (m0 - m1).norm() / m0.norm()
-    assert err < 1e-4, err  # the attention backward's reduce-adds are order-dependent
-    assert abs(h0["loss/train"] - h1["loss/train"]) < 1e-3 * max(1.0, abs(h0["loss/train"]))
+        hs = [tr.train_step(packed, 1e-3, {}).to_host() for _ in range(2)]
+        runs.append((tr.store.master.float().cpu(), hs, tr.model.streamer))
+    (m0, h0, _), (m1, _, _), (m2, h2, st) = runs
+    spread = (m0 - m1).norm() / m0.norm()  # order-dependent reduce-adds in the attention backward, through Adam
+    err = (m0 - m2).norm() / m0.norm()
+    assert err < 4 * spread + 1e-6, (err, spread)
+    for a, b in zip(h0, h2):
+        assert abs(a["loss/train"] - b["loss/train"]) < 1e-3 * max(1.0, abs(a["loss/train"]))
+        assert abs(a["loss/grad_norm"] - b["loss/grad_norm"]) < 1e-3 * a["loss/grad_norm"]
     host = sum(h.numel() for h in st.host)
-    assert st.bytes_copied >= 2 * host  # every layer came in for the forward and again for the backward
-    assert st.resident_bytes() < host  # only two layers' worth of base weights on the device
+    if cfg.num_hidden_layers > len(st.slots):
+        # the forward brought every layer in, the backward all but the two still resident
+        assert st.bytes_copied >= 2 * host - 2 * max(h.numel() for h in st.host)
+        assert st.resident_bytes() < host  # only two layers' worth of base weights on the device
+    else:
+        assert st.bytes_copied == host  # every layer fits the slots: each came in once
