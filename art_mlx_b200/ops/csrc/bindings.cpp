@@ -33,6 +33,10 @@ void rope_bwd(torch::Tensor dqk, torch::Tensor qkv, torch::Tensor pos, torch::Te
               int64_t nq, int64_t nkv, int64_t D, c10::optional<torch::Tensor> qn_w,
               c10::optional<torch::Tensor> kn_w, c10::optional<torch::Tensor> rstd,
               torch::Tensor dqkv, c10::optional<torch::Tensor> perm);
+void rope_bwd_f32(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv, torch::Tensor pos,
+                  torch::Tensor inv_freq, int64_t nq, int64_t nkv, int64_t D, c10::optional<torch::Tensor> qn_w,
+                  c10::optional<torch::Tensor> kn_w, c10::optional<torch::Tensor> rstd, torch::Tensor dqkv,
+                  c10::optional<torch::Tensor> perm);
 torch::Tensor swiglu_fwd(torch::Tensor gu);
 torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu);
 std::vector<torch::Tensor> logits_stats(torch::Tensor logits, torch::Tensor targets, bool entropy);
@@ -132,6 +136,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_bwd", &art::rope_bwd, py::arg("dqk"), py::arg("qkv"), py::arg("pos"), py::arg("inv_freq"),
         py::arg("nq"), py::arg("nkv"), py::arg("D"), py::arg("qn_w"), py::arg("kn_w"), py::arg("rstd"),
         py::arg("dqkv"), py::arg("perm") = py::none());
+  m.def("rope_bwd_f32", &art::rope_bwd_f32, py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("qkv"),
+        py::arg("pos"), py::arg("inv_freq"), py::arg("nq"), py::arg("nkv"), py::arg("D"), py::arg("qn_w"),
+        py::arg("kn_w"), py::arg("rstd"), py::arg("dqkv"), py::arg("perm") = py::none());
   m.def("swiglu_fwd", &art::swiglu_fwd);
   m.def("swiglu_bwd", &art::swiglu_bwd);
   m.def("logits_stats", &art::logits_stats);

@@ -397,7 +397,16 @@ __global__ void rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t l
 // Backward: dqk [T, nh*D] (bf16) -> writes dq, dk into dqkv [T, ld] columns of q and k.
 // Needs the raw (pre-norm) input to redo the norm when qk-norm is on.
 template <int D>
-__global__ void rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqk,
+__device__ __forceinline__ float grad_f(float x) { return x; }
+__device__ __forceinline__ float grad_f(__nv_bfloat16 x) { return bf2f(x); }
+
+// Gradients of q and k arrive as G (bf16, or the fp32 accumulators of the
+// attention backward) at row strides ldq / ldk and head stride hs; with
+// nv > 0 the value gradient (fp32 [T, nv, hs]) is converted into its slice of
+// dqkv by the same launch (warps past the q and k heads).
+template <int D, typename G>
+__global__ void rope_bwd_kernel(const G* __restrict__ dq, const G* __restrict__ dk, int64_t ldq, int64_t ldk,
+                                int hs, const float* __restrict__ dv, int nv,
                                 const __nv_bfloat16* __restrict__ qkv, int64_t ld,
                                 const int* __restrict__ pos, const float* __restrict__ inv_freq,
                                 const __nv_bfloat16* __restrict__ qn_w,
@@ -406,13 +415,21 @@ __global__ void rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqk,
                                 int64_t T, int nq, int nkv, const short* __restrict__ perm) {
   constexpr int PER = D / 32;
   const int nh = nq + nkv;
+  const int nwarp = nh + nv;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x / 32);
   const int lane = threadIdx.x & 31;
-  if (gw >= T * nh) return;
-  const int64_t t = gw / nh;
-  const int h = gw % nh;
+  if (gw >= T * nwarp) return;
+  const int64_t t = gw / nwarp;
+  const int h = gw % nwarp;
+  if (h >= nh) {  // value gradient: fp32 -> bf16 into its slice
+    const float* src = dv + (t * nv + (h - nh)) * (int64_t)hs;
+    __nv_bfloat16* dst = dqkv + t * ld + (int64_t)h * D;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) dst[lane + 32 * k] = f2bf(src[lane + 32 * k]);
+    return;
+  }
   const bool is_q = h < nq;
-  const __nv_bfloat16* g = dqk + t * (int64_t)nh * D + (int64_t)h * D;
+  const G* g = is_q ? dq + t * ldq + (int64_t)h * hs : dk + t * ldk + (int64_t)(h - nq) * hs;
   const float p = (float)pos[t];
   float ga[PER / 2], gb[PER / 2];
 #pragma unroll
@@ -420,7 +437,7 @@ __global__ void rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqk,
     const int i = lane * (PER / 2) + k;
     float s, c;
     sincosf(p * inv_freq[i], &s, &c);
-    const float u = bf2f(g[i]), v = bf2f(g[i + D / 2]);
+    const float u = grad_f(g[i]), v = grad_f(g[i + D / 2]);
     // transpose of the rotation
     ga[k] = u * c + v * s;
     gb[k] = v * c - u * s;
@@ -522,15 +539,54 @@ void rope_bwd(torch::Tensor dqk, torch::Tensor qkv, torch::Tensor pos, torch::Te
   const int threads = 256;
   const int64_t blocks = (warps + threads / 32 - 1) / (threads / 32);
   const bool norm = qn_w.has_value();
+  const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(dqk.data_ptr());
   if (warps > 0)
     ART_DISPATCH_HEAD_DIM(D, [&] {
-      rope_bwd_kernel<kD><<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-          reinterpret_cast<const __nv_bfloat16*>(dqk.data_ptr()),
+      rope_bwd_kernel<kD, __nv_bfloat16><<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+          g, g + nq * D, (int64_t)nh * D, (int64_t)nh * D, (int)D, nullptr, 0,
           reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0),
           pos.data_ptr<int>(), inv_freq.data_ptr<float>(),
           norm ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,
           norm ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr,
           norm ? rstd->data_ptr<float>() : nullptr,
+          reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), T, (int)nq, (int)nkv, pp);
+    });
+  ART_CUDA_CHECK(cudaGetLastError());
+}
+
+// The attention backward's fp32 accumulators dq [T, nq, hs], dk / dv
+// [T, nkv, hs] (hs >= D: narrow heads are padded) straight into dqkv: q and k
+// through the RoPE / q-k-norm backward, v converted, one launch, no bf16
+// intermediate.
+void rope_bwd_f32(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv, torch::Tensor pos,
+                  torch::Tensor inv_freq, int64_t nq, int64_t nkv, int64_t D, c10::optional<torch::Tensor> qn_w,
+                  c10::optional<torch::Tensor> kn_w, c10::optional<torch::Tensor> rstd, torch::Tensor dqkv,
+                  c10::optional<torch::Tensor> perm) {
+  for (auto* t : {&dq, &dk, &dv})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 3 &&
+                    t->size(2) >= D && t->size(0) == qkv.size(0),
+                "fp32 contiguous [T, heads, >= head_dim]");
+  TORCH_CHECK(dq.size(1) == nq && dk.size(1) == nkv && dv.size(1) == nkv && dk.size(2) == dq.size(2) &&
+                  dv.size(2) == dq.size(2),
+              "dq [T, nq, hs], dk / dv [T, nkv, hs]");
+  TORCH_CHECK(dqkv.stride(-1) == 1 && dqkv.stride(0) == qkv.stride(0) && dqkv.size(1) >= (nq + 2 * nkv) * D);
+  if (perm.has_value())
+    TORCH_CHECK(perm->is_cuda() && perm->scalar_type() == at::kShort && perm->numel() == D && perm->is_contiguous(),
+                "perm: int16 [head_dim]");
+  const short* pp = perm.has_value() ? perm->data_ptr<short>() : nullptr;
+  const int64_t T = qkv.size(0);
+  const int hs = (int)dq.size(2);
+  const int64_t warps = T * (nq + 2 * nkv);
+  const int threads = 256;
+  const int64_t blocks = (warps + threads / 32 - 1) / (threads / 32);
+  const bool norm = qn_w.has_value();
+  if (warps > 0)
+    ART_DISPATCH_HEAD_DIM(D, [&] {
+      rope_bwd_kernel<kD, float><<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+          dq.data_ptr<float>(), dk.data_ptr<float>(), (int64_t)nq * hs, (int64_t)nkv * hs, hs, dv.data_ptr<float>(),
+          (int)nkv, reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), pos.data_ptr<int>(),
+          inv_freq.data_ptr<float>(), norm ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,
+          norm ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr, norm ? rstd->data_ptr<float>() : nullptr,
           reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), T, (int)nq, (int)nkv, pp);
     });
   ART_CUDA_CHECK(cudaGetLastError());

@@ -448,16 +448,14 @@ class _RopeAttention(torch.autograd.Function):
         k = _pad_head(qk[:, nq * D :].view(T, nkv, D))
         v = _pad_head(qkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].unflatten(1, (nkv, D)))
         dqkv = torch.empty_like(qkv)
-        dqk = torch.empty_like(qk)
         win = meta.window
         dq_acc, dk_acc, dv_acc, _ = C.attn_bwd_tc(do, q, k, v, o, lse, meta.kend, meta.bwd_units, scale, 0,
                                                  meta.positions if win else None, win)
-        dqk[:, : nq * D].copy_(dq_acc[..., :D].reshape(T, nq * D))
-        dqk[:, nq * D :].copy_(dk_acc[..., :D].reshape(T, nkv * D))
-        dqkv[:, (nq + nkv) * D : (nq + 2 * nkv) * D].copy_(dv_acc[..., :D].reshape(T, nkv * D))
-        C.rope_bwd(dqk, qkv, meta.positions, inv_freq, nq, nkv, D,
-                   qn_w if has_norm else None, kn_w if has_norm else None,
-                   rstd if has_norm else None, dqkv, ctx.perm)
+        # the fp32 accumulators straight into dqkv (RoPE / norm backward for
+        # q and k, v converted) in one launch
+        C.rope_bwd_f32(dq_acc, dk_acc, dv_acc, qkv, meta.positions, inv_freq, nq, nkv, D,
+                       qn_w if has_norm else None, kn_w if has_norm else None,
+                       rstd if has_norm else None, dqkv, ctx.perm)
         return dqkv, None, None, None, None, None, None, None, None, None, None, None
 
 
