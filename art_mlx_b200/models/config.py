@@ -128,7 +128,8 @@ class ModelConfig:
         scaling = {k: v for k, v in {**rp, **rs}.items() if k != "rope_theta"}
         if (scaling.get("rope_type") or scaling.get("type") or "default") == "default":
             scaling = {}
-        family = {"qwen3_5_text": "qwen3_5", "qwen3_5_moe_text": "qwen3_5_moe", "gemma4_text": "gemma4"}.get(family, family)
+        aliases = {"qwen3_5_text": "qwen3_5", "qwen3_5_moe_text": "qwen3_5_moe", "gemma4_text": "gemma4"}
+        family = aliases.get(family, family)
         if family == "gemma4":
             return _gemma4_config(d, name)
         num_experts = d.get("num_experts", d.get("num_local_experts", 0)) or 0

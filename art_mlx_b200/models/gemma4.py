@@ -117,9 +117,11 @@ def _rope(x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor) -> torch.T
 def _inv_freq(kind: str, cfg: ModelConfig, device: torch.device) -> torch.Tensor:
     ex = cfg.ex
     if kind == "sliding":
-        typ, base, factor, partial, D = ex["rope_sliding_type"], ex["rope_sliding_theta"], ex["rope_sliding_factor"], 1.0, cfg.head_dim
+        typ, base, factor = ex["rope_sliding_type"], ex["rope_sliding_theta"], ex["rope_sliding_factor"]
+        partial, D = 1.0, cfg.head_dim
     else:
-        typ, base, factor, partial = ex["rope_full_type"], ex["rope_full_theta"], ex["rope_full_factor"], ex["rope_full_partial"]
+        typ, base, factor = ex["rope_full_type"], ex["rope_full_theta"], ex["rope_full_factor"]
+        partial = ex["rope_full_partial"]
         D = ex["global_head_dim"] if typ == "proportional" else cfg.head_dim
     if typ == "proportional":
         # the first int(partial * D / 2) frequencies rotate, the rest are zero
@@ -172,7 +174,8 @@ class Gemma4LM:
         for i in range(L):
             full, D, nkv, k_eq_v, shared, Fm = _layer_dims(cfg, i)
             ly = _G4Layer()
-            ly.index, ly.kind, ly.full, ly.D, ly.nkv, ly.k_eq_v, ly.shared = i, "attention", full, D, nkv, k_eq_v, shared
+            ly.index, ly.kind, ly.full, ly.D = i, "attention", full, D
+            ly.nkv, ly.k_eq_v, ly.shared = nkv, k_eq_v, shared
             ly.window = 0 if full else int(cfg.sliding_window or 0)
             ly.src = _share_source(cfg, i) if shared else i
             nq = cfg.num_attention_heads
@@ -335,7 +338,8 @@ class Gemma4LM:
     # ------------------------------------------------------------------ weights
     def _hf_map(self) -> dict[str, tuple[Any, str]]:
         """HF name -> (holder, attribute or key) of every base tensor."""
-        m: dict[str, tuple[Any, str]] = {"model.embed_tokens.weight": (self, "embed"), "model.norm.weight": (self, "final_norm")}
+        m: dict[str, tuple[Any, str]] = {"model.embed_tokens.weight": (self, "embed"),
+                                         "model.norm.weight": (self, "final_norm")}
         if not self.cfg.tie_word_embeddings:
             m["lm_head.weight"] = (self, "lm_head")
         if self.Hp:

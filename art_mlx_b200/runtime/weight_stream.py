@@ -64,7 +64,8 @@ class LayerWeightStreamer:
         skip = {t.untyped_storage().data_ptr() for t in (st.master, st.compute, st.grad) if t is not None}
         self.model = model
         self.device = dev
-        self.layers: list[list[tuple[torch.Tensor, int, int, tuple, tuple]]] = []  # (tensor, byte offset, nbytes)
+        # per layer: (tensor, byte offset of its storage in the layer's buffer, storage offset, shape, stride)
+        self.layers: list[list[tuple[torch.Tensor, int, int, tuple, tuple]]] = []
         self.host: list[torch.Tensor] = []
         biggest = 0
         for layer in model.layers:
@@ -97,7 +98,6 @@ class LayerWeightStreamer:
         self.ready = [torch.cuda.Event() for _ in range(slots)]
         self.copy_stream = torch.cuda.Stream(dev)
         self.current: int | None = None
-        self.last: int | None = None
         self.bytes_copied = 0
         # the device copies of the base weights are dropped: every view
         # now points at a slot (or at nothing until its layer is brought in)
@@ -137,12 +137,12 @@ class LayerWeightStreamer:
         """Called on entry to layer ``i``: the layer is resident (waited for on
         the compute stream) and the next one in the current direction is on
         its way."""
-        keep = {self.slot_of[self.current]} if self.current is not None and self.slot_of[self.current] is not None else set()
-        s = self._bring(i, keep)
+        cur = None if self.current is None else self.slot_of[self.current]
+        s = self._bring(i, set() if cur is None else {cur})
         self._attach(i, s)
         torch.cuda.current_stream(self.device).wait_event(self.ready[s])
         direction = 0 if self.current is None else (1 if i > self.current else -1)
-        self.last, self.current = self.current, i
+        self.current = i
         nxt = i + (direction or 1)
         if 0 <= nxt < len(self.layers) and len(self.slots) > 1:
             self._bring(nxt, {s})
