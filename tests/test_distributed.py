@@ -280,3 +280,16 @@ def test_cp_hybrid_two_gpus_matches_single_gpu():
     err = (res["master"] - master).norm() / master.norm()
     assert err < 2e-2, err
     assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 2e-2 * max(1.0, abs(metrics["loss/train"]))
+
+
+@pytest.mark.parametrize("cfg_name,tp,cp", [("moe-tiny", 1, 1), ("hybrid-tiny", 1, 4), ("moe-tiny", 1, 2)])
+def test_four_rank_layouts_gloo_match_single_process(cfg_name, tp, cp):
+    """More of the topology matrix at 4 CPU ranks against one process: experts
+    over 4 ranks (one expert each), context parallelism over 4 ranks on the
+    hybrid model (gated-DeltaNet summaries through three hand-offs), and CP 2
+    with the experts over all 4 ranks."""
+    res = _run(4, "gloo", cfg_name, tp_size=tp, cp_size=cp)
+    master, metrics, _ = _single(torch.device("cpu"), CONFIGS[cfg_name], "gloo")
+    err = (res["master"] - master).norm() / master.norm()
+    assert err < 1e-5, err
+    assert abs(res["metrics"]["loss/train"] - metrics["loss/train"]) < 1e-5
