@@ -301,6 +301,11 @@ class Gemma4LM:
             x = self._layer(ly, x, meta, pos, ple, kv, ctx)
         return _rms(x, self.final_norm, self.cfg.rms_norm_eps)
 
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        """Soft-capped logits ``cap * tanh(h W^T / cap)`` (fp32)."""
+        z = (h @ self.lm_head.t()).float()
+        return torch.tanh(z / self.softcap) * self.softcap if self.softcap else z
+
     def token_logprobs_hidden(self, h: torch.Tensor, targets: torch.Tensor, chunk: int = 4096,
                               entropy: bool = True) -> tuple[torch.Tensor, torch.Tensor | None]:
         """``log softmax(softcap(h W^T))[target]`` per row (fp32) and the

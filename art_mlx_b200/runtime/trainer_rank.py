@@ -220,13 +220,29 @@ class TrainerRank:
             ctx = {"group_ids": None if inp.group_ids is None else torch.tensor(list(inp.group_ids)),
                    "parent_ids": None if inp.parent_ids is None else torch.tensor(list(inp.parent_ids))}
             grad = self._active is None and torch.is_grad_enabled()
-            W = self.tr.model.lm_head
+            model = self.tr.model
+            W = model.lm_head
+            # families with their own logits (Gemma-4 soft-caps them) provide them
+            own_lp = getattr(model, "token_logprobs_hidden", None)
+            own_logits = getattr(model, "logits", None)
             with self._adapter(), torch.set_grad_enabled(grad):
-                h = self.tr.model.forward(toks.to(dev), meta, ctx)
+                h = model.forward(toks.to(dev), meta, ctx)
                 hs = h.index_select(0, sel.to(dev))
-                lp, ent = fused.lm_head_logprobs(hs, W, targets, self.tr.logprob_chunk, inp.entropy)
-                logits = hs @ W.t() if inp.logits else None
-            topk = top_k_logprobs(hs.detach(), W, inp.top_k) if inp.top_k else None
+                if own_lp is not None:
+                    lp, ent = own_lp(hs, targets, self.tr.logprob_chunk, inp.entropy)
+                else:
+                    lp, ent = fused.lm_head_logprobs(hs, W, targets, self.tr.logprob_chunk, inp.entropy)
+                logits = None
+                if inp.logits:
+                    logits = own_logits(hs) if own_logits is not None else hs @ W.t()
+            topk = None
+            if inp.top_k:
+                if own_logits is not None:
+                    with torch.no_grad():
+                        v, i = torch.log_softmax(own_logits(hs.detach()).float(), -1).topk(inp.top_k, dim=-1)
+                    topk = TopK(logprobs=v, tokens=i)
+                else:
+                    topk = top_k_logprobs(hs.detach(), W, inp.top_k)
             outs.append(ForwardOutput(logprobs=lp, entropy=ent, targets=targets, top_k=topk, logits=logits,
                                       hidden_states=hs if inp.hidden_states else None))
         return outs

@@ -100,3 +100,16 @@ def test_gemma4_step_gpu_matches_cpu_fp32():
     # the gradient (Adam's first update is close to its sign, too noisy a check in bf16)
     assert abs(mg["loss/grad_norm"] - mc["loss/grad_norm"]) < 0.1 * mc["loss/grad_norm"]
     assert torch.isfinite(tg.store.master).all()
+
+
+def test_trainer_rank_outputs_use_the_soft_capped_logits():
+    from art_mlx_b200.runtime.trainer_rank import ForwardInput, TrainerRank
+
+    tr = GRPOTrainer(_cfg(), LoRASpec(r=4, alpha=8), "cpu", seed=0)
+    rank = TrainerRank(tr)
+    toks = torch.randint(0, 512, (20,)).tolist()
+    out = rank.forward([ForwardInput(tokens=toks, top_k=3, logits=True)])[0]
+    ref = torch.log_softmax(out.logits.detach(), -1)
+    assert out.logits.abs().max() <= 30.0 + 1e-4  # capped
+    assert torch.allclose(out.logprobs.detach(), ref.gather(-1, out.targets.unsqueeze(-1)).squeeze(-1), atol=1e-5)
+    assert torch.allclose(out.top_k.logprobs, ref.topk(3, dim=-1).values, atol=1e-5)
