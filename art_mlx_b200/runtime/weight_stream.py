@@ -29,26 +29,45 @@ from typing import Any
 
 import torch
 
+from art_mlx_b200.ops.fused import LoRABinding
 
-def _collect(obj: Any, skip: set[int], seen: set[int], out: list[torch.Tensor]) -> None:
+
+def _collect(obj: Any, skip: set[int], seen: set[int], out: list[torch.Tensor], dev_type: str = "cuda") -> None:
+    """Append to ``out`` every tensor on ``dev_type`` reachable from ``obj``
+    whose storage is not in ``skip``.  LoRA bindings are not entered: they
+    hold views of the adapter store and caches derived from it, which change
+    with every optimizer step and are not frozen weights."""
     if isinstance(obj, torch.Tensor):
-        if obj.is_cuda and id(obj) not in seen and obj.untyped_storage().data_ptr() not in skip:
+        if obj.device.type == dev_type and id(obj) not in seen and obj.untyped_storage().data_ptr() not in skip:
             seen.add(id(obj))
             out.append(obj)
         return
+    if isinstance(obj, LoRABinding):
+        return
     if isinstance(obj, (list, tuple)):
         for x in obj:
-            _collect(x, skip, seen, out)
+            _collect(x, skip, seen, out, dev_type)
         return
     if isinstance(obj, dict):
         for x in obj.values():
-            _collect(x, skip, seen, out)
+            _collect(x, skip, seen, out, dev_type)
         return
     if hasattr(obj, "__dict__") and not isinstance(obj, (type, torch.nn.Module, torch.device)):
         for k, x in vars(obj).items():
             if k in ("ep", "etp", "cfg"):  # contexts shared by every layer stay where they are
                 continue
-            _collect(x, skip, seen, out)
+            _collect(x, skip, seen, out, dev_type)
+
+
+def base_tensors(model: Any, layer: Any, dev_type: str = "cuda") -> list[torch.Tensor]:
+    """The frozen base tensors of one decoder layer: everything the layer
+    reaches on the device except views of the model's LoRA store."""
+    st = model.store
+    held = (getattr(st, k, None) for k in ("master", "compute", "grad", "exp_avg", "exp_avg_sq"))
+    skip = {t.untyped_storage().data_ptr() for t in held if isinstance(t, torch.Tensor)}
+    out: list[torch.Tensor] = []
+    _collect(layer, skip, set(), out, dev_type)
+    return out
 
 
 class LayerWeightStreamer:
@@ -60,8 +79,6 @@ class LayerWeightStreamer:
         dev = model.device
         if dev.type != "cuda":
             raise RuntimeError("weight streaming moves device weights; the model is on the CPU")
-        st = model.store
-        skip = {t.untyped_storage().data_ptr() for t in (st.master, st.compute, st.grad) if t is not None}
         self.model = model
         self.device = dev
         # per layer: (tensor, byte offset of its storage in the layer's buffer, storage offset, shape, stride)
@@ -69,8 +86,7 @@ class LayerWeightStreamer:
         self.host: list[torch.Tensor] = []
         biggest = 0
         for layer in model.layers:
-            ts: list[torch.Tensor] = []
-            _collect(layer, skip, set(), ts)
+            ts = base_tensors(model, layer)
             # one entry per storage: views of one storage move together
             by_storage: dict[int, list[torch.Tensor]] = {}
             for t in ts:

@@ -12,6 +12,36 @@ from art_mlx_b200.runtime.trainer import GRPOTrainer
 from test_distributed import CONFIGS, GPU_CFG, _packed, _shape
 
 
+@pytest.mark.parametrize("name", ["tiny-qwen3", "moe-tiny"])
+def test_base_tensors_exclude_the_adapter(name):
+    """What a layer's host buffer would hold: its frozen matrices, never a
+    view of the LoRA store nor the caches its bindings derive from the store
+    (those change with every optimizer step)."""
+    from art_mlx_b200.ops.fused import LoRABinding
+    from art_mlx_b200.runtime.weight_stream import base_tensors
+
+    cfg = CONFIGS.get(name) or get_config(name)
+    tr = GRPOTrainer(cfg, LoRASpec(r=4, alpha=8), "cpu", seed=0)
+    tr.train_step(_packed(*_shape("gloo", cfg)), 1e-3, {})  # fills the bindings' caches
+    st = tr.store
+    store_ptrs = {t.untyped_storage().data_ptr() for t in (st.master, st.compute, st.grad, st.exp_avg, st.exp_avg_sq)}
+    layer = tr.model.layers[0]
+    caches = set()
+    for obj in vars(layer).values():
+        for b in (obj if isinstance(obj, (list, tuple)) else [obj]):
+            if isinstance(b, LoRABinding):
+                caches |= {id(getattr(b, k, None)) for k in ("_bd", "_bd_s", "_at_s", "_bdt")}
+    ts = base_tensors(tr.model, layer, "cpu")
+    assert ts and not any(t.untyped_storage().data_ptr() in store_ptrs for t in ts)
+    assert not any(id(t) in caches for t in ts)
+    ids = {id(t) for t in ts}
+    assert id(layer.qkv_w) in ids and id(layer.o_w) in ids
+    if layer.moe is not None:
+        assert id(layer.moe.gu_w_t) in ids and id(layer.moe.down_w_t) in ids and id(layer.moe.router_w) in ids
+    else:
+        assert id(layer.mlp.gu_w) in ids and id(layer.mlp.down_w) in ids
+
+
 def test_streaming_needs_a_gpu_model():
     tr = GRPOTrainer(get_config("tiny-qwen3"), LoRASpec(r=4, alpha=8), "cpu", seed=0)
     with pytest.raises(RuntimeError):
