@@ -119,7 +119,7 @@ def write_kernel_table(path: str, events, rank: int) -> None:
             f.write(f"{100 * d / busy:.2f}\t{d / 1e3:.2f}\t{n}\t{name[:160]}\n")
 
 
-BASELINE_VALUE = None  # BASELINE.md publishes no GPU number for this metric
+BASELINE_VALUE = None  # the reference publishes no GPU number for this metric
 METRIC = "trained tokens/sec per GRPO step (whole box, device-timed, max over ranks) 1/2/4/8 B200"
 
 
