@@ -161,3 +161,31 @@ def test_train_on_groups_steps_the_adapter(tmp_path):
     D.train_on_groups(c, groups, Tok(), learning_rate=1e-3)
     c.load_state("a")
     assert torch.equal(tr.store.master, saved)
+
+
+def test_a_langgraph_rollout_trains_through_the_datum_client():
+    """Choices built from LangChain response metadata carry token ids the
+    datum path reads, so an agent rollout trains without conversion code."""
+    import asyncio
+
+    from art_mlx_b200 import langgraph as lg
+    from test_langgraph import FakeChat, FakeModel, Msg
+
+    def ai(ids):
+        lp = {"content": [{"token": f"token_id:{t}", "logprob": -0.7, "bytes": None, "top_logprobs": []}
+                          for t in ids]}
+        return Msg("ai", "ok", response_metadata={"logprobs": lp, "finish_reason": "stop"})
+
+    async def rollout(ids, reward):
+        await lg.init_chat_model(FakeChat([ai(ids)])).ainvoke([Msg("human", "hi")])
+        return Trajectory(reward=reward)
+
+    w = lg.wrap_rollout(FakeModel(), rollout, log_dir=None)
+    trajs = [asyncio.run(w([5, 6, 7], 0.0)), asyncio.run(w([8, 9], 1.0))]
+    ds = D.trajectory_groups_to_datums([TrajectoryGroup(trajs)], Tok())
+    assert [d.target_tokens[-3:] for d in ds] == [[5, 6, 7], [9, 8, 9]]
+    assert ds[0].logprobs[-1] == pytest.approx(-0.7)
+    tr, c = _client()
+    before = tr.store.master.clone()
+    m = D.train_on_groups(c, [TrajectoryGroup(trajs)], Tok(), learning_rate=1e-3, loss_fn="ppo")
+    assert m["data/step_num_datums"] == 2 and not torch.equal(before, tr.store.master)
