@@ -41,7 +41,10 @@ class ForwardInput:
     tokens: Sequence[int]
     # positions t whose next token (tokens[t+1]) is scored; default: all but the last
     score_positions: Sequence[int] | None = None
-    # prefix-tree rows: per-token group / parent ids (None: one plain sequence)
+    # prefix-tree rows: per-token group / parent ids (None: one plain sequence).  The target of a
+    # scored position is the next token of the ROW, so every branch must repeat the token its
+    # first target is predicted from: pack with at most ``prompt_length - 1`` tokens shareable
+    # (``prefix_tree_pack(..., shareable_lengths=[P - 1, ...])``), never the whole prompt
     group_ids: Sequence[int] | None = None
     parent_ids: Sequence[int] | None = None
     positions: Sequence[int] | None = None
