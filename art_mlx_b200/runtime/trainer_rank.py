@@ -219,6 +219,12 @@ class TrainerRank:
             meta = AttnMeta.build(pos, kend, dev)
             sp = list(inp.score_positions) if inp.score_positions is not None else list(range(T - 1))
             sel = torch.tensor(sp, dtype=torch.long)
+            if inp.group_ids is not None:
+                # the target at t is the row token t + 1, which must be t's own continuation
+                cut = sel[(sel + 1) >= kend.index_select(0, sel).long()]
+                if cut.numel():
+                    raise ValueError(f"scored positions {cut.tolist()[:8]} end a branch of the prefix tree: the "
+                                     f"next row token is not their continuation")
             targets = toks[sel + 1].to(dev)
             ctx = {"group_ids": None if inp.group_ids is None else torch.tensor(list(inp.group_ids)),
                    "parent_ids": None if inp.parent_ids is None else torch.tensor(list(inp.parent_ids))}

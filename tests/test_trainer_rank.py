@@ -1,6 +1,7 @@
 """Low-level per-rank API: custom loss through autograd-attached logprobs,
 optimizer steps, LoRA slots (snapshot, save, load, base)."""
 
+import pytest
 import torch
 
 from art_mlx_b200.models.config import LoRASpec, get_config
@@ -84,3 +85,20 @@ def test_extra_outputs_checkpoint_slots_and_planner(tmp_path):
     assert plan_micro_batches([10, 10, 10, 50, 5], 25 * 4, 4) == [[0, 1], [2], [3], [4]]
     groups = list(rank.forward_micro_batches([ForwardInput(tokens=seq), ForwardInput(tokens=seq[:20])]))
     assert sum(len(g) for g, _ in groups) == 2
+
+
+def test_prefix_tree_rows_refuse_positions_that_end_a_branch():
+    """A scored position is valid only if the next row token continues it."""
+    from art_mlx_b200.preprocessing.prefix_tree import prefix_tree_pack
+
+    tr = GRPOTrainer(get_config("tiny-qwen3"), LoRASpec(r=4, alpha=8), "cpu", seed=0)
+    rank = TrainerRank(tr)
+    p = torch.tensor([1, 2, 3, 4])
+    a, b = torch.cat([p, torch.tensor([10, 11])]), torch.cat([p, torch.tensor([20, 21, 22])])
+    pk = prefix_tree_pack([a, b], max_depth=8, shareable_lengths=[3, 3])  # last prompt token in each branch
+    row = dict(tokens=pk.tokens[0].tolist(), group_ids=pk.group_ids[0].tolist(),
+               parent_ids=pk.parent_ids[0].tolist(), positions=pk.position_ids[0].tolist())
+    ok = rank.forward([ForwardInput(score_positions=[3, 4, 6, 7, 8], **row)])[0]
+    assert ok.targets.tolist() == [10, 11, 20, 21, 22]
+    with pytest.raises(ValueError):
+        rank.forward([ForwardInput(score_positions=[4, 5], **row)])  # 5 ends branch one; row token 6 is not its
